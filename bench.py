@@ -1,0 +1,386 @@
+#!/usr/bin/env python3
+"""Benchmark of the Q8_0 / Q4_0 GGML_OP_MUL_MAT hot path on B200.
+
+Workload (a "step" = one pass over it):
+    fc1  Q4_0 weight [4096 out x 1024 in],  x = N(0,1)        [4096 tokens x 1024]
+    fc2  Q4_0 weight [1024 out x 4096 in],  x = GELU(N(0,1))  [4096 tokens x 4096]
+    kv   Q8_0 weight [1024 out x 1024 in],  x = N(0,1)        [1374 tokens x 1024]
+each = activation quantize (fp32 -> Q8_0) + tcgen05 int8 block GEMM, weights
+~ N(0, 0.02) quantized once (ggml reference quantizer) and packed once on the
+device (the buffer-type upload), as a model's weights are.
+Metric: effective TOPS = sum 2*M*N*K / device time (int8 MACs count 2 ops).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b2q|reference]
+
+N > 1 runs under torchrun, one rank per GPU, each an independent replica of the
+workload (the path has no exchange step): "scaling": "weak", value = all ranks'
+ops / max-over-ranks device time.  --impl reference times the CPU
+implementation of the same path (the oracle's vectorised port of ggml's CPU
+mul_mat; ggml itself is absent from the reference checkout) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "sam-3d-objects-ggml_b200"))
+sys.path.insert(0, os.path.join(REPO, "oracle"))
+
+import numpy as np  # noqa: E402
+
+METRIC = "Q8_0/Q4_0 mul_mat effective TOPS"
+UNIT = "TOPS"
+INT8_SPEC_TOPS = 4500.0  # B200 dense int8 tensor peak (public spec)
+WORKLOAD = [
+    # name, wtype, M (tokens), N (out), K (in), gelu input
+    ("fc1_q4_0", 2, 4096, 4096, 1024, False),
+    ("fc2_q4_0", 2, 4096, 1024, 4096, True),
+    ("kv_q8_0", 8, 1374, 1024, 1024, False),
+]
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+
+
+def ops_of(M, N, K):
+    return 2.0 * M * N * K
+
+
+def config_dict():
+    return {
+        "workload": "configs[1]: fc1 Q4_0 4096x1024->4096, fc2 Q4_0 4096x4096->1024 (GELU in), "
+                    "kv Q8_0 1374x1024->1024; activation quantize + int8 block GEMM each",
+        "weights": "N(0,0.02) -> ggml reference quantizer, packed once on device",
+        "activations": "N(0,1) fp32 (fc2: GELU-tanh of N(0,1)), seed 1234",
+        "act_quantizer": "ggml-cpu x86 from_float semantics (B2Q_ACT_X86)",
+        "l2": "flushed between steps (256 MiB write, outside the per-step events)",
+        "parallelism": "replicas (one independent workload per GPU)",
+    }
+
+
+def make_inputs(seed=1234):
+    import oracle as O
+    from_gelu = None
+    rng = np.random.default_rng(seed)
+    out = []
+    for name, wtype, M, N, K, gelu in WORKLOAD:
+        w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+        x = rng.standard_normal((M, K)).astype(np.float32)
+        if gelu:
+            x64 = x.astype(np.float64)
+            x = (0.5 * x64 * (1.0 + np.tanh(0.7978845608028654 * (x64 + 0.044715 * x64 ** 3)))).astype(np.float32)
+        out.append((name, wtype, M, N, K, O.quantize(w, wtype), x))
+    del from_gelu
+    return out
+
+
+# --------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._period = period_s
+        self._h = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            import torch
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
+            try:
+                self._h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            except Exception:
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._nv = pynvml
+        except Exception as e:  # noqa: BLE001
+            self.error = f"nvml unavailable: {e}"
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            except Exception:
+                pass
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._h is not None:
+            self._t.join()
+
+    def summary(self):
+        if self._h is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": getattr(self, "error", "")}
+        rs = [v for k, v in self.REASONS.items() if self.reasons & k and k != 0x1]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": rs, "samples": len(self.samples),
+                "source": "nvml, sampled every 5 ms during the timed region"}
+
+
+# -------------------------------------------------------------------- GPU arm
+def run_gpu(args, rank, world, local_rank):
+    import torch
+    import b2q
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    stream = torch.cuda.current_stream()
+    inputs = make_inputs()
+    gemms = []
+    for name, wtype, M, N, K, wq, x in inputs:
+        w_raw = torch.from_numpy(wq).to(dev)
+        packed = b2q.weight_pack(wtype, w_raw, K)
+        x_host = torch.from_numpy(x).pin_memory()
+        x_dev = x_host.to(dev)
+        act = b2q._empty_aligned(b2q.act_prepared_size(M, K), dev)
+        y_dev = torch.empty((M, N), dtype=torch.float32, device=dev)
+        y_host = torch.empty((M, N), dtype=torch.float32).pin_memory()
+        ws = b2q.workspace(M, N, K, True, dev)
+        gemms.append(dict(name=name, wtype=wtype, M=M, N=N, K=K, packed=packed, x_host=x_host,
+                          x_dev=x_dev, act=act, y_dev=y_dev, y_host=y_host, ws=ws))
+        del w_raw
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize()
+
+    def step(evs=None):
+        for i, g in enumerate(gemms):
+            b2q.act_prepare(g["x_dev"], out=g["act"], stream=stream)
+            if evs is not None:
+                evs[2 * i + 1].record(stream)
+            b2q.mul_mat_prepared(g["packed"], g["N"], g["K"], g["act"], g["M"], out=g["y_dev"],
+                                 stream=stream)
+            if evs is not None:
+                evs[2 * i + 2].record(stream)
+
+    launches_per_step = 2 * len(gemms)
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+
+    nev = 1 + 2 * len(gemms)
+    all_evs = [[torch.cuda.Event(enable_timing=True) for _ in range(nev)] for _ in range(args.steps)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        for s in range(args.steps):
+            flush.zero_()
+            all_evs[s][0].record(stream)
+            step(all_evs[s])
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    status = b2q.device_status(clear=True)
+    if status:
+        raise RuntimeError(f"device status 0x{status:x}")
+
+    step_ms = [e[0].elapsed_time(e[-1]) for e in all_evs]
+    quant_ms = [[e[2 * i].elapsed_time(e[2 * i + 1]) for e in all_evs] for i in range(len(gemms))]
+    gemm_ms = [[e[2 * i + 1].elapsed_time(e[2 * i + 2]) for e in all_evs] for i in range(len(gemms))]
+    total_ms = sum(step_ms)
+    step_ops = sum(ops_of(g["M"], g["N"], g["K"]) for g in gemms)
+
+    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_total_ms = float(t.item())
+    value = world * step_ops * args.steps / (max_total_ms * 1e-3) / 1e12
+
+    # ---- end to end through the public C ABI, host buffers, copies inside the timing
+    e2e_steps = max(1, min(args.steps, 20))
+    h2d = sum(g["x_host"].numel() * 4 for g in gemms)
+    d2h = sum(g["y_host"].numel() * 4 for g in gemms)
+
+    def e2e_step():
+        for g in gemms:
+            g["x_dev"].copy_(g["x_host"], non_blocking=True)
+            b2q.mul_mat_packed(g["packed"], g["N"], g["K"], g["x_dev"], out=g["y_dev"], ws=g["ws"],
+                               stream=stream)
+            g["y_host"].copy_(g["y_dev"], non_blocking=True)
+
+    for _ in range(min(args.warmup, 3)):
+        e2e_step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = world * step_ops * e2e_steps / (float(t.item()) * 1e-3) / 1e12
+
+    gemm_total_ms = sum(sum(v) for v in gemm_ms)
+    gemm_ops = step_ops * args.steps
+    achieved = gemm_ops / (gemm_total_ms * 1e-3) / 1e12
+    breakdown = []
+    for i, g in enumerate(gemms):
+        gm = statistics.median(gemm_ms[i])
+        qm = statistics.median(quant_ms[i])
+        o = ops_of(g["M"], g["N"], g["K"])
+        breakdown.append({"name": g["name"], "M": g["M"], "N": g["N"], "K": g["K"],
+                          "gemm_us_median": round(gm * 1e3, 2), "quantize_us_median": round(qm * 1e3, 2),
+                          "gemm_tops": round(o / (gm * 1e-3) / 1e12, 1),
+                          "gemm_frac_of_int8_spec": round(o / (gm * 1e-3) / 1e12 / INT8_SPEC_TOPS, 4)})
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    traffic = None
+    try:
+        traffic = json.load(open(os.path.join(REPO, "profiles", "gemm_traffic.json")))
+    except Exception:
+        pass
+    roofline = {
+        "bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05 kind::i8 + per-block scale epilogue)",
+        "achieved": round(achieved, 1), "peak": INT8_SPEC_TOPS, "unit": "TOPS",
+        "frac": round(achieved / INT8_SPEC_TOPS, 4),
+        "peak_source": "B200 dense int8 spec (MEASURED_PEAKS.json has no int8 entry)",
+        "traffic": traffic.get("bytes_per_step") if isinstance(traffic, dict) else None,
+    }
+    if peaks.get("bf16_tflops"):
+        roofline["frac_of_2x_measured_bf16"] = round(achieved / (2 * peaks["bf16_tflops"]), 4)
+
+    result = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(max_total_ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "i8 (int8 x int8 -> int32 per block, fp32 scale epilogue)",
+        "data": "synthetic", "config": config_dict(), "roofline": roofline,
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                "path": "b2q_mul_mat_packed per GEMM, pinned host x -> device -> host y"},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk.summary(), "breakdown": breakdown,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(inputs, budget_s=args.cpu_budget)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+# -------------------------------------------------------------------- CPU arm
+def cpu_sample_run(inputs, frac):
+    """Oracle (vectorised port of ggml's CPU mul_mat) over the first `frac` of
+    each GEMM's token rows; returns (ops, seconds, threads)."""
+    import oracle as O
+    ops, secs, thr = 0.0, 0.0, O.num_threads()
+    for name, wtype, M, N, K, wq, x in inputs:
+        rows = max(1, int(round(M * frac)))
+        xs = np.ascontiguousarray(x[:rows])
+        t0 = time.perf_counter()
+        O.mul_mat(wtype, wq, xs, O.ACT_X86, fast=True)
+        secs += time.perf_counter() - t0
+        ops += ops_of(rows, N, K)
+    return ops, secs, thr
+
+
+def pick_frac(inputs, target_s):
+    ops, secs, _ = cpu_sample_run(inputs, 0.01)
+    full_ops = sum(ops_of(M, N, K) for _, _, M, N, K, _, _ in inputs)
+    rate = ops / max(secs, 1e-6)
+    return min(1.0, max(0.01, target_s * rate / full_ops))
+
+
+def cpu_baseline(inputs, budget_s=15.0):
+    import oracle as O
+    frac = pick_frac(inputs, budget_s)
+    ops, secs, thr = cpu_sample_run(inputs, frac)
+    return {"value": round(ops / secs / 1e12, 4), "unit": UNIT, "cores": thr, "kind": "port",
+            "isa": O.isa(),
+            "sample": f"first {frac:.3f} of each GEMM's token rows (fc1, fc2, kv), {secs:.1f} s, "
+                      f"oracle port of ggml CPU mul_mat incl. activation quantize"}
+
+
+def run_reference(args):
+    inputs = make_inputs()
+    per_step_s = min(3.0, 150.0 / max(1, args.steps + args.warmup))
+    frac = pick_frac(inputs, per_step_s)
+    for _ in range(args.warmup):
+        cpu_sample_run(inputs, frac)
+    tot_ops, tot_s, thr = 0.0, 0.0, 1
+    for _ in range(args.steps):
+        o, s, thr = cpu_sample_run(inputs, frac)
+        tot_ops += o
+        tot_s += s
+    import oracle as O
+    value = tot_ops / tot_s / 1e12
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(tot_s / args.steps * 1e3, 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "i8", "data": "synthetic",
+        "config": config_dict(),
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": thr, "kind": "port",
+                         "isa": O.isa(),
+                         "sample": f"first {frac:.3f} of each GEMM's token rows per step"},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "ggml (the reference's arithmetic) is an empty submodule in the reference checkout; "
+                "timed is the oracle's vectorised C port of ggml's CPU Q8_0/Q4_0 mul_mat, all host threads",
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["b2q", "reference"], default="b2q")
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return
+    res = run_gpu(args, rank, world, local_rank)
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,159 @@
+/*
+ * b2q.h -- C ABI of the B200 (sm_100a) quantized mul_mat library (libb2q).
+ *
+ * The library replaces, for one operator, the arithmetic that ggml runs when a
+ * cpp_ggml graph evaluates GGML_OP_MUL_MAT with GGUF block-quantized weights:
+ *
+ *     y = ggml_mul_mat(ctx, w, x)      w: ne=[K,N] Q8_0 | Q4_0   (row n contiguous over K)
+ *                                      x: ne=[K,M] F32           (row m contiguous over K)
+ *                                      y: ne=[N,M] F32, y[m*N + n] = sum_k w[n,k] x[m,k]
+ *
+ * reached from gb_linear (cpp_ggml/src/graph_builder.cpp:44-60) at every SS
+ * flow linear (cpp_ggml/src/ss_flow_graph.cpp:85-112) and SLat flow linear
+ * (cpp_ggml/src/slat_flow_graph.cpp:29-40), and exercised directly by
+ * cpp_ggml/src/matmul_backend_test.cpp:36-37.  Semantics are those of the ggml
+ * CPU backend: every x row is quantized to Q8_0 (32 int8 + fp16 scale per
+ * block), then y[m][n] = sum_b fp32(dw[n,b]) * fp32(da[m,b]) * S_b with the
+ * int32 block dot S_b = sum_{i<32} qw * qa  (Q4_0: qw = nibble - 8).
+ *
+ * Conventions
+ *   - All data pointers are DEVICE pointers owned by the caller.  `stream` is a
+ *     cudaStream_t (NULL = legacy default stream).  Compute calls are
+ *     asynchronous, allocate nothing and never synchronise.
+ *   - Row strides are in BYTES, like ggml's nb[1]; a weight may be a row-offset
+ *     view of a larger tensor (cpp_ggml/src/ss_flow_graph.cpp:38-44).
+ *   - Every call returns a b2q_status; nothing aborts, nothing traps on device.
+ *     Device-side waits are bounded; a wait that gives up records a code that
+ *     b2q_device_status() returns.
+ *   - Type ids use ggml's enum ggml_type numbering so a ggml backend can pass
+ *     tensor->type straight through.
+ */
+#ifndef B2Q_H
+#define B2Q_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B2Q_API __attribute__((visibility("default")))
+#else
+#define B2Q_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum b2q_type { B2Q_TYPE_F32 = 0, B2Q_TYPE_Q4_0 = 2, B2Q_TYPE_Q8_0 = 8 };
+
+/* Activation-quantizer variant (fp32 -> Q8_0 rounding).
+ *   B2Q_ACT_X86: the from_float of ggml's CPU backend on x86 (the host the
+ *                reference runs on): inverse scale 127/amax, ties to even.
+ *   B2Q_ACT_REF: ggml's scalar reference quantizer: inverse 1/d, ties away
+ *                from zero. */
+enum b2q_act_variant { B2Q_ACT_X86 = 0, B2Q_ACT_REF = 1 };
+
+enum b2q_status {
+    B2Q_OK = 0,
+    B2Q_ERR_INVALID_ARG = 1,  /* null pointer, negative/zero size, K % 32 != 0, ... */
+    B2Q_ERR_UNSUPPORTED = 2,  /* type combination or device not supported (needs sm_100) */
+    B2Q_ERR_MISALIGNED = 3,   /* pointer or stride violates the stated alignment */
+    B2Q_ERR_WORKSPACE = 4,    /* workspace / packed buffer too small */
+    B2Q_ERR_CUDA = 5,         /* a CUDA runtime call failed (launch, attribute, ...) */
+    B2Q_ERR_DEVICE = 6,       /* a kernel reported a device-side error (bounded wait gave up) */
+    B2Q_ERR_TOO_LARGE = 7     /* size beyond what the entry point supports */
+};
+
+B2Q_API const char* b2q_status_string(int status);
+B2Q_API const char* b2q_version(void);
+
+/* ------------------------------------------------------------ quantize
+ * fp32 rows -> ggml block_q8_0 rows (34 bytes per 32 values).
+ * Replaces the CPU backend's from_float for GGML_TYPE_Q8_0, which ggml's CPU
+ * mul_mat applies to every src1 row before the dot products (the conversion
+ * noted at cpp_ggml/src/matmul_backend_test.cpp:171-174).
+ * x: nrows rows of k floats (x_row_stride_bytes apart, multiple of 4);
+ * y: nrows rows of k/32 blocks (y_row_stride_bytes apart, even).  k % 32 == 0. */
+B2Q_API int b2q_quantize_q8_0(const float* x, int64_t nrows, int64_t k, int64_t x_row_stride_bytes,
+                      void* y, int64_t y_row_stride_bytes, int variant, void* stream);
+
+/* --------------------------------------------------------- weight packing
+ * One-time re-layout of a GGUF weight (Q8_0 or Q4_0 blocks, as loaded by
+ * cpp_ggml/src/gguf_loader.cpp:113-133) into the GEMM's layout: int8 codes
+ * [n][k] (Q4_0 nibbles widened to code-8) and fp32 scales [k/32][ldn].
+ * This is what a ggml buffer type's set_tensor hook runs on upload; the
+ * packed buffer then serves every later mul_mat with that weight. */
+B2Q_API size_t b2q_weight_packed_size(int64_t n, int64_t k);
+B2Q_API int b2q_weight_pack(int wtype, const void* w, int64_t n, int64_t k, int64_t w_row_stride_bytes,
+                    void* packed, size_t packed_bytes, void* stream);
+
+/* --------------------------------------------------------------- mul_mat
+ * Scratch needed by b2q_mul_mat (packed_weight = 0) or b2q_mul_mat_packed
+ * (packed_weight = 1): the Q8_0 activations in the GEMM's layout, plus the
+ * packed weight when it is packed per call. */
+B2Q_API size_t b2q_mul_mat_workspace_size(int64_t m, int64_t n, int64_t k, int packed_weight);
+
+/* GGML_OP_MUL_MAT, src0 = w (Q8_0 | Q4_0 blocks), src1 = x (F32), dst = y (F32):
+ *   y[m][n] = sum_k w[n][k] x[m][k]  (+ bias[n] if bias != NULL: the
+ *   GGML_OP_ADD that gb_linear appends, graph_builder.cpp:58, fused).
+ * Replaces ggml's mul_mat for this type combination on the CPU backend and the
+ * CUDA backend's ggml_cuda_mul_mat dispatch for it (ggml patch
+ * 0001-sam3d-ggml-combined.patch:806-817 routes it to cuBLAS today).
+ * Runs: activation quantize (variant) -> weight pack into workspace ->
+ * tcgen05 int8 block GEMM with the per-block scale epilogue.
+ * Alignment: x rows 16-byte aligned for the vector path (any multiple of 4
+ * works), y 4-byte aligned, workspace 256-byte aligned. */
+B2Q_API int b2q_mul_mat(int wtype, const void* w, int64_t w_row_stride_bytes, int64_t n, int64_t k,
+                const float* x, int64_t m, int64_t x_row_stride_bytes, const float* bias,
+                float* y, int64_t y_row_stride_bytes, int variant, void* workspace,
+                size_t workspace_bytes, void* stream);
+
+/* Same with a weight packed once by b2q_weight_pack (the production path). */
+B2Q_API int b2q_mul_mat_packed(const void* packed, int64_t n, int64_t k, const float* x, int64_t m,
+                       int64_t x_row_stride_bytes, const float* bias, float* y,
+                       int64_t y_row_stride_bytes, int variant, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------- two-phase form of mul_mat
+ * ggml's CPU mul_mat first converts all of src1 to Q8_0 into its work buffer
+ * (from_float into params->wdata), then runs the dots.  The same two phases
+ * as separate calls: one prepared activation can feed several mul_mats that
+ * share an input (the q / k / v row views of one fused qkv weight,
+ * cpp_ggml/src/ss_flow_graph.cpp:241-245), and each kernel can be timed alone.
+ * The prepared buffer holds int8 codes [m][k] and fp32 scales [k/32][ldm]. */
+B2Q_API size_t b2q_act_prepared_size(int64_t m, int64_t k);
+B2Q_API int b2q_act_prepare(const float* x, int64_t m, int64_t k, int64_t x_row_stride_bytes,
+                            int variant, void* act, size_t act_bytes, void* stream);
+B2Q_API int b2q_mul_mat_prepared(const void* packed, int64_t n, int64_t k, const void* act,
+                                 int64_t m, const float* bias, float* y,
+                                 int64_t y_row_stride_bytes, void* stream);
+
+/* ------------------------------------------------------------ debug / check
+ * int32 per-block dot products S_b computed by the tensor-core GEMM itself
+ * (the value its epilogue reads from tensor memory), for parity checks:
+ *   dots[(m*n_rows + n)*(k/32) + b] = S_b(weight row n, activation row m).
+ * a: Q8_0 activation blocks (ggml layout, a_row_stride_bytes apart).
+ * Requires m*n*(k/32) <= 2^28.  No counterpart exists in ggml (its vec_dot
+ * keeps S_b in registers); this exposes the int8 MMA's exact results. */
+B2Q_API int b2q_block_dots(int wtype, const void* w, int64_t w_row_stride_bytes, int64_t n, int64_t k,
+                   const void* a, int64_t m, int64_t a_row_stride_bytes, int32_t* dots,
+                   void* workspace, size_t workspace_bytes, void* stream);
+B2Q_API size_t b2q_block_dots_workspace_size(int64_t m, int64_t n, int64_t k);
+
+/* Plain CUDA-core kernel with ggml's x86 accumulation order (8 fp32 lanes of
+ * 4-product int32 partials, pairwise lane reduction): bit-exact fp32 output
+ * for the CPU backend's mul_mat on pre-quantized activations.  A reference
+ * path for checks, not a fast path.  a: Q8_0 activation blocks. */
+B2Q_API int b2q_mul_mat_q_simt(int wtype, const void* w, int64_t w_row_stride_bytes, int64_t n,
+                       int64_t k, const void* a, int64_t m, int64_t a_row_stride_bytes,
+                       float* y, int64_t y_row_stride_bytes, void* stream);
+
+/* Device status word written by kernels whose bounded waits gave up:
+ * *code = 0 when none; clear != 0 resets it.  Synchronises the device. */
+B2Q_API int b2q_device_status(unsigned int* code, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2Q_H */

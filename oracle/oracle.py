@@ -1,0 +1,169 @@
+"""ctypes view of the CPU oracle (``oracle/_build/libb2q_oracle.so``).
+
+TEST INFRASTRUCTURE ONLY: imported by ``tests/``, ``__graft_entry__.smoke()``
+and the ``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` as the
+checker.  The product library never loads it.
+
+The oracle restates ggml's Q8_0 / Q4_0 ``GGML_OP_MUL_MAT`` on the CPU backend
+(ggml v0.21.0, pinned by the reference at cpp_ggml/CMakeLists.txt:126; the
+submodule is empty in the reference checkout).  Weight quantizers and the
+scalar Q8_0 quantizer are pinned byte-for-byte against gguf-py 0.19.0
+(``gguf.quants``), the reference converter's dependency
+(cpp_ggml/scripts/gguf_schema.py:11, cpp_ggml/scripts/gguf_torch_loader.py:26).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "libb2q_oracle.so")
+
+QK = 32
+TYPE_F32, TYPE_Q4_0, TYPE_Q8_0 = 0, 2, 8
+ACT_X86, ACT_REF = 0, 1
+BLOCK_BYTES = {TYPE_Q8_0: 34, TYPE_Q4_0: 18}
+
+_lib = None
+
+
+def build() -> str:
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        P, I64, I = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+        L.b2q_orc_fp32_to_fp16.restype = ctypes.c_uint16
+        L.b2q_orc_fp32_to_fp16.argtypes = [ctypes.c_float]
+        L.b2q_orc_fp16_to_fp32.restype = ctypes.c_float
+        L.b2q_orc_fp16_to_fp32.argtypes = [ctypes.c_uint16]
+        L.b2q_orc_fp32_to_fp16_n.argtypes = [P, P, I64]
+        L.b2q_orc_quantize_rows.argtypes = [I, P, P, I64, I64, I]
+        L.b2q_orc_dequantize_row.argtypes = [I, P, P, I64]
+        L.b2q_orc_vec_dot.restype = ctypes.c_float
+        L.b2q_orc_vec_dot.argtypes = [I, P, P, I64]
+        L.b2q_orc_block_dots.argtypes = [I, P, I64, I64, P, I64, I64, I64, P]
+        L.b2q_orc_mul_mat_q.argtypes = [I, P, I64, I64, P, I64, I64, I64, P, I64, I]
+        L.b2q_orc_mul_mat.argtypes = [I, P, I64, I64, P, I64, I64, I64, I, P, I64, I]
+        L.b2q_orc_mul_mat.restype = I
+        L.b2q_orc_mul_mat_q_fast.argtypes = [I, P, I64, I64, P, I64, I64, I64, P, I64, I]
+        L.b2q_orc_mul_mat_q_fast.restype = I
+        L.b2q_orc_mul_mat_fast.argtypes = [I, P, I64, I64, P, I64, I64, I64, I, P, I64, I]
+        L.b2q_orc_mul_mat_fast.restype = I
+        L.b2q_orc_mul_mat_f64.argtypes = [I, P, I64, I64, P, I64, I64, I64, P]
+        L.b2q_orc_philox4x32_10.argtypes = [ctypes.c_uint64, ctypes.c_uint64, P]
+        L.b2q_orc_fill_normal.argtypes = [P, I64, ctypes.c_uint64, ctypes.c_float, ctypes.c_float]
+        L.b2q_orc_num_threads.restype = I
+        L.b2q_orc_isa.restype = ctypes.c_char_p
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def fp32_to_fp16_bits(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=np.uint16)
+    lib().b2q_orc_fp32_to_fp16_n(_p(x), _p(out), x.size)
+    return out
+
+
+def quantize(x: np.ndarray, wtype: int, act_variant: int | None = None) -> np.ndarray:
+    """Quantize rows of ``x`` [rows, K] into ggml blocks [rows, K/32*bytes] (uint8).
+
+    ``act_variant`` None -> the ggml reference quantizer (weights);
+    ACT_X86 / ACT_REF -> the activation quantizer variant (Q8_0 only).
+    """
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, k = x.shape
+    assert k % QK == 0
+    out = np.empty((rows, k // QK * BLOCK_BYTES[wtype]), dtype=np.uint8)
+    v = -1 if act_variant is None else int(act_variant)
+    lib().b2q_orc_quantize_rows(wtype, _p(x), _p(out), rows, k, v)
+    return out
+
+
+def dequantize(q: np.ndarray, wtype: int, k: int) -> np.ndarray:
+    q = np.ascontiguousarray(q, dtype=np.uint8)
+    rows = q.shape[0]
+    out = np.empty((rows, k), dtype=np.float32)
+    for r in range(rows):
+        lib().b2q_orc_dequantize_row(wtype, _p(q[r]), _p(out[r]), k)
+    return out
+
+
+def block_dots(wtype: int, w: np.ndarray, a: np.ndarray, K: int) -> np.ndarray:
+    """int32 [M, N, K/32]: per-block dot products of weight rows and Q8_0 activation rows."""
+    w = np.ascontiguousarray(w)
+    a = np.ascontiguousarray(a)
+    N, M = w.shape[0], a.shape[0]
+    out = np.empty((M, N, K // QK), dtype=np.int32)
+    lib().b2q_orc_block_dots(wtype, _p(w), w.shape[1], N, _p(a), a.shape[1], M, K, _p(out))
+    return out
+
+
+def mul_mat_q(wtype: int, w: np.ndarray, a: np.ndarray, K: int, nthreads: int = 0,
+              fast: bool = False) -> np.ndarray:
+    """Y [M, N] fp32 from weight blocks [N, .] and Q8_0 activation blocks [M, .]."""
+    w = np.ascontiguousarray(w)
+    a = np.ascontiguousarray(a)
+    N, M = w.shape[0], a.shape[0]
+    y = np.empty((M, N), dtype=np.float32)
+    fn = lib().b2q_orc_mul_mat_q_fast if fast else lib().b2q_orc_mul_mat_q
+    fn(wtype, _p(w), w.shape[1], N, _p(a), a.shape[1], M, K, _p(y), N, nthreads)
+    return y
+
+
+def mul_mat(wtype: int, w: np.ndarray, x: np.ndarray, act_variant: int = ACT_X86,
+            nthreads: int = 0, fast: bool = True) -> np.ndarray:
+    """GGML_OP_MUL_MAT(src0 = w blocks [N, .], src1 = x fp32 [M, K]) -> [M, N] fp32."""
+    w = np.ascontiguousarray(w)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M, K = x.shape
+    N = w.shape[0]
+    y = np.empty((M, N), dtype=np.float32)
+    fn = lib().b2q_orc_mul_mat_fast if fast else lib().b2q_orc_mul_mat
+    rc = fn(wtype, _p(w), w.shape[1], N, _p(x), K, M, K, act_variant, _p(y), N, nthreads)
+    if rc < 0:
+        raise MemoryError("oracle mul_mat failed to allocate")
+    return y
+
+
+def mul_mat_f64(wtype: int, w: np.ndarray, a: np.ndarray, K: int) -> np.ndarray:
+    w = np.ascontiguousarray(w)
+    a = np.ascontiguousarray(a)
+    N, M = w.shape[0], a.shape[0]
+    y = np.empty((M, N), dtype=np.float64)
+    lib().b2q_orc_mul_mat_f64(wtype, _p(w), w.shape[1], N, _p(a), a.shape[1], M, K, _p(y))
+    return y
+
+
+def philox(seed: int, counter: int) -> np.ndarray:
+    out = np.empty(4, dtype=np.uint32)
+    lib().b2q_orc_philox4x32_10(seed, counter, _p(out))
+    return out
+
+
+def normal(n: int, seed: int, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    lib().b2q_orc_fill_normal(_p(out), n, seed, mean, std)
+    return out
+
+
+def num_threads() -> int:
+    return lib().b2q_orc_num_threads()
+
+
+def isa() -> str:
+    return lib().b2q_orc_isa().decode()

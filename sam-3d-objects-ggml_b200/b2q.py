@@ -1,0 +1,248 @@
+"""Python view of libb2q's C ABI (include/b2q.h) for tests and the benchmark.
+
+The product is the C-ABI shared library ``lib/libb2q.so``; this module binds it
+with ctypes and uses torch only for device memory and streams.  Function names
+and argument meaning follow the C ABI, which in turn follows ggml's
+``ggml_mul_mat(ctx, w, x)`` contract (cpp_ggml/src/graph_builder.cpp:44-60):
+``w`` is a [N, K] block-quantized weight (rows of ggml blocks), ``x`` a [M, K]
+fp32 activation, the result ``y`` is [M, N] fp32.
+
+There is no fallback: if the library is missing or the device is not sm_100,
+every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import subprocess
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libb2q.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "b2q.h")
+
+TYPE_F32, TYPE_Q4_0, TYPE_Q8_0 = 0, 2, 8
+ACT_X86, ACT_REF = 0, 1
+QK = 32
+BLOCK_BYTES = {TYPE_Q8_0: 34, TYPE_Q4_0: 18}
+
+OK = 0
+STATUS = {
+    0: "OK", 1: "INVALID_ARG", 2: "UNSUPPORTED", 3: "MISALIGNED", 4: "WORKSPACE",
+    5: "CUDA", 6: "DEVICE", 7: "TOO_LARGE",
+}
+
+
+class B2QError(RuntimeError):
+    def __init__(self, fn: str, status: int):
+        self.status = status
+        super().__init__(f"{fn} failed: {STATUS.get(status, status)} ({_lib_obj().b2q_status_string(status).decode()})")
+
+
+_lib = None
+
+
+def build() -> str:
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+def _lib_obj():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(f"{LIB_PATH} is not built (run __graft_entry__.build())")
+        L = ctypes.CDLL(LIB_PATH)
+        P, I64, I, SZ = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
+        sig = {
+            "b2q_status_string": (ctypes.c_char_p, [I]),
+            "b2q_version": (ctypes.c_char_p, []),
+            "b2q_quantize_q8_0": (I, [P, I64, I64, I64, P, I64, I, P]),
+            "b2q_weight_packed_size": (SZ, [I64, I64]),
+            "b2q_weight_pack": (I, [I, P, I64, I64, I64, P, SZ, P]),
+            "b2q_mul_mat_workspace_size": (SZ, [I64, I64, I64, I]),
+            "b2q_mul_mat": (I, [I, P, I64, I64, I64, P, I64, I64, P, P, I64, I, P, SZ, P]),
+            "b2q_mul_mat_packed": (I, [P, I64, I64, P, I64, I64, P, P, I64, I, P, SZ, P]),
+            "b2q_act_prepared_size": (SZ, [I64, I64]),
+            "b2q_act_prepare": (I, [P, I64, I64, I64, I, P, SZ, P]),
+            "b2q_mul_mat_prepared": (I, [P, I64, I64, P, I64, P, P, I64, P]),
+            "b2q_block_dots": (I, [I, P, I64, I64, I64, P, I64, I64, P, P, SZ, P]),
+            "b2q_block_dots_workspace_size": (SZ, [I64, I64, I64]),
+            "b2q_mul_mat_q_simt": (I, [I, P, I64, I64, I64, P, I64, I64, P, I64, P]),
+            "b2q_device_status": (I, [ctypes.POINTER(ctypes.c_uint), I]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def lib():
+    return _lib_obj()
+
+
+def header_functions() -> list[str]:
+    """Names of every function include/b2q.h declares."""
+    text = open(HEADER).read()
+    return re.findall(r"^B2Q_API\s+[\w\s\*]+?\b(b2q_\w+)\s*\(", text, flags=re.M)
+
+
+def _check(fn: str, rc: int) -> None:
+    if rc != OK:
+        raise B2QError(fn, rc)
+
+
+# ----------------------------------------------------------------- torch glue
+def _torch():
+    import torch
+    return torch
+
+
+def _ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream=None) -> int:
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _empty_aligned(nbytes: int, device) -> "object":
+    """uint8 device buffer whose data_ptr is 256-byte aligned (caching allocator
+    blocks are 512-byte aligned; checked anyway)."""
+    torch = _torch()
+    buf = torch.empty(max(nbytes, 1) + 256, dtype=torch.uint8, device=device)
+    off = (-buf.data_ptr()) % 256
+    return buf[off:off + max(nbytes, 1)]
+
+
+def row_bytes(wtype: int, k: int) -> int:
+    return k // QK * BLOCK_BYTES[wtype]
+
+
+def quantize_q8_0(x, variant: int = ACT_X86, out=None, stream=None):
+    """fp32 [M, K] device tensor -> ggml block_q8_0 rows, uint8 [M, K/32*34]."""
+    torch = _torch()
+    assert x.dtype == torch.float32 and x.dim() == 2
+    m, k = x.shape
+    if out is None:
+        out = torch.empty((m, row_bytes(TYPE_Q8_0, k)), dtype=torch.uint8, device=x.device)
+    rc = lib().b2q_quantize_q8_0(_ptr(x), m, k, x.stride(0) * 4, _ptr(out), out.stride(0),
+                                 variant, _stream(stream))
+    _check("b2q_quantize_q8_0", rc)
+    return out
+
+
+def weight_packed_size(n: int, k: int) -> int:
+    return lib().b2q_weight_packed_size(n, k)
+
+
+def weight_pack(wtype: int, w, k: int, stream=None):
+    """Raw ggml weight blocks uint8 [N, row_bytes] -> packed device buffer."""
+    n = w.shape[0]
+    size = weight_packed_size(n, k)
+    packed = _empty_aligned(size, w.device)
+    rc = lib().b2q_weight_pack(wtype, _ptr(w), n, k, w.stride(0), _ptr(packed), size, _stream(stream))
+    _check("b2q_weight_pack", rc)
+    return packed
+
+
+def workspace_size(m: int, n: int, k: int, packed_weight: bool) -> int:
+    return lib().b2q_mul_mat_workspace_size(m, n, k, 1 if packed_weight else 0)
+
+
+def workspace(m: int, n: int, k: int, packed_weight: bool, device):
+    return _empty_aligned(workspace_size(m, n, k, packed_weight), device)
+
+
+def mul_mat(wtype: int, w, x, k: int | None = None, bias=None, variant: int = ACT_X86,
+            out=None, ws=None, stream=None):
+    """ggml_mul_mat(w, x) (+ bias): w raw blocks uint8 [N, >=row_bytes], x fp32 [M, K] -> [M, N]."""
+    torch = _torch()
+    m, kk = x.shape
+    k = kk if k is None else k
+    n = w.shape[0]
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=x.device)
+    if ws is None:
+        ws = workspace(m, n, k, False, x.device)
+    rc = lib().b2q_mul_mat(wtype, _ptr(w), w.stride(0), n, k, _ptr(x), m, x.stride(0) * 4,
+                           _ptr(bias), _ptr(out), out.stride(0) * 4, variant, _ptr(ws), ws.numel(),
+                           _stream(stream))
+    _check("b2q_mul_mat", rc)
+    return out
+
+
+def mul_mat_packed(packed, n: int, k: int, x, bias=None, variant: int = ACT_X86, out=None,
+                   ws=None, stream=None):
+    torch = _torch()
+    m = x.shape[0]
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=x.device)
+    if ws is None:
+        ws = workspace(m, n, k, True, x.device)
+    rc = lib().b2q_mul_mat_packed(_ptr(packed), n, k, _ptr(x), m, x.stride(0) * 4, _ptr(bias),
+                                  _ptr(out), out.stride(0) * 4, variant, _ptr(ws), ws.numel(),
+                                  _stream(stream))
+    _check("b2q_mul_mat_packed", rc)
+    return out
+
+
+def act_prepared_size(m: int, k: int) -> int:
+    return lib().b2q_act_prepared_size(m, k)
+
+
+def act_prepare(x, variant: int = ACT_X86, out=None, stream=None):
+    """fp32 [M, K] -> prepared Q8_0 activations (device buffer, GEMM layout)."""
+    m, k = x.shape
+    size = act_prepared_size(m, k)
+    if out is None:
+        out = _empty_aligned(size, x.device)
+    rc = lib().b2q_act_prepare(_ptr(x), m, k, x.stride(0) * 4, variant, _ptr(out), out.numel(),
+                               _stream(stream))
+    _check("b2q_act_prepare", rc)
+    return out
+
+
+def mul_mat_prepared(packed, n: int, k: int, act, m: int, bias=None, out=None, stream=None):
+    torch = _torch()
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=act.device)
+    rc = lib().b2q_mul_mat_prepared(_ptr(packed), n, k, _ptr(act), m, _ptr(bias), _ptr(out),
+                                    out.stride(0) * 4, _stream(stream))
+    _check("b2q_mul_mat_prepared", rc)
+    return out
+
+
+def block_dots(wtype: int, w, a, k: int, stream=None):
+    """int32 [M, N, K/32] block dots from the tensor-core kernel (a: Q8_0 blocks [M, .])."""
+    torch = _torch()
+    n, m = w.shape[0], a.shape[0]
+    dots = torch.empty((m, n, k // QK), dtype=torch.int32, device=w.device)
+    ws = _empty_aligned(lib().b2q_block_dots_workspace_size(m, n, k), w.device)
+    rc = lib().b2q_block_dots(wtype, _ptr(w), w.stride(0), n, k, _ptr(a), m, a.stride(0),
+                              _ptr(dots), _ptr(ws), ws.numel(), _stream(stream))
+    _check("b2q_block_dots", rc)
+    return dots
+
+
+def mul_mat_q_simt(wtype: int, w, a, k: int, stream=None):
+    """CUDA-core check kernel, ggml x86 accumulation order: y [M, N] fp32."""
+    torch = _torch()
+    n, m = w.shape[0], a.shape[0]
+    y = torch.empty((m, n), dtype=torch.float32, device=w.device)
+    rc = lib().b2q_mul_mat_q_simt(wtype, _ptr(w), w.stride(0), n, k, _ptr(a), m, a.stride(0),
+                                  _ptr(y), y.stride(0) * 4, _stream(stream))
+    _check("b2q_mul_mat_q_simt", rc)
+    return y
+
+
+def device_status(clear: bool = True) -> int:
+    code = ctypes.c_uint(0)
+    rc = lib().b2q_device_status(ctypes.byref(code), 1 if clear else 0)
+    if rc not in (OK, 6):
+        raise B2QError("b2q_device_status", rc)
+    return code.value

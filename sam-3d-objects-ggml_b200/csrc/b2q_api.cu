@@ -1,0 +1,310 @@
+// b2q_api.cu -- the extern "C" boundary (include/b2q.h): argument validation,
+// workspace carving and kernel dispatch.  Host code only; never allocates,
+// never synchronises inside a compute call, returns a status code for every
+// failure instead of aborting.
+#include "../../include/b2q.h"
+#include "b2q_internal.h"
+
+#include <climits>
+#include <cstdint>
+
+namespace {
+
+using namespace b2q;
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Device check: the kernels are built for sm_100a only.
+int check_device(int* sms) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return B2Q_ERR_CUDA;
+  int major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+    return B2Q_ERR_CUDA;
+  if (major != 10 || minor != 0) return B2Q_ERR_UNSUPPORTED;
+  if (sms && cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return B2Q_ERR_CUDA;
+  return B2Q_OK;
+}
+
+int from_cuda(cudaError_t e) { return e == cudaSuccess ? B2Q_OK : B2Q_ERR_CUDA; }
+
+bool valid_wtype(int t) { return t == B2Q_TYPE_Q8_0 || t == B2Q_TYPE_Q4_0; }
+int64_t wblock_bytes(int t) { return t == B2Q_TYPE_Q8_0 ? kQ8Bytes : kQ4Bytes; }
+
+// Common checks of a weight operand in raw ggml block layout.
+int check_raw_weight(int wtype, const void* w, int64_t ldw, int64_t n, int64_t k) {
+  if (!valid_wtype(wtype)) return B2Q_ERR_UNSUPPORTED;
+  if (n < 0 || k <= 0 || k % kQK != 0) return B2Q_ERR_INVALID_ARG;
+  if (n > INT_MAX || k > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (n > 0 && !w) return B2Q_ERR_INVALID_ARG;
+  if (ldw < (k / kQK) * wblock_bytes(wtype)) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(w, 2) || ldw % 2 != 0) return B2Q_ERR_MISALIGNED;
+  return B2Q_OK;
+}
+
+struct Carve {
+  uint8_t* p;
+  size_t left;
+  uint8_t* take(size_t bytes) {
+    if (bytes > left) return nullptr;
+    uint8_t* r = p;
+    p += bytes;
+    left -= bytes;
+    return r;
+  }
+};
+
+SplitOperand split_at(uint8_t* base, int64_t rows, int64_t k) {
+  SplitOperand s;
+  s.codes = reinterpret_cast<const int8_t*>(base);
+  s.scales = reinterpret_cast<const float*>(base + round_up(rows * k, 256));
+  s.rows = rows;
+  s.ld = scale_ld(rows);
+  return s;
+}
+
+int run_gemm(const SplitOperand& w, const SplitOperand& a, int64_t m, int64_t n, int64_t k,
+             float* y, int64_t ldy_floats, const float* bias, int32_t* dots, int sms,
+             cudaStream_t s) {
+  GemmArgs g;
+  g.w = w;
+  g.a = a;
+  g.M = m;
+  g.N = n;
+  g.K = k;
+  g.y = y;
+  g.ldy = ldy_floats;
+  g.bias = bias;
+  g.dots = dots;
+  return from_cuda(launch_gemm_tc(g, sms, s));
+}
+
+// Activation quantize into the split layout + GEMM against a split weight.
+int mul_mat_split(const SplitOperand& w, int64_t n, int64_t k, const float* x, int64_t m,
+                  int64_t ldx, const float* bias, float* y, int64_t ldy, int variant, Carve& ws,
+                  int sms, cudaStream_t s) {
+  uint8_t* abuf = ws.take(split_bytes(m, k));
+  if (!abuf) return B2Q_ERR_WORKSPACE;
+  SplitOperand a = split_at(abuf, m, k);
+  const bool vec4 = aligned(x, 16) && ldx % 16 == 0;
+  cudaError_t e = launch_quantize_q8_0_split(x, m, k, ldx / 4, const_cast<int8_t*>(a.codes),
+                                             const_cast<float*>(a.scales), a.ld, variant, vec4, s);
+  if (e != cudaSuccess) return B2Q_ERR_CUDA;
+  return run_gemm(w, a, m, n, k, y, ldy / 4, bias, nullptr, sms, s);
+}
+
+int check_x_y(const float* x, int64_t m, int64_t k, int64_t ldx, float* y, int64_t n,
+              int64_t ldy, int variant) {
+  if (m < 0 || m > INT_MAX) return m < 0 ? B2Q_ERR_INVALID_ARG : B2Q_ERR_TOO_LARGE;
+  if (variant != B2Q_ACT_X86 && variant != B2Q_ACT_REF) return B2Q_ERR_INVALID_ARG;
+  if (m > 0 && (!x || !y)) return B2Q_ERR_INVALID_ARG;
+  if (ldx < k * 4 || ldy < n * 4) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(x, 4) || ldx % 4 != 0 || !aligned(y, 4) || ldy % 4 != 0) return B2Q_ERR_MISALIGNED;
+  return B2Q_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* b2q_status_string(int status) {
+  switch (status) {
+    case B2Q_OK: return "ok";
+    case B2Q_ERR_INVALID_ARG: return "invalid argument";
+    case B2Q_ERR_UNSUPPORTED: return "unsupported type or device (needs sm_100)";
+    case B2Q_ERR_MISALIGNED: return "misaligned pointer or stride";
+    case B2Q_ERR_WORKSPACE: return "workspace or packed buffer too small";
+    case B2Q_ERR_CUDA: return "CUDA runtime error";
+    case B2Q_ERR_DEVICE: return "device-side error (bounded wait gave up)";
+    case B2Q_ERR_TOO_LARGE: return "size beyond the supported maximum";
+    default: return "unknown status";
+  }
+}
+
+const char* b2q_version(void) { return "b2q 0.1.0 sm_100a"; }
+
+int b2q_quantize_q8_0(const float* x, int64_t nrows, int64_t k, int64_t x_row_stride_bytes,
+                      void* y, int64_t y_row_stride_bytes, int variant, void* stream) {
+  if (nrows < 0 || k <= 0 || k % kQK != 0) return B2Q_ERR_INVALID_ARG;
+  if (variant != B2Q_ACT_X86 && variant != B2Q_ACT_REF) return B2Q_ERR_INVALID_ARG;
+  if (nrows > 0 && (!x || !y)) return B2Q_ERR_INVALID_ARG;
+  if (x_row_stride_bytes < k * 4 || y_row_stride_bytes < (k / kQK) * kQ8Bytes) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(x, 4) || x_row_stride_bytes % 4 != 0 || !aligned(y, 2) || y_row_stride_bytes % 2 != 0)
+    return B2Q_ERR_MISALIGNED;
+  if (int rc = check_device(nullptr)) return rc;
+  const bool vec4 = aligned(x, 16) && x_row_stride_bytes % 16 == 0;
+  return from_cuda(launch_quantize_q8_0_blocks(x, nrows, k, x_row_stride_bytes / 4,
+                                               static_cast<uint8_t*>(y), y_row_stride_bytes,
+                                               variant, vec4, static_cast<cudaStream_t>(stream)));
+}
+
+size_t b2q_weight_packed_size(int64_t n, int64_t k) {
+  if (n < 0 || k <= 0 || k % kQK != 0) return 0;
+  return split_bytes(n, k);
+}
+
+int b2q_weight_pack(int wtype, const void* w, int64_t n, int64_t k, int64_t w_row_stride_bytes,
+                    void* packed, size_t packed_bytes, void* stream) {
+  if (int rc = check_raw_weight(wtype, w, w_row_stride_bytes, n, k)) return rc;
+  if (n > 0 && !packed) return B2Q_ERR_INVALID_ARG;
+  if (packed_bytes < split_bytes(n, k)) return B2Q_ERR_WORKSPACE;
+  if (!aligned(packed, 256)) return B2Q_ERR_MISALIGNED;
+  if (int rc = check_device(nullptr)) return rc;
+  SplitOperand s = split_at(static_cast<uint8_t*>(packed), n, k);
+  return from_cuda(launch_pack_weights(wtype, static_cast<const uint8_t*>(w), n, k, w_row_stride_bytes,
+                                       const_cast<int8_t*>(s.codes), const_cast<float*>(s.scales),
+                                       s.ld, static_cast<cudaStream_t>(stream)));
+}
+
+size_t b2q_mul_mat_workspace_size(int64_t m, int64_t n, int64_t k, int packed_weight) {
+  if (m < 0 || n < 0 || k <= 0 || k % kQK != 0) return 0;
+  return split_bytes(m, k) + (packed_weight ? 0 : split_bytes(n, k));
+}
+
+int b2q_mul_mat_packed(const void* packed, int64_t n, int64_t k, const float* x, int64_t m,
+                       int64_t x_row_stride_bytes, const float* bias, float* y,
+                       int64_t y_row_stride_bytes, int variant, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  if (n < 0 || k <= 0 || k % kQK != 0) return B2Q_ERR_INVALID_ARG;
+  if (n > INT_MAX || k > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (int rc = check_x_y(x, m, k, x_row_stride_bytes, y, n, y_row_stride_bytes, variant)) return rc;
+  if (n > 0 && !packed) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(packed, 256) || !aligned(workspace, 256) || (bias && !aligned(bias, 4)))
+    return B2Q_ERR_MISALIGNED;
+  if (m == 0 || n == 0) return B2Q_OK;
+  if (!workspace) return B2Q_ERR_WORKSPACE;
+  int sms = 0;
+  if (int rc = check_device(&sms)) return rc;
+  Carve ws{static_cast<uint8_t*>(workspace), workspace_bytes};
+  const SplitOperand w = split_at(static_cast<uint8_t*>(const_cast<void*>(packed)), n, k);
+  return mul_mat_split(w, n, k, x, m, x_row_stride_bytes, bias, y, y_row_stride_bytes, variant, ws,
+                       sms, static_cast<cudaStream_t>(stream));
+}
+
+int b2q_mul_mat(int wtype, const void* w, int64_t w_row_stride_bytes, int64_t n, int64_t k,
+                const float* x, int64_t m, int64_t x_row_stride_bytes, const float* bias,
+                float* y, int64_t y_row_stride_bytes, int variant, void* workspace,
+                size_t workspace_bytes, void* stream) {
+  if (int rc = check_raw_weight(wtype, w, w_row_stride_bytes, n, k)) return rc;
+  if (int rc = check_x_y(x, m, k, x_row_stride_bytes, y, n, y_row_stride_bytes, variant)) return rc;
+  if (!aligned(workspace, 256) || (bias && !aligned(bias, 4))) return B2Q_ERR_MISALIGNED;
+  if (m == 0 || n == 0) return B2Q_OK;
+  if (!workspace) return B2Q_ERR_WORKSPACE;
+  int sms = 0;
+  if (int rc = check_device(&sms)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Carve ws{static_cast<uint8_t*>(workspace), workspace_bytes};
+  uint8_t* wbuf = ws.take(split_bytes(n, k));
+  if (!wbuf) return B2Q_ERR_WORKSPACE;
+  const SplitOperand wsplit = split_at(wbuf, n, k);
+  if (launch_pack_weights(wtype, static_cast<const uint8_t*>(w), n, k, w_row_stride_bytes,
+                          const_cast<int8_t*>(wsplit.codes), const_cast<float*>(wsplit.scales),
+                          wsplit.ld, s) != cudaSuccess)
+    return B2Q_ERR_CUDA;
+  return mul_mat_split(wsplit, n, k, x, m, x_row_stride_bytes, bias, y, y_row_stride_bytes, variant,
+                       ws, sms, s);
+}
+
+size_t b2q_act_prepared_size(int64_t m, int64_t k) {
+  if (m < 0 || k <= 0 || k % kQK != 0) return 0;
+  return split_bytes(m, k);
+}
+
+int b2q_act_prepare(const float* x, int64_t m, int64_t k, int64_t x_row_stride_bytes, int variant,
+                    void* act, size_t act_bytes, void* stream) {
+  if (k <= 0 || k % kQK != 0) return B2Q_ERR_INVALID_ARG;
+  if (k > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (m < 0 || m > INT_MAX) return m < 0 ? B2Q_ERR_INVALID_ARG : B2Q_ERR_TOO_LARGE;
+  if (variant != B2Q_ACT_X86 && variant != B2Q_ACT_REF) return B2Q_ERR_INVALID_ARG;
+  if (m > 0 && (!x || !act)) return B2Q_ERR_INVALID_ARG;
+  if (x_row_stride_bytes < k * 4) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(x, 4) || x_row_stride_bytes % 4 != 0 || !aligned(act, 256)) return B2Q_ERR_MISALIGNED;
+  if (act_bytes < split_bytes(m, k)) return B2Q_ERR_WORKSPACE;
+  if (m == 0) return B2Q_OK;
+  if (int rc = check_device(nullptr)) return rc;
+  const SplitOperand a = split_at(static_cast<uint8_t*>(act), m, k);
+  const bool vec4 = aligned(x, 16) && x_row_stride_bytes % 16 == 0;
+  return from_cuda(launch_quantize_q8_0_split(x, m, k, x_row_stride_bytes / 4,
+                                              const_cast<int8_t*>(a.codes),
+                                              const_cast<float*>(a.scales), a.ld, variant, vec4,
+                                              static_cast<cudaStream_t>(stream)));
+}
+
+int b2q_mul_mat_prepared(const void* packed, int64_t n, int64_t k, const void* act, int64_t m,
+                         const float* bias, float* y, int64_t y_row_stride_bytes, void* stream) {
+  if (n < 0 || m < 0 || k <= 0 || k % kQK != 0) return B2Q_ERR_INVALID_ARG;
+  if (n > INT_MAX || m > INT_MAX || k > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (m > 0 && n > 0 && (!packed || !act || !y)) return B2Q_ERR_INVALID_ARG;
+  if (y_row_stride_bytes < n * 4) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(packed, 256) || !aligned(act, 256) || !aligned(y, 4) || y_row_stride_bytes % 4 != 0 ||
+      (bias && !aligned(bias, 4)))
+    return B2Q_ERR_MISALIGNED;
+  if (m == 0 || n == 0) return B2Q_OK;
+  int sms = 0;
+  if (int rc = check_device(&sms)) return rc;
+  const SplitOperand w = split_at(static_cast<uint8_t*>(const_cast<void*>(packed)), n, k);
+  const SplitOperand a = split_at(static_cast<uint8_t*>(const_cast<void*>(act)), m, k);
+  return run_gemm(w, a, m, n, k, y, y_row_stride_bytes / 4, bias, nullptr, sms,
+                  static_cast<cudaStream_t>(stream));
+}
+
+size_t b2q_block_dots_workspace_size(int64_t m, int64_t n, int64_t k) {
+  if (m < 0 || n < 0 || k <= 0 || k % kQK != 0) return 0;
+  return split_bytes(m, k) + split_bytes(n, k);
+}
+
+int b2q_block_dots(int wtype, const void* w, int64_t w_row_stride_bytes, int64_t n, int64_t k,
+                   const void* a, int64_t m, int64_t a_row_stride_bytes, int32_t* dots,
+                   void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_raw_weight(wtype, w, w_row_stride_bytes, n, k)) return rc;
+  if (int rc = check_raw_weight(B2Q_TYPE_Q8_0, a, a_row_stride_bytes, m, k)) return rc;
+  if (m > 0 && n > 0 && !dots) return B2Q_ERR_INVALID_ARG;
+  if (m * n * (k / kQK) > (int64_t(1) << 28)) return B2Q_ERR_TOO_LARGE;
+  if (!aligned(workspace, 256) || !aligned(dots, 4)) return B2Q_ERR_MISALIGNED;
+  if (m == 0 || n == 0) return B2Q_OK;
+  if (!workspace) return B2Q_ERR_WORKSPACE;
+  int sms = 0;
+  if (int rc = check_device(&sms)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Carve ws{static_cast<uint8_t*>(workspace), workspace_bytes};
+  uint8_t* wbuf = ws.take(split_bytes(n, k));
+  uint8_t* abuf = ws.take(split_bytes(m, k));
+  if (!wbuf || !abuf) return B2Q_ERR_WORKSPACE;
+  const SplitOperand ws_ = split_at(wbuf, n, k), as_ = split_at(abuf, m, k);
+  if (launch_pack_weights(wtype, static_cast<const uint8_t*>(w), n, k, w_row_stride_bytes,
+                          const_cast<int8_t*>(ws_.codes), const_cast<float*>(ws_.scales), ws_.ld,
+                          s) != cudaSuccess ||
+      launch_pack_weights(B2Q_TYPE_Q8_0, static_cast<const uint8_t*>(a), m, k, a_row_stride_bytes,
+                          const_cast<int8_t*>(as_.codes), const_cast<float*>(as_.scales), as_.ld,
+                          s) != cudaSuccess)
+    return B2Q_ERR_CUDA;
+  return run_gemm(ws_, as_, m, n, k, nullptr, 0, nullptr, dots, sms, s);
+}
+
+int b2q_mul_mat_q_simt(int wtype, const void* w, int64_t w_row_stride_bytes, int64_t n,
+                       int64_t k, const void* a, int64_t m, int64_t a_row_stride_bytes,
+                       float* y, int64_t y_row_stride_bytes, void* stream) {
+  if (int rc = check_raw_weight(wtype, w, w_row_stride_bytes, n, k)) return rc;
+  if (int rc = check_raw_weight(B2Q_TYPE_Q8_0, a, a_row_stride_bytes, m, k)) return rc;
+  if (m > 0 && n > 0 && !y) return B2Q_ERR_INVALID_ARG;
+  if (y_row_stride_bytes < n * 4) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(y, 4) || y_row_stride_bytes % 4 != 0) return B2Q_ERR_MISALIGNED;
+  if ((m + 7) / 8 > 65535) return B2Q_ERR_TOO_LARGE;
+  if (m == 0 || n == 0) return B2Q_OK;
+  if (int rc = check_device(nullptr)) return rc;
+  return from_cuda(launch_gemm_simt(wtype, static_cast<const uint8_t*>(w), w_row_stride_bytes, n, k,
+                                    static_cast<const uint8_t*>(a), a_row_stride_bytes, m, y,
+                                    y_row_stride_bytes / 4, static_cast<cudaStream_t>(stream)));
+}
+
+int b2q_device_status(unsigned int* code, int clear) {
+  if (!code) return B2Q_ERR_INVALID_ARG;
+  if (int rc = check_device(nullptr)) return rc;
+  if (cudaDeviceSynchronize() != cudaSuccess) return B2Q_ERR_CUDA;
+  if (read_device_status(code, clear != 0) != cudaSuccess) return B2Q_ERR_CUDA;
+  return *code ? B2Q_ERR_DEVICE : B2Q_OK;
+}
+
+}  // extern "C"

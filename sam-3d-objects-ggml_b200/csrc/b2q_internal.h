@@ -1,0 +1,70 @@
+// b2q_internal.h -- shared declarations between the C-ABI layer (b2q_api.cu)
+// and the kernel translation units.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace b2q {
+
+// Device status codes (g_device_status).
+enum : unsigned int {
+  kDevOk = 0,
+  kDevWaitProducer = 0x101,  // TMA producer gave up waiting for a free stage
+  kDevWaitMma = 0x102,       // MMA issuer gave up waiting for data / a free accumulator
+  kDevWaitEpilogue = 0x103,  // epilogue gave up waiting for an accumulator
+  kDevWaitDrain = 0x104,     // teardown gave up waiting for in-flight copies / MMAs
+};
+
+constexpr int kQK = 32;
+constexpr int kQ8Bytes = 34;
+constexpr int kQ4Bytes = 18;
+constexpr int kTypeQ4_0 = 2;
+constexpr int kTypeQ8_0 = 8;
+
+inline int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+// Layout of the GEMM operands in HBM ("split" layout):
+//   codes  int8  [rows][K]          row stride K bytes
+//   scales fp32  [K/32][ld]         ld = round_up(rows, 4)  (16-byte TMA strides)
+struct SplitOperand {
+  const int8_t* codes;
+  const float* scales;
+  int64_t rows;
+  int64_t ld;  // scale row stride in elements
+};
+
+inline int64_t scale_ld(int64_t rows) { return round_up(rows, 4); }
+inline size_t split_bytes(int64_t rows, int64_t k) {
+  return static_cast<size_t>(round_up(rows * k, 256) + round_up((k / kQK) * scale_ld(rows) * 4, 256));
+}
+
+// ---- launchers (return cudaSuccess or the launch error) ----
+cudaError_t launch_quantize_q8_0_blocks(const float* x, int64_t m, int64_t k, int64_t ldx_floats,
+                                        uint8_t* y, int64_t ldy_bytes, int variant, bool vec4,
+                                        cudaStream_t s);
+cudaError_t launch_quantize_q8_0_split(const float* x, int64_t m, int64_t k, int64_t ldx_floats,
+                                       int8_t* codes, float* scales, int64_t ld, int variant,
+                                       bool vec4, cudaStream_t s);
+cudaError_t launch_pack_weights(int wtype, const uint8_t* w, int64_t n, int64_t k,
+                                int64_t ldw_bytes, int8_t* codes, float* scales, int64_t ld,
+                                cudaStream_t s);
+cudaError_t launch_gemm_simt(int wtype, const uint8_t* w, int64_t ldw_bytes, int64_t n, int64_t k,
+                             const uint8_t* a, int64_t lda_bytes, int64_t m, float* y,
+                             int64_t ldy_floats, cudaStream_t s);
+
+struct GemmArgs {
+  SplitOperand w;     // weights: rows = N
+  SplitOperand a;     // activations: rows = M
+  int64_t M, N, K;
+  float* y;           // [M][ldy]
+  int64_t ldy;        // floats
+  const float* bias;  // [N] or nullptr
+  int32_t* dots;      // debug dump [M][N][K/32] or nullptr
+};
+cudaError_t launch_gemm_tc(const GemmArgs& args, int num_sms, cudaStream_t s);
+cudaError_t read_device_status(unsigned int* value, bool clear);
+
+}  // namespace b2q

@@ -1,0 +1,112 @@
+"""C-ABI checks that need no GPU: the library loads, exports every function
+include/b2q.h declares, and rejects bad arguments with status codes before any
+device work (fake, never-dereferenced pointers are passed)."""
+import ctypes
+import os
+import subprocess
+
+import pytest
+
+import b2q
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_library_exports_every_header_function(b2q_mod):
+    names = b2q.header_functions()
+    assert len(names) >= 12, names
+    out = subprocess.run(["nm", "-D", "--defined-only", b2q.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    missing = [n for n in names if n not in exported]
+    assert not missing, missing
+    # nothing else leaks out of the library under a b2q_ name
+    extra = sorted(n for n in exported if n.startswith("b2q_") and n not in names)
+    assert not extra, extra
+
+
+def test_version_and_status_strings(b2q_mod):
+    L = b2q.lib()
+    assert b"sm_100a" in L.b2q_version()
+    for code in range(8):
+        assert L.b2q_status_string(code)
+    assert L.b2q_status_string(99) == b"unknown status"
+
+
+def test_size_queries(b2q_mod):
+    L = b2q.lib()
+    # codes (rounded to 256) + fp32 scales [K/32][round_up(rows, 4)] (rounded to 256)
+    assert L.b2q_weight_packed_size(4096, 1024) == 4096 * 1024 + 32 * 4096 * 4
+    assert L.b2q_weight_packed_size(10, 64) == 768 + 256
+    assert L.b2q_weight_packed_size(10, 33) == 0
+    assert L.b2q_mul_mat_workspace_size(1374, 1024, 1024, 1) == \
+        1374 * 1024 + ((32 * 1376 * 4 + 255) // 256) * 256
+    assert L.b2q_mul_mat_workspace_size(4096, 4096, 1024, 0) == 2 * (4096 * 1024 + 32 * 4096 * 4)
+    assert L.b2q_mul_mat_workspace_size(-1, 4, 32, 0) == 0
+
+
+FAKE = 1 << 20  # aligned, non-null, never dereferenced
+
+
+@pytest.mark.parametrize("args,expect", [
+    # wtype 3 (Q4_1) is not supported
+    (dict(wtype=3), b2q.STATUS and 2),
+    (dict(k=33), 1),                                    # K not a multiple of 32
+    (dict(k=0), 1),
+    (dict(n=-1), 1),
+    (dict(w=0), 1),                                     # null weight with n > 0
+    (dict(ldw=10), 1),                                  # row stride below one row of blocks
+    (dict(ldw=1089), 3),                                # odd weight stride
+    (dict(w=FAKE + 1), 3),                              # weight not 2-byte aligned
+    (dict(x=FAKE + 2), 3),                              # activations not 4-byte aligned
+    (dict(ldx=4 * 1024 - 4), 1),                        # x row stride below K floats
+    (dict(ldy=4 * 64 + 2), 3),                          # y stride not a multiple of 4
+    (dict(variant=5), 1),
+    (dict(ws=FAKE + 128), 3),                           # workspace not 256-byte aligned
+    (dict(m=1 << 33), 7),                               # beyond int range
+])
+def test_mul_mat_argument_validation(b2q_mod, args, expect):
+    a = dict(wtype=8, w=FAKE, ldw=1088, n=64, k=1024, x=FAKE, m=16, ldx=4096, bias=None,
+             y=FAKE, ldy=256, variant=0, ws=FAKE, wsb=1 << 30)
+    a.update(args)
+    rc = b2q.lib().b2q_mul_mat(a["wtype"], a["w"], a["ldw"], a["n"], a["k"], a["x"], a["m"],
+                               a["ldx"], a["bias"], a["y"], a["ldy"], a["variant"], a["ws"],
+                               a["wsb"], None)
+    assert rc == expect
+
+
+def test_quantize_argument_validation(b2q_mod):
+    L = b2q.lib()
+    assert L.b2q_quantize_q8_0(FAKE, 4, 48, 192, FAKE, 34 * 2, 0, None) == 1      # k % 32
+    assert L.b2q_quantize_q8_0(FAKE, 4, 64, 128, FAKE, 34, 0, None) == 1          # y stride small
+    assert L.b2q_quantize_q8_0(FAKE, 4, 64, 256, FAKE + 1, 68, 0, None) == 3      # odd y
+    assert L.b2q_quantize_q8_0(FAKE, 4, 64, 256, FAKE, 68, 2, None) == 1          # variant
+    assert L.b2q_quantize_q8_0(None, 4, 64, 256, FAKE, 68, 0, None) == 1          # null x
+
+
+def test_pack_and_debug_validation(b2q_mod):
+    L = b2q.lib()
+    assert L.b2q_weight_pack(8, FAKE, 64, 1024, 1088, FAKE, 10, None) == 4       # too small
+    assert L.b2q_weight_pack(8, FAKE, 64, 1024, 1088, FAKE + 16, 1 << 24, None) == 3
+    assert L.b2q_weight_pack(1, FAKE, 64, 1024, 1088, FAKE, 1 << 24, None) == 2  # F16 weights
+    # block-dot debug entry refuses outputs beyond 2^28 dots
+    assert L.b2q_block_dots(8, FAKE, 1088, 4096, 1024, FAKE, 4096, 1088, FAKE, FAKE, 1 << 30, None) == 7
+    assert L.b2q_mul_mat_q_simt(8, FAKE, 1088, 64, 1024, FAKE, 1 << 20, 1088, FAKE, 256, None) == 7
+    code = ctypes.c_uint(0)
+    assert L.b2q_device_status(None, 0) == 1
+
+
+def test_empty_shapes_are_noops_without_device(b2q_mod):
+    L = b2q.lib()
+    # m == 0 or n == 0: validated, nothing launched, OK even without a GPU
+    assert L.b2q_mul_mat(8, FAKE, 1088, 64, 1024, FAKE, 0, 4096, None, FAKE, 256, 0, FAKE, 0, None) == 0
+    assert L.b2q_mul_mat_packed(FAKE, 0, 1024, FAKE, 16, 4096, None, FAKE, 0, 0, FAKE, 0, None) == 0
+
+
+def test_header_compiles_as_c(tmp_path):
+    src = tmp_path / "t.c"
+    src.write_text('#include "b2q.h"\nint main(void){return b2q_status_string(0)==0;}\n')
+    r = subprocess.run(["/usr/bin/gcc", "-std=c99", "-Wall", "-Werror", "-c",
+                        "-I", os.path.join(REPO, "include"), str(src), "-o", str(tmp_path / "t.o")],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr

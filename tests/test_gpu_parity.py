@@ -1,0 +1,209 @@
+"""GPU parity of the CUDA path against the CPU oracle, through the C ABI.
+
+Bars: quantize bytes bit-exact; int32 per-block dots
+bit-exact; fp32 mul_mat within relative Frobenius error 1e-5 of the ggml CPU
+semantics (RTOL below).  The CUDA-core check kernel must also be bit-exact in
+fp32 because it follows the CPU's accumulation order."""
+import numpy as np
+import pytest
+
+import b2q
+import oracle as O
+from helpers import gelu_tanh, make_case, reference_check, rel_frobenius, sample
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-5  # relative Frobenius tolerance of the fp32 result
+
+
+def to_dev(a, dev):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def to_np(t):
+    import torch
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+@pytest.fixture(autouse=True)
+def _no_device_errors(b2q_mod, dev):
+    yield
+    assert b2q.device_status(clear=True) == 0
+
+
+# ------------------------------------------------------------------ quantize
+@pytest.mark.parametrize("variant", [O.ACT_X86, O.ACT_REF])
+@pytest.mark.parametrize("M,K", [(1, 32), (33, 256), (7, 96), (1374, 1024), (4096, 1024)])
+def test_quantize_bit_exact(dev, variant, M, K):
+    rng = np.random.default_rng(M * 7 + K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    x[0, :32] = 0.0
+    if M > 3:
+        x[1, :32] = np.arange(32, dtype=np.float32) - 15.5
+        x[2, :32] = 1e-30
+        x[3, :32] = 3e4 * rng.standard_normal(32)
+    got = to_np(b2q.quantize_q8_0(to_dev(x, dev), variant))
+    assert np.array_equal(got, O.quantize(x, O.TYPE_Q8_0, variant))
+
+
+def test_quantize_unaligned_rows_use_scalar_loads(dev):
+    import torch
+    rng = np.random.default_rng(5)
+    big = rng.standard_normal((9, 1024 + 3)).astype(np.float32)
+    xb = to_dev(big, dev)
+    x = xb[:, 1:1 + 1024]                       # 4-byte aligned, not 16
+    got = to_np(b2q.quantize_q8_0(x, O.ACT_X86))
+    assert np.array_equal(got, O.quantize(big[:, 1:1 + 1024], O.TYPE_Q8_0, O.ACT_X86))
+    del torch
+
+
+def test_quantize_golden_ref_variant(dev):
+    g = np.load(__file__.replace("test_gpu_parity.py", "golden/q_golden.npz"))
+    got = to_np(b2q.quantize_q8_0(to_dev(g["x"], dev), O.ACT_REF))
+    assert np.array_equal(got, g["a_q8_ref"])
+
+
+# ---------------------------------------------------------------- block dots
+@pytest.mark.parametrize("wtype", [O.TYPE_Q8_0, O.TYPE_Q4_0])
+@pytest.mark.parametrize("M,N,K", [(1, 1, 32), (33, 65, 256), (129, 257, 96), (200, 130, 4096),
+                                   (300, 128, 160)])
+def test_tensor_core_block_dots_bit_exact(dev, wtype, M, N, K):
+    _, wq, x = make_case(M + N + K, M, N, K, wtype)
+    a = O.quantize(x, O.TYPE_Q8_0, O.ACT_X86)
+    got = to_np(b2q.block_dots(wtype, to_dev(wq, dev), to_dev(a, dev), K))
+    assert np.array_equal(got, O.block_dots(wtype, wq, a, K))
+
+
+@pytest.mark.parametrize("name,wtype", [("q8_0", O.TYPE_Q8_0), ("q4_0", O.TYPE_Q4_0)])
+def test_block_dots_golden(dev, name, wtype):
+    g = np.load(__file__.replace("test_gpu_parity.py", "golden/q_golden.npz"))
+    K = int(g["K"])
+    got = to_np(b2q.block_dots(wtype, to_dev(g[f"w_{name}"], dev), to_dev(g["a_q8_ref"], dev), K))
+    assert np.array_equal(got, g[f"dots_{name}"])
+
+
+# ------------------------------------------------------- CUDA-core check path
+@pytest.mark.parametrize("wtype", [O.TYPE_Q8_0, O.TYPE_Q4_0])
+@pytest.mark.parametrize("M,N,K", [(1, 1, 32), (33, 65, 256), (65, 100, 1024), (17, 40, 4096)])
+def test_simt_fp32_bit_exact(dev, wtype, M, N, K):
+    _, wq, x = make_case(3 * M + N + K, M, N, K, wtype)
+    a = O.quantize(x, O.TYPE_Q8_0, O.ACT_X86)
+    got = to_np(b2q.mul_mat_q_simt(wtype, to_dev(wq, dev), to_dev(a, dev), K))
+    ref = O.mul_mat_q(wtype, wq, a, K)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+# ----------------------------------------------------------- tcgen05 mul_mat
+SHAPES = [(1, 64, 32), (31, 65, 256), (32, 65, 256), (33, 65, 256), (65, 65, 256),
+          (127, 129, 96), (128, 128, 128), (129, 257, 1024), (256, 384, 224),
+          (1374, 1024, 1024)]
+
+
+@pytest.mark.parametrize("wtype", [O.TYPE_Q8_0, O.TYPE_Q4_0])
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_mul_mat_matches_oracle(dev, wtype, M, N, K):
+    _, wq, x = make_case(M * 31 + N * 7 + K, M, N, K, wtype)
+    y = to_np(b2q.mul_mat(wtype, to_dev(wq, dev), to_dev(x, dev)))
+    ref = O.mul_mat(wtype, wq, x, O.ACT_X86)
+    assert np.all(np.isfinite(y))
+    assert rel_frobenius(y, ref) <= RTOL
+
+
+@pytest.mark.parametrize("wtype,M,N,K,gelu", [
+    (O.TYPE_Q8_0, 4096, 4096, 1024, False),    # fc1, Q8_0
+    (O.TYPE_Q4_0, 4096, 4096, 1024, False),    # fc1, Q4_0
+    (O.TYPE_Q4_0, 4096, 1024, 4096, True),     # fc2, Q4_0, GELU inputs
+    (O.TYPE_Q8_0, 1374, 1024, 1024, False),    # small-M cross-attention kv
+])
+def test_baseline_shapes_match_oracle(dev, wtype, M, N, K, gelu):
+    _, wq, x = make_case(M + N + K + gelu, M, N, K, wtype, gelu=gelu)
+    y = to_np(b2q.mul_mat(wtype, to_dev(wq, dev), to_dev(x, dev)))
+    ref = O.mul_mat(wtype, wq, x, O.ACT_X86)
+    assert rel_frobenius(y, ref) <= RTOL
+
+
+@pytest.mark.parametrize("variant", [O.ACT_X86, O.ACT_REF])
+def test_variants_follow_oracle(dev, variant):
+    _, wq, x = make_case(99, 200, 96, 512, O.TYPE_Q8_0)
+    y = to_np(b2q.mul_mat(O.TYPE_Q8_0, to_dev(wq, dev), to_dev(x, dev), variant=variant))
+    assert rel_frobenius(y, O.mul_mat(O.TYPE_Q8_0, wq, x, variant)) <= RTOL
+
+
+def test_packed_path_bitwise_equals_raw_path(dev):
+    import torch
+    M, N, K = 300, 200, 640
+    _, wq, x = make_case(7, M, N, K, O.TYPE_Q4_0)
+    w_d, x_d = to_dev(wq, dev), to_dev(x, dev)
+    packed = b2q.weight_pack(O.TYPE_Q4_0, w_d, K)
+    y1 = b2q.mul_mat_packed(packed, N, K, x_d)
+    y0 = b2q.mul_mat(O.TYPE_Q4_0, w_d, x_d)
+    torch.cuda.synchronize()
+    assert torch.equal(y0, y1)
+
+
+def test_bias_is_fused_add(dev):
+    import torch
+    M, N, K = 129, 300, 256
+    _, wq, x = make_case(8, M, N, K, O.TYPE_Q8_0)
+    bias = np.random.default_rng(1).standard_normal(N).astype(np.float32)
+    w_d, x_d = to_dev(wq, dev), to_dev(x, dev)
+    y0 = b2q.mul_mat(O.TYPE_Q8_0, w_d, x_d)
+    y1 = b2q.mul_mat(O.TYPE_Q8_0, w_d, x_d, bias=to_dev(bias, dev))
+    torch.cuda.synchronize()
+    # mul_mat then GGML_OP_ADD in fp32 == fused epilogue add, bit for bit
+    assert torch.equal(y1, y0 + to_dev(bias, dev))
+
+
+def test_row_offset_view_and_strided_output(dev):
+    """matrix_rows (cpp_ggml/src/ss_flow_graph.cpp:38-44): src0 is a row range of
+    a fused qkv weight; dst rows are written with a stride wider than N."""
+    import torch
+    C, K, M = 96, 256, 70
+    _, wq, x = make_case(12, M, 3 * C, K, O.TYPE_Q8_0)
+    w_d, x_d = to_dev(wq, dev), to_dev(x, dev)
+    out = torch.full((M, 2 * C + 8), -7.0, dtype=torch.float32, device=dev)
+    kview = w_d[C:2 * C]                       # rows C..2C-1, row stride = full row bytes
+    b2q.mul_mat(O.TYPE_Q8_0, kview, x_d, out=out[:, 4:4 + C])
+    y = to_np(out)
+    ref = O.mul_mat(O.TYPE_Q8_0, wq[C:2 * C], x, O.ACT_X86)
+    assert rel_frobenius(y[:, 4:4 + C], ref) <= RTOL
+    assert np.all(y[:, :4] == -7.0) and np.all(y[:, 4 + C:] == -7.0)
+
+
+def test_repeat_calls_are_deterministic(dev):
+    import torch
+    _, wq, x = make_case(13, 1000, 512, 1024, O.TYPE_Q8_0)
+    w_d, x_d = to_dev(wq, dev), to_dev(x, dev)
+    y0 = b2q.mul_mat(O.TYPE_Q8_0, w_d, x_d)
+    y1 = b2q.mul_mat(O.TYPE_Q8_0, w_d, x_d)
+    torch.cuda.synchronize()
+    assert torch.equal(y0, y1)
+
+
+@pytest.mark.parametrize("wtype", [O.TYPE_Q8_0, O.TYPE_Q4_0])
+@pytest.mark.parametrize("M", [31, 32, 33, 65])
+def test_reference_regression_check(dev, wtype, M):
+    """The reference's matmul regression test, run through the C ABI: hash
+    inputs, K = 256, N = 65, two iterations on the same weight buffer
+    (cpp_ggml/src/matmul_backend_test.cpp:24-98; criteria in helpers)."""
+    K, N = 256, 65
+    w = sample(np.arange(K * N), 13).reshape(N, K)
+    wq = O.quantize(w, wtype)
+    w_deq = O.dequantize(wq, wtype, K)
+    w_d = to_dev(wq, dev)
+    for it in range(2):
+        x = sample(np.arange(K * M), 19 + it).reshape(M, K)
+        y = to_np(b2q.mul_mat(wtype, w_d, to_dev(x, dev)))
+        r = reference_check(y, w_deq, x, it)
+        assert r["ok"], r
+        assert rel_frobenius(y, O.mul_mat(wtype, wq, x, O.ACT_X86)) <= RTOL
+
+
+def test_gelu_inputs_large_k(dev):
+    # fc2-like: GELU(N(0,1)) activations, K = 4096, ragged N
+    _, wq, x = make_case(21, 300, 200, 4096, O.TYPE_Q8_0, gelu=True)
+    y = to_np(b2q.mul_mat(O.TYPE_Q8_0, to_dev(wq, dev), to_dev(x, dev)))
+    assert rel_frobenius(y, O.mul_mat(O.TYPE_Q8_0, wq, x, O.ACT_X86)) <= RTOL
+    assert np.allclose(gelu_tanh(np.zeros(1, np.float32)), 0)

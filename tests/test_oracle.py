@@ -1,0 +1,135 @@
+"""CPU tests of the oracle: pinned against gguf-py's golden vectors and the
+reference test's pass criteria.  No GPU."""
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+from helpers import make_case, reference_check, rel_frobenius, sample
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "q_golden.npz")
+
+
+@pytest.fixture(scope="module")
+def golden(oracle_mod):
+    return np.load(GOLDEN)
+
+
+def test_fp16_rounding_matches_ieee(oracle_mod):
+    rng = np.random.default_rng(0)
+    parts = [rng.standard_normal(20000).astype(np.float32) * s
+             for s in (1e-9, 3e-8, 1e-6, 6e-5, 1e-3, 1.0, 300.0, 6e4, 7e4)]
+    edge = np.array([0.0, -0.0, 65504, 65519.996, 65520, -65520, 6.1035156e-05, 5.9604645e-08,
+                     2.9802322e-08, 2.9802326e-08, 8.940697e-08, np.inf, -np.inf], np.float32)
+    x = np.concatenate(parts + [edge])
+    with np.errstate(over="ignore"):
+        ref = x.astype(np.float16).view(np.uint16)
+    assert np.array_equal(O.fp32_to_fp16_bits(x), ref)
+
+
+def test_philox_known_answer(oracle_mod):
+    # Random123 known-answer vector for philox4x32_10, key 0, counter 0.
+    assert [int(v) for v in O.philox(0, 0)] == [0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]
+
+
+def test_normal_generator_moments(oracle_mod):
+    z = O.normal(1 << 18, seed=7)
+    assert abs(z.mean()) < 0.01 and abs(z.std() - 1.0) < 0.01
+    assert np.array_equal(z, O.normal(1 << 18, seed=7))
+
+
+@pytest.mark.parametrize("name,wtype", [("q8_0", O.TYPE_Q8_0), ("q4_0", O.TYPE_Q4_0)])
+def test_weight_quantizer_matches_golden(golden, name, wtype):
+    mine = O.quantize(golden["w"], wtype)
+    assert np.array_equal(mine, golden[f"w_{name}"])
+    K = int(golden["K"])
+    assert np.array_equal(O.dequantize(mine, wtype, K), golden[f"w_{name}_dequant"])
+
+
+def test_activation_ref_variant_matches_golden(golden):
+    assert np.array_equal(O.quantize(golden["x"], O.TYPE_Q8_0, O.ACT_REF), golden["a_q8_ref"])
+
+
+def test_activation_variants_share_scales_and_nearly_all_codes(golden):
+    x = golden["x"]
+    a_x86 = O.quantize(x, O.TYPE_Q8_0, O.ACT_X86).reshape(x.shape[0], -1, 34)
+    a_ref = O.quantize(x, O.TYPE_Q8_0, O.ACT_REF).reshape(x.shape[0], -1, 34)
+    assert np.array_equal(a_x86[:, :, :2], a_ref[:, :, :2])       # d = amax/127 in both
+    diff = a_x86[:, :, 2:].view(np.int8).astype(int) - a_ref[:, :, 2:].view(np.int8).astype(int)
+    assert np.all(np.abs(diff) <= 1)                              # only rounding ties differ
+    # the planted exact-tie block (x = j - 15.5, amax 15.5 -> |x|*127/15.5 has no .5 ties
+    # in fp32, but 1/d vs 127/amax rounding can still move a code by one)
+    assert np.mean(diff != 0) < 0.01
+
+
+@pytest.mark.parametrize("name,wtype", [("q8_0", O.TYPE_Q8_0), ("q4_0", O.TYPE_Q4_0)])
+def test_block_dots_match_golden(golden, name, wtype):
+    K = int(golden["K"])
+    dots = O.block_dots(wtype, golden[f"w_{name}"], golden["a_q8_ref"], K)
+    assert np.array_equal(dots, golden[f"dots_{name}"])
+
+
+@pytest.mark.parametrize("name,wtype", [("q8_0", O.TYPE_Q8_0), ("q4_0", O.TYPE_Q4_0)])
+def test_mul_mat_matches_golden_products(golden, name, wtype):
+    K = int(golden["K"])
+    y = O.mul_mat_q(wtype, golden[f"w_{name}"], golden["a_q8_ref"], K)
+    # fp32 accumulation of the exact per-block products: within 1e-6 of fp64
+    assert rel_frobenius(y, golden[f"y_blockscale_{name}"]) < 1e-6
+    assert rel_frobenius(y, golden[f"y_f64_{name}"]) < 1e-6
+
+
+@pytest.mark.parametrize("wtype", [O.TYPE_Q8_0, O.TYPE_Q4_0])
+@pytest.mark.parametrize("M,N,K", [(1, 1, 32), (31, 65, 256), (33, 17, 96), (65, 130, 1024)])
+def test_fast_variant_bit_identical(wtype, M, N, K):
+    _, wq, x = make_case(M * 1000 + N + K, M, N, K, wtype)
+    a = O.quantize(x, O.TYPE_Q8_0, O.ACT_X86)
+    y0 = O.mul_mat_q(wtype, wq, a, K, fast=False)
+    y1 = O.mul_mat_q(wtype, wq, a, K, fast=True, nthreads=3)
+    assert np.array_equal(y0.view(np.uint32), y1.view(np.uint32))
+    yq = O.mul_mat(wtype, wq, x, O.ACT_X86, fast=True)
+    assert np.array_equal(y0.view(np.uint32), yq.view(np.uint32))
+
+
+def test_single_vec_dot_lane_order():
+    # one block where lane order matters: d*partial products accumulate per lane
+    rng = np.random.default_rng(3)
+    _, wq, x = make_case(11, 1, 1, 4096, O.TYPE_Q8_0)
+    a = O.quantize(x, O.TYPE_Q8_0, O.ACT_X86)
+    y = O.mul_mat_q(O.TYPE_Q8_0, wq, a, 4096)
+    f64 = O.mul_mat_f64(O.TYPE_Q8_0, wq, a, 4096)
+    assert abs(float(y[0, 0]) - f64[0, 0]) <= 1e-5 * max(1.0, abs(f64[0, 0]))
+    del rng
+
+
+@pytest.mark.parametrize("wtype", [O.TYPE_Q8_0, O.TYPE_Q4_0])
+@pytest.mark.parametrize("M", [31, 32, 33, 65])
+def test_reference_test_criteria_on_oracle(wtype, M):
+    """The reference's regression check (matmul_backend_test.cpp:24-98), shapes
+    M in {31,32,33,65}, K = 256, N = 65, two iterations, applied to the oracle's
+    quantized mul_mat (ggml's CPU path for Q8_0 / Q4_0 weights)."""
+    K, N = 256, 65
+    w = sample(np.arange(K * N), 13).reshape(N, K)
+    wq = O.quantize(w, wtype)
+    w_deq = O.dequantize(wq, wtype, K)
+    for it in range(2):
+        x = sample(np.arange(K * M), 19 + it).reshape(M, K)
+        y = O.mul_mat(wtype, wq, x, O.ACT_X86)
+        r = reference_check(y, w_deq, x, it)
+        assert r["ok"], r
+
+
+def test_zero_and_degenerate_rows():
+    K = 64
+    x = np.zeros((3, K), np.float32)
+    x[1, :32] = 1e-30          # underflows to a zero fp16 scale
+    x[2, :] = -0.0
+    a = O.quantize(x, O.TYPE_Q8_0, O.ACT_X86).reshape(3, -1, 34)
+    assert np.all(a[:, :, :2] == 0)          # every fp16 scale is zero
+    assert np.all(a[0, :, 2:] == 0) and np.all(a[2, :, 2:] == 0)
+    # 1e-30: d = amax/127 underflows in fp16 but the fp32 inverse does not,
+    # so ggml stores codes of 127 next to a zero scale.
+    assert np.all(a[1, 0, 2:].view(np.int8) == 127)
+    w = np.ones((2, K), np.float32)
+    y = O.mul_mat(O.TYPE_Q8_0, O.quantize(w, O.TYPE_Q8_0), x, O.ACT_X86)
+    assert np.all(y == 0)
