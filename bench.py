@@ -155,6 +155,10 @@ def run_gpu(args, rank, world, local_rank):
 
     stream = torch.cuda.current_stream()
     inputs = make_inputs()
+    if args.only:
+        inputs = [t for t in inputs if t[0] == args.only]
+        if not inputs:
+            raise SystemExit(f"--only: no workload entry named {args.only}")
     gemms = []
     for name, wtype, M, N, K, wq, x in inputs:
         w_raw = torch.from_numpy(wq).to(dev)
@@ -168,7 +172,7 @@ def run_gpu(args, rank, world, local_rank):
         gemms.append(dict(name=name, wtype=wtype, M=M, N=N, K=K, packed=packed, x_host=x_host,
                           x_dev=x_dev, act=act, y_dev=y_dev, y_host=y_host, ws=ws))
         del w_raw
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES if not args.only else 1, dtype=torch.uint8, device=dev)
     torch.cuda.synchronize()
 
     def step(evs=None):
@@ -218,7 +222,7 @@ def run_gpu(args, rank, world, local_rank):
     value = world * step_ops * args.steps / (max_total_ms * 1e-3) / 1e12
 
     # ---- end to end through the public C ABI, host buffers, copies inside the timing
-    e2e_steps = max(1, min(args.steps, 20))
+    e2e_steps = 0 if args.no_e2e else max(1, min(args.steps, 20))
     h2d = sum(g["x_host"].numel() * 4 for g in gemms)
     d2h = sum(g["y_host"].numel() * 4 for g in gemms)
 
@@ -229,7 +233,7 @@ def run_gpu(args, rank, world, local_rank):
                                stream=stream)
             g["y_host"].copy_(g["y_dev"], non_blocking=True)
 
-    for _ in range(min(args.warmup, 3)):
+    for _ in range(min(args.warmup, 3) if e2e_steps else 0):
         e2e_step()
     torch.cuda.synchronize()
     if dist:
@@ -244,7 +248,7 @@ def run_gpu(args, rank, world, local_rank):
     t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = world * step_ops * e2e_steps / (float(t.item()) * 1e-3) / 1e12
+    e2e_value = (world * step_ops * e2e_steps / (float(t.item()) * 1e-3) / 1e12) if e2e_steps else None
 
     gemm_total_ms = sum(sum(v) for v in gemm_ms)
     gemm_ops = step_ops * args.steps
@@ -284,12 +288,15 @@ def run_gpu(args, rank, world, local_rank):
         "ms_per_step": round(max_total_ms / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "i8 (int8 x int8 -> int32 per block, fp32 scale epilogue)",
         "data": "synthetic", "config": config_dict(), "roofline": roofline,
-        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+        "e2e": {"value": round(e2e_value, 2) if e2e_value else None, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "path": "b2q_mul_mat_packed per GEMM, pinned host x -> device -> host y"},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(), "breakdown": breakdown,
     }
+    if args.only:
+        result["config"]["workload"] = f"single GEMM {args.only} (profiling case)"
+        result["config"]["l2"] = "not flushed (profiling case)"
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(inputs, budget_s=args.cpu_budget)
     if dist:
@@ -322,13 +329,20 @@ def pick_frac(inputs, target_s):
 
 
 def cpu_baseline(inputs, budget_s=15.0):
+    """Bounded sample of the same workload on the host cores: whole passes over
+    the workload (or the leading fraction of each GEMM's token rows when one
+    pass exceeds the budget), repeated until ~budget_s of CPU work."""
     import oracle as O
     frac = pick_frac(inputs, budget_s)
-    ops, secs, thr = cpu_sample_run(inputs, frac)
+    ops, secs, reps, thr = 0.0, 0.0, 0, 1
+    while secs < budget_s and reps < 1000:
+        o, s, thr = cpu_sample_run(inputs, frac)
+        ops, secs, reps = ops + o, secs + s, reps + 1
     return {"value": round(ops / secs / 1e12, 4), "unit": UNIT, "cores": thr, "kind": "port",
             "isa": O.isa(),
-            "sample": f"first {frac:.3f} of each GEMM's token rows (fc1, fc2, kv), {secs:.1f} s, "
-                      f"oracle port of ggml CPU mul_mat incl. activation quantize"}
+            "sample": f"{reps} pass(es) over the first {frac:.3f} of each GEMM's token rows "
+                      f"(fc1, fc2, kv), {secs:.1f} s, oracle port of ggml CPU mul_mat incl. "
+                      f"activation quantize"}
 
 
 def run_reference(args):
@@ -367,6 +381,8 @@ def main():
     ap.add_argument("--impl", choices=["b2q", "reference"], default="b2q")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--only", default=None, help="run one workload entry (profiling case)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -29,6 +29,12 @@ inline int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 // Layout of the GEMM operands in HBM ("split" layout):
 //   codes  int8  [rows][K]          row stride K bytes
 //   scales fp32  [K/32][ld]         ld = round_up(rows, 4)  (16-byte TMA strides)
+// The fp32 scales are stored pre-multiplied by a power of two (exact for fp16
+// values): weights by 2^kWeightScaleExp2, activations by 2^kActScaleExp2.  The
+// GEMM epilogue relies on these factors to fold int32 dots read as fp32
+// subnormals into normal fp32 values (see b2q_gemm_tc.cu).
+constexpr float kWeightScaleMul = 0x1p100f;  // 2^100
+constexpr float kActScaleMul = 0x1p49f;      // 2^49
 struct SplitOperand {
   const int8_t* codes;
   const float* scales;

@@ -34,6 +34,12 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
 
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (TMA, tensor core) before they are consumed there.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void fence_mbarrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
@@ -54,14 +60,19 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
       : "memory");
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps (up to the hint) instead of spinning, and wakes when the phase
+// completes, so waiting warps do not take issue slots from working ones.
+constexpr uint32_t kSuspendHintNs = 1000000;  // 1 ms
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.b32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
@@ -201,6 +212,16 @@ __host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
          | (1u << 10)                            // B = signed 8-bit
          | (static_cast<uint32_t>(n >> 3) << 17) // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);  // M / 16
+}
+
+// Per-warpgroup register reallocation (all 4 warps of a warpgroup execute it).
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 __device__ __forceinline__ uint32_t elect_one() {

@@ -9,8 +9,8 @@
 // Each division, product and rounding is one IEEE fp32 operation, so the codes
 // and scales are bit-identical to the CPU's.
 //
-// Mapping: one warp quantizes a 128-value segment (4 blocks) of one row per
-// step; each lane loads one 128-bit float4, so 8 lanes own one block and the
+// Mapping: a warp quantizes 128-value segments (4 blocks) of a row; each lane
+// loads one 128-bit float4 per segment, so 8 lanes own one block and the
 // block's absmax is three xor-shuffles inside that 8-lane group.
 #include "b2q_internal.h"
 #include "b2q_ptx.cuh"
@@ -66,6 +66,10 @@ __device__ __forceinline__ float4 load4(const float* p) {
 
 // SPLIT = true : codes int8 [m][k] + fp32 scales [k/32][ld] (GEMM layout)
 // SPLIT = false: ggml block_q8_0 rows (34-byte blocks)
+// Each warp step handles kUnroll consecutive segments, all loads issued first,
+// so every warp keeps kUnroll * 512 bytes in flight.
+constexpr int kUnroll = 4;
+
 template <int VARIANT, bool SPLIT, bool VEC4>
 __global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float* __restrict__ x, int64_t m,
                                                             int64_t k, int64_t ldx,
@@ -76,26 +80,36 @@ __global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float* __restr
   const int64_t segs = (k + 127) / 128;
   const int64_t total = m * segs;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
-  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32; w < total;
-       w += warps) {
-    const int64_t row = w / segs;
-    const int64_t k0 = (w - row * segs) * 128 + lane * 4;
-    const bool valid = k0 < k;  // k % 32 == 0: a block is all-valid or all-invalid
-    const float4 v = valid ? load4<VEC4>(x + row * ldx + k0) : make_float4(0.f, 0.f, 0.f, 0.f);
-    const BlockQuant q = quantize_lane<VARIANT>(v);
-    if (!valid) continue;
-    const int64_t blk = k0 / kQK;
-    const int sub = lane & 7;
-    const __half dh = __float2half_rn(q.d);
-    if (SPLIT) {
-      *reinterpret_cast<uint32_t*>(codes + row * k + k0) = q.packed;
-      if (sub == 0) scales[blk * ld + row] = __half2float(dh);
-    } else {
-      uint8_t* b = yb + row * ldy + blk * kQ8Bytes;
-      uint16_t* b16 = reinterpret_cast<uint16_t*>(b + 2 + 4 * sub);
-      b16[0] = static_cast<uint16_t>(q.packed & 0xffffu);
-      b16[1] = static_cast<uint16_t>(q.packed >> 16);
-      if (sub == 0) *reinterpret_cast<uint16_t*>(b) = __half_as_ushort(dh);
+  for (int64_t w0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32 * kUnroll;
+       w0 < total; w0 += warps * kUnroll) {
+    float4 v[kUnroll];
+    int64_t row[kUnroll], k0[kUnroll];
+    bool valid[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t w = w0 + u;
+      row[u] = w / segs;
+      k0[u] = (w - row[u] * segs) * 128 + lane * 4;
+      valid[u] = w < total && k0[u] < k;  // k % 32 == 0: a block is all-valid or all-invalid
+      v[u] = valid[u] ? load4<VEC4>(x + row[u] * ldx + k0[u]) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const BlockQuant q = quantize_lane<VARIANT>(v[u]);
+      if (!valid[u]) continue;
+      const int64_t blk = k0[u] / kQK;
+      const int sub = lane & 7;
+      const __half dh = __float2half_rn(q.d);
+      if (SPLIT) {
+        *reinterpret_cast<uint32_t*>(codes + row[u] * k + k0[u]) = q.packed;
+        if (sub == 0) scales[blk * ld + row[u]] = __half2float(dh) * kActScaleMul;
+      } else {
+        uint8_t* b = yb + row[u] * ldy + blk * kQ8Bytes;
+        uint16_t* b16 = reinterpret_cast<uint16_t*>(b + 2 + 4 * sub);
+        b16[0] = static_cast<uint16_t>(q.packed & 0xffffu);
+        b16[1] = static_cast<uint16_t>(q.packed >> 16);
+        if (sub == 0) *reinterpret_cast<uint16_t*>(b) = __half_as_ushort(dh);
+      }
     }
   }
 }
@@ -103,7 +117,7 @@ __global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float* __restr
 template <bool SPLIT, bool VEC4>
 cudaError_t launch_q(const float* x, int64_t m, int64_t k, int64_t ldx, uint8_t* yb, int64_t ldy,
                      int8_t* codes, float* scales, int64_t ld, int variant, cudaStream_t s) {
-  const int64_t warps_needed = m * ((k + 127) / 128);
+  const int64_t warps_needed = (m * ((k + 127) / 128) + kUnroll - 1) / kUnroll;
   if (warps_needed == 0) return cudaSuccess;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -118,7 +132,8 @@ cudaError_t launch_q(const float* x, int64_t m, int64_t k, int64_t ldx, uint8_t*
 }
 
 // ---------------------------------------------------------------- weights
-// One thread per (row, block): raw GGUF block -> 32 int8 codes + fp32 scale.
+// One thread per (row, block): raw GGUF block -> 32 int8 codes + fp32 scale
+// (stored times 2^100, see b2q_internal.h).
 template <int WTYPE>
 __global__ void __launch_bounds__(256) pack_weights_kernel(const uint8_t* __restrict__ w, int64_t n,
                                                            int64_t k, int64_t ldw,
@@ -152,7 +167,7 @@ __global__ void __launch_bounds__(256) pack_weights_kernel(const uint8_t* __rest
     uint4* dst = reinterpret_cast<uint4*>(codes + row * k + b * kQK);
     dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
     dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
-    scales[b * ld + row] = d;
+    scales[b * ld + row] = d * kWeightScaleMul;
   }
 }
 
