@@ -114,6 +114,29 @@ B2Q_API int b2q_mul_mat_packed(const void* packed, int64_t n, int64_t k, const f
                        int64_t y_row_stride_bytes, int variant, void* workspace,
                        size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------- no-allocation form
+ * b2q_mul_mat_packed for callers that may not allocate device memory and have
+ * no workspace to lend: code that runs after its memory plan is fixed (a ggml
+ * backend computing a graph whose buffers the graph allocator has already
+ * placed), or a serving loop that must not call cudaMalloc/cudaFree, which can
+ * synchronise the device.  No counterpart exists in the reference: ggml's CPU
+ * mul_mat takes its quantized-activation scratch from the work buffer that
+ * ggml_graph_plan sizes and the caller provides.
+ * The activations go to one fixed device array of B2Q_NOALLOC_SCRATCH_BYTES
+ * (32 MiB per device, reserved when the library's CUDA module loads), so
+ * b2q_act_prepared_size(m, k) must not exceed it (about 29.8 M values: m = 4096
+ * rows up to k = 7168); larger sizes return B2Q_ERR_TOO_LARGE.  The first call on
+ * each device sets up (looks up the array's address, with that device current);
+ * make it before any stream capture begins.  Every call on a device shares the
+ * array, which keeps the last call's contents: calls that can overlap on one
+ * device (several streams or threads) race, so serialise them.
+ * Arguments, alignment and results are those of b2q_mul_mat_packed. */
+#define B2Q_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
+B2Q_API int b2q_mul_mat_packed_noalloc(const void* packed, int64_t n, int64_t k, const float* x,
+                                       int64_t m, int64_t x_row_stride_bytes, const float* bias,
+                                       float* y, int64_t y_row_stride_bytes, int variant,
+                                       void* stream);
+
 /* ------------------------------------------------- two-phase form of mul_mat
  * ggml's CPU mul_mat first converts all of src1 to Q8_0 into its work buffer
  * (from_float into params->wdata), then runs the dots.  The same two phases

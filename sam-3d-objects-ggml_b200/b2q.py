@@ -63,6 +63,7 @@ def _lib_obj():
             "b2q_mul_mat_workspace_size": (SZ, [I64, I64, I64, I]),
             "b2q_mul_mat": (I, [I, P, I64, I64, I64, P, I64, I64, P, P, I64, I, P, SZ, P]),
             "b2q_mul_mat_packed": (I, [P, I64, I64, P, I64, I64, P, P, I64, I, P, SZ, P]),
+            "b2q_mul_mat_packed_noalloc": (I, [P, I64, I64, P, I64, I64, P, P, I64, I, P]),
             "b2q_act_prepared_size": (SZ, [I64, I64]),
             "b2q_act_prepare": (I, [P, I64, I64, I64, I, P, SZ, P]),
             "b2q_mul_mat_prepared": (I, [P, I64, I64, P, I64, P, P, I64, P]),
@@ -188,6 +189,24 @@ def mul_mat_packed(packed, n: int, k: int, x, bias=None, variant: int = ACT_X86,
                                   _ptr(out), out.stride(0) * 4, variant, _ptr(ws), ws.numel(),
                                   _stream(stream))
     _check("b2q_mul_mat_packed", rc)
+    return out
+
+
+NOALLOC_SCRATCH_BYTES = 32 << 20  # B2Q_NOALLOC_SCRATCH_BYTES
+
+
+def mul_mat_packed_noalloc(packed, n: int, k: int, x, bias=None, variant: int = ACT_X86, out=None,
+                           stream=None):
+    """mul_mat_packed with the activations in the library's fixed device array
+    (no workspace); calls on one device must not overlap."""
+    torch = _torch()
+    m = x.shape[0]
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=x.device)
+    rc = lib().b2q_mul_mat_packed_noalloc(_ptr(packed), n, k, _ptr(x), m, x.stride(0) * 4,
+                                          _ptr(bias), _ptr(out), out.stride(0) * 4, variant,
+                                          _stream(stream))
+    _check("b2q_mul_mat_packed_noalloc", rc)
     return out
 
 
