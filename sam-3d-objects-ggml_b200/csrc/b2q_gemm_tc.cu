@@ -2,12 +2,12 @@
 //
 //   y[m][n] = sum_b  dw[n,b] * da[m,b] * S_b(n,m),   S_b = sum_{i<32} qw[n,32b+i] * qa[m,32b+i]
 //
-// Per 32-value block b, one tcgen05.mma (kind::i8, M = 128 weight rows, N = BN
-// tokens, K = 32) computes that block's int32 dots S_b into a fresh TMEM
+// Per 32-value block b, one tcgen05.mma (kind::i8, M = 128 weight rows, N = 128
+// tokens, K = 32) computes that block's int32 dots S_b into its own TMEM
 // accumulator slot.  Scales change every 32 of K, so int32 cannot be carried
-// across blocks; epilogue warps drain every slot and apply the scales in fp32,
-// while the tensor core fills the next slots.  The epilogue's per-(n, m, b)
-// arithmetic, not the tensor core, bounds this kernel.
+// across blocks; epilogue warps read every slot and apply the scales in fp32,
+// while the tensor core fills the next slots.  The per-(n, m, b) epilogue --
+// TMEM reads and two FMAs per element -- not the tensor core, bounds the kernel.
 //
 // Exact int32 -> fp32 fold without any conversion instruction:
 //   a second, constant MMA (kind::i8, unsigned x unsigned, both operands one 4 KB
@@ -21,21 +21,30 @@
 //   i.e. two fp32 FMAs per (row, token, block) -- issued as packed f32x2 pairs --
 //   the same two roundings as round(S*dw)*da, with every intermediate normal.
 //
-// TMEM access: each epilogue warp reads its 32 rows x 64 columns of a slot with
-// two tcgen05.ld.16x256b.x8 (thread i: rows i/4, i/4+8 (+16, +24), columns
-// 8g + 2(i%4) + {0,1}), so a thread needs 16 activation scales (8 LDS.64 with
-// 4 distinct addresses per warp) and 4 weight scales per block.  The two halves
-// are software-pipelined: each load is in flight while the other half is
-// scaled, and a slot is released as soon as both halves are in registers.
+// Epilogue data path: thread t of epilogue warp w owns weight row 32*(w%4) + t
+// (its TMEM lane) and 64 of the 128 token columns, read with two
+// tcgen05.ld.32x32b.x32 (the widest-bandwidth load shape).  Its weight scale is
+// one scalar per block; the 64 activation scales are warp-uniform broadcast
+// loads.  The next block's 64 values are loaded into a second register buffer
+// while the current block is scaled (tcgen05.wait::ld covers all of a thread's
+// loads, so the double buffer is what keeps 64 KB of TMEM reads in flight per
+// SM).  The four slots are handed between MMA and epilogue in pairs of
+// consecutive blocks: one commit, one wait and one release per two blocks.
+// Every hand-off makes all eight epilogue warps meet, and each meeting costs
+// more than the latency of the barrier itself, so halving them pays; the loop
+// is specialised per half of a pair so the hot path carries no hand-off tests.
+// K is padded to whole stages (the padding blocks read zero codes and scales
+// through the tensor maps' out-of-bounds fill and add exactly nothing).
+// Output stores: for each token, the 32 threads of a warp write 32 consecutive
+// floats of y's row (128-byte coalesced), bias fused.
 //
 // Roles (384 threads = 3 warpgroups, 1 CTA per SM, persistent over tiles):
 //   warp 0      TMA producer: weight codes [128 x 128B], activation codes
-//               [BN x 128B] (128B swizzle), weight scales [4 x 128] and
-//               activation scales [4 x BN] fp32 per stage (4 blocks of K)
+//               [128 x 128B] (128B swizzle), weight scales [4 x 128] and
+//               activation scales [4 x 128] fp32 per stage (4 blocks of K)
 //   warp 1      TMEM allocator + single-thread MMA issuer
 //   warps 2,3   idle (complete warpgroup 0, which runs on 40 registers)
-//   warps 4..11 epilogue (232 registers): warp w owns TMEM lanes 32*(w%4)..
-//               (weight rows) and half of the BN accumulator columns (tokens)
+//   warps 4..11 epilogue (232 registers)
 // Every wait is bounded (b2q_ptx.cuh); on give-up the CTA drains its in-flight
 // copies and MMAs, frees TMEM and exits, leaving a code in g_device_status.
 #include "b2q_internal.h"
@@ -50,10 +59,12 @@ __device__ unsigned int g_device_status = 0;
 namespace {
 
 constexpr int kBM = 128;             // weight rows per tile (MMA M, TMEM lanes)
+constexpr int kBN = 128;             // tokens per tile (MMA N, columns per slot)
 constexpr int kKBS = 4;              // 32-value blocks per pipeline stage
 constexpr int kStageK = kKBS * kQK;  // 128 bytes of K per operand row per stage
 constexpr int kEpiWarps = 8;
-constexpr int kEpiWarp0 = 4;  // epilogue = warpgroups 1 and 2
+constexpr int kEpiWarp0 = 4;         // epilogue = warpgroups 1 and 2
+constexpr int kCols = kBN / 2;       // token columns per epilogue thread
 constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;
 // Register split (setmaxnreg works per warpgroup).  The kernel is compiled for
 // 384 threads at kLaunchRegs registers each (the per-SM-subpartition cap for
@@ -66,30 +77,31 @@ constexpr int kRegsControl = 40;
 constexpr int kRegsEpilogue = 232;
 static_assert(128 * kRegsControl + 256 * kRegsEpilogue <= kThreads * kLaunchRegs, "register split");
 constexpr uint32_t kTmemCols = 512;
+constexpr int kSlots = static_cast<int>(kTmemCols) / kBN;  // accumulator slots (blocks in flight)
+constexpr int kPairs = kSlots / 2;  // slots are handed over in pairs of consecutive blocks
+static_assert(kKBS % 2 == 0, "a stage holds whole slot pairs");
 constexpr uint32_t kOffset = 1u << 20;        // added to every S by the constant MMA
 constexpr int kOffsetTileBytes = 4096;        // 128 rows x 32 bytes, every 16-byte chunk = P
 constexpr float kNegTwoPowM129 = -0x1p-129f;  // subnormal, exact
 
-template <int BN, int STAGES>
+template <int STAGES>
 struct Cfg {
   static constexpr int A_BYTES = kBM * kStageK;
-  static constexpr int B_BYTES = BN * kStageK;
+  static constexpr int B_BYTES = kBN * kStageK;
   static constexpr int SW_BYTES = kKBS * kBM * 4;
-  static constexpr int SA_BYTES = kKBS * BN * 4;
+  static constexpr int SA_BYTES = kKBS * kBN * 4;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SW_BYTES + SA_BYTES;
-  static constexpr int ACC_SLOTS = static_cast<int>(kTmemCols) / BN;
-  static constexpr int COLS = BN / 2;  // accumulator columns per epilogue warp
   static constexpr int OFF_TILE = STAGES * STAGE_BYTES;
   static constexpr int BAR_OFF = OFF_TILE + kOffsetTileBytes;
-  static constexpr int NBARS = 2 * STAGES + 2 * ACC_SLOTS + 1;
+  static constexpr int NBARS = 2 * STAGES + 2 * kPairs + 1;
   static constexpr int SMEM = BAR_OFF + NBARS * 8 + 16 + 1024;  // + alignment slack
   static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte swizzle alignment");
   static_assert(STAGES <= 16, "stage bitmasks");
-  static_assert(BN == 128, "the epilogue drains 64 columns per warp");
 };
 
 struct TcParams {
-  int M, N, KB, n_tiles, num_tiles;
+  int M, N, KB, n_tiles, num_tiles;  // KB: blocks of K per tile, rounded up to whole stages
+  int KB_real;                       // blocks of K in the data (the rest read as zeros)
   float* y;
   int64_t ldy;
   const float* bias;
@@ -114,63 +126,103 @@ __host__ __device__ constexpr uint32_t idesc_u8(int m, int n) {
   return (2u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
-// 16 lanes x 256 bits x 8: thread i receives, for g = 0..7,
-//   r[4g+0], r[4g+1] = lane (base + i/4),     columns 8g + 2(i%4) + {0, 1}
-//   r[4g+2], r[4g+3] = lane (base + 8 + i/4), same columns
-__device__ __forceinline__ void tmem_ld_16x256b_x8(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.16x256b.x8.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr)
-      : "memory");
+// This thread's 64 columns of one accumulator slot (two 32-column loads).
+__device__ __forceinline__ void load_slot(uint32_t taddr, uint32_t (&r)[kCols]) {
+  tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+  tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
 }
 
-// Scale and accumulate one 16-lane half: rows (ra, rb) = (i/4, i/4+8) of the
-// half; acc[8*k + g] holds row k (0..3 over both halves) and columns
-// 8g + 2(i%4) + {0, 1}.
-__device__ __forceinline__ void fold_half(float2 (&acc)[32], int k0, const uint32_t (&r)[32],
-                                          const float2 (&da)[8], float2 wa, float2 ca, float2 wb,
-                                          float2 cb) {
-#pragma unroll
-  for (int g = 0; g < 8; ++g) {
-    const float2 ta = ffma2(make_float2(__uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1])), wa, ca);
-    const float2 tb = ffma2(make_float2(__uint_as_float(r[4 * g + 2]), __uint_as_float(r[4 * g + 3])), wb, cb);
-    acc[8 * k0 + g] = ffma2(ta, da[g], acc[8 * k0 + g]);
-    acc[8 * (k0 + 1) + g] = ffma2(tb, da[g], acc[8 * (k0 + 1) + g]);
+// Where the epilogue of one CTA stands in its flat sequence of blocks.
+struct EpiState {
+  int g;  // block counter over all of this CTA's tiles (slot g % kSlots, pair g / 2)
+  uint32_t stage, phase;
+};
+
+// One block of the epilogue: scale and accumulate block g (already in `cur`)
+// while block g + 1 streams into `nxt`.  Blocks come in slot pairs, so the two
+// steps of a pair are specialised: the FIRST step (g even) loads the second
+// block of its own pair and then hands the pair back; the SECOND step (g odd)
+// waits for the next pair before loading its first block.  kb: block within
+// the tile (stage boundaries fall on even blocks).  Returns false when a
+// bounded wait gave up.
+template <int STAGES, bool DUMP, bool FIRST>
+__device__ __forceinline__ bool epi_step(uint32_t (&cur)[kCols], uint32_t (&nxt)[kCols], float2 (&acc)[kCols / 2],
+                                         EpiState& st, int kb, int tile, const TcParams& p, int total,
+                                         uint8_t* smem, uint64_t* full, uint64_t* empty, uint64_t* acc_full,
+                                         uint64_t* acc_empty, volatile int* abort_flag, uint32_t tbase,
+                                         int row, int chalf, int lane) {
+  using C = Cfg<STAGES>;
+  const int j = kb & (kKBS - 1);
+  if (FIRST && j == 0 &&
+      !mbar_wait(&full[st.stage], st.phase, &g_device_status, kDevWaitEpilogue, abort_flag))
+    return false;
+  const uint32_t nb = static_cast<uint32_t>(st.g + 1);
+  const uint32_t npair = (nb >> 1) & (kPairs - 1);
+  const bool more = FIRST || st.g + 1 < total;  // a pair is never split
+  if (more) {
+    if (!FIRST &&
+        !mbar_wait(&acc_full[npair], (nb / kSlots) & 1u, &g_device_status, kDevWaitEpilogue, abort_flag))
+      return false;
+    tc_fence_after();
+    load_slot(tbase + (nb & (kSlots - 1)) * kBN, nxt);
   }
-}
-
-// Debug path: raw int32 block dots S = D - 2^20 of one 16-lane half.
-__device__ __forceinline__ void dump_half(const TcParams& p, const uint32_t (&r)[32], int64_t n_a,
-                                          int64_t m_base, int KB, int blk) {
-  for (int g = 0; g < 8; ++g)
-    for (int k = 0; k < 4; ++k) {
-      const int64_t n = n_a + ((k & 2) ? 8 : 0);
-      const int64_t m = m_base + 8 * g + (k & 1);
-      if (n < p.N && m < p.M) p.dots[(m * p.N + n) * KB + blk] = static_cast<int32_t>(r[4 * g + k] - kOffset);
+  const uint8_t* sb = smem + st.stage * C::STAGE_BYTES;
+  const float* sw = reinterpret_cast<const float*>(sb + C::A_BYTES + C::B_BYTES);
+  const float* sa = sw + kKBS * kBM;
+  const float w = sw[j * kBM + row];
+  const float2 w2 = make_float2(w, w);
+  const float2 c2 = make_float2(w * kNegTwoPowM129, w * kNegTwoPowM129);
+  const float4* da4 = reinterpret_cast<const float4*>(sa + j * kBN + chalf * kCols);
+  if (DUMP && kb < p.KB_real) {
+    const int64_t n = static_cast<int64_t>(tile % p.n_tiles) * kBM + row;
+    const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * kBN + chalf * kCols;
+    for (int c = 0; c < kCols; ++c) {
+      const int64_t m = m0 + c;
+      if (n < p.N && m < p.M) p.dots[(m * p.N + n) * p.KB_real + kb] = static_cast<int32_t>(cur[c] - kOffset);
     }
+  }
+#pragma unroll
+  for (int i = 0; i < kCols / 4; ++i) {
+    const float4 d = da4[i];
+    const float2 t0 = ffma2(make_float2(__uint_as_float(cur[4 * i]), __uint_as_float(cur[4 * i + 1])), w2, c2);
+    const float2 t1 = ffma2(make_float2(__uint_as_float(cur[4 * i + 2]), __uint_as_float(cur[4 * i + 3])), w2, c2);
+    acc[2 * i] = ffma2(t0, make_float2(d.x, d.y), acc[2 * i]);
+    acc[2 * i + 1] = ffma2(t1, make_float2(d.z, d.w), acc[2 * i + 1]);
+  }
+  if (more) {
+    tmem_wait_ld();
+    if (FIRST) {  // both blocks of the pair are in registers: hand the pair back
+      tc_fence_before();
+      mbar_arrive(&acc_empty[npair]);
+    }
+  }
+  if (!FIRST && j == kKBS - 1) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st.stage]);
+    if (++st.stage == STAGES) {
+      st.stage = 0;
+      st.phase ^= 1u;
+    }
+  }
+  ++st.g;
+  return true;
 }
 
-template <int BN, int STAGES, bool DUMP>
+template <int STAGES, bool DUMP>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_wc, const __grid_constant__ CUtensorMap tm_ac,
                    const __grid_constant__ CUtensorMap tm_ws, const __grid_constant__ CUtensorMap tm_as,
                    const TcParams p) {
-  using C = Cfg<BN, STAGES>;
+  using C = Cfg<STAGES>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
+  // Offset arithmetic on the __shared__ array itself (no integer round trip), so
+  // the compiler keeps the shared address space and emits shared-memory loads.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
-  uint64_t* acc_empty = acc_full + C::ACC_SLOTS;
-  uint64_t* mma_done = acc_empty + C::ACC_SLOTS;
+  uint64_t* acc_empty = acc_full + kPairs;
+  uint64_t* mma_done = acc_empty + kPairs;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -182,9 +234,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kEpiWarps);
     }
-    for (int a = 0; a < C::ACC_SLOTS; ++a) {
+    for (int a = 0; a < kPairs; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], kEpiWarps);
+      mbar_init(&acc_empty[a], kEpiWarps * 32);  // every epilogue thread arrives
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -214,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_holder;
 
   const int KB = p.KB;
-  const int n_ks = (KB + kKBS - 1) / kKBS;
+  const int n_ks = KB / kKBS;
 
   if (warp < kEpiWarp0) {
     // ------------------------------------------------- warpgroup 0 (control)
@@ -226,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
           const int n0 = (tile % p.n_tiles) * kBM;
-          const int m0 = (tile / p.n_tiles) * BN;
+          const int m0 = (tile / p.n_tiles) * kBN;
           for (int ks = 0; ks < n_ks; ++ks) {
             if (!mbar_wait(&empty[stage], phase ^ 1u, &g_device_status, kDevWaitProducer, abort_flag)) {
               ok = false;
@@ -254,10 +306,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
       // -------------------------------------------------------- MMA issuer
       if (elect_one()) {
-        constexpr uint32_t idesc = idesc_i8(kBM, BN);
-        constexpr uint32_t idesc_off = idesc_u8(kBM, BN);
+        constexpr uint32_t idesc = idesc_i8(kBM, kBN);
+        constexpr uint32_t idesc_off = idesc_u8(kBM, kBN);
         const uint64_t off_desc = smem_desc_k_noswz(smem_u32(smem + C::OFF_TILE));
-        uint32_t stage = 0, phase = 0, slot = 0, acc_phase = 0;
+        uint32_t stage = 0, phase = 0, q = 0;  // q: pair counter; pair q fills slots 2(q % kPairs) + {0, 1}
         bool ok = true;
         for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
           for (int ks = 0; ok && ks < n_ks; ++ks) {
@@ -268,21 +320,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const uint32_t a_base = smem_u32(smem + stage * C::STAGE_BYTES);
             const uint32_t b_base = a_base + C::A_BYTES;
-            const int nblk = min(kKBS, KB - ks * kKBS);
-            for (int j = 0; j < nblk; ++j) {
-              if (!mbar_wait(&acc_empty[slot], acc_phase ^ 1u, &g_device_status, kDevWaitMma, abort_flag)) {
+            for (int j2 = 0; j2 < kKBS; j2 += 2, ++q) {
+              const uint32_t pair = q & (kPairs - 1);
+              if (!mbar_wait(&acc_empty[pair], ((q / kPairs) & 1u) ^ 1u, &g_device_status, kDevWaitMma, abort_flag)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
-              const uint32_t d = tmem_base + slot * BN;
-              mma_i8(d, smem_desc_k_sw128(a_base + j * kQK), smem_desc_k_sw128(b_base + j * kQK), idesc, 0u);
-              mma_i8(d, off_desc, off_desc, idesc_off, 1u);
-              mma_commit(&acc_full[slot]);
-              if (++slot == C::ACC_SLOTS) {
-                slot = 0;
-                acc_phase ^= 1u;
+#pragma unroll
+              for (int j = j2; j < j2 + 2; ++j) {
+                const uint32_t d = tmem_base + (2 * pair + (j - j2)) * kBN;
+                mma_i8(d, smem_desc_k_sw128(a_base + j * kQK), smem_desc_k_sw128(b_base + j * kQK), idesc, 0u);
+                mma_i8(d, off_desc, off_desc, idesc_off, 1u);
               }
+              mma_commit(&acc_full[pair]);
             }
             if (++stage == STAGES) {
               stage = 0;
@@ -299,96 +350,44 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------ warpgroups 1-2: epilogue
     setmaxnreg_inc<kRegsEpilogue>();
     const int quarter = warp & 3;               // TMEM lane quarter this warp may access
-    const int chalf = (warp - kEpiWarp0) >> 2;  // which half of the BN columns
-    const int row0 = quarter * 32 + (lane >> 2);  // this thread's rows: row0 + {0, 8, 16, 24}
-    const int col0 = chalf * C::COLS + 2 * (lane & 3);  // columns col0 + 8g + {0, 1}
-    const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + chalf * C::COLS;
-    // Half-slot software pipeline: the first 16-lane half of a block's slot is
-    // loaded while the previous block is still being scaled; the slot is handed
-    // back to the MMA as soon as both halves sit in registers.
+    const int chalf = (warp - kEpiWarp0) >> 2;  // which 64 of the 128 token columns
+    const int row = quarter * 32 + lane;        // this thread's weight row (TMEM lane)
+    const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + chalf * kCols;
     const int my_tiles = (p.num_tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
                          static_cast<int>(gridDim.x);
     const int total = my_tiles * KB;
-    uint32_t stage = 0, phase = 0, slot = 0, acc_phase = 0;
-    uint32_t r0[32], r1[32];
+    EpiState st{0, 0u, 0u};
+    uint32_t ra[kCols], rb[kCols];
+    float2 acc[kCols / 2];
     bool ok = total > 0 && mbar_wait(&acc_full[0], 0, &g_device_status, kDevWaitEpilogue, abort_flag);
     if (ok) {
+      // Block 0 of this CTA goes into buffer A before the pipelined loop.
       tc_fence_after();
-      tmem_ld_16x256b_x8(tbase, r0);
+      load_slot(tbase, ra);
       tmem_wait_ld();
     }
-    int g = 0;
     for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-      const int n0 = (tile % p.n_tiles) * kBM;
-      const int m0 = (tile / p.n_tiles) * BN;
-      float2 acc[32];
 #pragma unroll
-      for (int c = 0; c < 32; ++c) acc[c] = make_float2(0.0f, 0.0f);
-      for (int ks = 0; ok && ks < n_ks; ++ks) {
-        if (!mbar_wait(&full[stage], phase, &g_device_status, kDevWaitEpilogue, abort_flag)) {
+      for (int c = 0; c < kCols / 2; ++c) acc[c] = make_float2(0.0f, 0.0f);
+      for (int kb = 0; kb < KB; kb += 2) {  // KB is a whole number of stages, so even
+        if (!epi_step<STAGES, DUMP, true>(ra, rb, acc, st, kb, tile, p, total, smem, full, empty, acc_full,
+                                          acc_empty, abort_flag, tbase, row, chalf, lane) ||
+            !epi_step<STAGES, DUMP, false>(rb, ra, acc, st, kb + 1, tile, p, total, smem, full, empty, acc_full,
+                                           acc_empty, abort_flag, tbase, row, chalf, lane)) {
           ok = false;
           break;
         }
-        const uint8_t* sb = smem + stage * C::STAGE_BYTES;
-        const float* sw = reinterpret_cast<const float*>(sb + C::A_BYTES + C::B_BYTES);
-        const float* sa = sw + kKBS * kBM;
-        const int nblk = min(kKBS, KB - ks * kKBS);
-        for (int j = 0; j < nblk; ++j, ++g) {
-          const uint32_t taddr = tbase + slot * BN;
-          tmem_ld_16x256b_x8(taddr + (16u << 16), r1);  // second half of this block
-          const float* swj = sw + j * kBM + row0;
-          const float w0 = swj[0], w1 = swj[8], w2 = swj[16], w3 = swj[24];
-          const float2* saj = reinterpret_cast<const float2*>(sa + j * BN + col0);
-          float2 da[8];
-#pragma unroll
-          for (int q = 0; q < 8; ++q) da[q] = saj[4 * q];
-          if (DUMP) dump_half(p, r0, n0 + row0, m0 + col0, KB, ks * kKBS + j);
-          fold_half(acc, 0, r0, da, make_float2(w0, w0), make_float2(w0 * kNegTwoPowM129, w0 * kNegTwoPowM129),
-                    make_float2(w1, w1), make_float2(w1 * kNegTwoPowM129, w1 * kNegTwoPowM129));
-          tmem_wait_ld();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[slot]);  // both halves are in registers
-          if (++slot == C::ACC_SLOTS) {
-            slot = 0;
-            acc_phase ^= 1u;
-          }
-          if (g + 1 < total) {  // prefetch the next block's first half
-            if (!mbar_wait(&acc_full[slot], acc_phase, &g_device_status, kDevWaitEpilogue, abort_flag)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            tmem_ld_16x256b_x8(tbase + slot * BN, r0);
-          }
-          if (DUMP) dump_half(p, r1, n0 + row0 + 16, m0 + col0, KB, ks * kKBS + j);
-          fold_half(acc, 2, r1, da, make_float2(w2, w2), make_float2(w2 * kNegTwoPowM129, w2 * kNegTwoPowM129),
-                    make_float2(w3, w3), make_float2(w3 * kNegTwoPowM129, w3 * kNegTwoPowM129));
-          tmem_wait_ld();
-        }
-        if (!ok) break;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[stage]);
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
       }
-      if (!ok) break;
-      if (p.y) {
-        // acc[8k + g] = rows row0 + 8k, columns col0 + 8g + {0, 1}
+      if (!ok || !p.y) continue;
+      const int64_t n = static_cast<int64_t>(tile % p.n_tiles) * kBM + row;
+      const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * kBN + chalf * kCols;
+      if (n < p.N) {
+        const float bv = p.bias ? p.bias[n] : 0.0f;
+        float* yp = p.y + m0 * p.ldy + n;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int64_t n = static_cast<int64_t>(n0) + row0 + 8 * k;
-          if (n >= p.N) continue;
-          const float bv = p.bias ? p.bias[n] : 0.0f;
-#pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            const int64_t m = static_cast<int64_t>(m0) + col0 + 8 * g;
-            const float2 v = acc[8 * k + g];
-            if (m < p.M) p.y[m * p.ldy + n] = p.bias ? v.x + bv : v.x;
-            if (m + 1 < p.M) p.y[(m + 1) * p.ldy + n] = p.bias ? v.y + bv : v.y;
-          }
+        for (int c = 0; c < kCols / 2; ++c) {
+          if (m0 + 2 * c < p.M) yp[(2 * c) * p.ldy] = p.bias ? acc[c].x + bv : acc[c].x;
+          if (m0 + 2 * c + 1 < p.M) yp[(2 * c + 1) * p.ldy] = p.bias ? acc[c].y + bv : acc[c].y;
         }
       }
     }
@@ -434,32 +433,33 @@ bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uin
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int STAGES, bool DUMP>
+template <int STAGES, bool DUMP>
 cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
-  using C = Cfg<BN, STAGES>;
+  using C = Cfg<STAGES>;
   const int64_t KB = g.K / kQK;
   CUtensorMap tm_wc, tm_ac, tm_ws, tm_as;
   if (!make_map_2d(&tm_wc, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.w.codes, g.K, g.N, g.K, kStageK, kBM,
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map_2d(&tm_ac, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.a.codes, g.K, g.M, g.K, kStageK, BN,
+      !make_map_2d(&tm_ac, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.a.codes, g.K, g.M, g.K, kStageK, kBN,
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map_2d(&tm_ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, g.w.scales, g.N, KB, g.w.ld * 4, kBM,
                    kKBS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_map_2d(&tm_as, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, g.a.scales, g.M, KB, g.a.ld * 4, BN,
+      !make_map_2d(&tm_as, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, g.a.scales, g.M, KB, g.a.ld * 4, kBN,
                    kKBS, CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
   TcParams p;
   p.M = static_cast<int>(g.M);
   p.N = static_cast<int>(g.N);
-  p.KB = static_cast<int>(KB);
+  p.KB = static_cast<int>((KB + kKBS - 1) / kKBS * kKBS);
+  p.KB_real = static_cast<int>(KB);
   p.n_tiles = static_cast<int>((g.N + kBM - 1) / kBM);
-  const int m_tiles = static_cast<int>((g.M + BN - 1) / BN);
+  const int m_tiles = static_cast<int>((g.M + kBN - 1) / kBN);
   p.num_tiles = p.n_tiles * m_tiles;
   p.y = g.y;
   p.ldy = g.ldy;
   p.bias = g.bias;
   p.dots = g.dots;
-  auto kern = gemm_tc_kernel<BN, STAGES, DUMP>;
+  auto kern = gemm_tc_kernel<STAGES, DUMP>;
   cudaFuncAttributes fa;
   cudaError_t e = cudaFuncGetAttributes(&fa, kern);
   if (e != cudaSuccess) return e;
@@ -482,8 +482,8 @@ cudaError_t read_device_status(unsigned int* value, bool clear) {
 
 cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, cudaStream_t s) {
   if (g.M == 0 || g.N == 0) return cudaSuccess;
-  if (g.dots) return launch_cfg<128, 4, true>(g, num_sms, s);
-  return launch_cfg<128, 4, false>(g, num_sms, s);
+  if (g.dots) return launch_cfg<4, true>(g, num_sms, s);
+  return launch_cfg<4, false>(g, num_sms, s);
 }
 
 }  // namespace b2q
