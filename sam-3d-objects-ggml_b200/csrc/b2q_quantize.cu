@@ -9,9 +9,8 @@
 // Each division, product and rounding is one IEEE fp32 operation, so the codes
 // and scales are bit-identical to the CPU's.
 //
-// Mapping: a warp quantizes 128-value segments (4 blocks) of a row; each lane
-// loads one 128-bit float4 per segment, so 8 lanes own one block and the
-// block's absmax is three xor-shuffles inside that 8-lane group.
+// Mapping: one lane per 32-value block, a warp per 32 rows x 1 block (see
+// quantize_q8_0_kernel).
 #include "b2q_internal.h"
 #include "b2q_ptx.cuh"
 
@@ -22,40 +21,13 @@ namespace b2q {
 namespace {
 
 template <int VARIANT>
-__device__ __forceinline__ int quantize_one(float v, float inv) {
+__device__ __forceinline__ uint32_t quantize_code(float v, float inv) {
   const float s = __fmul_rn(v, inv);
   if (VARIANT == 0) {
-    int q = __float2int_rn(s);  // round to nearest, ties to even
-    return max(-128, min(127, q));
+    const int q = __float2int_rn(s);  // round to nearest, ties to even
+    return static_cast<uint32_t>(max(-128, min(127, q))) & 0xffu;
   }
-  return static_cast<int>(roundf(s));  // ties away from zero
-}
-
-struct BlockQuant {
-  uint32_t packed;  // 4 codes of this lane, little-endian
-  float d;          // fp32 block scale before the fp16 store
-};
-
-template <int VARIANT>
-__device__ __forceinline__ BlockQuant quantize_lane(float4 v) {
-  float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-  BlockQuant r;
-  r.d = __fdiv_rn(amax, 127.0f);
-  float inv;
-  if (VARIANT == 0)
-    inv = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-  else
-    inv = r.d != 0.0f ? __fdiv_rn(1.0f, r.d) : 0.0f;
-  const int q0 = quantize_one<VARIANT>(v.x, inv);
-  const int q1 = quantize_one<VARIANT>(v.y, inv);
-  const int q2 = quantize_one<VARIANT>(v.z, inv);
-  const int q3 = quantize_one<VARIANT>(v.w, inv);
-  r.packed = (static_cast<uint32_t>(q0) & 0xffu) | ((static_cast<uint32_t>(q1) & 0xffu) << 8) |
-             ((static_cast<uint32_t>(q2) & 0xffu) << 16) | ((static_cast<uint32_t>(q3) & 0xffu) << 24);
-  return r;
+  return static_cast<uint32_t>(static_cast<int>(roundf(s))) & 0xffu;  // ties away from zero
 }
 
 template <bool VEC4>
@@ -64,12 +36,13 @@ __device__ __forceinline__ float4 load4(const float* p) {
   return make_float4(__ldg(p), __ldg(p + 1), __ldg(p + 2), __ldg(p + 3));
 }
 
-// SPLIT = true : codes int8 [m][k] + fp32 scales [k/32][ld] (GEMM layout)
-// SPLIT = false: ggml block_q8_0 rows (34-byte blocks)
-// Each warp step handles kUnroll consecutive segments, all loads issued first,
-// so every warp keeps kUnroll * 512 bytes in flight.
-constexpr int kUnroll = 4;
-
+// One lane quantizes one whole 32-value block: lane i of a warp takes row
+// 32*rg + i, so a warp covers one block column of 32 consecutive rows.  The
+// block's absmax, scale and inverse are computed once (no cross-lane work and
+// no per-lane duplicates), the 32 codes leave as two 16-byte stores, and the
+// 32 lanes' scales of the split layout form one coalesced 128-byte store.
+// Work units (row group, block) are spread over the grid's warps; all eight
+// 16-byte loads of a unit are issued before any arithmetic.
 template <int VARIANT, bool SPLIT, bool VEC4>
 __global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float* __restrict__ x, int64_t m,
                                                             int64_t k, int64_t ldx,
@@ -77,38 +50,47 @@ __global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float* __restr
                                                             int8_t* __restrict__ codes,
                                                             float* __restrict__ scales, int64_t ld) {
   const int lane = threadIdx.x & 31;
-  const int64_t segs = (k + 127) / 128;
-  const int64_t total = m * segs;
+  const int64_t kb = k / kQK;
+  const int64_t units = (m + 31) / 32 * kb;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
-  for (int64_t w0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32 * kUnroll;
-       w0 < total; w0 += warps * kUnroll) {
-    float4 v[kUnroll];
-    int64_t row[kUnroll], k0[kUnroll];
-    bool valid[kUnroll];
+  for (int64_t u = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32; u < units; u += warps) {
+    const int64_t rg = u / kb;
+    const int64_t b = u - rg * kb;
+    const int64_t row = rg * 32 + lane;
+    if (row >= m) continue;
+    const float* src = x + row * ldx + b * kQK;
+    float4 v[8];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int64_t w = w0 + u;
-      row[u] = w / segs;
-      k0[u] = (w - row[u] * segs) * 128 + lane * 4;
-      valid[u] = w < total && k0[u] < k;  // k % 32 == 0: a block is all-valid or all-invalid
-      v[u] = valid[u] ? load4<VEC4>(x + row[u] * ldx + k0[u]) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    for (int i = 0; i < 8; ++i) v[i] = load4<VEC4>(src + 4 * i);
+    float amax = 0.0f;
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const BlockQuant q = quantize_lane<VARIANT>(v[u]);
-      if (!valid[u]) continue;
-      const int64_t blk = k0[u] / kQK;
-      const int sub = lane & 7;
-      const __half dh = __float2half_rn(q.d);
-      if (SPLIT) {
-        *reinterpret_cast<uint32_t*>(codes + row[u] * k + k0[u]) = q.packed;
-        if (sub == 0) scales[blk * ld + row[u]] = __half2float(dh) * kActScaleMul;
-      } else {
-        uint8_t* b = yb + row[u] * ldy + blk * kQ8Bytes;
-        uint16_t* b16 = reinterpret_cast<uint16_t*>(b + 2 + 4 * sub);
-        b16[0] = static_cast<uint16_t>(q.packed & 0xffffu);
-        b16[1] = static_cast<uint16_t>(q.packed >> 16);
-        if (sub == 0) *reinterpret_cast<uint16_t*>(b) = __half_as_ushort(dh);
+    for (int i = 0; i < 8; ++i)
+      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+    const float d = __fdiv_rn(amax, 127.0f);
+    float inv;
+    if (VARIANT == 0)
+      inv = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+    else
+      inv = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    uint32_t q[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      q[i] = quantize_code<VARIANT>(v[i].x, inv) | (quantize_code<VARIANT>(v[i].y, inv) << 8) |
+             (quantize_code<VARIANT>(v[i].z, inv) << 16) | (quantize_code<VARIANT>(v[i].w, inv) << 24);
+    const __half dh = __float2half_rn(d);
+    if (SPLIT) {
+      uint4* dst = reinterpret_cast<uint4*>(codes + row * k + b * kQK);
+      dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
+      dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
+      scales[b * ld + row] = __half2float(dh) * kActScaleMul;
+    } else {
+      // ggml block_q8_0: fp16 d then 32 codes; 34-byte blocks are 2-byte aligned
+      uint16_t* dst = reinterpret_cast<uint16_t*>(yb + row * ldy + b * kQ8Bytes);
+      dst[0] = __half_as_ushort(dh);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        dst[1 + 2 * i] = static_cast<uint16_t>(q[i] & 0xffffu);
+        dst[2 + 2 * i] = static_cast<uint16_t>(q[i] >> 16);
       }
     }
   }
@@ -117,12 +99,13 @@ __global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float* __restr
 template <bool SPLIT, bool VEC4>
 cudaError_t launch_q(const float* x, int64_t m, int64_t k, int64_t ldx, uint8_t* yb, int64_t ldy,
                      int8_t* codes, float* scales, int64_t ld, int variant, cudaStream_t s) {
-  const int64_t warps_needed = (m * ((k + 127) / 128) + kUnroll - 1) / kUnroll;
-  if (warps_needed == 0) return cudaSuccess;
+  const int64_t units = (m + 31) / 32 * (k / kQK);
+  if (units == 0) return cudaSuccess;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t blocks_needed = (warps_needed + 7) / 8;
+  // 8 warps per block; at most 8 resident blocks per SM, one unit per warp when that fits
+  const int64_t blocks_needed = (units + 7) / 8;
   const int grid = static_cast<int>(blocks_needed < sms * 8 ? blocks_needed : sms * 8);
   if (variant == 0)
     quantize_q8_0_kernel<0, SPLIT, VEC4><<<grid, 256, 0, s>>>(x, m, k, ldx, yb, ldy, codes, scales, ld);
