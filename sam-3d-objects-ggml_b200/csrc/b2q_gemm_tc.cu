@@ -59,12 +59,11 @@ __device__ unsigned int g_device_status = 0;
 namespace {
 
 constexpr int kBM = 128;             // weight rows per tile (MMA M, TMEM lanes)
-constexpr int kBN = 128;             // tokens per tile (MMA N, columns per slot)
+constexpr int kSlotCols = 128;       // TMEM columns per accumulator slot (the widest tile)
 constexpr int kKBS = 4;              // 32-value blocks per pipeline stage
 constexpr int kStageK = kKBS * kQK;  // 128 bytes of K per operand row per stage
 constexpr int kEpiWarps = 8;
 constexpr int kEpiWarp0 = 4;         // epilogue = warpgroups 1 and 2
-constexpr int kCols = kBN / 2;       // token columns per epilogue thread
 constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;
 // Register split (setmaxnreg works per warpgroup).  The kernel is compiled for
 // 384 threads at kLaunchRegs registers each (the per-SM-subpartition cap for
@@ -77,20 +76,25 @@ constexpr int kRegsControl = 40;
 constexpr int kRegsEpilogue = 232;
 static_assert(128 * kRegsControl + 256 * kRegsEpilogue <= kThreads * kLaunchRegs, "register split");
 constexpr uint32_t kTmemCols = 512;
-constexpr int kSlots = static_cast<int>(kTmemCols) / kBN;  // accumulator slots (blocks in flight)
+constexpr int kSlots = static_cast<int>(kTmemCols) / kSlotCols;  // accumulator slots (blocks in flight)
 constexpr int kPairs = kSlots / 2;  // slots are handed over in pairs of consecutive blocks
 static_assert(kKBS % 2 == 0, "a stage holds whole slot pairs");
 constexpr uint32_t kOffset = 1u << 20;        // added to every S by the constant MMA
 constexpr int kOffsetTileBytes = 4096;        // 128 rows x 32 bytes, every 16-byte chunk = P
 constexpr float kNegTwoPowM129 = -0x1p-129f;  // subnormal, exact
 
-template <int STAGES>
+// BN: tokens per tile (MMA N), 64..128 in steps of 16; the host picks it per
+// shape so that the tiles spread evenly over the SMs (see pick_bn).
+template <int STAGES, int BN>
 struct Cfg {
+  static_assert(BN % 16 == 0 && BN >= 64 && BN <= kSlotCols, "tile width");
+  static constexpr int COLS = BN / 2;  // token columns per epilogue thread
   static constexpr int A_BYTES = kBM * kStageK;
-  static constexpr int B_BYTES = kBN * kStageK;
+  static constexpr int B_BYTES = BN * kStageK;
   static constexpr int SW_BYTES = kKBS * kBM * 4;
-  static constexpr int SA_BYTES = kKBS * kBN * 4;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SW_BYTES + SA_BYTES;
+  static constexpr int SA_BYTES = kKBS * BN * 4;
+  static constexpr int TX_BYTES = A_BYTES + B_BYTES + SW_BYTES + SA_BYTES;  // bytes the TMA delivers per stage
+  static constexpr int STAGE_BYTES = (TX_BYTES + 1023) / 1024 * 1024;          // stage pitch in smem
   static constexpr int OFF_TILE = STAGES * STAGE_BYTES;
   static constexpr int BAR_OFF = OFF_TILE + kOffsetTileBytes;
   static constexpr int NBARS = 2 * STAGES + 2 * kPairs + 1;
@@ -126,10 +130,18 @@ __host__ __device__ constexpr uint32_t idesc_u8(int m, int n) {
   return (2u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
-// This thread's 64 columns of one accumulator slot (two 32-column loads).
-__device__ __forceinline__ void load_slot(uint32_t taddr, uint32_t (&r)[kCols]) {
-  tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-  tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+// This thread's COLS columns of one accumulator slot, in 32/16/8-column loads.
+template <int COLS>
+__device__ __forceinline__ void load_slot(uint32_t taddr, uint32_t (&r)[COLS]) {
+  static_assert(COLS % 8 == 0, "slot columns");
+  int c = 0;
+#pragma unroll
+  for (; c + 32 <= COLS; c += 32) tmem_ld_32x32b_x32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(&r[c]));
+  if (c + 16 <= COLS) {
+    tmem_ld_32x32b_x16(taddr + c, &r[c]);
+    c += 16;
+  }
+  if (c + 8 <= COLS) tmem_ld_32x32b_x8(taddr + c, &r[c]);
 }
 
 // Where the epilogue of one CTA stands in its flat sequence of blocks.
@@ -145,13 +157,13 @@ struct EpiState {
 // waits for the next pair before loading its first block.  kb: block within
 // the tile (stage boundaries fall on even blocks).  Returns false when a
 // bounded wait gave up.
-template <int STAGES, bool DUMP, bool FIRST>
-__device__ __forceinline__ bool epi_step(uint32_t (&cur)[kCols], uint32_t (&nxt)[kCols], float2 (&acc)[kCols / 2],
+template <int STAGES, int BN, bool DUMP, bool FIRST, int COLS = BN / 2>
+__device__ __forceinline__ bool epi_step(uint32_t (&cur)[COLS], uint32_t (&nxt)[COLS], float2 (&acc)[COLS / 2],
                                          EpiState& st, int kb, int tile, const TcParams& p, int total,
                                          uint8_t* smem, uint64_t* full, uint64_t* empty, uint64_t* acc_full,
                                          uint64_t* acc_empty, volatile int* abort_flag, uint32_t tbase,
                                          int row, int chalf, int lane) {
-  using C = Cfg<STAGES>;
+  using C = Cfg<STAGES, BN>;
   const int j = kb & (kKBS - 1);
   if (FIRST && j == 0 &&
       !mbar_wait(&full[st.stage], st.phase, &g_device_status, kDevWaitEpilogue, abort_flag))
@@ -164,7 +176,7 @@ __device__ __forceinline__ bool epi_step(uint32_t (&cur)[kCols], uint32_t (&nxt)
         !mbar_wait(&acc_full[npair], (nb / kSlots) & 1u, &g_device_status, kDevWaitEpilogue, abort_flag))
       return false;
     tc_fence_after();
-    load_slot(tbase + (nb & (kSlots - 1)) * kBN, nxt);
+    load_slot<COLS>(tbase + (nb & (kSlots - 1)) * kSlotCols, nxt);
   }
   const uint8_t* sb = smem + st.stage * C::STAGE_BYTES;
   const float* sw = reinterpret_cast<const float*>(sb + C::A_BYTES + C::B_BYTES);
@@ -172,17 +184,17 @@ __device__ __forceinline__ bool epi_step(uint32_t (&cur)[kCols], uint32_t (&nxt)
   const float w = sw[j * kBM + row];
   const float2 w2 = make_float2(w, w);
   const float2 c2 = make_float2(w * kNegTwoPowM129, w * kNegTwoPowM129);
-  const float4* da4 = reinterpret_cast<const float4*>(sa + j * kBN + chalf * kCols);
+  const float4* da4 = reinterpret_cast<const float4*>(sa + j * BN + chalf * COLS);
   if (DUMP && kb < p.KB_real) {
     const int64_t n = static_cast<int64_t>(tile % p.n_tiles) * kBM + row;
-    const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * kBN + chalf * kCols;
-    for (int c = 0; c < kCols; ++c) {
+    const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * BN + chalf * COLS;
+    for (int c = 0; c < COLS; ++c) {
       const int64_t m = m0 + c;
       if (n < p.N && m < p.M) p.dots[(m * p.N + n) * p.KB_real + kb] = static_cast<int32_t>(cur[c] - kOffset);
     }
   }
 #pragma unroll
-  for (int i = 0; i < kCols / 4; ++i) {
+  for (int i = 0; i < COLS / 4; ++i) {
     const float4 d = da4[i];
     const float2 t0 = ffma2(make_float2(__uint_as_float(cur[4 * i]), __uint_as_float(cur[4 * i + 1])), w2, c2);
     const float2 t1 = ffma2(make_float2(__uint_as_float(cur[4 * i + 2]), __uint_as_float(cur[4 * i + 3])), w2, c2);
@@ -208,12 +220,13 @@ __device__ __forceinline__ bool epi_step(uint32_t (&cur)[kCols], uint32_t (&nxt)
   return true;
 }
 
-template <int STAGES, bool DUMP>
+template <int STAGES, int BN, bool DUMP>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_wc, const __grid_constant__ CUtensorMap tm_ac,
                    const __grid_constant__ CUtensorMap tm_ws, const __grid_constant__ CUtensorMap tm_as,
                    const TcParams p) {
-  using C = Cfg<STAGES>;
+  using C = Cfg<STAGES, BN>;
+  constexpr int COLS = C::COLS;
   extern __shared__ uint8_t smem_raw[];
   // Offset arithmetic on the __shared__ array itself (no integer round trip), so
   // the compiler keeps the shared address space and emits shared-memory loads.
@@ -278,14 +291,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
           const int n0 = (tile % p.n_tiles) * kBM;
-          const int m0 = (tile / p.n_tiles) * kBN;
+          const int m0 = (tile / p.n_tiles) * BN;
           for (int ks = 0; ks < n_ks; ++ks) {
             if (!mbar_wait(&empty[stage], phase ^ 1u, &g_device_status, kDevWaitProducer, abort_flag)) {
               ok = false;
               break;
             }
             uint8_t* sb = smem + stage * C::STAGE_BYTES;
-            mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+            mbar_arrive_expect_tx(&full[stage], C::TX_BYTES);
             tma_load_2d(sb, &tm_wc, &full[stage], ks * kStageK, n0);
             tma_load_2d(sb + C::A_BYTES, &tm_ac, &full[stage], ks * kStageK, m0);
             tma_load_2d(sb + C::A_BYTES + C::B_BYTES, &tm_ws, &full[stage], n0, ks * kKBS);
@@ -306,8 +319,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
       // -------------------------------------------------------- MMA issuer
       if (elect_one()) {
-        constexpr uint32_t idesc = idesc_i8(kBM, kBN);
-        constexpr uint32_t idesc_off = idesc_u8(kBM, kBN);
+        constexpr uint32_t idesc = idesc_i8(kBM, BN);
+        constexpr uint32_t idesc_off = idesc_u8(kBM, BN);
         const uint64_t off_desc = smem_desc_k_noswz(smem_u32(smem + C::OFF_TILE));
         uint32_t stage = 0, phase = 0, q = 0;  // q: pair counter; pair q fills slots 2(q % kPairs) + {0, 1}
         bool ok = true;
@@ -329,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               tc_fence_after();
 #pragma unroll
               for (int j = j2; j < j2 + 2; ++j) {
-                const uint32_t d = tmem_base + (2 * pair + (j - j2)) * kBN;
+                const uint32_t d = tmem_base + (2 * pair + (j - j2)) * kSlotCols;
                 mma_i8(d, smem_desc_k_sw128(a_base + j * kQK), smem_desc_k_sw128(b_base + j * kQK), idesc, 0u);
                 mma_i8(d, off_desc, off_desc, idesc_off, 1u);
               }
@@ -352,13 +365,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;               // TMEM lane quarter this warp may access
     const int chalf = (warp - kEpiWarp0) >> 2;  // which 64 of the 128 token columns
     const int row = quarter * 32 + lane;        // this thread's weight row (TMEM lane)
-    const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + chalf * kCols;
+    const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + chalf * COLS;
     const int my_tiles = (p.num_tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
                          static_cast<int>(gridDim.x);
     const int total = my_tiles * KB;
     EpiState st{0, 0u, 0u};
-    uint32_t ra[kCols], rb[kCols];
-    float2 acc[kCols / 2];
+    uint32_t ra[COLS], rb[COLS];
+    float2 acc[COLS / 2];
     bool ok = total > 0 && mbar_wait(&acc_full[0], 0, &g_device_status, kDevWaitEpilogue, abort_flag);
     if (ok) {
       // Block 0 of this CTA goes into buffer A before the pipelined loop.
@@ -368,11 +381,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
 #pragma unroll
-      for (int c = 0; c < kCols / 2; ++c) acc[c] = make_float2(0.0f, 0.0f);
+      for (int c = 0; c < COLS / 2; ++c) acc[c] = make_float2(0.0f, 0.0f);
       for (int kb = 0; kb < KB; kb += 2) {  // KB is a whole number of stages, so even
-        if (!epi_step<STAGES, DUMP, true>(ra, rb, acc, st, kb, tile, p, total, smem, full, empty, acc_full,
+        if (!epi_step<STAGES, BN, DUMP, true>(ra, rb, acc, st, kb, tile, p, total, smem, full, empty, acc_full,
                                           acc_empty, abort_flag, tbase, row, chalf, lane) ||
-            !epi_step<STAGES, DUMP, false>(rb, ra, acc, st, kb + 1, tile, p, total, smem, full, empty, acc_full,
+            !epi_step<STAGES, BN, DUMP, false>(rb, ra, acc, st, kb + 1, tile, p, total, smem, full, empty, acc_full,
                                            acc_empty, abort_flag, tbase, row, chalf, lane)) {
           ok = false;
           break;
@@ -380,12 +393,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok || !p.y) continue;
       const int64_t n = static_cast<int64_t>(tile % p.n_tiles) * kBM + row;
-      const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * kBN + chalf * kCols;
+      const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * BN + chalf * COLS;
       if (n < p.N) {
         const float bv = p.bias ? p.bias[n] : 0.0f;
         float* yp = p.y + m0 * p.ldy + n;
 #pragma unroll
-        for (int c = 0; c < kCols / 2; ++c) {
+        for (int c = 0; c < COLS / 2; ++c) {
           if (m0 + 2 * c < p.M) yp[(2 * c) * p.ldy] = p.bias ? acc[c].x + bv : acc[c].x;
           if (m0 + 2 * c + 1 < p.M) yp[(2 * c + 1) * p.ldy] = p.bias ? acc[c].y + bv : acc[c].y;
         }
@@ -433,18 +446,18 @@ bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uin
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int STAGES, bool DUMP>
+template <int STAGES, int BN, bool DUMP>
 cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
-  using C = Cfg<STAGES>;
+  using C = Cfg<STAGES, BN>;
   const int64_t KB = g.K / kQK;
   CUtensorMap tm_wc, tm_ac, tm_ws, tm_as;
   if (!make_map_2d(&tm_wc, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.w.codes, g.K, g.N, g.K, kStageK, kBM,
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map_2d(&tm_ac, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.a.codes, g.K, g.M, g.K, kStageK, kBN,
+      !make_map_2d(&tm_ac, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.a.codes, g.K, g.M, g.K, kStageK, BN,
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map_2d(&tm_ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, g.w.scales, g.N, KB, g.w.ld * 4, kBM,
                    kKBS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_map_2d(&tm_as, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, g.a.scales, g.M, KB, g.a.ld * 4, kBN,
+      !make_map_2d(&tm_as, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, g.a.scales, g.M, KB, g.a.ld * 4, BN,
                    kKBS, CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
   TcParams p;
@@ -453,13 +466,13 @@ cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
   p.KB = static_cast<int>((KB + kKBS - 1) / kKBS * kKBS);
   p.KB_real = static_cast<int>(KB);
   p.n_tiles = static_cast<int>((g.N + kBM - 1) / kBM);
-  const int m_tiles = static_cast<int>((g.M + kBN - 1) / kBN);
+  const int m_tiles = static_cast<int>((g.M + BN - 1) / BN);
   p.num_tiles = p.n_tiles * m_tiles;
   p.y = g.y;
   p.ldy = g.ldy;
   p.bias = g.bias;
   p.dots = g.dots;
-  auto kern = gemm_tc_kernel<STAGES, DUMP>;
+  auto kern = gemm_tc_kernel<STAGES, BN, DUMP>;
   cudaFuncAttributes fa;
   cudaError_t e = cudaFuncGetAttributes(&fa, kern);
   if (e != cudaSuccess) return e;
@@ -469,6 +482,28 @@ cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
   const int grid = p.num_tiles < num_sms ? p.num_tiles : num_sms;
   kern<<<grid, kThreads, C::SMEM, s>>>(tm_wc, tm_ac, tm_ws, tm_as, p);
   return cudaGetLastError();
+}
+
+// Tile width for an M x N problem: the candidate whose busiest SM finishes
+// first.  One tile costs about (0.3 + 0.7 * BN / 128) of a 128-wide tile (the
+// per-block hand-offs and MMA issue do not shrink with the width); ties go to
+// the wider tile.  Wide problems keep 128 (fc1-like shapes fill every wave);
+// narrow or short ones (few tiles per SM) trade width for balance.
+int pick_bn(int64_t m, int64_t n, int num_sms) {
+  static const int cands[] = {128, 112, 96, 80, 64};
+  const int64_t n_tiles = (n + kBM - 1) / kBM;
+  int best = 128;
+  double best_cost = 1e300;
+  for (int bn : cands) {
+    const int64_t tiles = n_tiles * ((m + bn - 1) / bn);
+    const int64_t rounds = (tiles + num_sms - 1) / num_sms;
+    const double cost = static_cast<double>(rounds) * (0.3 + 0.7 * bn / 128.0);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
 }
 
 }  // namespace
@@ -482,8 +517,14 @@ cudaError_t read_device_status(unsigned int* value, bool clear) {
 
 cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, cudaStream_t s) {
   if (g.M == 0 || g.N == 0) return cudaSuccess;
-  if (g.dots) return launch_cfg<4, true>(g, num_sms, s);
-  return launch_cfg<4, false>(g, num_sms, s);
+  if (g.dots) return launch_cfg<4, 128, true>(g, num_sms, s);
+  switch (pick_bn(g.M, g.N, num_sms)) {
+    case 112: return launch_cfg<4, 112, false>(g, num_sms, s);
+    case 96: return launch_cfg<4, 96, false>(g, num_sms, s);
+    case 80: return launch_cfg<4, 80, false>(g, num_sms, s);
+    case 64: return launch_cfg<4, 64, false>(g, num_sms, s);
+    default: return launch_cfg<4, 128, false>(g, num_sms, s);
+  }
 }
 
 }  // namespace b2q
