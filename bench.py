@@ -306,16 +306,26 @@ def run_gpu(args, rank, world, local_rank):
 
 
 # -------------------------------------------------------------------- CPU arm
+def host_threads() -> int:
+    """Every core this process may run on.  Passed to the oracle explicitly:
+    torchrun sets OMP_NUM_THREADS=1 in each rank, which would otherwise leave
+    the CPU arm (rank 0 alone) on one core."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_sample_run(inputs, frac):
     """Oracle (vectorised port of ggml's CPU mul_mat) over the first `frac` of
     each GEMM's token rows; returns (ops, seconds, threads)."""
     import oracle as O
-    ops, secs, thr = 0.0, 0.0, O.num_threads()
+    ops, secs, thr = 0.0, 0.0, host_threads()
     for name, wtype, M, N, K, wq, x in inputs:
         rows = max(1, int(round(M * frac)))
         xs = np.ascontiguousarray(x[:rows])
         t0 = time.perf_counter()
-        O.mul_mat(wtype, wq, xs, O.ACT_X86, fast=True)
+        O.mul_mat(wtype, wq, xs, O.ACT_X86, nthreads=thr, fast=True)
         secs += time.perf_counter() - t0
         ops += ops_of(rows, N, K)
     return ops, secs, thr
