@@ -356,6 +356,113 @@ def run_gpu(args, rank, world, local_rank):
     return result
 
 
+# ------------------------------------------------- column-parallel (multi-GPU)
+COLPAR_SHAPE = ("slat_qkv_q4_0", 2, 20480, 3072, 1024)  # name, wtype, M tokens, N out, K in
+
+
+def run_colpar(args, rank, world, local_rank):
+    """One large SLat linear split by output rows over the ranks (survey §8(e)):
+    every rank needs the whole [M][N] output.  Times the fused kernel (GEMM
+    epilogue storing each tile into every rank's buffer over NVLink) against
+    GEMM + NCCL all-gather + transpose.  Each iteration ends with a one-element
+    all-reduce so that every rank's work of the iteration is complete; both
+    variants pay it."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import b2q
+    import colpar
+    import oracle as O
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    name, wtype, M, N, K = COLPAR_SHAPE
+    rng = np.random.default_rng(4321)  # same weights and inputs on every rank
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    wq = O.quantize(w, wtype)
+    start, stop = colpar.slices(N, world)[rank]
+    n = stop - start
+    stream = torch.cuda.current_stream()
+    w_d = torch.from_numpy(wq[start:stop]).to(dev)
+    packed = b2q.weight_pack(wtype, w_d, K)
+    act = b2q.act_prepare(torch.from_numpy(x).to(dev))
+    bufs = colpar.PeerBuffers(M, N)
+    tick = torch.zeros(1, device=dev)
+    equal = all(b - a == n for a, b in colpar.slices(N, world))
+    slice_out = torch.empty((M, n), dtype=torch.float32, device=dev)
+    gathered = torch.empty((world * M, n), dtype=torch.float32, device=dev) if equal else None
+    out = torch.empty((M, N), dtype=torch.float32, device=dev)
+
+    def fused():
+        colpar.fused(packed, n, K, act, M, bufs, start, stream=stream)
+        if world > 1:
+            dist.all_reduce(tick)
+
+    def baseline():
+        if world > 1:
+            colpar.nccl_baseline(packed, n, K, act, M, N, slice_out, gathered, out, stream=stream)
+            dist.all_reduce(tick)
+        else:
+            b2q.mul_mat_prepared(packed, n, K, act, M, out=out, stream=stream)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ms_fused = timed(fused)
+    ms_base = timed(baseline) if (equal or world == 1) else None
+    # parity of the fused result against a single-GPU GEMM of the whole weight (rank 0)
+    ok = None
+    if rank == 0:
+        full = b2q.mul_mat(wtype, torch.from_numpy(wq).to(dev), torch.from_numpy(x).to(dev))
+        ok = bool(torch.equal(bufs.to_tensor(dev), full))
+    status = b2q.device_status(clear=True)
+    if world > 1:
+        dist.barrier()
+    bufs.close()
+    if world > 1:
+        dist.destroy_process_group()
+    ops = 2.0 * M * N * K
+    gathered_bytes = M * N * 4 * (world - 1) // world  # each rank receives the others' slices
+    return {
+        "metric": "column-parallel Q4_0 mul_mat effective TOPS (output all-gathered to every rank)",
+        "value": round(ops / (ms_fused * 1e-3) / 1e12, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_fused, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "i8",
+        "data": "synthetic",
+        "config": {"workload": f"{name}: M={M} tokens, K={K} -> N={N}, weight rows split over {world} rank(s), "
+                               "every rank ends with the full [M][N] fp32 output",
+                   "parallelism": f"column-parallel tp{world}"},
+        "fused": {"ms": round(ms_fused, 4), "tops": round(ops / (ms_fused * 1e-3) / 1e12, 2),
+                  "path": "b2q_mul_mat_prepared_peers: GEMM epilogue stores tiles into every rank's "
+                          "buffer (CUDA-IPC peer pointers, NVLink)"},
+        "nccl_baseline": None if ms_base is None else {
+            "ms": round(ms_base, 4), "tops": round(ops / (ms_base * 1e-3) / 1e12, 2),
+            "path": "b2q_mul_mat_prepared on the slice + all_gather_into_tensor + transpose copy"
+                    if world > 1 else "b2q_mul_mat_prepared on the whole weight"},
+        "nvlink_bytes_in_per_rank": gathered_bytes,
+        "nvlink_gbs_in_per_rank": round(gathered_bytes / (ms_fused * 1e-3) / 1e9, 1) if world > 1 else 0.0,
+        "parity_rank0_bitwise_vs_single_gpu": ok,
+        "device_status": status,
+    }
+
+
 # -------------------------------------------------------------------- CPU arm
 def host_threads() -> int:
     """Every core this process may run on.  Passed to the oracle explicitly:
@@ -444,6 +551,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--only", default=None, help="run one workload entry (profiling case)")
+    ap.add_argument("--colpar", action="store_true",
+                    help="column-parallel SLat linear (one GEMM split over the ranks, all-gathered output)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -454,7 +563,7 @@ def main():
         if rank == 0:
             print(json.dumps(run_reference(args)), flush=True)
         return
-    res = run_gpu(args, rank, world, local_rank)
+    res = run_colpar(args, rank, world, local_rank) if args.colpar else run_gpu(args, rank, world, local_rank)
     if rank == 0:
         print(json.dumps(res), flush=True)
 

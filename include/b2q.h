@@ -151,6 +151,26 @@ B2Q_API int b2q_mul_mat_prepared(const void* packed, int64_t n, int64_t k, const
                                  int64_t m, const float* bias, float* y,
                                  int64_t y_row_stride_bytes, void* stream);
 
+/* ------------------------------------------- column-parallel form (multi-GPU)
+ * One rank of a tensor-parallel group for a single large mul_mat (the SLat
+ * flow transformer's linears at 8k-20k tokens): the weight is split by output
+ * rows across the ranks and every rank needs the full [M][N_total] output.
+ * This rank holds the packed rows [y_col0, y_col0 + n) of the weight and writes
+ * its output columns straight into the full-width y buffer of EVERY rank:
+ * y_peers[q] (host array of n_peers <= 8 device pointers this GPU can store to:
+ * its own buffer and its peers' through CUDA IPC / peer access over NVLink),
+ * element (m, j) to y_peers[q][m * y_row_stride_bytes/4 + y_col0 + j].  That is
+ * the GEMM and the all-gather of its outputs in one kernel, each tile leaving
+ * over NVLink while the next tiles compute.  No counterpart in the reference
+ * (it runs one process per GPU with no tensor parallelism); it replaces the
+ * column-parallel plan "ggml_mul_mat on a weight row slice, then ncclAllGather
+ * and a [P][M][N/P] -> [M][N] transpose".  The call only launches: the ranks
+ * must synchronise (every rank's kernel complete) before any rank reads y. */
+B2Q_API int b2q_mul_mat_prepared_peers(const void* packed, int64_t n, int64_t k, const void* act,
+                                       int64_t m, const float* bias, float* const* y_peers,
+                                       int n_peers, int64_t y_col0, int64_t y_row_stride_bytes,
+                                       void* stream);
+
 /* ------------------------------------------------------------ debug / check
  * int32 per-block dot products S_b computed by the tensor-core GEMM itself
  * (the value its epilogue reads from tensor memory), for parity checks:

@@ -67,6 +67,8 @@ def _lib_obj():
             "b2q_act_prepared_size": (SZ, [I64, I64]),
             "b2q_act_prepare": (I, [P, I64, I64, I64, I, P, SZ, P]),
             "b2q_mul_mat_prepared": (I, [P, I64, I64, P, I64, P, P, I64, P]),
+            "b2q_mul_mat_prepared_peers": (I, [P, I64, I64, P, I64, P, ctypes.POINTER(ctypes.c_void_p), I, I64,
+                                               I64, P]),
             "b2q_block_dots": (I, [I, P, I64, I64, I64, P, I64, I64, P, P, SZ, P]),
             "b2q_block_dots_workspace_size": (SZ, [I64, I64, I64]),
             "b2q_mul_mat_q_simt": (I, [I, P, I64, I64, I64, P, I64, I64, P, I64, P]),
@@ -208,6 +210,16 @@ def mul_mat_packed_noalloc(packed, n: int, k: int, x, bias=None, variant: int = 
                                           _stream(stream))
     _check("b2q_mul_mat_packed_noalloc", rc)
     return out
+
+
+def mul_mat_prepared_peers(packed, n: int, k: int, act, m: int, y_peers, y_col0: int,
+                           y_row_stride_bytes: int, bias=None, stream=None):
+    """Column-parallel mul_mat: this rank's weight rows [y_col0, y_col0 + n)
+    written into every buffer of y_peers (a list of device addresses)."""
+    arr = (ctypes.c_void_p * len(y_peers))(*[int(p) for p in y_peers])
+    rc = lib().b2q_mul_mat_prepared_peers(_ptr(packed), n, k, _ptr(act), m, _ptr(bias), arr, len(y_peers),
+                                          y_col0, y_row_stride_bytes, _stream(stream))
+    _check("b2q_mul_mat_prepared_peers", rc)
 
 
 def act_prepared_size(m: int, k: int) -> int:

@@ -250,6 +250,40 @@ int b2q_mul_mat_prepared(const void* packed, int64_t n, int64_t k, const void* a
                   static_cast<cudaStream_t>(stream));
 }
 
+int b2q_mul_mat_prepared_peers(const void* packed, int64_t n, int64_t k, const void* act, int64_t m,
+                               const float* bias, float* const* y_peers, int n_peers, int64_t y_col0,
+                               int64_t y_row_stride_bytes, void* stream) {
+  if (n < 0 || m < 0 || k <= 0 || k % kQK != 0 || y_col0 < 0) return B2Q_ERR_INVALID_ARG;
+  if (n > INT_MAX || m > INT_MAX || k > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (n_peers < 1 || n_peers > kMaxPeers || !y_peers) return B2Q_ERR_INVALID_ARG;
+  if (m > 0 && n > 0 && (!packed || !act)) return B2Q_ERR_INVALID_ARG;
+  if (y_row_stride_bytes < (y_col0 + n) * 4) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(packed, 256) || !aligned(act, 256) || y_row_stride_bytes % 4 != 0 ||
+      (bias && !aligned(bias, 4)))
+    return B2Q_ERR_MISALIGNED;
+  for (int q = 0; q < n_peers; ++q) {
+    if (!y_peers[q]) return B2Q_ERR_INVALID_ARG;
+    if (!aligned(y_peers[q], 4)) return B2Q_ERR_MISALIGNED;
+  }
+  if (m == 0 || n == 0) return B2Q_OK;
+  int sms = 0;
+  if (int rc = check_device(&sms)) return rc;
+  GemmArgs g;
+  g.w = split_at(static_cast<uint8_t*>(const_cast<void*>(packed)), n, k);
+  g.a = split_at(static_cast<uint8_t*>(const_cast<void*>(act)), m, k);
+  g.M = m;
+  g.N = n;
+  g.K = k;
+  g.y = y_peers[0];
+  g.ldy = y_row_stride_bytes / 4;
+  g.bias = bias;
+  g.dots = nullptr;
+  g.n_peers = n_peers;
+  g.y_col0 = y_col0;
+  for (int q = 0; q < n_peers; ++q) g.y_peer[q] = y_peers[q];
+  return from_cuda(launch_gemm_tc(g, sms, static_cast<cudaStream_t>(stream)));
+}
+
 size_t b2q_block_dots_workspace_size(int64_t m, int64_t n, int64_t k) {
   if (m < 0 || n < 0 || k <= 0 || k % kQK != 0) return 0;
   return split_bytes(m, k) + split_bytes(n, k);

@@ -110,6 +110,13 @@ struct TcParams {
   int64_t ldy;
   const float* bias;
   int32_t* dots;
+  // Column-parallel output (n_peers > 0): every element also goes to
+  // y_peer[q][m * ldy + y_col0 + n] for each q -- this rank's slice of the
+  // output columns, written straight into every rank's full-width buffer
+  // (peer pointers are P2P-mapped memory of other GPUs).
+  int n_peers;
+  int64_t y_col0;
+  float* y_peer[kMaxPeers];
 };
 
 // Shared-memory descriptor for the constant offset tile: K-major, no swizzle,
@@ -396,11 +403,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * BN + chalf * COLS;
       if (n < p.N) {
         const float bv = p.bias ? p.bias[n] : 0.0f;
-        float* yp = p.y + m0 * p.ldy + n;
+        if (p.n_peers == 0) {
+          float* yp = p.y + m0 * p.ldy + n;
 #pragma unroll
-        for (int c = 0; c < COLS / 2; ++c) {
-          if (m0 + 2 * c < p.M) yp[(2 * c) * p.ldy] = p.bias ? acc[c].x + bv : acc[c].x;
-          if (m0 + 2 * c + 1 < p.M) yp[(2 * c + 1) * p.ldy] = p.bias ? acc[c].y + bv : acc[c].y;
+          for (int c = 0; c < COLS / 2; ++c) {
+            if (m0 + 2 * c < p.M) yp[(2 * c) * p.ldy] = p.bias ? acc[c].x + bv : acc[c].x;
+            if (m0 + 2 * c + 1 < p.M) yp[(2 * c + 1) * p.ldy] = p.bias ? acc[c].y + bv : acc[c].y;
+          }
+        } else {
+          // Gather fused into the epilogue: the tile goes to every rank's buffer
+          // (NVLink stores for the peers), overlapping with the next tiles' math.
+          const int64_t off = m0 * p.ldy + p.y_col0 + n;
+          for (int q = 0; q < p.n_peers; ++q) {
+            float* yp = p.y_peer[q] + off;
+#pragma unroll
+            for (int c = 0; c < COLS / 2; ++c) {
+              if (m0 + 2 * c < p.M) yp[(2 * c) * p.ldy] = p.bias ? acc[c].x + bv : acc[c].x;
+              if (m0 + 2 * c + 1 < p.M) yp[(2 * c + 1) * p.ldy] = p.bias ? acc[c].y + bv : acc[c].y;
+            }
+          }
         }
       }
     }
@@ -472,6 +493,9 @@ cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
   p.ldy = g.ldy;
   p.bias = g.bias;
   p.dots = g.dots;
+  p.n_peers = g.n_peers;
+  p.y_col0 = g.y_col0;
+  for (int q = 0; q < kMaxPeers; ++q) p.y_peer[q] = q < g.n_peers ? g.y_peer[q] : nullptr;
   auto kern = gemm_tc_kernel<STAGES, BN, DUMP>;
   cudaFuncAttributes fa;
   cudaError_t e = cudaFuncGetAttributes(&fa, kern);

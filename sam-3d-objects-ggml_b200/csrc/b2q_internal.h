@@ -61,6 +61,8 @@ cudaError_t launch_gemm_simt(int wtype, const uint8_t* w, int64_t ldw_bytes, int
                              const uint8_t* a, int64_t lda_bytes, int64_t m, float* y,
                              int64_t ldy_floats, cudaStream_t s);
 
+constexpr int kMaxPeers = 8;  // ranks of one NVLink domain a column-parallel GEMM writes to
+
 struct GemmArgs {
   SplitOperand w;     // weights: rows = N
   SplitOperand a;     // activations: rows = M
@@ -69,6 +71,9 @@ struct GemmArgs {
   int64_t ldy;        // floats
   const float* bias;  // [N] or nullptr
   int32_t* dots;      // debug dump [M][N][K/32] or nullptr
+  int n_peers = 0;    // > 0: write y_peer[q][m*ldy + y_col0 + n] for every q instead of y
+  int64_t y_col0 = 0;
+  float* y_peer[kMaxPeers] = {};
 };
 cudaError_t launch_gemm_tc(const GemmArgs& args, int num_sms, cudaStream_t s);
 cudaError_t read_device_status(unsigned int* value, bool clear);

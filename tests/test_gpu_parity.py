@@ -111,6 +111,23 @@ def test_mul_mat_matches_oracle(dev, wtype, M, N, K):
     assert rel_frobenius(y, ref) <= RTOL
 
 
+# The GEMM picks its tile width (tokens per tile) per shape; on a 148-SM B200
+# these shapes select 80, 96, 112 and 128 respectively, each with a ragged
+# last token tile.  Bias and a padded output row pitch ride along.
+@pytest.mark.parametrize("wtype", [O.TYPE_Q8_0, O.TYPE_Q4_0])
+@pytest.mark.parametrize("M,N,K", [(912, 1280, 256), (1136, 1280, 256), (1360, 1280, 256), (1584, 1280, 256)])
+def test_every_tile_width_matches_oracle(dev, wtype, M, N, K):
+    import torch
+    _, wq, x = make_case(M + N + K, M, N, K, wtype)
+    bias = np.random.default_rng(M).standard_normal(N).astype(np.float32)
+    out = torch.full((M, N + 8), float("nan"), dtype=torch.float32, device=dev)
+    b2q.mul_mat(wtype, to_dev(wq, dev), to_dev(x, dev), bias=to_dev(bias, dev), out=out[:, :N])
+    got = to_np(out)
+    ref = O.mul_mat(wtype, wq, x, O.ACT_X86) + bias[None, :]
+    assert np.all(np.isnan(got[:, N:]))  # nothing written past the row
+    assert rel_frobenius(got[:, :N], ref) <= RTOL
+
+
 @pytest.mark.parametrize("wtype,M,N,K,gelu", [
     (O.TYPE_Q8_0, 4096, 4096, 1024, False),    # fc1, Q8_0
     (O.TYPE_Q4_0, 4096, 4096, 1024, False),    # fc1, Q4_0
