@@ -50,6 +50,16 @@ def ops_of(M, N, K):
     return 2.0 * M * N * K
 
 
+def max_over_ranks(ms: float, dist=None, device="cpu") -> float:
+    """The job's time is its slowest rank's: MAX all-reduce of a per-rank time
+    (identity on one process).  NCCL needs a device tensor, gloo a host one."""
+    import torch
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    if dist is not None and dist.is_initialized() and dist.get_world_size() > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def config_dict():
     return {
         "workload": "configs[1]: fc1 Q4_0 4096x1024->4096, fc2 Q4_0 4096x4096->1024 (GELU in), "
@@ -229,10 +239,7 @@ def run_gpu(args, rank, world, local_rank):
     total_ms = sum(step_ms)
     step_ops = sum(ops_of(g["M"], g["N"], g["K"]) for g in gemms)
 
-    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    max_total_ms = float(t.item())
+    max_total_ms = max_over_ranks(total_ms, dist, dev)
     value = world * step_ops * args.steps / (max_total_ms * 1e-3) / 1e12
 
     # ---- end to end through the public C ABI, host buffers, copies inside the timing
@@ -282,10 +289,8 @@ def run_gpu(args, rank, world, local_rank):
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
-    t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = (world * step_ops * e2e_steps / (float(t.item()) * 1e-3) / 1e12) if e2e_steps else None
+    e2e_max_ms = max_over_ranks(e2e_ms, dist, dev)
+    e2e_value = (world * step_ops * e2e_steps / (e2e_max_ms * 1e-3) / 1e12) if e2e_steps else None
 
     gemm_total_ms = sum(sum(v) for v in gemm_ms)
     gemm_ops = step_ops * args.steps
@@ -420,10 +425,7 @@ def run_colpar(args, rank, world, local_rank):
             fn()
         e1.record(stream)
         torch.cuda.synchronize()
-        t = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return max_over_ranks(e0.elapsed_time(e1) / args.steps, dist if world > 1 else None, dev)
 
     ms_fused = timed(fused)
     ms_base = timed(baseline) if (equal or world == 1) else None
