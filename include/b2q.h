@@ -191,6 +191,16 @@ B2Q_API int b2q_mul_mat_q_simt(int wtype, const void* w, int64_t w_row_stride_by
                        int64_t k, const void* a, int64_t m, int64_t a_row_stride_bytes,
                        float* y, int64_t y_row_stride_bytes, void* stream);
 
+/* Fault-free test of the failure path: launches the GEMM of
+ * b2q_mul_mat_prepared with its TMA producer withholding every stage, so the
+ * MMA and epilogue waits run out (after ~2 s), the kernel drains, frees its
+ * tensor memory and ends, and b2q_device_status then returns B2Q_ERR_DEVICE
+ * with the code of the wait that gave up.  y is not written.  Nothing faults,
+ * traps or hangs; the context stays usable.  No counterpart in the reference
+ * (its failures are bool returns and aborting asserts). */
+B2Q_API int b2q_selftest_stalled_mul_mat(const void* packed, int64_t n, int64_t k, const void* act,
+                                         int64_t m, float* y, int64_t y_row_stride_bytes, void* stream);
+
 /* Device status word written by kernels whose bounded waits gave up:
  * *code = 0 when none; clear != 0 resets it.  Synchronises the device. */
 B2Q_API int b2q_device_status(unsigned int* code, int clear);

@@ -73,6 +73,7 @@ def _lib_obj():
             "b2q_block_dots_workspace_size": (SZ, [I64, I64, I64]),
             "b2q_mul_mat_q_simt": (I, [I, P, I64, I64, I64, P, I64, I64, P, I64, P]),
             "b2q_device_status": (I, [ctypes.POINTER(ctypes.c_uint), I]),
+            "b2q_selftest_stalled_mul_mat": (I, [P, I64, I64, P, I64, P, I64, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)

@@ -333,6 +333,29 @@ int b2q_mul_mat_q_simt(int wtype, const void* w, int64_t w_row_stride_bytes, int
                                     y_row_stride_bytes / 4, static_cast<cudaStream_t>(stream)));
 }
 
+int b2q_selftest_stalled_mul_mat(const void* packed, int64_t n, int64_t k, const void* act, int64_t m,
+                                 float* y, int64_t y_row_stride_bytes, void* stream) {
+  if (n <= 0 || m <= 0 || k <= 0 || k % kQK != 0) return B2Q_ERR_INVALID_ARG;
+  if (n > INT_MAX || m > INT_MAX || k > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (!packed || !act || !y || y_row_stride_bytes < n * 4) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(packed, 256) || !aligned(act, 256) || !aligned(y, 4) || y_row_stride_bytes % 4 != 0)
+    return B2Q_ERR_MISALIGNED;
+  int sms = 0;
+  if (int rc = check_device(&sms)) return rc;
+  GemmArgs g;
+  g.w = split_at(static_cast<uint8_t*>(const_cast<void*>(packed)), n, k);
+  g.a = split_at(static_cast<uint8_t*>(const_cast<void*>(act)), m, k);
+  g.M = m;
+  g.N = n;
+  g.K = k;
+  g.y = y;
+  g.ldy = y_row_stride_bytes / 4;
+  g.bias = nullptr;
+  g.dots = nullptr;
+  g.inject_stall = 1;
+  return from_cuda(launch_gemm_tc(g, sms, static_cast<cudaStream_t>(stream)));
+}
+
 int b2q_device_status(unsigned int* code, int clear) {
   if (!code) return B2Q_ERR_INVALID_ARG;
   if (int rc = check_device(nullptr)) return rc;

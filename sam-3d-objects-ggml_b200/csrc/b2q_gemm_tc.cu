@@ -117,6 +117,7 @@ struct TcParams {
   int n_peers;
   int64_t y_col0;
   float* y_peer[kMaxPeers];
+  int inject_stall;  // failure-path self-test: the producer withholds every stage
 };
 
 // Shared-memory descriptor for the constant offset tile: K-major, no swizzle,
@@ -295,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------------------------------------------------- producer
       if (elect_one()) {
         uint32_t stage = 0, phase = 0, issued_mask = 0, issued_par = 0;
-        bool ok = true;
+        bool ok = p.inject_stall == 0;  // a withheld stage leaves the consumers' waits to run out
         for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
           const int n0 = (tile % p.n_tiles) * kBM;
           const int m0 = (tile / p.n_tiles) * BN;
@@ -495,6 +496,7 @@ cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
   p.dots = g.dots;
   p.n_peers = g.n_peers;
   p.y_col0 = g.y_col0;
+  p.inject_stall = g.inject_stall;
   for (int q = 0; q < kMaxPeers; ++q) p.y_peer[q] = q < g.n_peers ? g.y_peer[q] : nullptr;
   auto kern = gemm_tc_kernel<STAGES, BN, DUMP>;
   cudaFuncAttributes fa;

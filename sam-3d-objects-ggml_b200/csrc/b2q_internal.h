@@ -74,6 +74,7 @@ struct GemmArgs {
   int n_peers = 0;    // > 0: write y_peer[q][m*ldy + y_col0 + n] for every q instead of y
   int64_t y_col0 = 0;
   float* y_peer[kMaxPeers] = {};
+  int inject_stall = 0;  // self-test of the bounded waits (b2q_selftest_stalled_mul_mat)
 };
 cudaError_t launch_gemm_tc(const GemmArgs& args, int num_sms, cudaStream_t s);
 cudaError_t read_device_status(unsigned int* value, bool clear);
