@@ -110,14 +110,17 @@ struct TcParams {
   int64_t ldy;
   const float* bias;
   int32_t* dots;
-  // Column-parallel output (n_peers > 0): every element also goes to
-  // y_peer[q][m * ldy + y_col0 + n] for each q -- this rank's slice of the
-  // output columns, written straight into every rank's full-width buffer
-  // (peer pointers are P2P-mapped memory of other GPUs).
-  int n_peers;
-  int64_t y_col0;
-  float* y_peer[kMaxPeers];
-  int inject_stall;  // failure-path self-test: the producer withholds every stage
+};
+
+// Column-parallel output (PEERS kernels only): every element goes to
+// ptr[q][m * ldy + col0 + n] for each q -- this rank's slice of the output
+// columns, written straight into every rank's full-width buffer (pointers into
+// P2P-mapped memory of the other GPUs).  A separate kernel parameter: growing
+// TcParams by these 80 bytes slowed the plain kernel's tile loop by 8%.
+struct PeerParams {
+  int n;
+  int64_t col0;
+  float* ptr[kMaxPeers];
 };
 
 // Shared-memory descriptor for the constant offset tile: K-major, no swizzle,
@@ -228,11 +231,11 @@ __device__ __forceinline__ bool epi_step(uint32_t (&cur)[COLS], uint32_t (&nxt)[
   return true;
 }
 
-template <int STAGES, int BN, bool DUMP>
+template <int STAGES, int BN, bool DUMP, bool PEERS, bool STALL>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_wc, const __grid_constant__ CUtensorMap tm_ac,
                    const __grid_constant__ CUtensorMap tm_ws, const __grid_constant__ CUtensorMap tm_as,
-                   const TcParams p) {
+                   const TcParams p, const __grid_constant__ PeerParams pp) {
   using C = Cfg<STAGES, BN>;
   constexpr int COLS = C::COLS;
   extern __shared__ uint8_t smem_raw[];
@@ -296,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------------------------------------------------- producer
       if (elect_one()) {
         uint32_t stage = 0, phase = 0, issued_mask = 0, issued_par = 0;
-        bool ok = p.inject_stall == 0;  // a withheld stage leaves the consumers' waits to run out
+        bool ok = !STALL;  // self-test: withheld stages leave the consumers' waits to run out
         for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
           const int n0 = (tile % p.n_tiles) * kBM;
           const int m0 = (tile / p.n_tiles) * BN;
@@ -404,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * BN + chalf * COLS;
       if (n < p.N) {
         const float bv = p.bias ? p.bias[n] : 0.0f;
-        if (p.n_peers == 0) {
+        if (!PEERS) {  // the column-parallel store is its own instantiation: it slows this loop
           float* yp = p.y + m0 * p.ldy + n;
 #pragma unroll
           for (int c = 0; c < COLS / 2; ++c) {
@@ -414,9 +417,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           // Gather fused into the epilogue: the tile goes to every rank's buffer
           // (NVLink stores for the peers), overlapping with the next tiles' math.
-          const int64_t off = m0 * p.ldy + p.y_col0 + n;
-          for (int q = 0; q < p.n_peers; ++q) {
-            float* yp = p.y_peer[q] + off;
+          const int64_t off = m0 * p.ldy + pp.col0 + n;
+#pragma unroll
+          for (int q = 0; q < kMaxPeers; ++q) {  // static indices: the pointers stay in the param bank
+            if (q >= pp.n) break;
+            float* yp = pp.ptr[q] + off;
 #pragma unroll
             for (int c = 0; c < COLS / 2; ++c) {
               if (m0 + 2 * c < p.M) yp[(2 * c) * p.ldy] = p.bias ? acc[c].x + bv : acc[c].x;
@@ -468,7 +473,7 @@ bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uin
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int STAGES, int BN, bool DUMP>
+template <int STAGES, int BN, bool DUMP, bool PEERS = false, bool STALL = false>
 cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
   using C = Cfg<STAGES, BN>;
   const int64_t KB = g.K / kQK;
@@ -494,11 +499,11 @@ cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
   p.ldy = g.ldy;
   p.bias = g.bias;
   p.dots = g.dots;
-  p.n_peers = g.n_peers;
-  p.y_col0 = g.y_col0;
-  p.inject_stall = g.inject_stall;
-  for (int q = 0; q < kMaxPeers; ++q) p.y_peer[q] = q < g.n_peers ? g.y_peer[q] : nullptr;
-  auto kern = gemm_tc_kernel<STAGES, BN, DUMP>;
+  PeerParams pp;
+  pp.n = PEERS ? g.n_peers : 0;
+  pp.col0 = g.y_col0;
+  for (int q = 0; q < kMaxPeers; ++q) pp.ptr[q] = q < pp.n ? g.y_peer[q] : nullptr;
+  auto kern = gemm_tc_kernel<STAGES, BN, DUMP, PEERS, STALL>;
   cudaFuncAttributes fa;
   cudaError_t e = cudaFuncGetAttributes(&fa, kern);
   if (e != cudaSuccess) return e;
@@ -506,7 +511,7 @@ cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const int grid = p.num_tiles < num_sms ? p.num_tiles : num_sms;
-  kern<<<grid, kThreads, C::SMEM, s>>>(tm_wc, tm_ac, tm_ws, tm_as, p);
+  kern<<<grid, kThreads, C::SMEM, s>>>(tm_wc, tm_ac, tm_ws, tm_as, p, pp);
   return cudaGetLastError();
 }
 
@@ -544,6 +549,16 @@ cudaError_t read_device_status(unsigned int* value, bool clear) {
 cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, cudaStream_t s) {
   if (g.M == 0 || g.N == 0) return cudaSuccess;
   if (g.dots) return launch_cfg<4, 128, true>(g, num_sms, s);
+  if (g.inject_stall) return launch_cfg<4, 128, false, false, true>(g, num_sms, s);
+  if (g.n_peers > 0) {
+    switch (pick_bn(g.M, g.N, num_sms)) {
+      case 112: return launch_cfg<4, 112, false, true>(g, num_sms, s);
+      case 96: return launch_cfg<4, 96, false, true>(g, num_sms, s);
+      case 80: return launch_cfg<4, 80, false, true>(g, num_sms, s);
+      case 64: return launch_cfg<4, 64, false, true>(g, num_sms, s);
+      default: return launch_cfg<4, 128, false, true>(g, num_sms, s);
+    }
+  }
   switch (pick_bn(g.M, g.N, num_sms)) {
     case 112: return launch_cfg<4, 112, false>(g, num_sms, s);
     case 96: return launch_cfg<4, 96, false>(g, num_sms, s);
