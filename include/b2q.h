@@ -151,6 +151,29 @@ B2Q_API int b2q_mul_mat_prepared(const void* packed, int64_t n, int64_t k, const
                                  int64_t m, const float* bias, float* y,
                                  int64_t y_row_stride_bytes, void* stream);
 
+/* ------------------------------------- fused MLP hidden layer (fc1 -> fc2)
+ * The DiT feed-forward block computes fc2(gelu(fc1(x) + b1)) + b2
+ * (cpp_ggml/src/ss_flow_graph.cpp:380-384; graph_builder.cpp:191-197): two
+ * mul_mats with ggml_gelu between them, and fc2's mul_mat quantizes the GELU
+ * output to Q8_0 before its dot products.  This entry runs fc1 with the bias,
+ * the GELU and that Q8_0 quantize fused into the GEMM's epilogue, writing
+ * fc2's prepared activations (the b2q_act_prepare layout for m rows and
+ * k_next = n) instead of the fp32 hidden state.  act_out then equals, byte for
+ * byte on the written regions, b2q_act_prepare(gelu(b2q_mul_mat_prepared(...)))
+ * with the same variant: no fp32 [m][n] tensor is written or read back.
+ * GELU is ggml_gelu as the ggml CPU backend computes it (its fp16-table form:
+ * 0 for x <= -10, x for x >= 10, else the tanh form at fp16(x), rounded to
+ * fp16).  Requires n % 32 == 0; act_out_bytes >= b2q_act_prepared_size(m, n).
+ * No single reference counterpart: it replaces the op sequence
+ * ggml_mul_mat -> ggml_add -> ggml_gelu -> (next ggml_mul_mat's from_float). */
+B2Q_API int b2q_mul_mat_prepared_gelu_q8(const void* packed, int64_t n, int64_t k, const void* act,
+                                         int64_t m, const float* bias, void* act_out,
+                                         size_t act_out_bytes, int variant, void* stream);
+/* ggml_gelu (GGML_OP_UNARY, GGML_UNARY_OP_GELU) on an fp32 [rows][cols]
+ * matrix, the same arithmetic as the fused epilogue above; x == y allowed. */
+B2Q_API int b2q_gelu(const float* x, int64_t rows, int64_t cols, int64_t x_row_stride_bytes,
+                     float* y, int64_t y_row_stride_bytes, void* stream);
+
 /* ------------------------------------------- column-parallel form (multi-GPU)
  * One rank of a tensor-parallel group for a single large mul_mat (the SLat
  * flow transformer's linears at 8k-20k tokens): the weight is split by output

@@ -334,6 +334,34 @@ void b2q_orc_fill_normal(float* x, int64_t n, uint64_t seed, float mean, float s
     }
 }
 
+/* ------------------------------------------------------------------ GELU */
+
+/* ggml-cpu/vec.h (v0.21.0): GELU_COEF_A, SQRT_2_OVER_PI and ggml_gelu_f32,
+ * tabulated over fp16 inputs (GGML_GELU_FP16).  See b2q_oracle.h. */
+static float gelu_f32(float f, int contract) {
+  const float kA = 0.044715f;
+  const float kS = 0.79788456080286535587989211986876f;
+  const float inner = contract ? fmaf(kA * f, f, 1.0f) : 1.0f + (kA * f) * f;
+  return (0.5f * f) * (1.0f + tanhf((kS * f) * inner));
+}
+
+void b2q_orc_gelu_table(uint16_t* table, int contract) {
+  for (uint32_t h = 0; h < 65536u; ++h)
+    table[h] = b2q_orc_fp32_to_fp16(gelu_f32(b2q_orc_fp16_to_fp32((uint16_t)h), contract));
+}
+
+float b2q_orc_gelu(float x, int contract) {
+  if (x <= -10.0f) return 0.0f;
+  if (x >= 10.0f) return x;
+  const float f = b2q_orc_fp16_to_fp32(b2q_orc_fp32_to_fp16(x));
+  return b2q_orc_fp16_to_fp32(b2q_orc_fp32_to_fp16(gelu_f32(f, contract)));
+}
+
+void b2q_orc_gelu_n(const float* x, float* y, int64_t n, int contract) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i) y[i] = b2q_orc_gelu(x[i], contract);
+}
+
 int b2q_orc_num_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

@@ -108,6 +108,19 @@ void b2q_orc_philox4x32_10(uint64_t seed, uint64_t counter, uint32_t out[4]);
 /* Normal(mean, std) fp32 values via Box-Muller on Philox words. */
 void b2q_orc_fill_normal(float* x, int64_t n, uint64_t seed, float mean, float std);
 
+/* ggml_gelu on the CPU backend (ggml v0.21.0 ggml-cpu/vec.h, the
+ * GGML_GELU_FP16 build, which is the default): outside (-10, 10) the result is
+ * 0 (x <= -10) or x (x >= 10); inside, x is rounded to fp16 and looked up in a
+ * 65536-entry table whose entry h is
+ *   fp16( 0.5f*f*(1.0f + tanhf(SQRT_2_OVER_PI*f*(1.0f + GELU_COEF_A*f*f))) ),
+ * f = fp32(h), evaluated left to right, one IEEE op per step.  contract != 0
+ * evaluates 1 + GELU_COEF_A*f*f as one fmaf, as a compiler that contracts
+ * (-ffp-contract=fast with FMA enabled) builds the table. */
+float b2q_orc_gelu(float x, int contract);
+void b2q_orc_gelu_n(const float* x, float* y, int64_t n, int contract);
+/* The 65536-entry table itself (fp16 bits), for exhaustive comparisons. */
+void b2q_orc_gelu_table(uint16_t* table, int contract);
+
 int b2q_orc_num_threads(void);
 const char* b2q_orc_isa(void);
 

@@ -62,6 +62,10 @@ def lib():
         L.b2q_orc_mul_mat_f64.argtypes = [I, P, I64, I64, P, I64, I64, I64, P]
         L.b2q_orc_philox4x32_10.argtypes = [ctypes.c_uint64, ctypes.c_uint64, P]
         L.b2q_orc_fill_normal.argtypes = [P, I64, ctypes.c_uint64, ctypes.c_float, ctypes.c_float]
+        L.b2q_orc_gelu.restype = ctypes.c_float
+        L.b2q_orc_gelu.argtypes = [ctypes.c_float, I]
+        L.b2q_orc_gelu_n.argtypes = [P, P, I64, I]
+        L.b2q_orc_gelu_table.argtypes = [P, I]
         L.b2q_orc_num_threads.restype = I
         L.b2q_orc_isa.restype = ctypes.c_char_p
         _lib = L
@@ -167,3 +171,18 @@ def num_threads() -> int:
 
 def isa() -> str:
     return lib().b2q_orc_isa().decode()
+
+
+def gelu(x: np.ndarray, contract: bool = False) -> np.ndarray:
+    """ggml_gelu (CPU backend, fp16-table build) elementwise; see b2q_oracle.h."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().b2q_orc_gelu_n(_p(x), _p(y), x.size, int(contract))
+    return y
+
+
+def gelu_table(contract: bool = False) -> np.ndarray:
+    """The 65536 fp16 table entries (uint16 bits), indexed by the fp16 input bits."""
+    t = np.empty(65536, dtype=np.uint16)
+    lib().b2q_orc_gelu_table(_p(t), int(contract))
+    return t

@@ -67,6 +67,8 @@ def _lib_obj():
             "b2q_act_prepared_size": (SZ, [I64, I64]),
             "b2q_act_prepare": (I, [P, I64, I64, I64, I, P, SZ, P]),
             "b2q_mul_mat_prepared": (I, [P, I64, I64, P, I64, P, P, I64, P]),
+            "b2q_mul_mat_prepared_gelu_q8": (I, [P, I64, I64, P, I64, P, P, SZ, I, P]),
+            "b2q_gelu": (I, [P, I64, I64, I64, P, I64, P]),
             "b2q_mul_mat_prepared_peers": (I, [P, I64, I64, P, I64, P, ctypes.POINTER(ctypes.c_void_p), I, I64,
                                                I64, P]),
             "b2q_block_dots": (I, [I, P, I64, I64, I64, P, I64, I64, P, P, SZ, P]),
@@ -246,6 +248,32 @@ def mul_mat_prepared(packed, n: int, k: int, act, m: int, bias=None, out=None, s
     rc = lib().b2q_mul_mat_prepared(_ptr(packed), n, k, _ptr(act), m, _ptr(bias), _ptr(out),
                                     out.stride(0) * 4, _stream(stream))
     _check("b2q_mul_mat_prepared", rc)
+    return out
+
+
+def mul_mat_prepared_gelu_q8(packed, n: int, k: int, act, m: int, bias=None,
+                             variant: int = ACT_X86, out=None, stream=None):
+    """fc1 with bias + GELU + Q8_0 quantize fused: returns the prepared
+    activations of the next mul_mat (m rows, k_next = n) instead of fp32 y."""
+    size = act_prepared_size(m, n)
+    if out is None:
+        out = _empty_aligned(size, act.device)
+    rc = lib().b2q_mul_mat_prepared_gelu_q8(_ptr(packed), n, k, _ptr(act), m, _ptr(bias), _ptr(out),
+                                            out.numel() * out.element_size(), variant,
+                                            _stream(stream))
+    _check("b2q_mul_mat_prepared_gelu_q8", rc)
+    return out
+
+
+def gelu(x, out=None, stream=None):
+    """ggml_gelu (CPU-backend arithmetic) on an fp32 [rows, cols] CUDA tensor."""
+    torch = _torch()
+    rows, cols = x.shape
+    if out is None:
+        out = torch.empty((rows, cols), dtype=torch.float32, device=x.device)
+    rc = lib().b2q_gelu(_ptr(x), rows, cols, x.stride(0) * 4, _ptr(out), out.stride(0) * 4,
+                        _stream(stream))
+    _check("b2q_gelu", rc)
     return out
 
 

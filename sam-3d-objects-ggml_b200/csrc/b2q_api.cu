@@ -250,6 +250,50 @@ int b2q_mul_mat_prepared(const void* packed, int64_t n, int64_t k, const void* a
                   static_cast<cudaStream_t>(stream));
 }
 
+int b2q_mul_mat_prepared_gelu_q8(const void* packed, int64_t n, int64_t k, const void* act, int64_t m,
+                                 const float* bias, void* act_out, size_t act_out_bytes, int variant,
+                                 void* stream) {
+  if (n < 0 || m < 0 || k <= 0 || k % kQK != 0 || n % kQK != 0) return B2Q_ERR_INVALID_ARG;
+  if (n > INT_MAX || m > INT_MAX || k > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (variant != B2Q_ACT_X86 && variant != B2Q_ACT_REF) return B2Q_ERR_INVALID_ARG;
+  if (m > 0 && n > 0 && (!packed || !act || !act_out)) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(packed, 256) || !aligned(act, 256) || !aligned(act_out, 256) || (bias && !aligned(bias, 4)))
+    return B2Q_ERR_MISALIGNED;
+  if (n > 0 && act_out_bytes < split_bytes(m, n)) return B2Q_ERR_WORKSPACE;
+  if (m == 0 || n == 0) return B2Q_OK;
+  int sms = 0;
+  if (int rc = check_device(&sms)) return rc;
+  const SplitOperand out = split_at(static_cast<uint8_t*>(act_out), m, n);
+  GemmArgs g;
+  g.w = split_at(static_cast<uint8_t*>(const_cast<void*>(packed)), n, k);
+  g.a = split_at(static_cast<uint8_t*>(const_cast<void*>(act)), m, k);
+  g.M = m;
+  g.N = n;
+  g.K = k;
+  g.y = nullptr;
+  g.ldy = 0;
+  g.bias = bias;
+  g.dots = nullptr;
+  g.q_codes = const_cast<int8_t*>(out.codes);
+  g.q_scales = const_cast<float*>(out.scales);
+  g.q_ld = out.ld;
+  g.q_variant = variant;
+  return from_cuda(launch_gemm_tc(g, sms, static_cast<cudaStream_t>(stream)));
+}
+
+int b2q_gelu(const float* x, int64_t rows, int64_t cols, int64_t x_row_stride_bytes, float* y,
+             int64_t y_row_stride_bytes, void* stream) {
+  if (rows < 0 || cols < 0) return B2Q_ERR_INVALID_ARG;
+  if (rows > 0 && cols > 0 && (!x || !y)) return B2Q_ERR_INVALID_ARG;
+  if (x_row_stride_bytes < cols * 4 || y_row_stride_bytes < cols * 4) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(x, 4) || !aligned(y, 4) || x_row_stride_bytes % 4 != 0 || y_row_stride_bytes % 4 != 0)
+    return B2Q_ERR_MISALIGNED;
+  if (rows == 0 || cols == 0) return B2Q_OK;
+  if (int rc = check_device(nullptr)) return rc;
+  return from_cuda(launch_gelu(x, rows, cols, x_row_stride_bytes / 4, y, y_row_stride_bytes / 4,
+                               static_cast<cudaStream_t>(stream)));
+}
+
 int b2q_mul_mat_prepared_peers(const void* packed, int64_t n, int64_t k, const void* act, int64_t m,
                                const float* bias, float* const* y_peers, int n_peers, int64_t y_col0,
                                int64_t y_row_stride_bytes, void* stream) {

@@ -49,6 +49,7 @@
 // copies and MMAs, frees TMEM and exits, leaving a code in g_device_status.
 #include "b2q_internal.h"
 #include "b2q_ptx.cuh"
+#include "b2q_q8.cuh"
 
 namespace b2q {
 
@@ -99,6 +100,10 @@ struct Cfg {
   static constexpr int BAR_OFF = OFF_TILE + kOffsetTileBytes;
   static constexpr int NBARS = 2 * STAGES + 2 * kPairs + 1;
   static constexpr int SMEM = BAR_OFF + NBARS * 8 + 16 + 1024;  // + alignment slack
+  // GELU + Q8_0 variant only: a 32 x 33 fp32 transpose buffer per epilogue warp.
+  static constexpr int XPOSE_OFF = (BAR_OFF + NBARS * 8 + 16 + 127) / 128 * 128;
+  static constexpr int XPOSE_FLOATS = 32 * 33;
+  static constexpr int SMEM_XPOSE = XPOSE_OFF + 8 * XPOSE_FLOATS * 4 + 1024;
   static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte swizzle alignment");
   static_assert(STAGES <= 16, "stage bitmasks");
 };
@@ -112,15 +117,32 @@ struct TcParams {
   int32_t* dots;
 };
 
-// Column-parallel output (PEERS kernels only): every element goes to
-// ptr[q][m * ldy + col0 + n] for each q -- this rank's slice of the output
-// columns, written straight into every rank's full-width buffer (pointers into
-// P2P-mapped memory of the other GPUs).  A separate kernel parameter: growing
-// TcParams by these 80 bytes slowed the plain kernel's tile loop by 8%.
-struct PeerParams {
+// Kernel variants (one instantiation each, so the plain kernel carries none of
+// the others' code or parameters).
+enum Mode : int {
+  kModePlain = 0,   // y = w . x (+ bias)
+  kModeDump = 1,    // raw int32 block dots of every block (debug / parity)
+  kModePeers = 2,   // column-parallel: the tile goes into every rank's y buffer
+  kModeStall = 3,   // failure-path self-test: the producer withholds every stage
+  kModeGeluQ8 = 4,  // fused GELU + Q8_0 quantize of the output (next layer's input)
+};
+
+// Output arguments of the non-plain variants, a separate kernel parameter:
+// growing TcParams by such fields slowed the plain kernel's tile loop by 8%.
+//   peers: every element goes to ptr[q][m * ldy + col0 + n] for each q -- this
+//          rank's slice of the output columns, written straight into every
+//          rank's full-width buffer (P2P-mapped memory of the other GPUs);
+//   gelu+q8: quantize_q8_0(gelu(y)) into the split layout of the next
+//          mul_mat's activations: codes q_codes[m * q_k + n], scales
+//          q_scales[(n / 32) * q_ld + m].
+struct OutParams {
   int n;
   int64_t col0;
   float* ptr[kMaxPeers];
+  int8_t* q_codes;
+  float* q_scales;
+  int64_t q_ld, q_k;
+  int q_variant;
 };
 
 // Shared-memory descriptor for the constant offset tile: K-major, no swizzle,
@@ -231,11 +253,60 @@ __device__ __forceinline__ bool epi_step(uint32_t (&cur)[COLS], uint32_t (&nxt)[
   return true;
 }
 
-template <int STAGES, int BN, bool DUMP, bool PEERS, bool STALL>
+// Fused GELU + Q8_0 quantize of token columns m0+CB .. m0+CB+W-1 of one warp's
+// accumulators.  The warp's 32 lanes hold one 32-value block (lane = position
+// in the block) of each token's next-layer activations.  The GELU values go
+// through a 32 x 33 shared-memory transpose (conflict-free both ways), after
+// which lane c holds the whole block of column CB+c and quantizes it exactly as
+// the stand-alone quantizer does: fmaxf absmax from 0, one scale, 32 codes as
+// two 16-byte stores, and the lanes' scales as one coalesced store.
+template <int VARIANT, int CB, int W, int NACC>
+__device__ __forceinline__ void geluq_chunk(const float2 (&acc)[NACC], float bv, bool has_bias, int64_t m0,
+                                            int64_t M, int lane, int8_t* codes, int64_t q_k, float* qs, float* xp) {
+#pragma unroll
+  for (int c = 0; c < W; ++c) {
+    const float v = ((CB + c) & 1) ? acc[(CB + c) / 2].y : acc[(CB + c) / 2].x;
+    xp[c * 33 + lane] = gelu_ggml(has_bias ? v + bv : v);
+  }
+  __syncwarp();
+  const int64_t m = m0 + CB + lane;
+  if (lane < W && m < M) {
+    float z[kQK];
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kQK; ++j) {
+      z[j] = xp[lane * 33 + j];
+      amax = fmaxf(amax, fabsf(z[j]));
+    }
+    float d, inv;
+    q8_scale<VARIANT>(amax, d, inv);
+    uint32_t q[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      q[i] = quantize_code<VARIANT>(z[4 * i], inv) | (quantize_code<VARIANT>(z[4 * i + 1], inv) << 8) |
+             (quantize_code<VARIANT>(z[4 * i + 2], inv) << 16) | (quantize_code<VARIANT>(z[4 * i + 3], inv) << 24);
+    uint4* dst = reinterpret_cast<uint4*>(codes + m * q_k);
+    dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
+    dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
+    qs[m] = q8_split_scale(d);
+  }
+  __syncwarp();
+}
+
+template <int VARIANT, int COLS, int NACC>
+__device__ __forceinline__ void geluq_cols(const float2 (&acc)[NACC], float bv, bool has_bias, int64_t m0, int64_t M,
+                                           int lane, int8_t* codes, int64_t q_k, float* qs, float* xp) {
+  geluq_chunk<VARIANT, 0, (COLS < 32 ? COLS : 32)>(acc, bv, has_bias, m0, M, lane, codes, q_k, qs, xp);
+  if constexpr (COLS > 32) geluq_chunk<VARIANT, 32, COLS - 32>(acc, bv, has_bias, m0, M, lane, codes, q_k, qs, xp);
+}
+
+template <int STAGES, int BN, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_wc, const __grid_constant__ CUtensorMap tm_ac,
                    const __grid_constant__ CUtensorMap tm_ws, const __grid_constant__ CUtensorMap tm_as,
-                   const TcParams p, const __grid_constant__ PeerParams pp) {
+                   const TcParams p, const __grid_constant__ OutParams pp) {
+  constexpr bool DUMP = MODE == kModeDump, PEERS = MODE == kModePeers, STALL = MODE == kModeStall;
+  constexpr bool GELUQ = MODE == kModeGeluQ8;
   using C = Cfg<STAGES, BN>;
   constexpr int COLS = C::COLS;
   extern __shared__ uint8_t smem_raw[];
@@ -402,10 +473,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
       }
-      if (!ok || !p.y) continue;
+      if (!ok || (!GELUQ && !p.y)) continue;
       const int64_t n = static_cast<int64_t>(tile % p.n_tiles) * kBM + row;
       const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * BN + chalf * COLS;
-      if (n < p.N) {
+      if (GELUQ) {
+        // The warp's 32 weight rows are one Q8_0 block of the next layer's K
+        // (N % 32 == 0, so they are all valid or all not).
+        const int64_t nq = static_cast<int64_t>(tile % p.n_tiles) * kBM + quarter * 32;
+        if (nq < p.N && m0 < p.M) {
+          const float bv = p.bias ? p.bias[n] : 0.0f;
+          int8_t* codes = pp.q_codes + nq;
+          float* qs = pp.q_scales + (nq / kQK) * pp.q_ld;
+          float* xp = reinterpret_cast<float*>(smem + C::XPOSE_OFF) + (warp - kEpiWarp0) * C::XPOSE_FLOATS;
+          if (pp.q_variant == 0)
+            geluq_cols<0, COLS>(acc, bv, p.bias != nullptr, m0, p.M, lane, codes, pp.q_k, qs, xp);
+          else
+            geluq_cols<1, COLS>(acc, bv, p.bias != nullptr, m0, p.M, lane, codes, pp.q_k, qs, xp);
+        }
+      } else if (n < p.N) {
         const float bv = p.bias ? p.bias[n] : 0.0f;
         if (!PEERS) {  // the column-parallel store is its own instantiation: it slows this loop
           float* yp = p.y + m0 * p.ldy + n;
@@ -473,8 +558,9 @@ bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uin
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int STAGES, int BN, bool DUMP, bool PEERS = false, bool STALL = false>
+template <int STAGES, int BN, int MODE>
 cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
+  constexpr bool PEERS = MODE == kModePeers;
   using C = Cfg<STAGES, BN>;
   const int64_t KB = g.K / kQK;
   CUtensorMap tm_wc, tm_ac, tm_ws, tm_as;
@@ -499,19 +585,26 @@ cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
   p.ldy = g.ldy;
   p.bias = g.bias;
   p.dots = g.dots;
-  PeerParams pp;
+  OutParams pp;
   pp.n = PEERS ? g.n_peers : 0;
   pp.col0 = g.y_col0;
   for (int q = 0; q < kMaxPeers; ++q) pp.ptr[q] = q < pp.n ? g.y_peer[q] : nullptr;
-  auto kern = gemm_tc_kernel<STAGES, BN, DUMP, PEERS, STALL>;
+  pp.q_codes = g.q_codes;
+  pp.q_scales = g.q_scales;
+  pp.q_ld = g.q_ld;
+  pp.q_k = g.N;
+  pp.q_variant = g.q_variant;
+  auto kern = gemm_tc_kernel<STAGES, BN, MODE>;
   cudaFuncAttributes fa;
   cudaError_t e = cudaFuncGetAttributes(&fa, kern);
   if (e != cudaSuccess) return e;
   if (fa.numRegs != kLaunchRegs) return cudaErrorInvalidConfiguration;  // see the register split
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  constexpr int smem_bytes = MODE == kModeGeluQ8 ? C::SMEM_XPOSE : C::SMEM;
+  static_assert(smem_bytes <= 227 * 1024, "shared memory per CTA");
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
   if (e != cudaSuccess) return e;
   const int grid = p.num_tiles < num_sms ? p.num_tiles : num_sms;
-  kern<<<grid, kThreads, C::SMEM, s>>>(tm_wc, tm_ac, tm_ws, tm_as, p, pp);
+  kern<<<grid, kThreads, smem_bytes, s>>>(tm_wc, tm_ac, tm_ws, tm_as, p, pp);
   return cudaGetLastError();
 }
 
@@ -546,26 +639,27 @@ cudaError_t read_device_status(unsigned int* value, bool clear) {
   return cudaMemcpyToSymbol(g_device_status, &zero, sizeof(unsigned int));
 }
 
+template <int MODE>
+cudaError_t launch_picked(const GemmArgs& g, int num_sms, cudaStream_t s) {
+  switch (pick_bn(g.M, g.N, num_sms)) {
+    case 112: return launch_cfg<4, 112, MODE>(g, num_sms, s);
+    case 96: return launch_cfg<4, 96, MODE>(g, num_sms, s);
+    case 80: return launch_cfg<4, 80, MODE>(g, num_sms, s);
+    case 64: return launch_cfg<4, 64, MODE>(g, num_sms, s);
+    default: return launch_cfg<4, 128, MODE>(g, num_sms, s);
+  }
+}
+
 cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, cudaStream_t s) {
   if (g.M == 0 || g.N == 0) return cudaSuccess;
-  if (g.dots) return launch_cfg<4, 128, true>(g, num_sms, s);
-  if (g.inject_stall) return launch_cfg<4, 128, false, false, true>(g, num_sms, s);
-  if (g.n_peers > 0) {
-    switch (pick_bn(g.M, g.N, num_sms)) {
-      case 112: return launch_cfg<4, 112, false, true>(g, num_sms, s);
-      case 96: return launch_cfg<4, 96, false, true>(g, num_sms, s);
-      case 80: return launch_cfg<4, 80, false, true>(g, num_sms, s);
-      case 64: return launch_cfg<4, 64, false, true>(g, num_sms, s);
-      default: return launch_cfg<4, 128, false, true>(g, num_sms, s);
-    }
+  if (g.dots) return launch_cfg<4, 128, kModeDump>(g, num_sms, s);
+  if (g.inject_stall) return launch_cfg<4, 128, kModeStall>(g, num_sms, s);
+  if (g.q_codes) {
+    if (g.N % kQK != 0 || !g.q_scales) return cudaErrorInvalidValue;
+    return launch_picked<kModeGeluQ8>(g, num_sms, s);
   }
-  switch (pick_bn(g.M, g.N, num_sms)) {
-    case 112: return launch_cfg<4, 112, false>(g, num_sms, s);
-    case 96: return launch_cfg<4, 96, false>(g, num_sms, s);
-    case 80: return launch_cfg<4, 80, false>(g, num_sms, s);
-    case 64: return launch_cfg<4, 64, false>(g, num_sms, s);
-    default: return launch_cfg<4, 128, false>(g, num_sms, s);
-  }
+  if (g.n_peers > 0) return launch_picked<kModePeers>(g, num_sms, s);
+  return launch_picked<kModePlain>(g, num_sms, s);
 }
 
 }  // namespace b2q

@@ -61,6 +61,9 @@ cudaError_t launch_gemm_simt(int wtype, const uint8_t* w, int64_t ldw_bytes, int
                              const uint8_t* a, int64_t lda_bytes, int64_t m, float* y,
                              int64_t ldy_floats, cudaStream_t s);
 
+cudaError_t launch_gelu(const float* x, int64_t rows, int64_t cols, int64_t ldx_floats, float* y,
+                        int64_t ldy_floats, cudaStream_t s);
+
 constexpr int kMaxPeers = 8;  // ranks of one NVLink domain a column-parallel GEMM writes to
 
 struct GemmArgs {
@@ -75,6 +78,13 @@ struct GemmArgs {
   int64_t y_col0 = 0;
   float* y_peer[kMaxPeers] = {};
   int inject_stall = 0;  // self-test of the bounded waits (b2q_selftest_stalled_mul_mat)
+  // Fused GELU + Q8_0 epilogue (q_codes != nullptr): instead of y, write
+  // quantize_q8_0(gelu(y)) into the split layout of the next mul_mat's
+  // activations (rows = M tokens, K_next = N): codes [M][N], scales [N/32][q_ld].
+  int8_t* q_codes = nullptr;
+  float* q_scales = nullptr;
+  int64_t q_ld = 0;
+  int q_variant = 0;
 };
 cudaError_t launch_gemm_tc(const GemmArgs& args, int num_sms, cudaStream_t s);
 cudaError_t read_device_status(unsigned int* value, bool clear);

@@ -13,22 +13,13 @@
 // quantize_q8_0_kernel).
 #include "b2q_internal.h"
 #include "b2q_ptx.cuh"
+#include "b2q_q8.cuh"
 
 #include <cuda_fp16.h>
 
 namespace b2q {
 
 namespace {
-
-template <int VARIANT>
-__device__ __forceinline__ uint32_t quantize_code(float v, float inv) {
-  const float s = __fmul_rn(v, inv);
-  if (VARIANT == 0) {
-    const int q = __float2int_rn(s);  // round to nearest, ties to even
-    return static_cast<uint32_t>(max(-128, min(127, q))) & 0xffu;
-  }
-  return static_cast<uint32_t>(static_cast<int>(roundf(s))) & 0xffu;  // ties away from zero
-}
 
 template <bool VEC4>
 __device__ __forceinline__ float4 load4(const float* p) {
@@ -66,12 +57,8 @@ __global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float* __restr
 #pragma unroll
     for (int i = 0; i < 8; ++i)
       amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
-    const float d = __fdiv_rn(amax, 127.0f);
-    float inv;
-    if (VARIANT == 0)
-      inv = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-    else
-      inv = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    float d, inv;
+    q8_scale<VARIANT>(amax, d, inv);
     uint32_t q[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
@@ -82,7 +69,7 @@ __global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float* __restr
       uint4* dst = reinterpret_cast<uint4*>(codes + row * k + b * kQK);
       dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
       dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
-      scales[b * ld + row] = __half2float(dh) * kActScaleMul;
+      scales[b * ld + row] = q8_split_scale(d);
     } else {
       // ggml block_q8_0: fp16 d then 32 codes; 34-byte blocks are 2-byte aligned
       uint16_t* dst = reinterpret_cast<uint16_t*>(yb + row * ldy + b * kQ8Bytes);
@@ -112,6 +99,28 @@ cudaError_t launch_q(const float* x, int64_t m, int64_t k, int64_t ldx, uint8_t*
   else
     quantize_q8_0_kernel<1, SPLIT, VEC4><<<grid, 256, 0, s>>>(x, m, k, ldx, yb, ldy, codes, scales, ld);
   return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------- GELU
+// y = gelu_ggml(x) elementwise over rows x cols (row pitches in floats).  Each
+// thread takes 4 consecutive values of a row; 16-byte loads and stores when
+// both pitches and bases allow (cols % 4 == 0 is required by the caller then).
+template <bool VEC4>
+__global__ void __launch_bounds__(256) gelu_kernel(const float* x, int64_t rows, int64_t cols, int64_t ldx,
+                                                   float* y, int64_t ldy) {  // x == y allowed: no __restrict__
+  const int64_t quads = (cols + 3) / 4;
+  const int64_t total = rows * quads;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / quads, c = (i - r * quads) * 4;
+    if (VEC4) {
+      const float4 v = *reinterpret_cast<const float4*>(x + r * ldx + c);
+      *reinterpret_cast<float4*>(y + r * ldy + c) = make_float4(gelu_ggml(v.x), gelu_ggml(v.y), gelu_ggml(v.z),
+                                                                gelu_ggml(v.w));
+    } else {
+      for (int64_t j = c; j < c + 4 && j < cols; ++j) y[r * ldy + j] = gelu_ggml(x[r * ldx + j]);
+    }
+  }
 }
 
 // ---------------------------------------------------------------- weights
@@ -168,6 +177,24 @@ cudaError_t launch_quantize_q8_0_split(const float* x, int64_t m, int64_t k, int
                                        bool vec4, cudaStream_t s) {
   return vec4 ? launch_q<true, true>(x, m, k, ldx_floats, nullptr, 0, codes, scales, ld, variant, s)
               : launch_q<true, false>(x, m, k, ldx_floats, nullptr, 0, codes, scales, ld, variant, s);
+}
+
+cudaError_t launch_gelu(const float* x, int64_t rows, int64_t cols, int64_t ldx_floats, float* y,
+                        int64_t ldy_floats, cudaStream_t s) {
+  const int64_t total = rows * ((cols + 3) / 4);
+  if (total == 0) return cudaSuccess;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t blocks = (total + 255) / 256;
+  const int grid = static_cast<int>(blocks < sms * 16 ? blocks : sms * 16);
+  const bool vec4 = cols % 4 == 0 && ldx_floats % 4 == 0 && ldy_floats % 4 == 0 &&
+                    reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0;
+  if (vec4)
+    gelu_kernel<true><<<grid, 256, 0, s>>>(x, rows, cols, ldx_floats, y, ldy_floats);
+  else
+    gelu_kernel<false><<<grid, 256, 0, s>>>(x, rows, cols, ldx_floats, y, ldy_floats);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_pack_weights(int wtype, const uint8_t* w, int64_t n, int64_t k,

@@ -96,6 +96,28 @@ def test_pack_and_debug_validation(b2q_mod):
     assert L.b2q_device_status(None, 0) == 1
 
 
+def test_fused_gelu_q8_and_gelu_validation(b2q_mod):
+    L = b2q.lib()
+    need = L.b2q_act_prepared_size(16, 64)
+    f = L.b2q_mul_mat_prepared_gelu_q8
+    assert f(FAKE, 48, 1024, FAKE, 16, None, FAKE, 1 << 20, 0, None) == 1        # n % 32
+    assert f(FAKE, 64, 1000, FAKE, 16, None, FAKE, 1 << 20, 0, None) == 1        # k % 32
+    assert f(FAKE, 64, 1024, FAKE, 16, None, FAKE, 1 << 20, 2, None) == 1        # variant
+    assert f(FAKE, 64, 1024, FAKE, 16, None, FAKE + 64, 1 << 20, 0, None) == 3   # act_out alignment
+    assert f(FAKE, 64, 1024, FAKE, 16, FAKE + 2, FAKE, 1 << 20, 0, None) == 3    # bias alignment
+    assert f(FAKE, 64, 1024, FAKE, 16, None, FAKE, need - 1, 0, None) == 4       # act_out too small
+    assert f(FAKE, 64, 1024, FAKE, 16, None, None, 1 << 20, 0, None) == 1        # null act_out
+    assert f(FAKE, 64, 1024, FAKE, 1 << 33, None, FAKE, 1 << 40, 0, None) == 7   # beyond int range
+    assert f(FAKE, 64, 1024, FAKE, 0, None, FAKE, 0, 0, None) == 0               # m == 0: no-op
+    g = L.b2q_gelu
+    assert g(FAKE, 4, 8, 16, FAKE, 32, None) == 1                                # x stride < cols
+    assert g(FAKE, 4, 8, 32, FAKE, 30, None) == 1                                # y stride < cols
+    assert g(FAKE + 2, 4, 8, 32, FAKE, 32, None) == 3
+    assert g(FAKE, 4, 8, 34, FAKE, 32, None) == 3                                # stride % 4
+    assert g(None, 4, 8, 32, FAKE, 32, None) == 1
+    assert g(FAKE, 0, 8, 32, FAKE, 32, None) == 0                                # empty: no-op
+
+
 def test_empty_shapes_are_noops_without_device(b2q_mod):
     L = b2q.lib()
     # m == 0 or n == 0: validated, nothing launched, OK even without a GPU

@@ -1,0 +1,144 @@
+"""GPU parity of the feed-forward pieces next to the mul_mat: ggml_gelu and the
+fused fc1 -> bias -> GELU -> Q8_0-quantize epilogue (the DiT MLP,
+cpp_ggml/src/ss_flow_graph.cpp:380-384), through the C ABI.
+
+Bars: GELU bit-exact with the oracle's restatement of ggml's CPU GELU over all
+65536 fp16 inputs and over random fp32 inputs; the fused epilogue's prepared
+activations byte-identical to the unfused sequence on the GPU
+(mul_mat_prepared -> gelu -> act_prepare); the fc1 -> fc2 chain within
+CHAIN_RTOL of the oracle's chain."""
+import numpy as np
+import pytest
+
+import b2q
+import oracle as O
+from helpers import make_case, rel_frobenius
+
+pytestmark = pytest.mark.gpu
+
+# The chain compares against an oracle whose fc1 output differs from the GPU's
+# by fp32 accumulation order (<= 1e-5 relative); GELU rounds to fp16 and the
+# next quantize rounds to 8 bits, so such a difference can move one fp16 step
+# or one Q8_0 code of the hidden state, which fc2 then carries.
+CHAIN_RTOL = 1e-4
+
+
+def to_dev(a, dev):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def to_np(t):
+    import torch
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def split_view(buf: np.ndarray, m: int, k: int):
+    """Prepared-activation buffer -> (codes int8 [m][k], scales fp32 [k/32][m])."""
+    codes = buf[:m * k].view(np.int8).reshape(m, k)
+    off = (m * k + 255) // 256 * 256
+    ld = (m + 3) // 4 * 4
+    scales = buf[off:off + (k // 32) * ld * 4].view(np.float32).reshape(k // 32, ld)[:, :m]
+    return codes, scales
+
+
+@pytest.fixture(autouse=True)
+def _no_device_errors(b2q_mod, dev):
+    yield
+    assert b2q.device_status(clear=True) == 0
+
+
+def same_bits(a: np.ndarray, b: np.ndarray) -> bool:
+    """Equal as fp32 values, NaN matching NaN (payloads may differ)."""
+    na, nb = np.isnan(a), np.isnan(b)
+    return bool(np.array_equal(na, nb) and np.array_equal(a[~na].view(np.uint32), b[~nb].view(np.uint32)))
+
+
+# ---------------------------------------------------------------------- GELU
+def test_gelu_every_fp16_input(dev):
+    """All 65536 fp16 bit patterns (as fp32, +-inf and NaN included): the
+    computed GELU equals ggml's tabulated one everywhere."""
+    x = np.arange(65536, dtype=np.uint16).view(np.float16).astype(np.float32)
+    y = to_np(b2q.gelu(to_dev(x.reshape(256, 256), dev))).reshape(-1)
+    ref = O.gelu(x)
+    bad = ~((y == ref) | (np.isnan(y) & np.isnan(ref)))
+    assert not bad.any(), (int(bad.sum()), x[bad][:8], y[bad][:8], ref[bad][:8])
+
+
+@pytest.mark.parametrize("rows,cols,pitch", [(513, 1024, 1024), (7, 45, 48), (33, 100, 101)])
+def test_gelu_random_fp32(dev, rows, cols, pitch):
+    """fp32 inputs that are not fp16 values (rounding to fp16 first), strided
+    rows, the scalar tail path, and the in-place form."""
+    import torch
+    rng = np.random.default_rng(rows * 31 + cols)
+    x = (rng.standard_normal((rows, pitch)) * 4).astype(np.float32)
+    x[0, :min(cols, 6)] = [-10.0, 10.0, -9.9999, 9.9999, 0.0, -0.0][:min(cols, 6)]
+    x_d = to_dev(x, dev)
+    y = to_np(b2q.gelu(x_d[:, :cols]))
+    assert same_bits(y, O.gelu(x[:, :cols]))
+    b2q.gelu(x_d[:, :cols], out=x_d[:, :cols])  # in place
+    z = to_np(x_d)
+    assert same_bits(z[:, :cols], y) and same_bits(z[:, cols:], x[:, cols:])
+    torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------- fused epilogue
+@pytest.mark.parametrize("variant", [O.ACT_X86, O.ACT_REF])
+@pytest.mark.parametrize("wtype,M,N,K", [
+    (O.TYPE_Q8_0, 300, 1056, 512),     # ragged M; last weight tile has one valid quarter
+    (O.TYPE_Q4_0, 1374, 1024, 1024),   # kv-like M
+    (O.TYPE_Q8_0, 4096, 4096, 1024),   # fc1 of the SS block (BASELINE C1)
+    (O.TYPE_Q4_0, 97, 96, 256),        # tiny: one partial tile
+])
+def test_fused_gelu_q8_equals_unfused(dev, variant, wtype, M, N, K):
+    import torch
+    _, wq, x = make_case(M + N + K, M, N, K, wtype)
+    bias = np.random.default_rng(5).standard_normal(N).astype(np.float32)
+    w_d, x_d, b_d = to_dev(wq, dev), to_dev(x, dev), to_dev(bias, dev)
+    packed = b2q.weight_pack(wtype, w_d, K)
+    act = b2q.act_prepare(x_d, variant)
+    fused = b2q.mul_mat_prepared_gelu_q8(packed, N, K, act, M, bias=b_d, variant=variant)
+    y = b2q.mul_mat_prepared(packed, N, K, act, M, bias=b_d)
+    h = b2q.gelu(y)
+    unfused = b2q.act_prepare(h, variant)
+    torch.cuda.synchronize()
+    fc, fs = split_view(to_np(fused), M, N)
+    uc, us = split_view(to_np(unfused), M, N)
+    assert np.array_equal(fc, uc)
+    assert np.array_equal(fs.view(np.uint32), us.view(np.uint32))
+
+
+def test_fused_without_bias(dev):
+    import torch
+    M, N, K = 200, 256, 384
+    _, wq, x = make_case(44, M, N, K, O.TYPE_Q8_0)
+    w_d, x_d = to_dev(wq, dev), to_dev(x, dev)
+    packed = b2q.weight_pack(O.TYPE_Q8_0, w_d, K)
+    act = b2q.act_prepare(x_d)
+    fused = b2q.mul_mat_prepared_gelu_q8(packed, N, K, act, M)
+    unfused = b2q.act_prepare(b2q.gelu(b2q.mul_mat_prepared(packed, N, K, act, M)))
+    torch.cuda.synchronize()
+    fc, fs = split_view(to_np(fused), M, N)
+    uc, us = split_view(to_np(unfused), M, N)
+    assert np.array_equal(fc, uc) and np.array_equal(fs.view(np.uint32), us.view(np.uint32))
+
+
+def test_mlp_chain_matches_oracle(dev):
+    """fc2(gelu(fc1(x) + b1)) + b2 with the fused epilogue between the two
+    GEMMs, against the oracle's unfused chain (fc1 Q8_0, fc2 Q4_0)."""
+    M, C, H = 500, 256, 1024
+    rng = np.random.default_rng(77)
+    x = rng.standard_normal((M, C)).astype(np.float32)
+    w1 = O.quantize((rng.standard_normal((H, C)) * 0.05).astype(np.float32), O.TYPE_Q8_0)
+    w2 = O.quantize((rng.standard_normal((C, H)) * 0.05).astype(np.float32), O.TYPE_Q4_0)
+    b1 = rng.standard_normal(H).astype(np.float32)
+    b2 = rng.standard_normal(C).astype(np.float32)
+    p1 = b2q.weight_pack(O.TYPE_Q8_0, to_dev(w1, dev), C)
+    p2 = b2q.weight_pack(O.TYPE_Q4_0, to_dev(w2, dev), H)
+    act1 = b2q.act_prepare(to_dev(x, dev))
+    act2 = b2q.mul_mat_prepared_gelu_q8(p1, H, C, act1, M, bias=to_dev(b1, dev))
+    y = to_np(b2q.mul_mat_prepared(p2, C, H, act2, M, bias=to_dev(b2, dev)))
+    h = O.gelu(O.mul_mat(O.TYPE_Q8_0, w1, x, O.ACT_X86) + b1)
+    ref = O.mul_mat(O.TYPE_Q4_0, w2, h, O.ACT_X86) + b2
+    assert rel_frobenius(y, ref) <= CHAIN_RTOL

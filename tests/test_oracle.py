@@ -133,3 +133,28 @@ def test_zero_and_degenerate_rows():
     w = np.ones((2, K), np.float32)
     y = O.mul_mat(O.TYPE_Q8_0, O.quantize(w, O.TYPE_Q8_0), x, O.ACT_X86)
     assert np.all(y == 0)
+
+
+def test_gelu_table_follows_the_tanh_formula():
+    """ggml's fp16 GELU table (restated in the oracle) against the same tanh
+    form in fp64: each entry within one fp16 step of the fp64 value plus the
+    fp32 formula's own error (1 + tanh cancels for x < 0: a few fp32 ulps of 1,
+    times 0.5|x|), 0 / identity outside (-10, 10), NaN through, and the
+    contracted (FMA) build of the table differs from the uncontracted one in
+    few entries."""
+    h = np.arange(65536, dtype=np.uint16)
+    fin = np.isfinite(h.view(np.float16)) & (np.abs(h.view(np.float16)) < 10)
+    f = h[fin].view(np.float16).astype(np.float64)
+    t = O.gelu_table(False)[fin].view(np.float16).astype(np.float64)
+    exact = 0.5 * f * (1.0 + np.tanh(0.7978845608028654 * f * (1.0 + 0.044715 * f * f)))
+    step = np.abs(np.spacing(exact.astype(np.float16)).astype(np.float64))
+    assert np.all(np.abs(t - exact) <= step + 0.5 * np.abs(f) * 4 * 2.0 ** -24)
+    assert np.count_nonzero(O.gelu_table(False) != O.gelu_table(True)) <= 8
+    x = np.array([-np.inf, -1e6, -10.0, -9.99, 9.99, 10.0, 1e6, np.inf, np.nan, 0.0], np.float32)
+    y = O.gelu(x)
+    assert list(y[:3]) == [0.0, 0.0, 0.0] and list(y[5:8]) == [10.0, 1e6, np.inf]
+    assert np.isnan(y[8]) and y[9] == 0.0
+    # inside (-10, 10): x rounded to fp16, then the table entry
+    xs = np.random.default_rng(3).uniform(-9.9, 9.9, 4096).astype(np.float32)
+    idx = xs.astype(np.float16).view(np.uint16)
+    assert np.array_equal(O.gelu(xs), O.gelu_table(False)[idx].view(np.float16).astype(np.float32))
