@@ -350,6 +350,8 @@ def run_gpu(args, rank, world, local_rank):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(), "breakdown": breakdown,
     }
+    if not args.only and not args.no_mlp:
+        result["mlp_branch"] = mlp_branch(b2q, gemms, flush, stream, dev)
     if args.only:
         result["config"]["workload"] = f"single GEMM {args.only} (profiling case)"
         result["config"]["l2"] = "not flushed (profiling case)"
@@ -359,6 +361,63 @@ def run_gpu(args, rank, world, local_rank):
         dist.barrier()
         dist.destroy_process_group()
     return result
+
+
+# ------------------------------------------------------ fused MLP (next row)
+def mlp_branch(b2q, gemms, flush, stream, dev, iters=10):
+    """The DiT feed-forward branch fc2(gelu(fc1(x) + b1)) + b2 on the fc1 and
+    fc2 weights of the workload, from fc1's prepared activations to fc2's fp32
+    output, with and without the fused GELU + Q8_0 epilogue.  Reported beside
+    the headline (its ops are not part of `value`); L2 flushed before each
+    iteration, CUDA events on the launching stream."""
+    import torch
+    by = {g["name"]: g for g in gemms}
+    f1, f2 = by.get("fc1_q4_0"), by.get("fc2_q4_0")
+    if f1 is None or f2 is None or f1["N"] != f2["K"] or f1["M"] != f2["M"]:
+        return None
+    M, H, C = f1["M"], f1["N"], f2["N"]
+    g = torch.Generator(device=dev).manual_seed(7)
+    b1 = torch.randn(H, device=dev, generator=g)
+    b2 = torch.randn(C, device=dev, generator=g)
+    b2q.act_prepare(f1["x_dev"], out=f1["act"], stream=stream)
+    hid = torch.empty((M, H), dtype=torch.float32, device=dev)
+    act2 = b2q._empty_aligned(b2q.act_prepared_size(M, H), dev)
+    y = torch.empty((M, C), dtype=torch.float32, device=dev)
+
+    def unfused():
+        b2q.mul_mat_prepared(f1["packed"], H, f1["K"], f1["act"], M, bias=b1, out=hid, stream=stream)
+        b2q.gelu(hid, out=hid, stream=stream)
+        b2q.act_prepare(hid, out=act2, stream=stream)
+        b2q.mul_mat_prepared(f2["packed"], C, H, act2, M, bias=b2, out=y, stream=stream)
+
+    def fused():
+        b2q.mul_mat_prepared_gelu_q8(f1["packed"], H, f1["K"], f1["act"], M, bias=b1, out=act2, stream=stream)
+        b2q.mul_mat_prepared(f2["packed"], C, H, act2, M, bias=b2, out=y, stream=stream)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(iters)]
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        return statistics.median(e0.elapsed_time(e1) * 1e3 for e0, e1 in evs)
+
+    u, f = timed(unfused), timed(fused)
+    y_f = y.clone()
+    unfused()
+    torch.cuda.synchronize()
+    return {"shape": {"M": M, "C": C, "hidden": H, "weights": "Q4_0"},
+            "unfused_us": round(u, 2), "fused_us": round(f, 2), "speedup": round(u / f, 3),
+            "launches": {"unfused": 4, "fused": 2},
+            "fused_equals_unfused": bool(torch.equal(y, y_f)),
+            "hidden_fp32_bytes_avoided": 2 * 4 * M * H,
+            "path": "unfused: mul_mat_prepared(+b1) -> gelu -> act_prepare -> mul_mat_prepared(+b2); "
+                    "fused: mul_mat_prepared_gelu_q8(+b1) -> mul_mat_prepared(+b2)"}
 
 
 # ------------------------------------------------- column-parallel (multi-GPU)
@@ -552,6 +611,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-mlp", action="store_true", help="skip the fused-MLP side measurement")
     ap.add_argument("--only", default=None, help="run one workload entry (profiling case)")
     ap.add_argument("--colpar", action="store_true",
                     help="column-parallel SLat linear (one GEMM split over the ranks, all-gathered output)")
