@@ -475,13 +475,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok || (!GELUQ && !p.y)) continue;
       const int64_t n = static_cast<int64_t>(tile % p.n_tiles) * kBM + row;
-      const float bv = p.bias && n < p.N ? p.bias[n] : 0.0f;
       const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * BN + chalf * COLS;
       if (GELUQ) {
         // The warp's 32 weight rows are one Q8_0 block of the next layer's K
         // (N % 32 == 0, so they are all valid or all not).
         const int64_t nq = static_cast<int64_t>(tile % p.n_tiles) * kBM + quarter * 32;
         if (nq < p.N && m0 < p.M) {
+          const float bv = p.bias ? p.bias[n] : 0.0f;
           int8_t* codes = pp.q_codes + nq;
           float* qs = pp.q_scales + (nq / kQK) * pp.q_ld;
           float* xp = reinterpret_cast<float*>(smem + C::XPOSE_OFF) + (warp - kEpiWarp0) * C::XPOSE_FLOATS;
@@ -491,13 +491,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             geluq_cols<1, COLS>(acc, bv, p.bias != nullptr, m0, p.M, lane, codes, pp.q_k, qs, xp);
         }
       } else if (n < p.N) {
-        {  // ggml_add after the mul_mat: one fp32 rounding per element (x * 1 + b).  Without
-           // a bias bv = +0, an identity here: the sums start at +0, so none is -0.
+        const float bv = p.bias ? p.bias[n] : 0.0f;
+        if (!PEERS) {  // the column-parallel store is its own instantiation: it slows this loop
+          // ggml_add after the mul_mat: one fp32 rounding per element (x * 1 + b), in one
+          // packed pass (a select per store costs this kernel 10%).  Without a bias
+          // bv = +0, an identity here: the sums start at +0, so none is -0.
           const float2 b2 = make_float2(bv, bv), one = make_float2(1.0f, 1.0f);
 #pragma unroll
           for (int c = 0; c < COLS / 2; ++c) acc[c] = ffma2(acc[c], one, b2);
-        }
-        if (!PEERS) {  // the column-parallel store is its own instantiation: it slows this loop
           float* yp = p.y + m0 * p.ldy + n;
 #pragma unroll
           for (int c = 0; c < COLS / 2; ++c) {
@@ -514,8 +515,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             float* yp = pp.ptr[q] + off;
 #pragma unroll
             for (int c = 0; c < COLS / 2; ++c) {
-              if (m0 + 2 * c < p.M) yp[(2 * c) * p.ldy] = acc[c].x;
-              if (m0 + 2 * c + 1 < p.M) yp[(2 * c + 1) * p.ldy] = acc[c].y;
+              if (m0 + 2 * c < p.M) yp[(2 * c) * p.ldy] = p.bias ? acc[c].x + bv : acc[c].x;
+              if (m0 + 2 * c + 1 < p.M) yp[(2 * c + 1) * p.ldy] = p.bias ? acc[c].y + bv : acc[c].y;
             }
           }
         }
