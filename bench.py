@@ -408,11 +408,32 @@ def mlp_branch(b2q, gemms, flush, stream, dev, iters=10):
         return statistics.median(e0.elapsed_time(e1) * 1e3 for e0, e1 in evs)
 
     u, f = timed(unfused), timed(fused)
+
+    def hot(fn, n=20):  # one kernel back to back, hot L2
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return round(e0.elapsed_time(e1) / n * 1e3, 2)
+
+    kernels = {
+        "fc1_bias": hot(lambda: b2q.mul_mat_prepared(f1["packed"], H, f1["K"], f1["act"], M, bias=b1, out=hid,
+                                                     stream=stream)),
+        "fc1_bias_gelu_q8": hot(lambda: b2q.mul_mat_prepared_gelu_q8(f1["packed"], H, f1["K"], f1["act"], M,
+                                                                     bias=b1, out=act2, stream=stream)),
+        "gelu": hot(lambda: b2q.gelu(hid, out=hid, stream=stream)),
+        "act_prepare_hidden": hot(lambda: b2q.act_prepare(hid, out=act2, stream=stream)),
+    }
     y_f = y.clone()
     unfused()
     torch.cuda.synchronize()
     return {"shape": {"M": M, "C": C, "hidden": H, "weights": "Q4_0"},
             "unfused_us": round(u, 2), "fused_us": round(f, 2), "speedup": round(u / f, 3),
+            "kernels_us_hot_l2": kernels,
             "launches": {"unfused": 4, "fused": 2},
             "fused_equals_unfused": bool(torch.equal(y, y_f)),
             "hidden_fp32_bytes_avoided": 2 * 4 * M * H,
