@@ -174,6 +174,25 @@ B2Q_API int b2q_mul_mat_prepared_gelu_q8(const void* packed, int64_t n, int64_t 
 B2Q_API int b2q_gelu(const float* x, int64_t rows, int64_t cols, int64_t x_row_stride_bytes,
                      float* y, int64_t y_row_stride_bytes, void* stream);
 
+/* ----------------------------------------- DiT pre-norm (LayerNorm + modulate)
+ * h = ggml_norm(x, eps) (LayerNorm over each row of c values, no affine), then
+ * the adaLN modulate h = (h * mod_scale + h) + mod_shift with mod_scale and
+ * mod_shift per column (cpp_ggml/src/ss_flow_graph.cpp:45-53; used before
+ * every self-attention and MLP branch, :200-204, :378-379; gb_layer_norm at
+ * graph_builder.cpp:62-68).  Either modulation vector may be NULL (that term is
+ * skipped; both NULL is plain ggml_norm).  mean and variance are accumulated in
+ * double as ggml's CPU norm does.  Requires c % 32 == 0, c <= 4096, x and y
+ * 16-byte aligned with row strides multiples of 16 bytes.
+ * b2q_norm_modulate writes fp32 y; b2q_norm_modulate_q8 writes the next
+ * mul_mat's prepared Q8_0 activations (b2q_act_prepare layout for m rows and
+ * k = c), equal byte for byte to b2q_act_prepare(b2q_norm_modulate(...)). */
+B2Q_API int b2q_norm_modulate(const float* x, int64_t m, int64_t c, int64_t x_row_stride_bytes, float eps,
+                              const float* mod_scale, const float* mod_shift, float* y,
+                              int64_t y_row_stride_bytes, void* stream);
+B2Q_API int b2q_norm_modulate_q8(const float* x, int64_t m, int64_t c, int64_t x_row_stride_bytes, float eps,
+                                 const float* mod_scale, const float* mod_shift, int variant, void* act,
+                                 size_t act_bytes, void* stream);
+
 /* ------------------------------------------- column-parallel form (multi-GPU)
  * One rank of a tensor-parallel group for a single large mul_mat (the SLat
  * flow transformer's linears at 8k-20k tokens): the weight is split by output

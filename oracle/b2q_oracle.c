@@ -362,6 +362,34 @@ void b2q_orc_gelu_n(const float* x, float* y, int64_t n, int contract) {
   for (int64_t i = 0; i < n; ++i) y[i] = b2q_orc_gelu(x[i], contract);
 }
 
+/* ---------------------------------------------------------- LayerNorm */
+
+void b2q_orc_norm_modulate(const float* x, int64_t m, int64_t c, int64_t ldx_floats, float eps,
+                           const float* scale, const float* shift, float* y, int64_t ldy_floats) {
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < m; ++r) {
+    const float* xr = x + r * ldx_floats;
+    float* yr = y + r * ldy_floats;
+    double sum = 0.0;
+    for (int64_t i = 0; i < c; ++i) sum += (double)xr[i];
+    const float mean = (float)sum / (float)c;
+    double sum2 = 0.0;
+    for (int64_t i = 0; i < c; ++i) {
+      const float v = xr[i] - mean;
+      yr[i] = v;
+      sum2 += (double)(v * v);
+    }
+    const float var = (float)(sum2 / (double)c);
+    const float rs = 1.0f / sqrtf(var + eps);
+    for (int64_t i = 0; i < c; ++i) {
+      float h = yr[i] * rs;
+      if (scale) h = h * scale[i] + h;
+      if (shift) h = h + shift[i];
+      yr[i] = h;
+    }
+  }
+}
+
 int b2q_orc_num_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

@@ -121,6 +121,16 @@ void b2q_orc_gelu_n(const float* x, float* y, int64_t n, int contract);
 /* The 65536-entry table itself (fp16 bits), for exhaustive comparisons. */
 void b2q_orc_gelu_table(uint16_t* table, int contract);
 
+/* ggml_norm (LayerNorm without affine) then the adaLN modulate of the SS-flow
+ * blocks, per row of c values (cpp_ggml/src/ss_flow_graph.cpp:45-53,
+ * graph_builder.cpp:62-68; ggml v0.21.0 ggml-cpu ops.cpp norm_f32):
+ *   sum = Σx (double, sequential) cast to float; mean = sum / c (float);
+ *   v = x - mean; var = (Σ (v*v as float), double) / c, cast to float;
+ *   h = v * (1 / sqrtf(var + eps)); h = (h*scale + h) if scale; h = h + shift if shift.
+ * scale / shift are per column, either may be NULL. */
+void b2q_orc_norm_modulate(const float* x, int64_t m, int64_t c, int64_t ldx_floats, float eps,
+                           const float* scale, const float* shift, float* y, int64_t ldy_floats);
+
 int b2q_orc_num_threads(void);
 const char* b2q_orc_isa(void);
 

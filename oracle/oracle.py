@@ -66,6 +66,7 @@ def lib():
         L.b2q_orc_gelu.argtypes = [ctypes.c_float, I]
         L.b2q_orc_gelu_n.argtypes = [P, P, I64, I]
         L.b2q_orc_gelu_table.argtypes = [P, I]
+        L.b2q_orc_norm_modulate.argtypes = [P, I64, I64, I64, ctypes.c_float, P, P, P, I64]
         L.b2q_orc_num_threads.restype = I
         L.b2q_orc_isa.restype = ctypes.c_char_p
         _lib = L
@@ -186,3 +187,15 @@ def gelu_table(contract: bool = False) -> np.ndarray:
     t = np.empty(65536, dtype=np.uint16)
     lib().b2q_orc_gelu_table(_p(t), int(contract))
     return t
+
+
+def norm_modulate(x: np.ndarray, eps: float = 1e-6, scale=None, shift=None) -> np.ndarray:
+    """ggml_norm then h*(1+scale)+shift per column; see b2q_oracle.h."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    m, c = x.shape
+    y = np.empty_like(x)
+    sc = None if scale is None else np.ascontiguousarray(scale, dtype=np.float32)
+    sh = None if shift is None else np.ascontiguousarray(shift, dtype=np.float32)
+    lib().b2q_orc_norm_modulate(_p(x), m, c, c, eps, None if sc is None else _p(sc),
+                                None if sh is None else _p(sh), _p(y), c)
+    return y

@@ -69,6 +69,8 @@ def _lib_obj():
             "b2q_mul_mat_prepared": (I, [P, I64, I64, P, I64, P, P, I64, P]),
             "b2q_mul_mat_prepared_gelu_q8": (I, [P, I64, I64, P, I64, P, P, SZ, I, P]),
             "b2q_gelu": (I, [P, I64, I64, I64, P, I64, P]),
+            "b2q_norm_modulate": (I, [P, I64, I64, I64, ctypes.c_float, P, P, P, I64, P]),
+            "b2q_norm_modulate_q8": (I, [P, I64, I64, I64, ctypes.c_float, P, P, I, P, SZ, P]),
             "b2q_mul_mat_prepared_peers": (I, [P, I64, I64, P, I64, P, ctypes.POINTER(ctypes.c_void_p), I, I64,
                                                I64, P]),
             "b2q_block_dots": (I, [I, P, I64, I64, I64, P, I64, I64, P, P, SZ, P]),
@@ -274,6 +276,31 @@ def gelu(x, out=None, stream=None):
     rc = lib().b2q_gelu(_ptr(x), rows, cols, x.stride(0) * 4, _ptr(out), out.stride(0) * 4,
                         _stream(stream))
     _check("b2q_gelu", rc)
+    return out
+
+
+def norm_modulate(x, eps: float = 1e-6, scale=None, shift=None, out=None, stream=None):
+    """ggml_norm + adaLN modulate, fp32 [M, C] -> fp32 [M, C] (CUDA tensors)."""
+    torch = _torch()
+    m, c = x.shape
+    if out is None:
+        out = torch.empty((m, c), dtype=torch.float32, device=x.device)
+    rc = lib().b2q_norm_modulate(_ptr(x), m, c, x.stride(0) * 4, eps, _ptr(scale), _ptr(shift), _ptr(out),
+                                 out.stride(0) * 4, _stream(stream))
+    _check("b2q_norm_modulate", rc)
+    return out
+
+
+def norm_modulate_q8(x, eps: float = 1e-6, scale=None, shift=None, variant: int = ACT_X86, out=None,
+                     stream=None):
+    """ggml_norm + adaLN modulate straight into the next mul_mat's prepared Q8_0 activations."""
+    m, c = x.shape
+    size = act_prepared_size(m, c)
+    if out is None:
+        out = _empty_aligned(size, x.device)
+    rc = lib().b2q_norm_modulate_q8(_ptr(x), m, c, x.stride(0) * 4, eps, _ptr(scale), _ptr(shift), variant,
+                                    _ptr(out), out.numel() * out.element_size(), _stream(stream))
+    _check("b2q_norm_modulate_q8", rc)
     return out
 
 

@@ -105,6 +105,17 @@ int check_x_y(const float* x, int64_t m, int64_t k, int64_t ldx, float* y, int64
   return B2Q_OK;
 }
 
+int check_norm(const float* x, int64_t m, int64_t c, int64_t x_rs, float eps, const float* ms, const float* sh) {
+  if (m < 0 || c <= 0 || c % kQK != 0) return B2Q_ERR_INVALID_ARG;
+  if (c > kNormMaxC || m > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (!(eps >= 0.0f)) return B2Q_ERR_INVALID_ARG;
+  if (m > 0 && !x) return B2Q_ERR_INVALID_ARG;
+  if (x_rs < c * 4) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(x, 16) || x_rs % 16 != 0 || (ms && !aligned(ms, 4)) || (sh && !aligned(sh, 4)))
+    return B2Q_ERR_MISALIGNED;
+  return B2Q_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -292,6 +303,36 @@ int b2q_gelu(const float* x, int64_t rows, int64_t cols, int64_t x_row_stride_by
   if (int rc = check_device(nullptr)) return rc;
   return from_cuda(launch_gelu(x, rows, cols, x_row_stride_bytes / 4, y, y_row_stride_bytes / 4,
                                static_cast<cudaStream_t>(stream)));
+}
+
+int b2q_norm_modulate(const float* x, int64_t m, int64_t c, int64_t x_row_stride_bytes, float eps,
+                      const float* mod_scale, const float* mod_shift, float* y, int64_t y_row_stride_bytes,
+                      void* stream) {
+  if (int rc = check_norm(x, m, c, x_row_stride_bytes, eps, mod_scale, mod_shift)) return rc;
+  if (m > 0 && !y) return B2Q_ERR_INVALID_ARG;
+  if (y_row_stride_bytes < c * 4) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(y, 16) || y_row_stride_bytes % 16 != 0) return B2Q_ERR_MISALIGNED;
+  if (m == 0) return B2Q_OK;
+  if (int rc = check_device(nullptr)) return rc;
+  return from_cuda(launch_norm_modulate(x, m, c, x_row_stride_bytes / 4, eps, mod_scale, mod_shift, y,
+                                        y_row_stride_bytes / 4, nullptr, nullptr, 0, 0,
+                                        static_cast<cudaStream_t>(stream)));
+}
+
+int b2q_norm_modulate_q8(const float* x, int64_t m, int64_t c, int64_t x_row_stride_bytes, float eps,
+                         const float* mod_scale, const float* mod_shift, int variant, void* act, size_t act_bytes,
+                         void* stream) {
+  if (int rc = check_norm(x, m, c, x_row_stride_bytes, eps, mod_scale, mod_shift)) return rc;
+  if (variant != B2Q_ACT_X86 && variant != B2Q_ACT_REF) return B2Q_ERR_INVALID_ARG;
+  if (m > 0 && !act) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(act, 256)) return B2Q_ERR_MISALIGNED;
+  if (act_bytes < split_bytes(m, c)) return B2Q_ERR_WORKSPACE;
+  if (m == 0) return B2Q_OK;
+  if (int rc = check_device(nullptr)) return rc;
+  const SplitOperand a = split_at(static_cast<uint8_t*>(act), m, c);
+  return from_cuda(launch_norm_modulate(x, m, c, x_row_stride_bytes / 4, eps, mod_scale, mod_shift, nullptr, 0,
+                                        const_cast<int8_t*>(a.codes), const_cast<float*>(a.scales), a.ld,
+                                        variant, static_cast<cudaStream_t>(stream)));
 }
 
 int b2q_mul_mat_prepared_peers(const void* packed, int64_t n, int64_t k, const void* act, int64_t m,

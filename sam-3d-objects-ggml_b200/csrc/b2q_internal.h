@@ -61,6 +61,12 @@ cudaError_t launch_gemm_simt(int wtype, const uint8_t* w, int64_t ldw_bytes, int
                              const uint8_t* a, int64_t lda_bytes, int64_t m, float* y,
                              int64_t ldy_floats, cudaStream_t s);
 
+// ggml_norm + adaLN modulate, fp32 out (codes == nullptr) or Q8_0 split out.
+constexpr int64_t kNormMaxC = 4096;
+cudaError_t launch_norm_modulate(const float* x, int64_t m, int64_t c, int64_t ldx_floats, float eps,
+                                 const float* mscale, const float* mshift, float* y, int64_t ldy_floats,
+                                 int8_t* codes, float* qscales, int64_t qld, int variant, cudaStream_t s);
+
 cudaError_t launch_gelu(const float* x, int64_t rows, int64_t cols, int64_t ldx_floats, float* y,
                         int64_t ldy_floats, cudaStream_t s);
 

@@ -118,6 +118,26 @@ def test_fused_gelu_q8_and_gelu_validation(b2q_mod):
     assert g(FAKE, 0, 8, 32, FAKE, 32, None) == 0                                # empty: no-op
 
 
+def test_norm_modulate_validation(b2q_mod):
+    L = b2q.lib()
+    f, q = L.b2q_norm_modulate, L.b2q_norm_modulate_q8
+    assert f(FAKE, 4, 48, 192, 1e-6, None, None, FAKE, 192, None) == 1            # c % 32
+    assert f(FAKE, 4, 8192, 32768, 1e-6, None, None, FAKE, 32768, None) == 7      # c > 4096
+    assert f(FAKE, 4, 64, 128, 1e-6, None, None, FAKE, 256, None) == 1            # x stride < c
+    assert f(FAKE, 4, 64, 256, -1.0, None, None, FAKE, 256, None) == 1            # eps < 0
+    assert f(FAKE + 4, 4, 64, 256, 1e-6, None, None, FAKE, 256, None) == 3        # x not 16-byte aligned
+    assert f(FAKE, 4, 64, 260, 1e-6, None, None, FAKE, 256, None) == 3            # stride % 16
+    assert f(FAKE, 4, 64, 256, 1e-6, FAKE + 2, None, FAKE, 256, None) == 3        # scale alignment
+    assert f(FAKE, 4, 64, 256, 1e-6, None, None, None, 256, None) == 1            # null y
+    assert f(FAKE, 4, 64, 256, 1e-6, None, None, FAKE + 8, 256, None) == 3        # y alignment
+    assert f(FAKE, 0, 64, 256, 1e-6, None, None, FAKE, 256, None) == 0            # empty: no-op
+    need = L.b2q_act_prepared_size(4, 64)
+    assert q(FAKE, 4, 64, 256, 1e-6, None, None, 2, FAKE, need, None) == 1        # variant
+    assert q(FAKE, 4, 64, 256, 1e-6, None, None, 0, FAKE + 16, need, None) == 3   # act alignment
+    assert q(FAKE, 4, 64, 256, 1e-6, None, None, 0, FAKE, need - 1, None) == 4    # act too small
+    assert q(FAKE, 0, 64, 256, 1e-6, None, None, 0, FAKE, 0, None) == 0
+
+
 def test_empty_shapes_are_noops_without_device(b2q_mod):
     L = b2q.lib()
     # m == 0 or n == 0: validated, nothing launched, OK even without a GPU

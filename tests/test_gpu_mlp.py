@@ -142,3 +142,62 @@ def test_mlp_chain_matches_oracle(dev):
     h = O.gelu(O.mul_mat(O.TYPE_Q8_0, w1, x, O.ACT_X86) + b1)
     ref = O.mul_mat(O.TYPE_Q4_0, w2, h, O.ACT_X86) + b2
     assert rel_frobenius(y, ref) <= CHAIN_RTOL
+
+
+# ------------------------------------------------ pre-norm (LN + modulate)
+@pytest.mark.parametrize("M,C", [(4096, 1024), (300, 1024), (17, 2048), (5, 4096), (33, 96)])
+def test_norm_modulate_matches_oracle(dev, M, C):
+    rng = np.random.default_rng(M + C)
+    x = (rng.standard_normal((M, C)) * 2 + 0.3).astype(np.float32)
+    s = (rng.standard_normal(C) * 0.2).astype(np.float32)
+    t = (rng.standard_normal(C) * 0.2).astype(np.float32)
+    x_d, s_d, t_d = to_dev(x, dev), to_dev(s, dev), to_dev(t, dev)
+    for sc, sh, scd, shd in ((s, t, s_d, t_d), (None, None, None, None), (None, t, None, t_d)):
+        y = to_np(b2q.norm_modulate(x_d, 1e-6, scd, shd))
+        assert same_bits(y, O.norm_modulate(x, 1e-6, sc, sh))
+
+
+@pytest.mark.parametrize("variant", [O.ACT_X86, O.ACT_REF])
+@pytest.mark.parametrize("M,C", [(4096, 1024), (257, 1024), (9, 3072)])
+def test_norm_modulate_q8_equals_two_step(dev, variant, M, C):
+    """The fused pre-norm + quantize writes the same bytes as norm_modulate then
+    act_prepare, and the oracle's quantize of the oracle's pre-norm."""
+    import torch
+    rng = np.random.default_rng(3 * M + C)
+    x = rng.standard_normal((M, C)).astype(np.float32)
+    s = (rng.standard_normal(C) * 0.2).astype(np.float32)
+    t = (rng.standard_normal(C) * 0.2).astype(np.float32)
+    x_d, s_d, t_d = to_dev(x, dev), to_dev(s, dev), to_dev(t, dev)
+    fused = b2q.norm_modulate_q8(x_d, 1e-6, s_d, t_d, variant=variant)
+    two = b2q.act_prepare(b2q.norm_modulate(x_d, 1e-6, s_d, t_d), variant)
+    torch.cuda.synchronize()
+    fc, fs = split_view(to_np(fused), M, C)
+    tc, ts = split_view(to_np(two), M, C)
+    assert np.array_equal(fc, tc) and np.array_equal(fs.view(np.uint32), ts.view(np.uint32))
+    ref = O.quantize(O.norm_modulate(x, 1e-6, s, t), O.TYPE_Q8_0, variant).reshape(M, C // 32, 34)
+    assert np.array_equal(fc.reshape(M, C // 32, 32), ref[:, :, 2:].view(np.int8))
+    d16 = ref[:, :, :2].copy().view(np.float16).reshape(M, C // 32).astype(np.float32)
+    assert np.array_equal(fs.T, d16 * np.float32(2.0 ** 49))
+
+
+def test_prenorm_mlp_chain_matches_oracle(dev):
+    """LN + modulate -> fc1 (+b1, GELU, Q8_0 fused) -> fc2 (+b2): the whole
+    feed-forward branch of an SS block on the device, against the oracle."""
+    M, C, H = 384, 256, 1024
+    rng = np.random.default_rng(99)
+    x = (rng.standard_normal((M, C)) * 2).astype(np.float32)
+    s = (rng.standard_normal(C) * 0.2).astype(np.float32)
+    t = (rng.standard_normal(C) * 0.2).astype(np.float32)
+    w1 = O.quantize((rng.standard_normal((H, C)) * 0.05).astype(np.float32), O.TYPE_Q8_0)
+    w2 = O.quantize((rng.standard_normal((C, H)) * 0.05).astype(np.float32), O.TYPE_Q8_0)
+    b1 = rng.standard_normal(H).astype(np.float32)
+    b2 = rng.standard_normal(C).astype(np.float32)
+    p1 = b2q.weight_pack(O.TYPE_Q8_0, to_dev(w1, dev), C)
+    p2 = b2q.weight_pack(O.TYPE_Q8_0, to_dev(w2, dev), H)
+    act1 = b2q.norm_modulate_q8(to_dev(x, dev), 1e-6, to_dev(s, dev), to_dev(t, dev))
+    act2 = b2q.mul_mat_prepared_gelu_q8(p1, H, C, act1, M, bias=to_dev(b1, dev))
+    y = to_np(b2q.mul_mat_prepared(p2, C, H, act2, M, bias=to_dev(b2, dev)))
+    h = O.norm_modulate(x, 1e-6, s, t)
+    h = O.gelu(O.mul_mat(O.TYPE_Q8_0, w1, h, O.ACT_X86) + b1)
+    ref = O.mul_mat(O.TYPE_Q8_0, w2, h, O.ACT_X86) + b2
+    assert rel_frobenius(y, ref) <= CHAIN_RTOL

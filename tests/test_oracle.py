@@ -158,3 +158,23 @@ def test_gelu_table_follows_the_tanh_formula():
     xs = np.random.default_rng(3).uniform(-9.9, 9.9, 4096).astype(np.float32)
     idx = xs.astype(np.float16).view(np.uint16)
     assert np.array_equal(O.gelu(xs), O.gelu_table(False)[idx].view(np.float16).astype(np.float32))
+
+
+def test_norm_modulate_matches_fp64_layernorm():
+    """ggml_norm restated (double sums, float steps) against an fp64
+    LayerNorm; the modulate terms applied in ggml's order."""
+    rng = np.random.default_rng(11)
+    x = (rng.standard_normal((64, 1024)) * 3 + 0.5).astype(np.float32)
+    s = (rng.standard_normal(1024) * 0.1).astype(np.float32)
+    t = (rng.standard_normal(1024) * 0.1).astype(np.float32)
+    x64 = x.astype(np.float64)
+    ln = (x64 - x64.mean(1, keepdims=True)) / np.sqrt(x64.var(1, keepdims=True) + 1e-6)
+    assert np.abs(O.norm_modulate(x) - ln).max() < 2e-6
+    y = O.norm_modulate(x, 1e-6, s, t)
+    assert np.abs(y - (ln * (1 + s) + t)).max() < 4e-6
+    h = O.norm_modulate(x)
+    assert np.array_equal(y, ((h * s + h) + t).astype(np.float32))   # same float steps
+    assert np.array_equal(O.norm_modulate(x, 1e-6, None, t), (h + t).astype(np.float32))
+    # constant rows: variance 0, output 0 (x - mean = 0; 0 / sqrt(eps))
+    z = O.norm_modulate(np.full((2, 64), 3.25, np.float32))
+    assert np.all(z == 0)
