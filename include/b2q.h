@@ -169,6 +169,17 @@ B2Q_API int b2q_mul_mat_prepared(const void* packed, int64_t n, int64_t k, const
 B2Q_API int b2q_mul_mat_prepared_gelu_q8(const void* packed, int64_t n, int64_t k, const void* act,
                                          int64_t m, const float* bias, void* act_out,
                                          size_t act_out_bytes, int variant, void* stream);
+/* The end of a DiT branch: the output projection (attention to_out, or fc2),
+ * its bias, the adaLN gate and the residual add in one GEMM:
+ *   y[i][j] = resid[i][j] + gate[j] * (mul_mat(w, act)[i][j] + bias[j])
+ * with ggml's roundings (ggml_add of the bias, ggml_mul by the gate, ggml_add
+ * of the residual; cpp_ggml/src/ss_flow_graph.cpp:383-387 for the MLP branch).
+ * gate and bias may be NULL.  resid and y are either the same buffer with the
+ * same row stride (in-place update of the residual stream) or disjoint. */
+B2Q_API int b2q_mul_mat_prepared_gate_residual(const void* packed, int64_t n, int64_t k, const void* act,
+                                               int64_t m, const float* bias, const float* gate,
+                                               const float* resid, int64_t resid_row_stride_bytes, float* y,
+                                               int64_t y_row_stride_bytes, void* stream);
 /* ggml_gelu (GGML_OP_UNARY, GGML_UNARY_OP_GELU) on an fp32 [rows][cols]
  * matrix, the same arithmetic as the fused epilogue above; x == y allowed. */
 B2Q_API int b2q_gelu(const float* x, int64_t rows, int64_t cols, int64_t x_row_stride_bytes,

@@ -69,6 +69,7 @@ def _lib_obj():
             "b2q_mul_mat_prepared": (I, [P, I64, I64, P, I64, P, P, I64, P]),
             "b2q_mul_mat_prepared_gelu_q8": (I, [P, I64, I64, P, I64, P, P, SZ, I, P]),
             "b2q_gelu": (I, [P, I64, I64, I64, P, I64, P]),
+            "b2q_mul_mat_prepared_gate_residual": (I, [P, I64, I64, P, I64, P, P, P, I64, P, I64, P]),
             "b2q_norm_modulate": (I, [P, I64, I64, I64, ctypes.c_float, P, P, P, I64, P]),
             "b2q_norm_modulate_q8": (I, [P, I64, I64, I64, ctypes.c_float, P, P, I, P, SZ, P]),
             "b2q_mul_mat_prepared_peers": (I, [P, I64, I64, P, I64, P, ctypes.POINTER(ctypes.c_void_p), I, I64,
@@ -264,6 +265,19 @@ def mul_mat_prepared_gelu_q8(packed, n: int, k: int, act, m: int, bias=None,
                                             out.numel() * out.element_size(), variant,
                                             _stream(stream))
     _check("b2q_mul_mat_prepared_gelu_q8", rc)
+    return out
+
+
+def mul_mat_prepared_gate_residual(packed, n: int, k: int, act, m: int, resid, bias=None, gate=None,
+                                   out=None, stream=None):
+    """resid + gate * (mul_mat + bias), fp32 [m, n]; out=resid updates the residual in place."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=act.device)
+    rc = lib().b2q_mul_mat_prepared_gate_residual(_ptr(packed), n, k, _ptr(act), m, _ptr(bias), _ptr(gate),
+                                                  _ptr(resid), resid.stride(0) * 4, _ptr(out),
+                                                  out.stride(0) * 4, _stream(stream))
+    _check("b2q_mul_mat_prepared_gate_residual", rc)
     return out
 
 

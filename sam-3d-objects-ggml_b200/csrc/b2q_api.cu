@@ -292,6 +292,38 @@ int b2q_mul_mat_prepared_gelu_q8(const void* packed, int64_t n, int64_t k, const
   return from_cuda(launch_gemm_tc(g, sms, static_cast<cudaStream_t>(stream)));
 }
 
+int b2q_mul_mat_prepared_gate_residual(const void* packed, int64_t n, int64_t k, const void* act, int64_t m,
+                                       const float* bias, const float* gate, const float* resid,
+                                       int64_t resid_row_stride_bytes, float* y, int64_t y_row_stride_bytes,
+                                       void* stream) {
+  if (n < 0 || m < 0 || k <= 0 || k % kQK != 0) return B2Q_ERR_INVALID_ARG;
+  if (n > INT_MAX || m > INT_MAX || k > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (m > 0 && n > 0 && (!packed || !act || !y || !resid)) return B2Q_ERR_INVALID_ARG;
+  if (y_row_stride_bytes < n * 4 || resid_row_stride_bytes < n * 4) return B2Q_ERR_INVALID_ARG;
+  if (resid == y && resid_row_stride_bytes != y_row_stride_bytes) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(packed, 256) || !aligned(act, 256) || !aligned(y, 4) || y_row_stride_bytes % 4 != 0 ||
+      !aligned(resid, 4) || resid_row_stride_bytes % 4 != 0 || (bias && !aligned(bias, 4)) ||
+      (gate && !aligned(gate, 4)))
+    return B2Q_ERR_MISALIGNED;
+  if (m == 0 || n == 0) return B2Q_OK;
+  int sms = 0;
+  if (int rc = check_device(&sms)) return rc;
+  GemmArgs g;
+  g.w = split_at(static_cast<uint8_t*>(const_cast<void*>(packed)), n, k);
+  g.a = split_at(static_cast<uint8_t*>(const_cast<void*>(act)), m, k);
+  g.M = m;
+  g.N = n;
+  g.K = k;
+  g.y = y;
+  g.ldy = y_row_stride_bytes / 4;
+  g.bias = bias;
+  g.dots = nullptr;
+  g.gate = gate;
+  g.resid = resid;
+  g.ldr = resid_row_stride_bytes / 4;
+  return from_cuda(launch_gemm_tc(g, sms, static_cast<cudaStream_t>(stream)));
+}
+
 int b2q_gelu(const float* x, int64_t rows, int64_t cols, int64_t x_row_stride_bytes, float* y,
              int64_t y_row_stride_bytes, void* stream) {
   if (rows < 0 || cols < 0) return B2Q_ERR_INVALID_ARG;

@@ -125,6 +125,7 @@ enum Mode : int {
   kModePeers = 2,   // column-parallel: the tile goes into every rank's y buffer
   kModeStall = 3,   // failure-path self-test: the producer withholds every stage
   kModeGeluQ8 = 4,  // fused GELU + Q8_0 quantize of the output (next layer's input)
+  kModeGateRes = 5, // y = resid + gate * (w . x + bias): the DiT branch's gated residual
 };
 
 // Output arguments of the non-plain variants, a separate kernel parameter:
@@ -134,7 +135,9 @@ enum Mode : int {
 //          rank's full-width buffer (P2P-mapped memory of the other GPUs);
 //   gelu+q8: quantize_q8_0(gelu(y)) into the split layout of the next
 //          mul_mat's activations: codes q_codes[m * q_k + n], scales
-//          q_scales[(n / 32) * q_ld + m].
+//          q_scales[(n / 32) * q_ld + m];
+//   gate+residual: y[m * ldy + n] = resid[m * ldr + n] + gate[n] * (w . x + bias)[m][n],
+//          each step rounded as ggml's separate mul and add (gate may be null).
 struct OutParams {
   int n;
   int64_t col0;
@@ -143,6 +146,9 @@ struct OutParams {
   float* q_scales;
   int64_t q_ld, q_k;
   int q_variant;
+  const float* gate;
+  const float* resid;
+  int64_t ldr;
 };
 
 // Shared-memory descriptor for the constant offset tile: K-major, no swizzle,
@@ -306,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ CUtensorMap tm_ws, const __grid_constant__ CUtensorMap tm_as,
                    const TcParams p, const __grid_constant__ OutParams pp) {
   constexpr bool DUMP = MODE == kModeDump, PEERS = MODE == kModePeers, STALL = MODE == kModeStall;
-  constexpr bool GELUQ = MODE == kModeGeluQ8;
+  constexpr bool GELUQ = MODE == kModeGeluQ8, GATERES = MODE == kModeGateRes;
   using C = Cfg<STAGES, BN>;
   constexpr int COLS = C::COLS;
   extern __shared__ uint8_t smem_raw[];
@@ -500,10 +506,30 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int c = 0; c < COLS / 2; ++c) acc[c] = ffma2(acc[c], one, b2);
           float* yp = p.y + m0 * p.ldy + n;
+          if (GATERES) {
+            // ggml_mul(h, gate) then ggml_add(resid, h): two roundings.  The
+            // residual is read 16 columns at a time (its loads in flight together).
+            const float gv = pp.gate ? pp.gate[n] : 1.0f;
+            const float* rp = pp.resid + m0 * pp.ldr + n;
 #pragma unroll
-          for (int c = 0; c < COLS / 2; ++c) {
-            if (m0 + 2 * c < p.M) yp[(2 * c) * p.ldy] = acc[c].x;
-            if (m0 + 2 * c + 1 < p.M) yp[(2 * c + 1) * p.ldy] = acc[c].y;
+            for (int c0 = 0; c0 < COLS; c0 += 16) {
+              float r[16];
+#pragma unroll
+              for (int c = 0; c < 16 && c0 + c < COLS; ++c) r[c] = m0 + c0 + c < p.M ? rp[(c0 + c) * pp.ldr] : 0.0f;
+#pragma unroll
+              for (int c = 0; c < 16 && c0 + c < COLS; ++c) {
+                const int cc = c0 + c;
+                const float h = (cc & 1) ? acc[cc / 2].y : acc[cc / 2].x;
+                const float t = pp.gate ? __fmul_rn(h, gv) : h;
+                if (m0 + cc < p.M) yp[cc * p.ldy] = __fadd_rn(r[c], t);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < COLS / 2; ++c) {
+              if (m0 + 2 * c < p.M) yp[(2 * c) * p.ldy] = acc[c].x;
+              if (m0 + 2 * c + 1 < p.M) yp[(2 * c + 1) * p.ldy] = acc[c].y;
+            }
           }
         } else {
           // Gather fused into the epilogue: the tile goes to every rank's buffer
@@ -600,6 +626,9 @@ cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
   pp.q_ld = g.q_ld;
   pp.q_k = g.N;
   pp.q_variant = g.q_variant;
+  pp.gate = g.gate;
+  pp.resid = g.resid;
+  pp.ldr = g.ldr;
   auto kern = gemm_tc_kernel<STAGES, BN, MODE>;
   cudaFuncAttributes fa;
   cudaError_t e = cudaFuncGetAttributes(&fa, kern);
@@ -664,6 +693,7 @@ cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, cudaStream_t s) {
     if (g.N % kQK != 0 || !g.q_scales) return cudaErrorInvalidValue;
     return launch_picked<kModeGeluQ8>(g, num_sms, s);
   }
+  if (g.resid) return launch_picked<kModeGateRes>(g, num_sms, s);
   if (g.n_peers > 0) return launch_picked<kModePeers>(g, num_sms, s);
   return launch_picked<kModePlain>(g, num_sms, s);
 }

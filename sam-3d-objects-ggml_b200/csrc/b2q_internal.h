@@ -91,6 +91,11 @@ struct GemmArgs {
   float* q_scales = nullptr;
   int64_t q_ld = 0;
   int q_variant = 0;
+  // Gated residual epilogue (resid != nullptr): y = resid + gate[n] * (w.x + bias),
+  // resid [M][ldr]; gate [N] or nullptr (no gate).
+  const float* gate = nullptr;
+  const float* resid = nullptr;
+  int64_t ldr = 0;
 };
 cudaError_t launch_gemm_tc(const GemmArgs& args, int num_sms, cudaStream_t s);
 cudaError_t read_device_status(unsigned int* value, bool clear);

@@ -138,6 +138,16 @@ def test_norm_modulate_validation(b2q_mod):
     assert q(FAKE, 0, 64, 256, 1e-6, None, None, 0, FAKE, 0, None) == 0
 
 
+def test_gate_residual_validation(b2q_mod):
+    f = b2q.lib().b2q_mul_mat_prepared_gate_residual
+    assert f(FAKE, 64, 1000, FAKE, 16, None, None, FAKE, 256, FAKE, 256, None) == 1         # k % 32
+    assert f(FAKE, 64, 1024, FAKE, 16, None, None, None, 256, FAKE, 256, None) == 1         # null resid
+    assert f(FAKE, 64, 1024, FAKE, 16, None, None, FAKE, 128, FAKE, 256, None) == 1         # resid stride
+    assert f(FAKE, 64, 1024, FAKE, 16, None, None, FAKE, 512, FAKE, 256, None) == 1         # aliased, strides differ
+    assert f(FAKE, 64, 1024, FAKE, 16, None, FAKE + 1, FAKE + 4096, 256, FAKE, 256, None) == 3  # gate alignment
+    assert f(FAKE, 64, 1024, FAKE, 0, None, None, FAKE, 256, FAKE, 256, None) == 0          # m == 0
+
+
 def test_empty_shapes_are_noops_without_device(b2q_mod):
     L = b2q.lib()
     # m == 0 or n == 0: validated, nothing launched, OK even without a GPU

@@ -201,3 +201,47 @@ def test_prenorm_mlp_chain_matches_oracle(dev):
     h = O.gelu(O.mul_mat(O.TYPE_Q8_0, w1, h, O.ACT_X86) + b1)
     ref = O.mul_mat(O.TYPE_Q8_0, w2, h, O.ACT_X86) + b2
     assert rel_frobenius(y, ref) <= CHAIN_RTOL
+
+
+# -------------------------------------------------- gate + residual epilogue
+@pytest.mark.parametrize("M,N,K", [(4096, 1024, 4096), (300, 1056, 512), (97, 96, 256), (1374, 1024, 1024)])
+def test_gate_residual_equals_separate_ops(dev, M, N, K):
+    """resid + gate * (mul_mat + bias) in the epilogue equals the three ggml
+    ops run one after another (fp32, each rounded), bit for bit; in place too."""
+    import torch
+    _, wq, x = make_case(M * 3 + N, M, N, K, O.TYPE_Q4_0)
+    rng = np.random.default_rng(N)
+    bias = rng.standard_normal(N).astype(np.float32)
+    gate = rng.standard_normal(N).astype(np.float32)
+    resid = rng.standard_normal((M, N)).astype(np.float32)
+    w_d, x_d = to_dev(wq, dev), to_dev(x, dev)
+    b_d, g_d, r_d = to_dev(bias, dev), to_dev(gate, dev), to_dev(resid, dev)
+    packed = b2q.weight_pack(O.TYPE_Q4_0, w_d, K)
+    act = b2q.act_prepare(x_d)
+    h = b2q.mul_mat_prepared(packed, N, K, act, M, bias=b_d)
+    for bb, gg in ((b_d, g_d), (None, g_d), (b_d, None)):
+        hh = h if bb is not None else b2q.mul_mat_prepared(packed, N, K, act, M)
+        ref = r_d + (hh * gg if gg is not None else hh)
+        y = b2q.mul_mat_prepared_gate_residual(packed, N, K, act, M, r_d, bias=bb, gate=gg)
+        torch.cuda.synchronize()
+        assert torch.equal(y, ref)
+    r2 = r_d.clone()
+    b2q.mul_mat_prepared_gate_residual(packed, N, K, act, M, r2, bias=b_d, gate=g_d, out=r2)
+    torch.cuda.synchronize()
+    assert torch.equal(r2, r_d + h * g_d)
+
+
+def test_gate_residual_strided_rows(dev):
+    import torch
+    M, N, K = 130, 192, 256
+    _, wq, x = make_case(5, M, N, K, O.TYPE_Q8_0)
+    packed = b2q.weight_pack(O.TYPE_Q8_0, to_dev(wq, dev), K)
+    act = b2q.act_prepare(to_dev(x, dev))
+    big = torch.randn(M, N + 40, device=dev)
+    out = torch.full((M, N + 8), -3.0, device=dev)
+    g_d = torch.randn(N, device=dev)
+    b2q.mul_mat_prepared_gate_residual(packed, N, K, act, M, big[:, 20:20 + N], gate=g_d, out=out[:, 4:4 + N])
+    h = b2q.mul_mat_prepared(packed, N, K, act, M)
+    torch.cuda.synchronize()
+    assert torch.equal(out[:, 4:4 + N], big[:, 20:20 + N] + h * g_d)
+    assert bool((out[:, :4] == -3).all()) and bool((out[:, 4 + N:] == -3).all())
