@@ -365,34 +365,49 @@ def run_gpu(args, rank, world, local_rank):
 
 # ------------------------------------------------------ fused MLP (next row)
 def mlp_branch(b2q, gemms, flush, stream, dev, iters=10):
-    """The DiT feed-forward branch fc2(gelu(fc1(x) + b1)) + b2 on the fc1 and
-    fc2 weights of the workload, from fc1's prepared activations to fc2's fp32
-    output, with and without the fused GELU + Q8_0 epilogue.  Reported beside
-    the headline (its ops are not part of `value`); L2 flushed before each
-    iteration, CUDA events on the launching stream."""
+    """The SS block's feed-forward branch on the fc1 and fc2 weights of the
+    workload (cpp_ggml/src/ss_flow_graph.cpp:376-387):
+        x += gate * fc2(gelu(fc1(modulate(norm(x), scale, shift)) + b1)) + b2
+    from the fp32 residual stream x to its in-place update, run as ggml runs
+    it (one kernel per op) and fused (pre-norm + quantize, fc1 + GELU +
+    quantize, fc2 + gate + residual: 3 launches).  Reported beside the headline
+    (its ops are not part of `value`); L2 flushed before each iteration, CUDA
+    events on the launching stream."""
     import torch
     by = {g["name"]: g for g in gemms}
     f1, f2 = by.get("fc1_q4_0"), by.get("fc2_q4_0")
-    if f1 is None or f2 is None or f1["N"] != f2["K"] or f1["M"] != f2["M"]:
+    if f1 is None or f2 is None or f1["N"] != f2["K"] or f1["M"] != f2["M"] or f1["K"] != f2["N"]:
         return None
     M, H, C = f1["M"], f1["N"], f2["N"]
     g = torch.Generator(device=dev).manual_seed(7)
     b1 = torch.randn(H, device=dev, generator=g)
     b2 = torch.randn(C, device=dev, generator=g)
-    b2q.act_prepare(f1["x_dev"], out=f1["act"], stream=stream)
+    sc = torch.randn(C, device=dev, generator=g) * 0.1
+    sh = torch.randn(C, device=dev, generator=g) * 0.1
+    gate = torch.randn(C, device=dev, generator=g) * 0.1
+    x0 = torch.randn(M, C, device=dev, generator=g)
+    x = x0.clone()
+    hn = torch.empty((M, C), dtype=torch.float32, device=dev)
     hid = torch.empty((M, H), dtype=torch.float32, device=dev)
+    act1 = b2q._empty_aligned(b2q.act_prepared_size(M, C), dev)
     act2 = b2q._empty_aligned(b2q.act_prepared_size(M, H), dev)
     y = torch.empty((M, C), dtype=torch.float32, device=dev)
 
     def unfused():
-        b2q.mul_mat_prepared(f1["packed"], H, f1["K"], f1["act"], M, bias=b1, out=hid, stream=stream)
+        b2q.norm_modulate(x, 1e-6, sc, sh, out=hn, stream=stream)
+        b2q.act_prepare(hn, out=act1, stream=stream)
+        b2q.mul_mat_prepared(f1["packed"], H, C, act1, M, bias=b1, out=hid, stream=stream)
         b2q.gelu(hid, out=hid, stream=stream)
         b2q.act_prepare(hid, out=act2, stream=stream)
         b2q.mul_mat_prepared(f2["packed"], C, H, act2, M, bias=b2, out=y, stream=stream)
+        torch.mul(y, gate, out=y)
+        torch.add(x, y, out=x)
 
     def fused():
-        b2q.mul_mat_prepared_gelu_q8(f1["packed"], H, f1["K"], f1["act"], M, bias=b1, out=act2, stream=stream)
-        b2q.mul_mat_prepared(f2["packed"], C, H, act2, M, bias=b2, out=y, stream=stream)
+        b2q.norm_modulate_q8(x, 1e-6, sc, sh, out=act1, stream=stream)
+        b2q.mul_mat_prepared_gelu_q8(f1["packed"], H, C, act1, M, bias=b1, out=act2, stream=stream)
+        b2q.mul_mat_prepared_gate_residual(f2["packed"], C, H, act2, M, x, bias=b2, gate=gate, out=x,
+                                           stream=stream)
 
     def timed(fn):
         for _ in range(3):
@@ -421,24 +436,33 @@ def mlp_branch(b2q, gemms, flush, stream, dev, iters=10):
         return round(e0.elapsed_time(e1) / n * 1e3, 2)
 
     kernels = {
-        "fc1_bias": hot(lambda: b2q.mul_mat_prepared(f1["packed"], H, f1["K"], f1["act"], M, bias=b1, out=hid,
+        "norm_modulate_q8": hot(lambda: b2q.norm_modulate_q8(x0, 1e-6, sc, sh, out=act1, stream=stream)),
+        "fc1_bias": hot(lambda: b2q.mul_mat_prepared(f1["packed"], H, C, act1, M, bias=b1, out=hid,
                                                      stream=stream)),
-        "fc1_bias_gelu_q8": hot(lambda: b2q.mul_mat_prepared_gelu_q8(f1["packed"], H, f1["K"], f1["act"], M,
-                                                                     bias=b1, out=act2, stream=stream)),
+        "fc1_bias_gelu_q8": hot(lambda: b2q.mul_mat_prepared_gelu_q8(f1["packed"], H, C, act1, M, bias=b1,
+                                                                     out=act2, stream=stream)),
         "gelu": hot(lambda: b2q.gelu(hid, out=hid, stream=stream)),
         "act_prepare_hidden": hot(lambda: b2q.act_prepare(hid, out=act2, stream=stream)),
+        "fc2_bias": hot(lambda: b2q.mul_mat_prepared(f2["packed"], C, H, act2, M, bias=b2, out=y,
+                                                     stream=stream)),
+        "fc2_bias_gate_residual": hot(lambda: b2q.mul_mat_prepared_gate_residual(
+            f2["packed"], C, H, act2, M, x0, bias=b2, gate=gate, out=y, stream=stream)),
     }
-    y_f = y.clone()
+    # one update of the same stream, both ways, compared bit for bit
+    x.copy_(x0)
     unfused()
+    xu = x.clone()
+    x.copy_(x0)
+    fused()
     torch.cuda.synchronize()
     return {"shape": {"M": M, "C": C, "hidden": H, "weights": "Q4_0"},
             "unfused_us": round(u, 2), "fused_us": round(f, 2), "speedup": round(u / f, 3),
+            "launches": {"unfused": 8, "fused": 3},
             "kernels_us_hot_l2": kernels,
-            "launches": {"unfused": 4, "fused": 2},
-            "fused_equals_unfused": bool(torch.equal(y, y_f)),
-            "hidden_fp32_bytes_avoided": 2 * 4 * M * H,
-            "path": "unfused: mul_mat_prepared(+b1) -> gelu -> act_prepare -> mul_mat_prepared(+b2); "
-                    "fused: mul_mat_prepared_gelu_q8(+b1) -> mul_mat_prepared(+b2)"}
+            "fused_equals_unfused": bool(torch.equal(x, xu)),
+            "path": "unfused: norm_modulate -> act_prepare -> mul_mat_prepared(+b1) -> gelu -> act_prepare -> "
+                    "mul_mat_prepared(+b2) -> mul(gate) -> add(residual); fused: norm_modulate_q8 -> "
+                    "mul_mat_prepared_gelu_q8(+b1) -> mul_mat_prepared_gate_residual(+b2, gate, in place)"}
 
 
 # ------------------------------------------------- column-parallel (multi-GPU)

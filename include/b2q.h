@@ -192,8 +192,8 @@ B2Q_API int b2q_gelu(const float* x, int64_t rows, int64_t cols, int64_t x_row_s
  * every self-attention and MLP branch, :200-204, :378-379; gb_layer_norm at
  * graph_builder.cpp:62-68).  Either modulation vector may be NULL (that term is
  * skipped; both NULL is plain ggml_norm).  mean and variance are accumulated in
- * double as ggml's CPU norm does.  Requires c % 32 == 0, c <= 4096, x and y
- * 16-byte aligned with row strides multiples of 16 bytes.
+ * double as ggml's CPU norm does.  Requires c % 32 == 0, c <= 4096, x, y and
+ * the modulation vectors 16-byte aligned, row strides multiples of 16 bytes.
  * b2q_norm_modulate writes fp32 y; b2q_norm_modulate_q8 writes the next
  * mul_mat's prepared Q8_0 activations (b2q_act_prepare layout for m rows and
  * k = c), equal byte for byte to b2q_act_prepare(b2q_norm_modulate(...)). */

@@ -111,7 +111,7 @@ int check_norm(const float* x, int64_t m, int64_t c, int64_t x_rs, float eps, co
   if (!(eps >= 0.0f)) return B2Q_ERR_INVALID_ARG;
   if (m > 0 && !x) return B2Q_ERR_INVALID_ARG;
   if (x_rs < c * 4) return B2Q_ERR_INVALID_ARG;
-  if (!aligned(x, 16) || x_rs % 16 != 0 || (ms && !aligned(ms, 4)) || (sh && !aligned(sh, 4)))
+  if (!aligned(x, 16) || x_rs % 16 != 0 || (ms && !aligned(ms, 16)) || (sh && !aligned(sh, 16)))
     return B2Q_ERR_MISALIGNED;
   return B2Q_OK;
 }

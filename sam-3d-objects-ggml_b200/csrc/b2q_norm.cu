@@ -17,9 +17,10 @@
 // The double sums are exact for ordinary data (their terms span far fewer than
 // 53 bits), so the warp's tree order gives the same value as a sequential loop.
 //
-// Mapping: one warp per row; lane l holds blocks l, l+32, ... of the row (32
-// consecutive values each) in registers, so the quantize of a block needs no
-// cross-lane work, and the codes of a row leave as contiguous 16-byte stores.
+// Mapping: one warp per row.  Lane l holds the float4 groups 32*j + l of the
+// row (j = 0 .. c/128 - 1): every load, modulation read and store of a warp is
+// one contiguous 512-byte run.  A Q8_0 block is then 8 consecutive lanes, whose
+// absmax takes three xor-shuffles within the group.
 #include "b2q_internal.h"
 #include "b2q_q8.cuh"
 
@@ -35,9 +36,9 @@ __device__ __forceinline__ double warp_sum(double v) {
   return v;
 }
 
-// KB: blocks per lane (c <= 1024 * KB).  Q8: write the split-layout Q8_0
+// NJ: float4 groups per lane (c <= 128 * NJ).  Q8: write the split-layout Q8_0
 // activations (VARIANT = quantizer variant), else fp32 y.
-template <int KB, bool Q8, int VARIANT>
+template <int NJ, bool Q8, int VARIANT>
 __global__ void __launch_bounds__(256) norm_modulate_kernel(const float* __restrict__ x, int64_t m, int c,
                                                             int64_t ldx, float eps,
                                                             const float* __restrict__ mscale,
@@ -46,102 +47,98 @@ __global__ void __launch_bounds__(256) norm_modulate_kernel(const float* __restr
                                                             int8_t* __restrict__ codes,
                                                             float* __restrict__ qscales, int64_t qld) {
   const int lane = threadIdx.x & 31;
-  const int nb = c / kQK;
+  const int ng = c / 4;  // float4 groups per row
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
   for (int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32; row < m; row += warps) {
-    const float* xr = x + row * ldx;
-    float v[KB][kQK];
-    double s = 0.0;
+    const float4* xr = reinterpret_cast<const float4*>(x + row * ldx);
+    float4 v[NJ];
+    double s[4] = {0.0, 0.0, 0.0, 0.0};  // four chains; the sums are exact, so their order is free
 #pragma unroll
-    for (int i = 0; i < KB; ++i) {
-      const int b = lane + 32 * i;
-      if (b < nb) {
-        const float4* p = reinterpret_cast<const float4*>(xr + b * kQK);
+    for (int j = 0; j < NJ; ++j) {
+      const int g = 32 * j + lane;
+      v[j] = g < ng ? __ldg(xr + g) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      s[0] += static_cast<double>(v[j].x);
+      s[1] += static_cast<double>(v[j].y);
+      s[2] += static_cast<double>(v[j].z);
+      s[3] += static_cast<double>(v[j].w);
+    }
+    const double st = warp_sum((s[0] + s[1]) + (s[2] + s[3]));
+    const float mean = __fdiv_rn(__double2float_rn(st), static_cast<float>(c));
+    double q[4] = {0.0, 0.0, 0.0, 0.0};
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float4 q = __ldg(p + j);
-          v[i][4 * j] = q.x;
-          v[i][4 * j + 1] = q.y;
-          v[i][4 * j + 2] = q.z;
-          v[i][4 * j + 3] = q.w;
-        }
-#pragma unroll
-        for (int j = 0; j < kQK; ++j) s += static_cast<double>(v[i][j]);
+    for (int j = 0; j < NJ; ++j) {
+      if (32 * j + lane < ng) {
+        v[j].x = __fsub_rn(v[j].x, mean);
+        v[j].y = __fsub_rn(v[j].y, mean);
+        v[j].z = __fsub_rn(v[j].z, mean);
+        v[j].w = __fsub_rn(v[j].w, mean);
+        q[0] += static_cast<double>(__fmul_rn(v[j].x, v[j].x));
+        q[1] += static_cast<double>(__fmul_rn(v[j].y, v[j].y));
+        q[2] += static_cast<double>(__fmul_rn(v[j].z, v[j].z));
+        q[3] += static_cast<double>(__fmul_rn(v[j].w, v[j].w));
       }
     }
-    s = warp_sum(s);
-    const float mean = __fdiv_rn(__double2float_rn(s), static_cast<float>(c));
-    double s2 = 0.0;
-#pragma unroll
-    for (int i = 0; i < KB; ++i) {
-      if (lane + 32 * i < nb) {
-#pragma unroll
-        for (int j = 0; j < kQK; ++j) {
-          const float d = __fsub_rn(v[i][j], mean);
-          v[i][j] = d;
-          s2 += static_cast<double>(__fmul_rn(d, d));
-        }
-      }
-    }
-    s2 = warp_sum(s2);
-    const float var = __double2float_rn(__ddiv_rn(s2, static_cast<double>(c)));
+    const double qt = warp_sum((q[0] + q[1]) + (q[2] + q[3]));
+    const float var = __double2float_rn(__ddiv_rn(qt, static_cast<double>(c)));
     const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
 #pragma unroll
-    for (int i = 0; i < KB; ++i) {
-      const int b = lane + 32 * i;
-      if (b >= nb) continue;
-#pragma unroll
-      for (int j = 0; j < kQK; ++j) {
-        float h = __fmul_rn(v[i][j], rs);
-        if (mscale) h = __fadd_rn(__fmul_rn(h, __ldg(mscale + b * kQK + j)), h);
-        if (mshift) h = __fadd_rn(h, __ldg(mshift + b * kQK + j));
-        v[i][j] = h;
+    for (int j = 0; j < NJ; ++j) {
+      const int g = 32 * j + lane;
+      if (32 * j >= ng) break;  // warp-uniform; a block's 8 lanes are all in or all out below
+      const bool in = g < ng;
+      float h[4] = {__fmul_rn(v[j].x, rs), __fmul_rn(v[j].y, rs), __fmul_rn(v[j].z, rs), __fmul_rn(v[j].w, rs)};
+      if (mscale && in) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(mscale) + g);
+        h[0] = __fadd_rn(__fmul_rn(h[0], t.x), h[0]);
+        h[1] = __fadd_rn(__fmul_rn(h[1], t.y), h[1]);
+        h[2] = __fadd_rn(__fmul_rn(h[2], t.z), h[2]);
+        h[3] = __fadd_rn(__fmul_rn(h[3], t.w), h[3]);
+      }
+      if (mshift && in) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(mshift) + g);
+        h[0] = __fadd_rn(h[0], t.x);
+        h[1] = __fadd_rn(h[1], t.y);
+        h[2] = __fadd_rn(h[2], t.z);
+        h[3] = __fadd_rn(h[3], t.w);
       }
       if (Q8) {
-        float amax = 0.0f;
+        float amax = fmaxf(fmaxf(0.0f, fmaxf(fabsf(h[0]), fabsf(h[1]))), fmaxf(fabsf(h[2]), fabsf(h[3])));
 #pragma unroll
-        for (int j = 0; j < kQK; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+        for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         float d, inv;
         q8_scale<VARIANT>(amax, d, inv);
-        uint32_t q[8];
-#pragma unroll
-        for (int t = 0; t < 8; ++t)
-          q[t] = quantize_code<VARIANT>(v[i][4 * t], inv) | (quantize_code<VARIANT>(v[i][4 * t + 1], inv) << 8) |
-                 (quantize_code<VARIANT>(v[i][4 * t + 2], inv) << 16) |
-                 (quantize_code<VARIANT>(v[i][4 * t + 3], inv) << 24);
-        uint4* dst = reinterpret_cast<uint4*>(codes + row * static_cast<int64_t>(c) + b * kQK);
-        dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
-        dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
-        qscales[b * qld + row] = q8_split_scale(d);
-      } else {
-        float4* dst = reinterpret_cast<float4*>(y + row * ldy + b * kQK);
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          dst[j] = make_float4(v[i][4 * j], v[i][4 * j + 1], v[i][4 * j + 2], v[i][4 * j + 3]);
+        const uint32_t word = quantize_code<VARIANT>(h[0], inv) | (quantize_code<VARIANT>(h[1], inv) << 8) |
+                              (quantize_code<VARIANT>(h[2], inv) << 16) | (quantize_code<VARIANT>(h[3], inv) << 24);
+        if (in) {
+          reinterpret_cast<uint32_t*>(codes + row * static_cast<int64_t>(c))[g] = word;
+          if ((lane & 7) == 0) qscales[(g / 8) * qld + row] = q8_split_scale(d);
+        }
+      } else if (in) {
+        reinterpret_cast<float4*>(y + row * ldy)[g] = make_float4(h[0], h[1], h[2], h[3]);
       }
     }
   }
 }
 
-template <int KB, bool Q8, int VARIANT>
+template <int NJ, bool Q8, int VARIANT>
 cudaError_t launch_kb(const float* x, int64_t m, int c, int64_t ldx, float eps, const float* ms, const float* sh,
                       float* y, int64_t ldy, int8_t* codes, float* qs, int64_t qld, cudaStream_t s) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t blocks = (m + 7) / 8;  // 8 rows (warps) per block
-  const int cap = sms * (KB == 1 ? 8 : KB == 2 ? 4 : 2);
+  const int cap = sms * (NJ <= 8 ? 8 : NJ <= 16 ? 4 : 2);
   const int grid = static_cast<int>(blocks < cap ? blocks : cap);
-  norm_modulate_kernel<KB, Q8, VARIANT><<<grid, 256, 0, s>>>(x, m, c, ldx, eps, ms, sh, y, ldy, codes, qs, qld);
+  norm_modulate_kernel<NJ, Q8, VARIANT><<<grid, 256, 0, s>>>(x, m, c, ldx, eps, ms, sh, y, ldy, codes, qs, qld);
   return cudaGetLastError();
 }
 
 template <bool Q8, int VARIANT>
 cudaError_t launch_q(const float* x, int64_t m, int c, int64_t ldx, float eps, const float* ms, const float* sh,
                      float* y, int64_t ldy, int8_t* codes, float* qs, int64_t qld, cudaStream_t s) {
-  if (c <= 1024) return launch_kb<1, Q8, VARIANT>(x, m, c, ldx, eps, ms, sh, y, ldy, codes, qs, qld, s);
-  if (c <= 2048) return launch_kb<2, Q8, VARIANT>(x, m, c, ldx, eps, ms, sh, y, ldy, codes, qs, qld, s);
-  return launch_kb<4, Q8, VARIANT>(x, m, c, ldx, eps, ms, sh, y, ldy, codes, qs, qld, s);
+  if (c <= 1024) return launch_kb<8, Q8, VARIANT>(x, m, c, ldx, eps, ms, sh, y, ldy, codes, qs, qld, s);
+  if (c <= 2048) return launch_kb<16, Q8, VARIANT>(x, m, c, ldx, eps, ms, sh, y, ldy, codes, qs, qld, s);
+  return launch_kb<32, Q8, VARIANT>(x, m, c, ldx, eps, ms, sh, y, ldy, codes, qs, qld, s);
 }
 
 }  // namespace

@@ -127,7 +127,7 @@ def test_norm_modulate_validation(b2q_mod):
     assert f(FAKE, 4, 64, 256, -1.0, None, None, FAKE, 256, None) == 1            # eps < 0
     assert f(FAKE + 4, 4, 64, 256, 1e-6, None, None, FAKE, 256, None) == 3        # x not 16-byte aligned
     assert f(FAKE, 4, 64, 260, 1e-6, None, None, FAKE, 256, None) == 3            # stride % 16
-    assert f(FAKE, 4, 64, 256, 1e-6, FAKE + 2, None, FAKE, 256, None) == 3        # scale alignment
+    assert f(FAKE, 4, 64, 256, 1e-6, FAKE + 4, None, FAKE, 256, None) == 3        # scale alignment
     assert f(FAKE, 4, 64, 256, 1e-6, None, None, None, 256, None) == 1            # null y
     assert f(FAKE, 4, 64, 256, 1e-6, None, None, FAKE + 8, 256, None) == 3        # y alignment
     assert f(FAKE, 0, 64, 256, 1e-6, None, None, FAKE, 256, None) == 0            # empty: no-op
