@@ -5,6 +5,7 @@
 #include "../../include/b2q.h"
 #include "b2q_internal.h"
 
+#include <atomic>
 #include <climits>
 #include <cstdint>
 
@@ -16,15 +17,10 @@ bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p
 
 // Device check: the kernels are built for sm_100a only.
 int check_device(int* sms) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return B2Q_ERR_CUDA;
-  int major = 0, minor = 0;
-  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
-      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
-    return B2Q_ERR_CUDA;
-  if (major != 10 || minor != 0) return B2Q_ERR_UNSUPPORTED;
-  if (sms && cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-    return B2Q_ERR_CUDA;
+  const int n = current_device_sms();
+  if (n < 0) return B2Q_ERR_CUDA;
+  if (n == 0) return B2Q_ERR_UNSUPPORTED;
+  if (sms) *sms = n;
   return B2Q_OK;
 }
 
@@ -117,6 +113,29 @@ int check_norm(const float* x, int64_t m, int64_t c, int64_t x_rs, float eps, co
 }
 
 }  // namespace
+
+namespace b2q {
+
+int current_device_sms(int* device) {
+  constexpr int kMaxDevices = 64;
+  static std::atomic<int> cache[kMaxDevices];  // 0: not queried; -2: not sm_100; else SM count
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  if (device) *device = dev;
+  int v = dev < kMaxDevices ? cache[dev].load(std::memory_order_relaxed) : 0;
+  if (v == 0) {
+    int major = 0, minor = 0, sms = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return -1;
+    v = (major == 10 && minor == 0 && sms > 0) ? sms : -2;
+    if (dev < kMaxDevices) cache[dev].store(v, std::memory_order_relaxed);
+  }
+  return v == -2 ? 0 : v;
+}
+
+}  // namespace b2q
 
 extern "C" {
 

@@ -47,6 +47,8 @@
 //   warps 4..11 epilogue (232 registers)
 // Every wait is bounded (b2q_ptx.cuh); on give-up the CTA drains its in-flight
 // copies and MMAs, frees TMEM and exits, leaving a code in g_device_status.
+#include <atomic>
+
 #include "b2q_internal.h"
 #include "b2q_ptx.cuh"
 #include "b2q_q8.cuh"
@@ -630,14 +632,23 @@ cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
   pp.resid = g.resid;
   pp.ldr = g.ldr;
   auto kern = gemm_tc_kernel<STAGES, BN, MODE>;
-  cudaFuncAttributes fa;
-  cudaError_t e = cudaFuncGetAttributes(&fa, kern);
-  if (e != cudaSuccess) return e;
-  if (fa.numRegs != kLaunchRegs) return cudaErrorInvalidConfiguration;  // see the register split
   constexpr int smem_bytes = MODE == kModeGeluQ8 ? C::SMEM_XPOSE : C::SMEM;
   static_assert(smem_bytes <= 227 * 1024, "shared memory per CTA");
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
-  if (e != cudaSuccess) return e;
+  // Checked and set once per device (a bit per device; the calls cost more
+  // host time than the rest of the launch).
+  static std::atomic<uint64_t> ready{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
+  const uint64_t bit = dev < 64 ? (uint64_t{1} << dev) : 0;
+  if (!bit || !(ready.load(std::memory_order_acquire) & bit)) {
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs != kLaunchRegs) return cudaErrorInvalidConfiguration;  // see the register split
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    if (e != cudaSuccess) return e;
+    ready.fetch_or(bit, std::memory_order_acq_rel);
+  }
   const int grid = p.num_tiles < num_sms ? p.num_tiles : num_sms;
   kern<<<grid, kThreads, smem_bytes, s>>>(tm_wc, tm_ac, tm_ws, tm_as, p, pp);
   return cudaGetLastError();
@@ -693,6 +704,8 @@ cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, cudaStream_t s) {
     if (g.N % kQK != 0 || !g.q_scales) return cudaErrorInvalidValue;
     return launch_picked<kModeGeluQ8>(g, num_sms, s);
   }
+  // A handful of tokens: the weight streamed once on CUDA cores, same bits.
+  if (g.M <= kGemvMaxM && g.n_peers == 0) return launch_gemv(g, s);
   if (g.resid) return launch_picked<kModeGateRes>(g, num_sms, s);
   if (g.n_peers > 0) return launch_picked<kModePeers>(g, num_sms, s);
   return launch_picked<kModePlain>(g, num_sms, s);

@@ -47,6 +47,11 @@ inline size_t split_bytes(int64_t rows, int64_t k) {
   return static_cast<size_t>(round_up(rows * k, 256) + round_up((k / kQK) * scale_ld(rows) * 4, 256));
 }
 
+// The current device and its SM count, cached per device after the first
+// query (the launch paths call this on every call).  Returns the SM count;
+// 0 when the device is not compute capability 10.0; -1 when a query failed.
+int current_device_sms(int* device = nullptr);
+
 // ---- launchers (return cudaSuccess or the launch error) ----
 cudaError_t launch_quantize_q8_0_blocks(const float* x, int64_t m, int64_t k, int64_t ldx_floats,
                                         uint8_t* y, int64_t ldy_bytes, int variant, bool vec4,
@@ -98,6 +103,10 @@ struct GemmArgs {
   int64_t ldr = 0;
 };
 cudaError_t launch_gemm_tc(const GemmArgs& args, int num_sms, cudaStream_t s);
+// CUDA-core kernel for M <= kGemvMaxM tokens (plain, bias, gate + residual);
+// bit-identical to the tensor-core kernel (b2q_gemv.cu).
+constexpr int64_t kGemvMaxM = 8;
+cudaError_t launch_gemv(const GemmArgs& args, cudaStream_t s);
 cudaError_t read_device_status(unsigned int* value, bool clear);
 
 }  // namespace b2q

@@ -123,9 +123,8 @@ __global__ void __launch_bounds__(256) norm_modulate_kernel(const float* __restr
 template <int NJ, bool Q8, int VARIANT>
 cudaError_t launch_kb(const float* x, int64_t m, int c, int64_t ldx, float eps, const float* ms, const float* sh,
                       float* y, int64_t ldy, int8_t* codes, float* qs, int64_t qld, cudaStream_t s) {
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int sms = current_device_sms();
+  if (sms <= 0) sms = 148;
   const int64_t blocks = (m + 7) / 8;  // 8 rows (warps) per block
   const int cap = sms * (NJ <= 8 ? 8 : NJ <= 16 ? 4 : 2);
   const int grid = static_cast<int>(blocks < cap ? blocks : cap);

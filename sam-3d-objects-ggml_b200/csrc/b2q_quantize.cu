@@ -88,9 +88,8 @@ cudaError_t launch_q(const float* x, int64_t m, int64_t k, int64_t ldx, uint8_t*
                      int8_t* codes, float* scales, int64_t ld, int variant, cudaStream_t s) {
   const int64_t units = (m + 31) / 32 * (k / kQK);
   if (units == 0) return cudaSuccess;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int sms = current_device_sms();
+  if (sms <= 0) sms = 148;
   // 8 warps per block; at most 8 resident blocks per SM, one unit per warp when that fits
   const int64_t blocks_needed = (units + 7) / 8;
   const int grid = static_cast<int>(blocks_needed < sms * 8 ? blocks_needed : sms * 8);
@@ -183,9 +182,8 @@ cudaError_t launch_gelu(const float* x, int64_t rows, int64_t cols, int64_t ldx_
                         int64_t ldy_floats, cudaStream_t s) {
   const int64_t total = rows * ((cols + 3) / 4);
   if (total == 0) return cudaSuccess;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int sms = current_device_sms();
+  if (sms <= 0) sms = 148;
   const int64_t blocks = (total + 255) / 256;
   const int grid = static_cast<int>(blocks < sms * 16 ? blocks : sms * 16);
   const bool vec4 = cols % 4 == 0 && ldx_floats % 4 == 0 && ldy_floats % 4 == 0 &&

@@ -224,3 +224,38 @@ def test_gelu_inputs_large_k(dev):
     y = to_np(b2q.mul_mat(O.TYPE_Q8_0, to_dev(wq, dev), to_dev(x, dev)))
     assert rel_frobenius(y, O.mul_mat(O.TYPE_Q8_0, wq, x, O.ACT_X86)) <= RTOL
     assert np.allclose(gelu_tanh(np.zeros(1, np.float32)), 0)
+
+
+# ---------------------------------------------------- few tokens (M <= 8)
+@pytest.mark.parametrize("wtype,N,K", [
+    (O.TYPE_Q8_0, 6144, 1024),   # adaLN projection, M = 1 per sample (ss_flow_graph.cpp:183-185)
+    (O.TYPE_Q4_0, 1024, 4096),   # pose-group fc2, M = 4
+    (O.TYPE_Q4_0, 1003, 96),     # ragged rows, 3 blocks
+    (O.TYPE_Q8_0, 72, 8192),     # two K chunks
+])
+def test_few_tokens_bit_identical_to_tensor_core_path(dev, wtype, N, K):
+    """M <= 8 runs on the CUDA-core kernel; its rows equal the tensor-core
+    kernel's rows for the same tokens bit for bit (bias, gate and residual
+    included), and the oracle within RTOL."""
+    import torch
+    big = 64
+    _, wq, xb = make_case(N + K, big, N, K, wtype)
+    rng = np.random.default_rng(K)
+    bias = rng.standard_normal(N).astype(np.float32)
+    gate = rng.standard_normal(N).astype(np.float32)
+    resid = rng.standard_normal((big, N)).astype(np.float32)
+    packed = b2q.weight_pack(wtype, to_dev(wq, dev), K)
+    b_d, g_d, r_d = to_dev(bias, dev), to_dev(gate, dev), to_dev(resid, dev)
+    xb_d = to_dev(xb, dev)
+    act_b = b2q.act_prepare(xb_d)
+    y_tc = b2q.mul_mat_prepared(packed, N, K, act_b, big, bias=b_d)
+    z_tc = b2q.mul_mat_prepared_gate_residual(packed, N, K, act_b, big, r_d, bias=b_d, gate=g_d)
+    for M in (1, 2, 3, 4, 5, 8):
+        act = b2q.act_prepare(xb_d[:M].contiguous())
+        y = b2q.mul_mat_prepared(packed, N, K, act, M, bias=b_d)
+        z = b2q.mul_mat_prepared_gate_residual(packed, N, K, act, M, r_d[:M].contiguous(), bias=b_d, gate=g_d)
+        torch.cuda.synchronize()
+        assert torch.equal(y, y_tc[:M]), M
+        assert torch.equal(z, z_tc[:M]), M
+    y1 = to_np(b2q.mul_mat(wtype, to_dev(wq, dev), xb_d[:3].contiguous()))
+    assert rel_frobenius(y1, O.mul_mat(wtype, wq, xb[:3], O.ACT_X86)) <= RTOL
