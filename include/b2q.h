@@ -87,6 +87,18 @@ B2Q_API size_t b2q_weight_packed_size(int64_t n, int64_t k);
 B2Q_API int b2q_weight_pack(int wtype, const void* w, int64_t n, int64_t k, int64_t w_row_stride_bytes,
                     void* packed, size_t packed_bytes, void* stream);
 
+/* The same re-layout straight from host memory: the weight rows (raw GGUF
+ * blocks, w_row_stride_bytes apart, pageable or pinned) go to the device in
+ * chunks through the caller's staging buffer and are packed there, so the raw
+ * blocks never need a device allocation of their own.  This is the upload a
+ * ggml buffer type runs in set_tensor (ggml_backend_tensor_set from the GGUF
+ * loader, cpp_ggml/src/gguf_loader.cpp:133).  staging_bytes must hold at least
+ * one row of blocks (k/32 * 34 or 18 bytes); larger staging means fewer
+ * chunks.  Asynchronous on `stream`; host_w must stay valid until it is done. */
+B2Q_API int b2q_weight_upload(int wtype, const void* host_w, int64_t n, int64_t k, int64_t w_row_stride_bytes,
+                              void* staging, size_t staging_bytes, void* packed, size_t packed_bytes,
+                              void* stream);
+
 /* --------------------------------------------------------------- mul_mat
  * Scratch needed by b2q_mul_mat (packed_weight = 0) or b2q_mul_mat_packed
  * (packed_weight = 1): the Q8_0 activations in the GEMM's layout, plus the

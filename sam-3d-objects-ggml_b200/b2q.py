@@ -60,6 +60,7 @@ def _lib_obj():
             "b2q_quantize_q8_0": (I, [P, I64, I64, I64, P, I64, I, P]),
             "b2q_weight_packed_size": (SZ, [I64, I64]),
             "b2q_weight_pack": (I, [I, P, I64, I64, I64, P, SZ, P]),
+            "b2q_weight_upload": (I, [I, P, I64, I64, I64, P, SZ, P, SZ, P]),
             "b2q_mul_mat_workspace_size": (SZ, [I64, I64, I64, I]),
             "b2q_mul_mat": (I, [I, P, I64, I64, I64, P, I64, I64, P, P, I64, I, P, SZ, P]),
             "b2q_mul_mat_packed": (I, [P, I64, I64, P, I64, I64, P, P, I64, I, P, SZ, P]),
@@ -156,6 +157,24 @@ def weight_pack(wtype: int, w, k: int, stream=None):
     packed = _empty_aligned(size, w.device)
     rc = lib().b2q_weight_pack(wtype, _ptr(w), n, k, w.stride(0), _ptr(packed), size, _stream(stream))
     _check("b2q_weight_pack", rc)
+    return packed
+
+
+def weight_upload(wtype: int, host_w, k: int, staging_bytes: int = 8 << 20, device=None, stream=None):
+    """Raw ggml weight blocks in host memory (numpy uint8 [N, >=row_bytes]) ->
+    packed device buffer, through a staging buffer of staging_bytes."""
+    import numpy as np
+    torch = _torch()
+    host_w = np.asarray(host_w)
+    n = host_w.shape[0]
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    size = weight_packed_size(n, k)
+    packed = _empty_aligned(size, dev)
+    staging = _empty_aligned(staging_bytes, dev)
+    rc = lib().b2q_weight_upload(wtype, host_w.ctypes.data, n, k, host_w.strides[0], _ptr(staging), staging_bytes,
+                                 _ptr(packed), size, _stream(stream))
+    _check("b2q_weight_upload", rc)
+    torch.cuda.current_stream(dev).synchronize() if stream is None else stream.synchronize()
     return packed
 
 

@@ -188,6 +188,33 @@ int b2q_weight_pack(int wtype, const void* w, int64_t n, int64_t k, int64_t w_ro
                                        s.ld, static_cast<cudaStream_t>(stream)));
 }
 
+int b2q_weight_upload(int wtype, const void* host_w, int64_t n, int64_t k, int64_t w_row_stride_bytes,
+                      void* staging, size_t staging_bytes, void* packed, size_t packed_bytes, void* stream) {
+  if (int rc = check_raw_weight(wtype, host_w, w_row_stride_bytes, n, k)) return rc;
+  if (n > 0 && (!packed || !staging)) return B2Q_ERR_INVALID_ARG;
+  if (packed_bytes < split_bytes(n, k)) return B2Q_ERR_WORKSPACE;
+  const int64_t row_bytes = (k / kQK) * wblock_bytes(wtype);
+  if (n > 0 && staging_bytes < static_cast<size_t>(row_bytes)) return B2Q_ERR_WORKSPACE;
+  if (!aligned(packed, 256) || !aligned(staging, 2)) return B2Q_ERR_MISALIGNED;
+  if (n == 0) return B2Q_OK;
+  if (int rc = check_device(nullptr)) return rc;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const SplitOperand out = split_at(static_cast<uint8_t*>(packed), n, k);
+  const int64_t chunk = static_cast<int64_t>(staging_bytes / static_cast<size_t>(row_bytes));
+  const uint8_t* src = static_cast<const uint8_t*>(host_w);
+  for (int64_t r0 = 0; r0 < n; r0 += chunk) {
+    const int64_t rows = n - r0 < chunk ? n - r0 : chunk;
+    if (cudaMemcpy2DAsync(staging, row_bytes, src + r0 * w_row_stride_bytes, w_row_stride_bytes, row_bytes, rows,
+                          cudaMemcpyHostToDevice, s) != cudaSuccess)
+      return B2Q_ERR_CUDA;
+    if (launch_pack_weights(wtype, static_cast<const uint8_t*>(staging), rows, k, row_bytes,
+                            const_cast<int8_t*>(out.codes) + r0 * k, const_cast<float*>(out.scales) + r0, out.ld,
+                            s) != cudaSuccess)
+      return B2Q_ERR_CUDA;
+  }
+  return B2Q_OK;
+}
+
 size_t b2q_mul_mat_workspace_size(int64_t m, int64_t n, int64_t k, int packed_weight) {
   if (m < 0 || n < 0 || k <= 0 || k % kQK != 0) return 0;
   return split_bytes(m, k) + (packed_weight ? 0 : split_bytes(n, k));

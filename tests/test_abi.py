@@ -148,6 +148,19 @@ def test_gate_residual_validation(b2q_mod):
     assert f(FAKE, 64, 1024, FAKE, 0, None, None, FAKE, 256, FAKE, 256, None) == 0          # m == 0
 
 
+def test_weight_upload_validation(b2q_mod):
+    f = b2q.lib().b2q_weight_upload
+    big = 1 << 24
+    assert f(1, FAKE, 64, 1024, 1088, FAKE, big, FAKE, big, None) == 2            # F16 weights
+    assert f(8, FAKE, 64, 1000, 1088, FAKE, big, FAKE, big, None) == 1            # k % 32
+    assert f(8, FAKE, 64, 1024, 1000, FAKE, big, FAKE, big, None) == 1            # row stride < row
+    assert f(8, FAKE, 64, 1024, 1088, None, big, FAKE, big, None) == 1            # null staging
+    assert f(8, FAKE, 64, 1024, 1088, FAKE, 1087, FAKE, big, None) == 4           # staging < one row
+    assert f(8, FAKE, 64, 1024, 1088, FAKE, big, FAKE, 10, None) == 4             # packed too small
+    assert f(8, FAKE, 64, 1024, 1088, FAKE, big, FAKE + 16, big, None) == 3       # packed alignment
+    assert f(8, FAKE, 0, 1024, 1088, FAKE, 0, FAKE, 0, None) == 0                 # n == 0: no-op
+
+
 def test_empty_shapes_are_noops_without_device(b2q_mod):
     L = b2q.lib()
     # m == 0 or n == 0: validated, nothing launched, OK even without a GPU

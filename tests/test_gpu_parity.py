@@ -259,3 +259,31 @@ def test_few_tokens_bit_identical_to_tensor_core_path(dev, wtype, N, K):
         assert torch.equal(z, z_tc[:M]), M
     y1 = to_np(b2q.mul_mat(wtype, to_dev(wq, dev), xb_d[:3].contiguous()))
     assert rel_frobenius(y1, O.mul_mat(wtype, wq, xb[:3], O.ACT_X86)) <= RTOL
+
+
+@pytest.mark.parametrize("wtype,N,K,staging", [
+    (O.TYPE_Q8_0, 1000, 1024, 34 * 32 * 7),      # 7 rows per chunk, ragged last chunk
+    (O.TYPE_Q4_0, 4096, 1024, 8 << 20),          # one chunk
+    (O.TYPE_Q4_0, 65, 256, 18 * 8),              # one row per chunk
+])
+def test_weight_upload_from_host_equals_device_pack(dev, wtype, N, K, staging):
+    """Host GGUF rows (strided: a row-offset view of a wider tensor) uploaded in
+    chunks through a small staging buffer pack to the same bytes as packing the
+    rows already on the device, and serve mul_mat identically."""
+    import torch
+    _, wq, x = make_case(N + 3 * K, 40, N, K, wtype)
+    rb = wq.shape[1]
+    host = np.zeros((N, rb + 6), np.uint8)
+    host[:, 2:2 + rb] = wq
+    view = host[:, 2:2 + rb]
+    p_up = b2q.weight_upload(wtype, view, K, staging_bytes=staging, device=dev)
+    p_dev = b2q.weight_pack(wtype, to_dev(wq, dev), K)
+    torch.cuda.synchronize()
+    off, ld = (N * K + 255) // 256 * 256, (N + 3) // 4 * 4   # codes [N][K], then scales [K/32][ld]
+    a, b = to_np(p_up), to_np(p_dev)
+    assert np.array_equal(a[:N * K], b[:N * K])
+    sa = a[off:off + (K // 32) * ld * 4].view(np.float32).reshape(K // 32, ld)[:, :N]
+    sb = b[off:off + (K // 32) * ld * 4].view(np.float32).reshape(K // 32, ld)[:, :N]
+    assert np.array_equal(sa.view(np.uint32), sb.view(np.uint32))
+    x_d = to_dev(x, dev)
+    assert torch.equal(b2q.mul_mat_packed(p_up, N, K, x_d), b2q.mul_mat_packed(p_dev, N, K, x_d))
