@@ -108,6 +108,20 @@ void b2q_orc_philox4x32_10(uint64_t seed, uint64_t counter, uint32_t out[4]);
 /* Normal(mean, std) fp32 values via Box-Muller on Philox words. */
 void b2q_orc_fill_normal(float* x, int64_t n, uint64_t seed, float mean, float std);
 
+/* ---- Q4_K weights x Q8_K activations (b2q_oracle_k.c; layouts there) ---- */
+#define B2Q_ORC_TYPE_Q4_K 12
+#define B2Q_ORC_QK_K 256
+#define B2Q_ORC_Q4_K_BYTES 144
+#define B2Q_ORC_Q8_K_BYTES 292
+void b2q_orc_q4k_scale_min(const uint8_t* scales12, int j, int* sc, int* m);
+void b2q_orc_dequantize_row_q4_K(const uint8_t* y, float* x, int64_t k);
+void b2q_orc_quantize_row_q8_K(const float* x, uint8_t* y, int64_t k);
+float b2q_orc_vec_dot_q4_K_q8_K(const uint8_t* w, const uint8_t* a, int64_t k);
+/* Full mul_mat from fp32 activations (Q8_K quantize + dot).  Returns 0. */
+int b2q_orc_mul_mat_q4_K(const uint8_t* w, int64_t w_row_stride, int64_t N, const float* x,
+                         int64_t x_row_stride_floats, int64_t M, int64_t K, float* y,
+                         int64_t y_row_stride_floats, int nthreads);
+
 /* ggml_gelu on the CPU backend (ggml v0.21.0 ggml-cpu/vec.h, the
  * GGML_GELU_FP16 build, which is the default): outside (-10, 10) the result is
  * 0 (x <= -10) or x (x >= 10); inside, x is rounded to fp16 and looked up in a

@@ -23,7 +23,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "libb2q_oracle.so")
 
 QK = 32
-TYPE_F32, TYPE_Q4_0, TYPE_Q8_0 = 0, 2, 8
+TYPE_F32, TYPE_Q4_0, TYPE_Q8_0, TYPE_Q4_K = 0, 2, 8, 12
+QK_K, Q4_K_BYTES, Q8_K_BYTES = 256, 144, 292
 ACT_X86, ACT_REF = 0, 1
 BLOCK_BYTES = {TYPE_Q8_0: 34, TYPE_Q4_0: 18}
 
@@ -67,6 +68,12 @@ def lib():
         L.b2q_orc_gelu_n.argtypes = [P, P, I64, I]
         L.b2q_orc_gelu_table.argtypes = [P, I]
         L.b2q_orc_norm_modulate.argtypes = [P, I64, I64, I64, ctypes.c_float, P, P, P, I64]
+        L.b2q_orc_dequantize_row_q4_K.argtypes = [P, P, I64]
+        L.b2q_orc_quantize_row_q8_K.argtypes = [P, P, I64]
+        L.b2q_orc_vec_dot_q4_K_q8_K.restype = ctypes.c_float
+        L.b2q_orc_vec_dot_q4_K_q8_K.argtypes = [P, P, I64]
+        L.b2q_orc_mul_mat_q4_K.argtypes = [P, I64, I64, P, I64, I64, I64, P, I64, I]
+        L.b2q_orc_mul_mat_q4_K.restype = I
         L.b2q_orc_num_threads.restype = I
         L.b2q_orc_isa.restype = ctypes.c_char_p
         _lib = L
@@ -198,4 +205,46 @@ def norm_modulate(x: np.ndarray, eps: float = 1e-6, scale=None, shift=None) -> n
     sh = None if shift is None else np.ascontiguousarray(shift, dtype=np.float32)
     lib().b2q_orc_norm_modulate(_p(x), m, c, c, eps, None if sc is None else _p(sc),
                                 None if sh is None else _p(sh), _p(y), c)
+    return y
+
+
+# ------------------------------------------------------------ Q4_K / Q8_K
+def random_q4_k(n: int, k: int, seed: int) -> np.ndarray:
+    """Random valid Q4_K rows, uint8 [n, k/256*144]: d, dmin ~ |N(0, 0.01)| as
+    fp16, random 6-bit scales and mins, random 4-bit quants (weights are
+    quantized offline; any block bytes are a valid weight)."""
+    rng = np.random.default_rng(seed)
+    nb = k // QK_K
+    b = rng.integers(0, 256, size=(n, nb, Q4_K_BYTES), dtype=np.uint8)
+    d = np.abs(rng.standard_normal((n, nb)) * 0.01).astype(np.float16)
+    dm = np.abs(rng.standard_normal((n, nb)) * 0.01).astype(np.float16)
+    b[:, :, 0:2] = d.view(np.uint8).reshape(n, nb, 2)
+    b[:, :, 2:4] = dm.view(np.uint8).reshape(n, nb, 2)
+    return b.reshape(n, nb * Q4_K_BYTES)
+
+
+def dequantize_q4_k(w: np.ndarray, k: int) -> np.ndarray:
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    out = np.empty((w.shape[0], k), dtype=np.float32)
+    for r in range(w.shape[0]):
+        lib().b2q_orc_dequantize_row_q4_K(_p(w[r]), _p(out[r]), k)
+    return out
+
+
+def quantize_q8_k(x: np.ndarray) -> np.ndarray:
+    """fp32 [M, K] -> Q8_K rows uint8 [M, K/256*292]."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    m, k = x.shape
+    out = np.empty((m, k // QK_K * Q8_K_BYTES), dtype=np.uint8)
+    for r in range(m):
+        lib().b2q_orc_quantize_row_q8_K(_p(x[r]), _p(out[r]), k)
+    return out
+
+
+def mul_mat_q4_k(w: np.ndarray, x: np.ndarray, nthreads: int = 0) -> np.ndarray:
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n, (m, k) = w.shape[0], x.shape
+    y = np.empty((m, n), dtype=np.float32)
+    lib().b2q_orc_mul_mat_q4_K(_p(w), w.shape[1], n, _p(x), k, m, k, _p(y), n, nthreads)
     return y

@@ -78,5 +78,29 @@ def main() -> None:
     print("wrote", os.path.join(HERE, "q_golden.npz"))
 
 
+def main_q4_k() -> None:
+    """q4k_golden.npz: seeded random Q4_K blocks (any bytes with finite fp16
+    d / dmin are a valid weight; the quantizer runs offline) and gguf-py's
+    dequantization of them -- pins the block layout and the 6-bit scale / min
+    unpacking.  Includes blocks whose packed scale bytes have the high bits
+    set (the j >= 4 unpacking path)."""
+    rng = np.random.default_rng(4242)
+    n, k = 9, 512
+    nb = k // 256
+    b = rng.integers(0, 256, size=(n, nb, 144), dtype=np.uint8)
+    d = np.abs(rng.standard_normal((n, nb)) * 0.01).astype(np.float16)
+    dm = np.abs(rng.standard_normal((n, nb)) * 0.01).astype(np.float16)
+    b[:, :, 0:2] = d.view(np.uint8).reshape(n, nb, 2)
+    b[:, :, 2:4] = dm.view(np.uint8).reshape(n, nb, 2)
+    b[0, 0, 4:16] = 0xFF          # every scale and min at 63
+    b[1, 0, 4:16] = 0x00          # every scale and min at 0
+    w = b.reshape(n, nb * 144)
+    out = {"w_q4_k": w, "w_q4_k_dequant": gq.dequantize(w, T.Q4_K).astype(np.float32),
+           "gguf_version": np.array(importlib.metadata.version("gguf"))}
+    np.savez_compressed(os.path.join(HERE, "q4k_golden.npz"), **out)
+    print("wrote", os.path.join(HERE, "q4k_golden.npz"))
+
+
 if __name__ == "__main__":
     main()
+    main_q4_k()

@@ -178,3 +178,41 @@ def test_norm_modulate_matches_fp64_layernorm():
     # constant rows: variance 0, output 0 (x - mean = 0; 0 / sqrt(eps))
     z = O.norm_modulate(np.full((2, 64), 3.25, np.float32))
     assert np.all(z == 0)
+
+
+# ---------------------------------------------------------------- Q4_K / Q8_K
+def test_q4_k_dequantizer_matches_gguf_golden():
+    """Block layout and 6-bit scale/min unpacking, against gguf-py 0.19.0's
+    Q4_K dequantizer (tests/golden/make_golden.py)."""
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "q4k_golden.npz"))
+    w = g["w_q4_k"]
+    assert np.array_equal(O.dequantize_q4_k(w, 512), g["w_q4_k_dequant"])
+
+
+def test_q8_k_quantizer_edges():
+    x = np.zeros((3, 512), np.float32)
+    x[1, :256] = np.linspace(-2, 3, 256)
+    x[1, 256:] = -7.0                       # constant block: iscale = -127/-7 > 0, codes -127
+    x[2, 5], x[2, 9] = 4.0, -4.0            # tie in |x|: the first one sets the sign of d
+    q = O.quantize_q8_k(x).reshape(3, 2, 292)
+    d = q[:, :, :4].copy().view(np.float32)[:, :, 0]
+    codes = q[:, :, 4:260].view(np.int8)
+    bs = q[:, :, 260:].copy().view(np.int16)
+    assert np.all(d[0] == 0) and np.all(codes[0] == 0) and np.all(bs[0] == 0)
+    assert np.all(codes[1, 1] == -127) and d[1, 1] == np.float32(1.0) / (np.float32(-127.0) / np.float32(-7.0))
+    assert codes[2, 0, 5] == -127 and codes[2, 0, 9] == 127 and d[2, 0] < 0
+    assert np.array_equal(bs, codes.reshape(3, 2, 16, 16).astype(np.int32).sum(-1).astype(np.int16))
+    deq = d[:, :, None] * codes.astype(np.float32)
+    assert np.allclose(deq[1, 0], x[1, :256], atol=np.abs(d[1, 0]) * 0.5 + 1e-7)
+
+
+def test_q4_k_dot_matches_fp64_of_dequantized():
+    w = O.random_q4_k(17, 1024, 5)
+    x = np.random.default_rng(6).standard_normal((9, 1024)).astype(np.float32)
+    y = O.mul_mat_q4_k(w, x)
+    a = O.quantize_q8_k(x).reshape(9, 4, 292)
+    da = a[:, :, :4].copy().view(np.float32)[:, :, 0]
+    qa = a[:, :, 4:260].view(np.int8).astype(np.float64)
+    xa = (qa * da[:, :, None]).reshape(9, 1024)
+    y64 = xa @ O.dequantize_q4_k(w, 1024).astype(np.float64).T
+    assert rel_frobenius(y, y64) < 1e-6
