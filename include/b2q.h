@@ -44,14 +44,30 @@
 extern "C" {
 #endif
 
-enum b2q_type { B2Q_TYPE_F32 = 0, B2Q_TYPE_Q4_0 = 2, B2Q_TYPE_Q8_0 = 8 };
+enum b2q_type { B2Q_TYPE_F32 = 0, B2Q_TYPE_Q4_0 = 2, B2Q_TYPE_Q8_0 = 8, B2Q_TYPE_Q4_K = 12 };
 
 /* Activation-quantizer variant (fp32 -> Q8_0 rounding).
  *   B2Q_ACT_X86: the from_float of ggml's CPU backend on x86 (the host the
  *                reference runs on): inverse scale 127/amax, ties to even.
  *   B2Q_ACT_REF: ggml's scalar reference quantizer: inverse 1/d, ties away
- *                from zero. */
-enum b2q_act_variant { B2Q_ACT_X86 = 0, B2Q_ACT_REF = 1 };
+ *                from zero.
+ *   B2Q_ACT_Q8_K: fp32 -> Q8_K (256-value blocks, fp32 scale), the activation
+ *                format ggml's CPU backend uses against Q4_K weights; the only
+ *                variant Q4_K weights accept, and accepted only with them.
+ *
+ * Q4_K weights (ggml's shipped 4-bit k-quant, cpp_ggml/models/MODEL_CARD.md:54-74)
+ * need K % 256 == 0.  Their packed layout, and the prepared activations that go
+ * with it, span K' = b2q_packed_k(B2Q_TYPE_Q4_K, k) = 2k: every 32-value
+ * sub-block is stored as a block of quants and a block of ones that carries the
+ * min term.  Sizes and the prepared-activation entries take K' for Q4_K
+ * (b2q_weight_packed_size(n, K'), b2q_act_prepared_size(m, K'),
+ * b2q_mul_mat_workspace_size(m, n, K', ...), b2q_mul_mat_prepared*(..., K', ...));
+ * the entries that take fp32 x or raw weights take the logical k. */
+enum b2q_act_variant { B2Q_ACT_X86 = 0, B2Q_ACT_REF = 1, B2Q_ACT_Q8_K = 2 };
+
+/* K of the packed / prepared layouts for weight type wtype: k, or 2k for Q4_K
+ * (0 when k is not valid for the type). */
+B2Q_API int64_t b2q_packed_k(int wtype, int64_t k);
 
 enum b2q_status {
     B2Q_OK = 0,

@@ -21,9 +21,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libb2q.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "b2q.h")
 
-TYPE_F32, TYPE_Q4_0, TYPE_Q8_0 = 0, 2, 8
-ACT_X86, ACT_REF = 0, 1
-QK = 32
+TYPE_F32, TYPE_Q4_0, TYPE_Q8_0, TYPE_Q4_K = 0, 2, 8, 12
+ACT_X86, ACT_REF, ACT_Q8_K = 0, 1, 2
+QK, QK_K = 32, 256
 BLOCK_BYTES = {TYPE_Q8_0: 34, TYPE_Q4_0: 18}
 
 OK = 0
@@ -59,6 +59,7 @@ def _lib_obj():
             "b2q_version": (ctypes.c_char_p, []),
             "b2q_quantize_q8_0": (I, [P, I64, I64, I64, P, I64, I, P]),
             "b2q_weight_packed_size": (SZ, [I64, I64]),
+            "b2q_packed_k": (I64, [I, I64]),
             "b2q_weight_pack": (I, [I, P, I64, I64, I64, P, SZ, P]),
             "b2q_weight_upload": (I, [I, P, I64, I64, I64, P, SZ, P, SZ, P]),
             "b2q_mul_mat_workspace_size": (SZ, [I64, I64, I64, I]),
@@ -130,7 +131,18 @@ def _empty_aligned(nbytes: int, device) -> "object":
 
 
 def row_bytes(wtype: int, k: int) -> int:
+    if wtype == TYPE_Q4_K:
+        return k // QK_K * 144
     return k // QK * BLOCK_BYTES[wtype]
+
+
+def packed_k(wtype: int, k: int) -> int:
+    """K of the packed / prepared layouts (2k for Q4_K)."""
+    return lib().b2q_packed_k(wtype, k)
+
+
+def _kp(variant: int, k: int) -> int:
+    return 2 * k if variant == ACT_Q8_K else k
 
 
 def quantize_q8_0(x, variant: int = ACT_X86, out=None, stream=None):
@@ -153,7 +165,7 @@ def weight_packed_size(n: int, k: int) -> int:
 def weight_pack(wtype: int, w, k: int, stream=None):
     """Raw ggml weight blocks uint8 [N, row_bytes] -> packed device buffer."""
     n = w.shape[0]
-    size = weight_packed_size(n, k)
+    size = weight_packed_size(n, packed_k(wtype, k))
     packed = _empty_aligned(size, w.device)
     rc = lib().b2q_weight_pack(wtype, _ptr(w), n, k, w.stride(0), _ptr(packed), size, _stream(stream))
     _check("b2q_weight_pack", rc)
@@ -168,7 +180,7 @@ def weight_upload(wtype: int, host_w, k: int, staging_bytes: int = 8 << 20, devi
     host_w = np.asarray(host_w)
     n = host_w.shape[0]
     dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
-    size = weight_packed_size(n, k)
+    size = weight_packed_size(n, packed_k(wtype, k))
     packed = _empty_aligned(size, dev)
     staging = _empty_aligned(staging_bytes, dev)
     rc = lib().b2q_weight_upload(wtype, host_w.ctypes.data, n, k, host_w.strides[0], _ptr(staging), staging_bytes,
@@ -186,17 +198,20 @@ def workspace(m: int, n: int, k: int, packed_weight: bool, device):
     return _empty_aligned(workspace_size(m, n, k, packed_weight), device)
 
 
-def mul_mat(wtype: int, w, x, k: int | None = None, bias=None, variant: int = ACT_X86,
+def mul_mat(wtype: int, w, x, k: int | None = None, bias=None, variant: int | None = None,
             out=None, ws=None, stream=None):
-    """ggml_mul_mat(w, x) (+ bias): w raw blocks uint8 [N, >=row_bytes], x fp32 [M, K] -> [M, N]."""
+    """ggml_mul_mat(w, x) (+ bias): w raw blocks uint8 [N, >=row_bytes], x fp32 [M, K] -> [M, N].
+    variant defaults to ACT_X86 (ACT_Q8_K for Q4_K weights)."""
     torch = _torch()
     m, kk = x.shape
     k = kk if k is None else k
     n = w.shape[0]
+    if variant is None:
+        variant = ACT_Q8_K if wtype == TYPE_Q4_K else ACT_X86
     if out is None:
         out = torch.empty((m, n), dtype=torch.float32, device=x.device)
     if ws is None:
-        ws = workspace(m, n, k, False, x.device)
+        ws = workspace(m, n, packed_k(wtype, k) or k, False, x.device)
     rc = lib().b2q_mul_mat(wtype, _ptr(w), w.stride(0), n, k, _ptr(x), m, x.stride(0) * 4,
                            _ptr(bias), _ptr(out), out.stride(0) * 4, variant, _ptr(ws), ws.numel(),
                            _stream(stream))
@@ -211,7 +226,7 @@ def mul_mat_packed(packed, n: int, k: int, x, bias=None, variant: int = ACT_X86,
     if out is None:
         out = torch.empty((m, n), dtype=torch.float32, device=x.device)
     if ws is None:
-        ws = workspace(m, n, k, True, x.device)
+        ws = workspace(m, n, _kp(variant, k), True, x.device)
     rc = lib().b2q_mul_mat_packed(_ptr(packed), n, k, _ptr(x), m, x.stride(0) * 4, _ptr(bias),
                                   _ptr(out), out.stride(0) * 4, variant, _ptr(ws), ws.numel(),
                                   _stream(stream))
@@ -252,9 +267,10 @@ def act_prepared_size(m: int, k: int) -> int:
 
 
 def act_prepare(x, variant: int = ACT_X86, out=None, stream=None):
-    """fp32 [M, K] -> prepared Q8_0 activations (device buffer, GEMM layout)."""
+    """fp32 [M, K] -> prepared Q8_0 (or, with ACT_Q8_K, Q8_K) activations
+    (device buffer, GEMM layout over K or, for Q8_K, K' = 2K)."""
     m, k = x.shape
-    size = act_prepared_size(m, k)
+    size = act_prepared_size(m, _kp(variant, k))
     if out is None:
         out = _empty_aligned(size, x.device)
     rc = lib().b2q_act_prepare(_ptr(x), m, k, x.stride(0) * 4, variant, _ptr(out), out.numel(),

@@ -26,8 +26,12 @@ int check_device(int* sms) {
 
 int from_cuda(cudaError_t e) { return e == cudaSuccess ? B2Q_OK : B2Q_ERR_CUDA; }
 
-bool valid_wtype(int t) { return t == B2Q_TYPE_Q8_0 || t == B2Q_TYPE_Q4_0; }
-int64_t wblock_bytes(int t) { return t == B2Q_TYPE_Q8_0 ? kQ8Bytes : kQ4Bytes; }
+bool valid_wtype(int t) { return t == B2Q_TYPE_Q8_0 || t == B2Q_TYPE_Q4_0 || t == B2Q_TYPE_Q4_K; }
+// Bytes of one raw row of k values.
+int64_t raw_row_bytes(int t, int64_t k) {
+  if (t == B2Q_TYPE_Q4_K) return (k / kQKK) * kQ4KBytes;
+  return (k / kQK) * (t == B2Q_TYPE_Q8_0 ? kQ8Bytes : kQ4Bytes);
+}
 
 // Common checks of a weight operand in raw ggml block layout.
 int check_raw_weight(int wtype, const void* w, int64_t ldw, int64_t n, int64_t k) {
@@ -35,7 +39,8 @@ int check_raw_weight(int wtype, const void* w, int64_t ldw, int64_t n, int64_t k
   if (n < 0 || k <= 0 || k % kQK != 0) return B2Q_ERR_INVALID_ARG;
   if (n > INT_MAX || k > INT_MAX) return B2Q_ERR_TOO_LARGE;
   if (n > 0 && !w) return B2Q_ERR_INVALID_ARG;
-  if (ldw < (k / kQK) * wblock_bytes(wtype)) return B2Q_ERR_INVALID_ARG;
+  if (wtype == B2Q_TYPE_Q4_K && k % kQKK != 0) return B2Q_ERR_INVALID_ARG;
+  if (ldw < raw_row_bytes(wtype, k)) return B2Q_ERR_INVALID_ARG;
   if (!aligned(w, 2) || ldw % 2 != 0) return B2Q_ERR_MISALIGNED;
   return B2Q_OK;
 }
@@ -78,23 +83,30 @@ int run_gemm(const SplitOperand& w, const SplitOperand& a, int64_t m, int64_t n,
 }
 
 // Activation quantize into the split layout + GEMM against a split weight.
+// k is the logical K; with B2Q_ACT_Q8_K (Q4_K weights) the split layouts of w
+// and of the activations span K' = 2k.
 int mul_mat_split(const SplitOperand& w, int64_t n, int64_t k, const float* x, int64_t m,
                   int64_t ldx, const float* bias, float* y, int64_t ldy, int variant, Carve& ws,
                   int sms, cudaStream_t s) {
-  uint8_t* abuf = ws.take(split_bytes(m, k));
+  const int64_t kp = variant == B2Q_ACT_Q8_K ? 2 * k : k;
+  uint8_t* abuf = ws.take(split_bytes(m, kp));
   if (!abuf) return B2Q_ERR_WORKSPACE;
-  SplitOperand a = split_at(abuf, m, k);
+  SplitOperand a = split_at(abuf, m, kp);
   const bool vec4 = aligned(x, 16) && ldx % 16 == 0;
-  cudaError_t e = launch_quantize_q8_0_split(x, m, k, ldx / 4, const_cast<int8_t*>(a.codes),
-                                             const_cast<float*>(a.scales), a.ld, variant, vec4, s);
+  cudaError_t e = variant == B2Q_ACT_Q8_K
+                      ? launch_quantize_q8_k_split(x, m, k, ldx / 4, const_cast<int8_t*>(a.codes),
+                                                   const_cast<float*>(a.scales), a.ld, vec4, s)
+                      : launch_quantize_q8_0_split(x, m, k, ldx / 4, const_cast<int8_t*>(a.codes),
+                                                   const_cast<float*>(a.scales), a.ld, variant, vec4, s);
   if (e != cudaSuccess) return B2Q_ERR_CUDA;
-  return run_gemm(w, a, m, n, k, y, ldy / 4, bias, nullptr, sms, s);
+  return run_gemm(w, a, m, n, kp, y, ldy / 4, bias, nullptr, sms, s);
 }
 
 int check_x_y(const float* x, int64_t m, int64_t k, int64_t ldx, float* y, int64_t n,
               int64_t ldy, int variant) {
   if (m < 0 || m > INT_MAX) return m < 0 ? B2Q_ERR_INVALID_ARG : B2Q_ERR_TOO_LARGE;
-  if (variant != B2Q_ACT_X86 && variant != B2Q_ACT_REF) return B2Q_ERR_INVALID_ARG;
+  if (variant != B2Q_ACT_X86 && variant != B2Q_ACT_REF && variant != B2Q_ACT_Q8_K) return B2Q_ERR_INVALID_ARG;
+  if (variant == B2Q_ACT_Q8_K && k % kQKK != 0) return B2Q_ERR_INVALID_ARG;
   if (m > 0 && (!x || !y)) return B2Q_ERR_INVALID_ARG;
   if (ldx < k * 4 || ldy < n * 4) return B2Q_ERR_INVALID_ARG;
   if (!aligned(x, 4) || ldx % 4 != 0 || !aligned(y, 4) || ldy % 4 != 0) return B2Q_ERR_MISALIGNED;
@@ -170,6 +182,11 @@ int b2q_quantize_q8_0(const float* x, int64_t nrows, int64_t k, int64_t x_row_st
                                                variant, vec4, static_cast<cudaStream_t>(stream)));
 }
 
+int64_t b2q_packed_k(int wtype, int64_t k) {
+  if (!valid_wtype(wtype) || k <= 0 || k % (wtype == B2Q_TYPE_Q4_K ? kQKK : kQK) != 0) return 0;
+  return packed_k(wtype, k);
+}
+
 size_t b2q_weight_packed_size(int64_t n, int64_t k) {
   if (n < 0 || k <= 0 || k % kQK != 0) return 0;
   return split_bytes(n, k);
@@ -179,10 +196,11 @@ int b2q_weight_pack(int wtype, const void* w, int64_t n, int64_t k, int64_t w_ro
                     void* packed, size_t packed_bytes, void* stream) {
   if (int rc = check_raw_weight(wtype, w, w_row_stride_bytes, n, k)) return rc;
   if (n > 0 && !packed) return B2Q_ERR_INVALID_ARG;
-  if (packed_bytes < split_bytes(n, k)) return B2Q_ERR_WORKSPACE;
+  const int64_t kp = packed_k(wtype, k);
+  if (packed_bytes < split_bytes(n, kp)) return B2Q_ERR_WORKSPACE;
   if (!aligned(packed, 256)) return B2Q_ERR_MISALIGNED;
   if (int rc = check_device(nullptr)) return rc;
-  SplitOperand s = split_at(static_cast<uint8_t*>(packed), n, k);
+  SplitOperand s = split_at(static_cast<uint8_t*>(packed), n, kp);
   return from_cuda(launch_pack_weights(wtype, static_cast<const uint8_t*>(w), n, k, w_row_stride_bytes,
                                        const_cast<int8_t*>(s.codes), const_cast<float*>(s.scales),
                                        s.ld, static_cast<cudaStream_t>(stream)));
@@ -192,14 +210,15 @@ int b2q_weight_upload(int wtype, const void* host_w, int64_t n, int64_t k, int64
                       void* staging, size_t staging_bytes, void* packed, size_t packed_bytes, void* stream) {
   if (int rc = check_raw_weight(wtype, host_w, w_row_stride_bytes, n, k)) return rc;
   if (n > 0 && (!packed || !staging)) return B2Q_ERR_INVALID_ARG;
-  if (packed_bytes < split_bytes(n, k)) return B2Q_ERR_WORKSPACE;
-  const int64_t row_bytes = (k / kQK) * wblock_bytes(wtype);
+  const int64_t kp = packed_k(wtype, k);
+  if (packed_bytes < split_bytes(n, kp)) return B2Q_ERR_WORKSPACE;
+  const int64_t row_bytes = raw_row_bytes(wtype, k);
   if (n > 0 && staging_bytes < static_cast<size_t>(row_bytes)) return B2Q_ERR_WORKSPACE;
   if (!aligned(packed, 256) || !aligned(staging, 2)) return B2Q_ERR_MISALIGNED;
   if (n == 0) return B2Q_OK;
   if (int rc = check_device(nullptr)) return rc;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const SplitOperand out = split_at(static_cast<uint8_t*>(packed), n, k);
+  const SplitOperand out = split_at(static_cast<uint8_t*>(packed), n, kp);
   const int64_t chunk = static_cast<int64_t>(staging_bytes / static_cast<size_t>(row_bytes));
   const uint8_t* src = static_cast<const uint8_t*>(host_w);
   for (int64_t r0 = 0; r0 < n; r0 += chunk) {
@@ -208,7 +227,7 @@ int b2q_weight_upload(int wtype, const void* host_w, int64_t n, int64_t k, int64
                           cudaMemcpyHostToDevice, s) != cudaSuccess)
       return B2Q_ERR_CUDA;
     if (launch_pack_weights(wtype, static_cast<const uint8_t*>(staging), rows, k, row_bytes,
-                            const_cast<int8_t*>(out.codes) + r0 * k, const_cast<float*>(out.scales) + r0, out.ld,
+                            const_cast<int8_t*>(out.codes) + r0 * kp, const_cast<float*>(out.scales) + r0, out.ld,
                             s) != cudaSuccess)
       return B2Q_ERR_CUDA;
   }
@@ -235,7 +254,8 @@ int b2q_mul_mat_packed(const void* packed, int64_t n, int64_t k, const float* x,
   int sms = 0;
   if (int rc = check_device(&sms)) return rc;
   Carve ws{static_cast<uint8_t*>(workspace), workspace_bytes};
-  const SplitOperand w = split_at(static_cast<uint8_t*>(const_cast<void*>(packed)), n, k);
+  const int64_t kp = variant == B2Q_ACT_Q8_K ? 2 * k : k;  // Q8_K activations <=> Q4_K-packed weight
+  const SplitOperand w = split_at(static_cast<uint8_t*>(const_cast<void*>(packed)), n, kp);
   return mul_mat_split(w, n, k, x, m, x_row_stride_bytes, bias, y, y_row_stride_bytes, variant, ws,
                        sms, static_cast<cudaStream_t>(stream));
 }
@@ -246,6 +266,7 @@ int b2q_mul_mat(int wtype, const void* w, int64_t w_row_stride_bytes, int64_t n,
                 size_t workspace_bytes, void* stream) {
   if (int rc = check_raw_weight(wtype, w, w_row_stride_bytes, n, k)) return rc;
   if (int rc = check_x_y(x, m, k, x_row_stride_bytes, y, n, y_row_stride_bytes, variant)) return rc;
+  if ((wtype == B2Q_TYPE_Q4_K) != (variant == B2Q_ACT_Q8_K)) return B2Q_ERR_INVALID_ARG;
   if (!aligned(workspace, 256) || (bias && !aligned(bias, 4))) return B2Q_ERR_MISALIGNED;
   if (m == 0 || n == 0) return B2Q_OK;
   if (!workspace) return B2Q_ERR_WORKSPACE;
@@ -253,9 +274,10 @@ int b2q_mul_mat(int wtype, const void* w, int64_t w_row_stride_bytes, int64_t n,
   if (int rc = check_device(&sms)) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   Carve ws{static_cast<uint8_t*>(workspace), workspace_bytes};
-  uint8_t* wbuf = ws.take(split_bytes(n, k));
+  const int64_t kp = packed_k(wtype, k);
+  uint8_t* wbuf = ws.take(split_bytes(n, kp));
   if (!wbuf) return B2Q_ERR_WORKSPACE;
-  const SplitOperand wsplit = split_at(wbuf, n, k);
+  const SplitOperand wsplit = split_at(wbuf, n, kp);
   if (launch_pack_weights(wtype, static_cast<const uint8_t*>(w), n, k, w_row_stride_bytes,
                           const_cast<int8_t*>(wsplit.codes), const_cast<float*>(wsplit.scales),
                           wsplit.ld, s) != cudaSuccess)
@@ -274,15 +296,21 @@ int b2q_act_prepare(const float* x, int64_t m, int64_t k, int64_t x_row_stride_b
   if (k <= 0 || k % kQK != 0) return B2Q_ERR_INVALID_ARG;
   if (k > INT_MAX) return B2Q_ERR_TOO_LARGE;
   if (m < 0 || m > INT_MAX) return m < 0 ? B2Q_ERR_INVALID_ARG : B2Q_ERR_TOO_LARGE;
-  if (variant != B2Q_ACT_X86 && variant != B2Q_ACT_REF) return B2Q_ERR_INVALID_ARG;
+  if (variant != B2Q_ACT_X86 && variant != B2Q_ACT_REF && variant != B2Q_ACT_Q8_K) return B2Q_ERR_INVALID_ARG;
+  if (variant == B2Q_ACT_Q8_K && k % kQKK != 0) return B2Q_ERR_INVALID_ARG;
   if (m > 0 && (!x || !act)) return B2Q_ERR_INVALID_ARG;
   if (x_row_stride_bytes < k * 4) return B2Q_ERR_INVALID_ARG;
   if (!aligned(x, 4) || x_row_stride_bytes % 4 != 0 || !aligned(act, 256)) return B2Q_ERR_MISALIGNED;
-  if (act_bytes < split_bytes(m, k)) return B2Q_ERR_WORKSPACE;
+  const int64_t kp = variant == B2Q_ACT_Q8_K ? 2 * k : k;
+  if (act_bytes < split_bytes(m, kp)) return B2Q_ERR_WORKSPACE;
   if (m == 0) return B2Q_OK;
   if (int rc = check_device(nullptr)) return rc;
-  const SplitOperand a = split_at(static_cast<uint8_t*>(act), m, k);
+  const SplitOperand a = split_at(static_cast<uint8_t*>(act), m, kp);
   const bool vec4 = aligned(x, 16) && x_row_stride_bytes % 16 == 0;
+  if (variant == B2Q_ACT_Q8_K)
+    return from_cuda(launch_quantize_q8_k_split(x, m, k, x_row_stride_bytes / 4, const_cast<int8_t*>(a.codes),
+                                                const_cast<float*>(a.scales), a.ld, vec4,
+                                                static_cast<cudaStream_t>(stream)));
   return from_cuda(launch_quantize_q8_0_split(x, m, k, x_row_stride_bytes / 4,
                                               const_cast<int8_t*>(a.codes),
                                               const_cast<float*>(a.scales), a.ld, variant, vec4,
@@ -455,6 +483,7 @@ size_t b2q_block_dots_workspace_size(int64_t m, int64_t n, int64_t k) {
 int b2q_block_dots(int wtype, const void* w, int64_t w_row_stride_bytes, int64_t n, int64_t k,
                    const void* a, int64_t m, int64_t a_row_stride_bytes, int32_t* dots,
                    void* workspace, size_t workspace_bytes, void* stream) {
+  if (wtype == B2Q_TYPE_Q4_K) return B2Q_ERR_UNSUPPORTED;  // check path for the 32-value block types
   if (int rc = check_raw_weight(wtype, w, w_row_stride_bytes, n, k)) return rc;
   if (int rc = check_raw_weight(B2Q_TYPE_Q8_0, a, a_row_stride_bytes, m, k)) return rc;
   if (m > 0 && n > 0 && !dots) return B2Q_ERR_INVALID_ARG;
@@ -483,6 +512,7 @@ int b2q_block_dots(int wtype, const void* w, int64_t w_row_stride_bytes, int64_t
 int b2q_mul_mat_q_simt(int wtype, const void* w, int64_t w_row_stride_bytes, int64_t n,
                        int64_t k, const void* a, int64_t m, int64_t a_row_stride_bytes,
                        float* y, int64_t y_row_stride_bytes, void* stream) {
+  if (wtype == B2Q_TYPE_Q4_K) return B2Q_ERR_UNSUPPORTED;  // check path for the 32-value block types
   if (int rc = check_raw_weight(wtype, w, w_row_stride_bytes, n, k)) return rc;
   if (int rc = check_raw_weight(B2Q_TYPE_Q8_0, a, a_row_stride_bytes, m, k)) return rc;
   if (m > 0 && n > 0 && !y) return B2Q_ERR_INVALID_ARG;

@@ -23,6 +23,13 @@ constexpr int kQ8Bytes = 34;
 constexpr int kQ4Bytes = 18;
 constexpr int kTypeQ4_0 = 2;
 constexpr int kTypeQ8_0 = 8;
+constexpr int kTypeQ4_K = 12;  // ggml's k-quant, 256-value super-blocks (144 bytes)
+constexpr int kQKK = 256;
+constexpr int kQ4KBytes = 144;
+// Q4_K weights run on the same GEMM over K' = 2K: each 32-value sub-block
+// becomes a block of quants and a block of ones (the min term), against the
+// Q8_K activation sub-block duplicated (b2q_quantize.cu).
+inline int64_t packed_k(int wtype, int64_t k) { return wtype == kTypeQ4_K ? 2 * k : k; }
 
 inline int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 
@@ -59,6 +66,8 @@ cudaError_t launch_quantize_q8_0_blocks(const float* x, int64_t m, int64_t k, in
 cudaError_t launch_quantize_q8_0_split(const float* x, int64_t m, int64_t k, int64_t ldx_floats,
                                        int8_t* codes, float* scales, int64_t ld, int variant,
                                        bool vec4, cudaStream_t s);
+cudaError_t launch_quantize_q8_k_split(const float* x, int64_t m, int64_t k, int64_t ldx_floats, int8_t* codes,
+                                       float* scales, int64_t ld, bool vec4, cudaStream_t s);
 cudaError_t launch_pack_weights(int wtype, const uint8_t* w, int64_t n, int64_t k,
                                 int64_t ldw_bytes, int8_t* codes, float* scales, int64_t ld,
                                 cudaStream_t s);

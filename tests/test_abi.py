@@ -175,3 +175,23 @@ def test_header_compiles_as_c(tmp_path):
                         "-I", os.path.join(REPO, "include"), str(src), "-o", str(tmp_path / "t.o")],
                        capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
+
+
+def test_q4_k_validation(b2q_mod):
+    L = b2q.lib()
+    assert L.b2q_packed_k(12, 1024) == 2048 and L.b2q_packed_k(8, 1024) == 1024
+    assert L.b2q_packed_k(12, 96) == 0 and L.b2q_packed_k(3, 1024) == 0
+    big = 1 << 30
+    # raw Q4_K: k % 256, the variant must be Q8_K and Q8_K only goes with Q4_K
+    assert L.b2q_mul_mat(12, FAKE, 144 * 4, 64, 288, FAKE, 4, 4096, None, FAKE, 256, 2, FAKE, big, None) == 1
+    assert L.b2q_mul_mat(12, FAKE, 144 * 4, 64, 1024, FAKE, 4, 4096, None, FAKE, 256, 0, FAKE, big, None) == 1
+    assert L.b2q_mul_mat(8, FAKE, 1088, 64, 1024, FAKE, 4, 4096, None, FAKE, 256, 2, FAKE, big, None) == 1
+    assert L.b2q_mul_mat(12, FAKE, 144 * 3, 64, 1024, FAKE, 4, 4096, None, FAKE, 256, 2, FAKE, big, None) == 1
+    # pack: the buffer must hold the K' = 2K layout
+    assert L.b2q_weight_pack(12, FAKE, 64, 1024, 576, FAKE, L.b2q_weight_packed_size(64, 1024), None) == 4
+    # debug check paths are for the 32-value block types
+    assert L.b2q_block_dots(12, FAKE, 576, 64, 1024, FAKE, 4, 1088, FAKE, FAKE, big, None) == 2
+    assert L.b2q_mul_mat_q_simt(12, FAKE, 576, 64, 1024, FAKE, 4, 1088, FAKE, 256, None) == 2
+    # Q8_K activations: k % 256; the fused GELU quantize does not produce Q8_K
+    assert L.b2q_act_prepare(FAKE, 4, 96, 384, 2, FAKE, big, None) == 1
+    assert L.b2q_mul_mat_prepared_gelu_q8(FAKE, 256, 1024, FAKE, 4, None, FAKE, big, 2, None) == 1
