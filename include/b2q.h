@@ -56,18 +56,18 @@ enum b2q_type { B2Q_TYPE_F32 = 0, B2Q_TYPE_Q4_0 = 2, B2Q_TYPE_Q8_0 = 8, B2Q_TYPE
  *                variant Q4_K weights accept, and accepted only with them.
  *
  * Q4_K weights (ggml's shipped 4-bit k-quant, cpp_ggml/models/MODEL_CARD.md:54-74)
- * need K % 256 == 0.  Their packed layout, and the prepared activations that go
- * with it, span K' = b2q_packed_k(B2Q_TYPE_Q4_K, k) = 2k: every 32-value
- * sub-block is stored as a block of quants and a block of ones that carries the
- * min term.  Sizes and the prepared-activation entries take K' for Q4_K
- * (b2q_weight_packed_size(n, K'), b2q_act_prepared_size(m, K'),
- * b2q_mul_mat_workspace_size(m, n, K', ...), b2q_mul_mat_prepared*(..., K', ...));
- * the entries that take fp32 x or raw weights take the logical k. */
+ * need K % 256 == 0 and have their own packed layout (three int8 planes and
+ * the super-block scales) and prepared-activation layout (Q8_K codes and one
+ * fp32 scale per 256 values); size them with the typed functions below.  The
+ * untyped size functions and prepared entries serve Q8_0 / Q4_0. */
 enum b2q_act_variant { B2Q_ACT_X86 = 0, B2Q_ACT_REF = 1, B2Q_ACT_Q8_K = 2 };
 
-/* K of the packed / prepared layouts for weight type wtype: k, or 2k for Q4_K
- * (0 when k is not valid for the type). */
-B2Q_API int64_t b2q_packed_k(int wtype, int64_t k);
+/* Typed sizes (0 when the arguments are not valid for the type):
+ * the packed weight, the prepared activations of an activation variant, and
+ * the workspace of b2q_mul_mat (packed_weight = 0) / b2q_mul_mat_packed (1). */
+B2Q_API size_t b2q_weight_packed_bytes(int wtype, int64_t n, int64_t k);
+B2Q_API size_t b2q_act_prepared_bytes(int variant, int64_t m, int64_t k);
+B2Q_API size_t b2q_mul_mat_workspace_bytes(int wtype, int64_t m, int64_t n, int64_t k, int packed_weight);
 
 enum b2q_status {
     B2Q_OK = 0,
@@ -178,6 +178,20 @@ B2Q_API int b2q_act_prepare(const float* x, int64_t m, int64_t k, int64_t x_row_
 B2Q_API int b2q_mul_mat_prepared(const void* packed, int64_t n, int64_t k, const void* act,
                                  int64_t m, const float* bias, float* y,
                                  int64_t y_row_stride_bytes, void* stream);
+
+/* Q4_K on prepared operands: the packed Q4_K weight (b2q_weight_pack /
+ * b2q_weight_upload with B2Q_TYPE_Q4_K) against Q8_K activations
+ * (b2q_act_prepare with B2Q_ACT_Q8_K):
+ *   y = mul_mat(w, act) + bias,  or, with resid != NULL,
+ *   y = resid + gate * (mul_mat(w, act) + bias)   (gate may be NULL)
+ * in ggml's roundings for the add / mul steps.  The tensor cores accumulate
+ * each 256-value super-block exactly in int32 (three int8 weight planes), and
+ * the fp32 fold runs once per super-block.  resid and y: the same buffer with
+ * the same row stride, or disjoint. */
+B2Q_API int b2q_mul_mat_prepared_q4_k(const void* packed, int64_t n, int64_t k, const void* act, int64_t m,
+                                      const float* bias, const float* gate, const float* resid,
+                                      int64_t resid_row_stride_bytes, float* y, int64_t y_row_stride_bytes,
+                                      void* stream);
 
 /* ------------------------------------- fused MLP hidden layer (fc1 -> fc2)
  * The DiT feed-forward block computes fc2(gelu(fc1(x) + b1)) + b2

@@ -59,7 +59,10 @@ def _lib_obj():
             "b2q_version": (ctypes.c_char_p, []),
             "b2q_quantize_q8_0": (I, [P, I64, I64, I64, P, I64, I, P]),
             "b2q_weight_packed_size": (SZ, [I64, I64]),
-            "b2q_packed_k": (I64, [I, I64]),
+            "b2q_weight_packed_bytes": (SZ, [I, I64, I64]),
+            "b2q_act_prepared_bytes": (SZ, [I, I64, I64]),
+            "b2q_mul_mat_workspace_bytes": (SZ, [I, I64, I64, I64, I]),
+            "b2q_mul_mat_prepared_q4_k": (I, [P, I64, I64, P, I64, P, P, P, I64, P, I64, P]),
             "b2q_weight_pack": (I, [I, P, I64, I64, I64, P, SZ, P]),
             "b2q_weight_upload": (I, [I, P, I64, I64, I64, P, SZ, P, SZ, P]),
             "b2q_mul_mat_workspace_size": (SZ, [I64, I64, I64, I]),
@@ -136,13 +139,12 @@ def row_bytes(wtype: int, k: int) -> int:
     return k // QK * BLOCK_BYTES[wtype]
 
 
-def packed_k(wtype: int, k: int) -> int:
-    """K of the packed / prepared layouts (2k for Q4_K)."""
-    return lib().b2q_packed_k(wtype, k)
+def weight_packed_bytes(wtype: int, n: int, k: int) -> int:
+    return lib().b2q_weight_packed_bytes(wtype, n, k)
 
 
-def _kp(variant: int, k: int) -> int:
-    return 2 * k if variant == ACT_Q8_K else k
+def act_prepared_bytes(variant: int, m: int, k: int) -> int:
+    return lib().b2q_act_prepared_bytes(variant, m, k)
 
 
 def quantize_q8_0(x, variant: int = ACT_X86, out=None, stream=None):
@@ -165,7 +167,7 @@ def weight_packed_size(n: int, k: int) -> int:
 def weight_pack(wtype: int, w, k: int, stream=None):
     """Raw ggml weight blocks uint8 [N, row_bytes] -> packed device buffer."""
     n = w.shape[0]
-    size = weight_packed_size(n, packed_k(wtype, k))
+    size = weight_packed_bytes(wtype, n, k)
     packed = _empty_aligned(size, w.device)
     rc = lib().b2q_weight_pack(wtype, _ptr(w), n, k, w.stride(0), _ptr(packed), size, _stream(stream))
     _check("b2q_weight_pack", rc)
@@ -180,7 +182,7 @@ def weight_upload(wtype: int, host_w, k: int, staging_bytes: int = 8 << 20, devi
     host_w = np.asarray(host_w)
     n = host_w.shape[0]
     dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
-    size = weight_packed_size(n, packed_k(wtype, k))
+    size = weight_packed_bytes(wtype, n, k)
     packed = _empty_aligned(size, dev)
     staging = _empty_aligned(staging_bytes, dev)
     rc = lib().b2q_weight_upload(wtype, host_w.ctypes.data, n, k, host_w.strides[0], _ptr(staging), staging_bytes,
@@ -211,7 +213,7 @@ def mul_mat(wtype: int, w, x, k: int | None = None, bias=None, variant: int | No
     if out is None:
         out = torch.empty((m, n), dtype=torch.float32, device=x.device)
     if ws is None:
-        ws = workspace(m, n, packed_k(wtype, k) or k, False, x.device)
+        ws = _empty_aligned(lib().b2q_mul_mat_workspace_bytes(wtype, m, n, k, 0), x.device)
     rc = lib().b2q_mul_mat(wtype, _ptr(w), w.stride(0), n, k, _ptr(x), m, x.stride(0) * 4,
                            _ptr(bias), _ptr(out), out.stride(0) * 4, variant, _ptr(ws), ws.numel(),
                            _stream(stream))
@@ -226,7 +228,8 @@ def mul_mat_packed(packed, n: int, k: int, x, bias=None, variant: int = ACT_X86,
     if out is None:
         out = torch.empty((m, n), dtype=torch.float32, device=x.device)
     if ws is None:
-        ws = workspace(m, n, _kp(variant, k), True, x.device)
+        wt = TYPE_Q4_K if variant == ACT_Q8_K else TYPE_Q8_0
+        ws = _empty_aligned(lib().b2q_mul_mat_workspace_bytes(wt, m, n, k, 1), x.device)
     rc = lib().b2q_mul_mat_packed(_ptr(packed), n, k, _ptr(x), m, x.stride(0) * 4, _ptr(bias),
                                   _ptr(out), out.stride(0) * 4, variant, _ptr(ws), ws.numel(),
                                   _stream(stream))
@@ -268,9 +271,9 @@ def act_prepared_size(m: int, k: int) -> int:
 
 def act_prepare(x, variant: int = ACT_X86, out=None, stream=None):
     """fp32 [M, K] -> prepared Q8_0 (or, with ACT_Q8_K, Q8_K) activations
-    (device buffer, GEMM layout over K or, for Q8_K, K' = 2K)."""
+    (device buffer in the GEMM's layout)."""
     m, k = x.shape
-    size = act_prepared_size(m, _kp(variant, k))
+    size = act_prepared_bytes(variant, m, k)
     if out is None:
         out = _empty_aligned(size, x.device)
     rc = lib().b2q_act_prepare(_ptr(x), m, k, x.stride(0) * 4, variant, _ptr(out), out.numel(),
@@ -313,6 +316,20 @@ def mul_mat_prepared_gate_residual(packed, n: int, k: int, act, m: int, resid, b
                                                   _ptr(resid), resid.stride(0) * 4, _ptr(out),
                                                   out.stride(0) * 4, _stream(stream))
     _check("b2q_mul_mat_prepared_gate_residual", rc)
+    return out
+
+
+def mul_mat_prepared_q4_k(packed, n: int, k: int, act, m: int, bias=None, gate=None, resid=None, out=None,
+                          stream=None):
+    """Q4_K packed weight x prepared Q8_K activations -> fp32 [m, n]; with
+    resid: resid + gate * (w.x + bias) (out=resid updates it in place)."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=act.device)
+    rc = lib().b2q_mul_mat_prepared_q4_k(_ptr(packed), n, k, _ptr(act), m, _ptr(bias), _ptr(gate), _ptr(resid),
+                                         resid.stride(0) * 4 if resid is not None else 0, _ptr(out),
+                                         out.stride(0) * 4, _stream(stream))
+    _check("b2q_mul_mat_prepared_q4_k", rc)
     return out
 
 

@@ -83,23 +83,51 @@ int run_gemm(const SplitOperand& w, const SplitOperand& a, int64_t m, int64_t n,
 }
 
 // Activation quantize into the split layout + GEMM against a split weight.
-// k is the logical K; with B2Q_ACT_Q8_K (Q4_K weights) the split layouts of w
-// and of the activations span K' = 2k.
 int mul_mat_split(const SplitOperand& w, int64_t n, int64_t k, const float* x, int64_t m,
                   int64_t ldx, const float* bias, float* y, int64_t ldy, int variant, Carve& ws,
                   int sms, cudaStream_t s) {
-  const int64_t kp = variant == B2Q_ACT_Q8_K ? 2 * k : k;
-  uint8_t* abuf = ws.take(split_bytes(m, kp));
+  uint8_t* abuf = ws.take(split_bytes(m, k));
   if (!abuf) return B2Q_ERR_WORKSPACE;
-  SplitOperand a = split_at(abuf, m, kp);
+  SplitOperand a = split_at(abuf, m, k);
   const bool vec4 = aligned(x, 16) && ldx % 16 == 0;
-  cudaError_t e = variant == B2Q_ACT_Q8_K
-                      ? launch_quantize_q8_k_split(x, m, k, ldx / 4, const_cast<int8_t*>(a.codes),
-                                                   const_cast<float*>(a.scales), a.ld, vec4, s)
-                      : launch_quantize_q8_0_split(x, m, k, ldx / 4, const_cast<int8_t*>(a.codes),
-                                                   const_cast<float*>(a.scales), a.ld, variant, vec4, s);
+  cudaError_t e = launch_quantize_q8_0_split(x, m, k, ldx / 4, const_cast<int8_t*>(a.codes),
+                                             const_cast<float*>(a.scales), a.ld, variant, vec4, s);
   if (e != cudaSuccess) return B2Q_ERR_CUDA;
-  return run_gemm(w, a, m, n, kp, y, ldy / 4, bias, nullptr, sms, s);
+  return run_gemm(w, a, m, n, k, y, ldy / 4, bias, nullptr, sms, s);
+}
+
+// The Q4_K GEMM on prepared operands (plain, bias, gate, residual).
+int run_q4k(const Q4kWeight& w, const Q8kAct& a, int64_t m, int64_t n, int64_t k, const float* bias,
+            const float* gate, const float* resid, int64_t ldr, float* y, int64_t ldy, int sms, cudaStream_t s) {
+  Q4kArgs g;
+  g.w_codes = w.codes;
+  g.w_d = w.d;
+  g.w_dmin = w.dmin;
+  g.ldw = w.ld;
+  g.a_codes = a.codes;
+  g.a_d = a.d;
+  g.lda = a.ld;
+  g.M = m;
+  g.N = n;
+  g.K = k;
+  g.y = y;
+  g.ldy = ldy;
+  g.bias = bias;
+  g.gate = gate;
+  g.resid = resid;
+  g.ldr = ldr;
+  return from_cuda(launch_gemm_q4k(g, sms, s));
+}
+
+// Q8_K activation quantize + the Q4_K GEMM.
+int mul_mat_q4k(const Q4kWeight& w, int64_t n, int64_t k, const float* x, int64_t m, int64_t ldx,
+                const float* bias, float* y, int64_t ldy, Carve& ws, int sms, cudaStream_t s) {
+  uint8_t* abuf = ws.take(q8k_bytes(m, k));
+  if (!abuf) return B2Q_ERR_WORKSPACE;
+  const Q8kAct a = q8k_at(abuf, m, k);
+  const bool vec4 = aligned(x, 16) && ldx % 16 == 0;
+  if (launch_quantize_q8_k(x, m, k, ldx / 4, a.codes, a.d, a.ld, vec4, s) != cudaSuccess) return B2Q_ERR_CUDA;
+  return run_q4k(w, a, m, n, k, bias, nullptr, nullptr, 0, y, ldy / 4, sms, s);
 }
 
 int check_x_y(const float* x, int64_t m, int64_t k, int64_t ldx, float* y, int64_t n,
@@ -182,9 +210,41 @@ int b2q_quantize_q8_0(const float* x, int64_t nrows, int64_t k, int64_t x_row_st
                                                variant, vec4, static_cast<cudaStream_t>(stream)));
 }
 
-int64_t b2q_packed_k(int wtype, int64_t k) {
-  if (!valid_wtype(wtype) || k <= 0 || k % (wtype == B2Q_TYPE_Q4_K ? kQKK : kQK) != 0) return 0;
-  return packed_k(wtype, k);
+size_t b2q_weight_packed_bytes(int wtype, int64_t n, int64_t k) {
+  if (!valid_wtype(wtype) || n < 0 || k <= 0 || k % (wtype == B2Q_TYPE_Q4_K ? kQKK : kQK) != 0) return 0;
+  return wtype == B2Q_TYPE_Q4_K ? q4k_bytes(n, k) : split_bytes(n, k);
+}
+
+size_t b2q_act_prepared_bytes(int variant, int64_t m, int64_t k) {
+  if (m < 0 || k <= 0 || k % kQK != 0) return 0;
+  if (variant == B2Q_ACT_Q8_K) return k % kQKK == 0 ? q8k_bytes(m, k) : 0;
+  return variant == B2Q_ACT_X86 || variant == B2Q_ACT_REF ? split_bytes(m, k) : 0;
+}
+
+size_t b2q_mul_mat_workspace_bytes(int wtype, int64_t m, int64_t n, int64_t k, int packed_weight) {
+  if (wtype != B2Q_TYPE_Q4_K) return valid_wtype(wtype) ? b2q_mul_mat_workspace_size(m, n, k, packed_weight) : 0;
+  if (m < 0 || n < 0 || k <= 0 || k % kQKK != 0) return 0;
+  return q8k_bytes(m, k) + (packed_weight ? 0 : q4k_bytes(n, k));
+}
+
+int b2q_mul_mat_prepared_q4_k(const void* packed, int64_t n, int64_t k, const void* act, int64_t m,
+                              const float* bias, const float* gate, const float* resid,
+                              int64_t resid_row_stride_bytes, float* y, int64_t y_row_stride_bytes, void* stream) {
+  if (n < 0 || m < 0 || k <= 0 || k % kQKK != 0) return B2Q_ERR_INVALID_ARG;
+  if (n > INT_MAX / 3 || m > INT_MAX || k > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (m > 0 && n > 0 && (!packed || !act || !y)) return B2Q_ERR_INVALID_ARG;
+  if (y_row_stride_bytes < n * 4 || (resid && resid_row_stride_bytes < n * 4)) return B2Q_ERR_INVALID_ARG;
+  if (resid == y && resid && resid_row_stride_bytes != y_row_stride_bytes) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(packed, 256) || !aligned(act, 256) || !aligned(y, 4) || y_row_stride_bytes % 4 != 0 ||
+      (resid && (!aligned(resid, 4) || resid_row_stride_bytes % 4 != 0)) || (bias && !aligned(bias, 4)) ||
+      (gate && !aligned(gate, 4)))
+    return B2Q_ERR_MISALIGNED;
+  if (m == 0 || n == 0) return B2Q_OK;
+  int sms = 0;
+  if (int rc = check_device(&sms)) return rc;
+  return run_q4k(q4k_at(static_cast<uint8_t*>(const_cast<void*>(packed)), n, k),
+                 q8k_at(static_cast<uint8_t*>(const_cast<void*>(act)), m, k), m, n, k, bias, gate, resid,
+                 resid_row_stride_bytes / 4, y, y_row_stride_bytes / 4, sms, static_cast<cudaStream_t>(stream));
 }
 
 size_t b2q_weight_packed_size(int64_t n, int64_t k) {
@@ -196,11 +256,15 @@ int b2q_weight_pack(int wtype, const void* w, int64_t n, int64_t k, int64_t w_ro
                     void* packed, size_t packed_bytes, void* stream) {
   if (int rc = check_raw_weight(wtype, w, w_row_stride_bytes, n, k)) return rc;
   if (n > 0 && !packed) return B2Q_ERR_INVALID_ARG;
-  const int64_t kp = packed_k(wtype, k);
-  if (packed_bytes < split_bytes(n, kp)) return B2Q_ERR_WORKSPACE;
+  if (packed_bytes < (wtype == B2Q_TYPE_Q4_K ? q4k_bytes(n, k) : split_bytes(n, k))) return B2Q_ERR_WORKSPACE;
   if (!aligned(packed, 256)) return B2Q_ERR_MISALIGNED;
   if (int rc = check_device(nullptr)) return rc;
-  SplitOperand s = split_at(static_cast<uint8_t*>(packed), n, kp);
+  if (wtype == B2Q_TYPE_Q4_K) {
+    const Q4kWeight q = q4k_at(static_cast<uint8_t*>(packed), n, k);
+    return from_cuda(launch_pack_q4k(static_cast<const uint8_t*>(w), n, k, w_row_stride_bytes, q.codes, n * k, q.d,
+                                     q.dmin, q.ld, static_cast<cudaStream_t>(stream)));
+  }
+  SplitOperand s = split_at(static_cast<uint8_t*>(packed), n, k);
   return from_cuda(launch_pack_weights(wtype, static_cast<const uint8_t*>(w), n, k, w_row_stride_bytes,
                                        const_cast<int8_t*>(s.codes), const_cast<float*>(s.scales),
                                        s.ld, static_cast<cudaStream_t>(stream)));
@@ -210,15 +274,16 @@ int b2q_weight_upload(int wtype, const void* host_w, int64_t n, int64_t k, int64
                       void* staging, size_t staging_bytes, void* packed, size_t packed_bytes, void* stream) {
   if (int rc = check_raw_weight(wtype, host_w, w_row_stride_bytes, n, k)) return rc;
   if (n > 0 && (!packed || !staging)) return B2Q_ERR_INVALID_ARG;
-  const int64_t kp = packed_k(wtype, k);
-  if (packed_bytes < split_bytes(n, kp)) return B2Q_ERR_WORKSPACE;
+  const bool kq = wtype == B2Q_TYPE_Q4_K;
+  if (packed_bytes < (kq ? q4k_bytes(n, k) : split_bytes(n, k))) return B2Q_ERR_WORKSPACE;
   const int64_t row_bytes = raw_row_bytes(wtype, k);
   if (n > 0 && staging_bytes < static_cast<size_t>(row_bytes)) return B2Q_ERR_WORKSPACE;
   if (!aligned(packed, 256) || !aligned(staging, 2)) return B2Q_ERR_MISALIGNED;
   if (n == 0) return B2Q_OK;
   if (int rc = check_device(nullptr)) return rc;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const SplitOperand out = split_at(static_cast<uint8_t*>(packed), n, kp);
+  const SplitOperand out = split_at(static_cast<uint8_t*>(packed), n, k);
+  const Q4kWeight q = q4k_at(static_cast<uint8_t*>(packed), n, k);
   const int64_t chunk = static_cast<int64_t>(staging_bytes / static_cast<size_t>(row_bytes));
   const uint8_t* src = static_cast<const uint8_t*>(host_w);
   for (int64_t r0 = 0; r0 < n; r0 += chunk) {
@@ -226,10 +291,13 @@ int b2q_weight_upload(int wtype, const void* host_w, int64_t n, int64_t k, int64
     if (cudaMemcpy2DAsync(staging, row_bytes, src + r0 * w_row_stride_bytes, w_row_stride_bytes, row_bytes, rows,
                           cudaMemcpyHostToDevice, s) != cudaSuccess)
       return B2Q_ERR_CUDA;
-    if (launch_pack_weights(wtype, static_cast<const uint8_t*>(staging), rows, k, row_bytes,
-                            const_cast<int8_t*>(out.codes) + r0 * kp, const_cast<float*>(out.scales) + r0, out.ld,
-                            s) != cudaSuccess)
-      return B2Q_ERR_CUDA;
+    const cudaError_t e =
+        kq ? launch_pack_q4k(static_cast<const uint8_t*>(staging), rows, k, row_bytes, q.codes + r0 * k, n * k,
+                             q.d + r0, q.dmin + r0, q.ld, s)
+           : launch_pack_weights(wtype, static_cast<const uint8_t*>(staging), rows, k, row_bytes,
+                                 const_cast<int8_t*>(out.codes) + r0 * k, const_cast<float*>(out.scales) + r0, out.ld,
+                                 s);
+    if (e != cudaSuccess) return B2Q_ERR_CUDA;
   }
   return B2Q_OK;
 }
@@ -254,8 +322,10 @@ int b2q_mul_mat_packed(const void* packed, int64_t n, int64_t k, const float* x,
   int sms = 0;
   if (int rc = check_device(&sms)) return rc;
   Carve ws{static_cast<uint8_t*>(workspace), workspace_bytes};
-  const int64_t kp = variant == B2Q_ACT_Q8_K ? 2 * k : k;  // Q8_K activations <=> Q4_K-packed weight
-  const SplitOperand w = split_at(static_cast<uint8_t*>(const_cast<void*>(packed)), n, kp);
+  if (variant == B2Q_ACT_Q8_K)  // Q8_K activations <=> a Q4_K-packed weight
+    return mul_mat_q4k(q4k_at(static_cast<uint8_t*>(const_cast<void*>(packed)), n, k), n, k, x, m,
+                       x_row_stride_bytes, bias, y, y_row_stride_bytes, ws, sms, static_cast<cudaStream_t>(stream));
+  const SplitOperand w = split_at(static_cast<uint8_t*>(const_cast<void*>(packed)), n, k);
   return mul_mat_split(w, n, k, x, m, x_row_stride_bytes, bias, y, y_row_stride_bytes, variant, ws,
                        sms, static_cast<cudaStream_t>(stream));
 }
@@ -274,10 +344,18 @@ int b2q_mul_mat(int wtype, const void* w, int64_t w_row_stride_bytes, int64_t n,
   if (int rc = check_device(&sms)) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   Carve ws{static_cast<uint8_t*>(workspace), workspace_bytes};
-  const int64_t kp = packed_k(wtype, k);
-  uint8_t* wbuf = ws.take(split_bytes(n, kp));
+  if (wtype == B2Q_TYPE_Q4_K) {
+    uint8_t* qbuf = ws.take(q4k_bytes(n, k));
+    if (!qbuf) return B2Q_ERR_WORKSPACE;
+    const Q4kWeight q = q4k_at(qbuf, n, k);
+    if (launch_pack_q4k(static_cast<const uint8_t*>(w), n, k, w_row_stride_bytes, q.codes, n * k, q.d, q.dmin, q.ld,
+                        s) != cudaSuccess)
+      return B2Q_ERR_CUDA;
+    return mul_mat_q4k(q, n, k, x, m, x_row_stride_bytes, bias, y, y_row_stride_bytes, ws, sms, s);
+  }
+  uint8_t* wbuf = ws.take(split_bytes(n, k));
   if (!wbuf) return B2Q_ERR_WORKSPACE;
-  const SplitOperand wsplit = split_at(wbuf, n, kp);
+  const SplitOperand wsplit = split_at(wbuf, n, k);
   if (launch_pack_weights(wtype, static_cast<const uint8_t*>(w), n, k, w_row_stride_bytes,
                           const_cast<int8_t*>(wsplit.codes), const_cast<float*>(wsplit.scales),
                           wsplit.ld, s) != cudaSuccess)
@@ -301,16 +379,17 @@ int b2q_act_prepare(const float* x, int64_t m, int64_t k, int64_t x_row_stride_b
   if (m > 0 && (!x || !act)) return B2Q_ERR_INVALID_ARG;
   if (x_row_stride_bytes < k * 4) return B2Q_ERR_INVALID_ARG;
   if (!aligned(x, 4) || x_row_stride_bytes % 4 != 0 || !aligned(act, 256)) return B2Q_ERR_MISALIGNED;
-  const int64_t kp = variant == B2Q_ACT_Q8_K ? 2 * k : k;
-  if (act_bytes < split_bytes(m, kp)) return B2Q_ERR_WORKSPACE;
+  const bool kq = variant == B2Q_ACT_Q8_K;
+  if (act_bytes < (kq ? q8k_bytes(m, k) : split_bytes(m, k))) return B2Q_ERR_WORKSPACE;
   if (m == 0) return B2Q_OK;
   if (int rc = check_device(nullptr)) return rc;
-  const SplitOperand a = split_at(static_cast<uint8_t*>(act), m, kp);
   const bool vec4 = aligned(x, 16) && x_row_stride_bytes % 16 == 0;
-  if (variant == B2Q_ACT_Q8_K)
-    return from_cuda(launch_quantize_q8_k_split(x, m, k, x_row_stride_bytes / 4, const_cast<int8_t*>(a.codes),
-                                                const_cast<float*>(a.scales), a.ld, vec4,
-                                                static_cast<cudaStream_t>(stream)));
+  if (kq) {
+    const Q8kAct q = q8k_at(static_cast<uint8_t*>(act), m, k);
+    return from_cuda(launch_quantize_q8_k(x, m, k, x_row_stride_bytes / 4, q.codes, q.d, q.ld, vec4,
+                                          static_cast<cudaStream_t>(stream)));
+  }
+  const SplitOperand a = split_at(static_cast<uint8_t*>(act), m, k);
   return from_cuda(launch_quantize_q8_0_split(x, m, k, x_row_stride_bytes / 4,
                                               const_cast<int8_t*>(a.codes),
                                               const_cast<float*>(a.scales), a.ld, variant, vec4,

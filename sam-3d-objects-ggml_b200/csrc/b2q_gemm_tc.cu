@@ -696,6 +696,12 @@ cudaError_t launch_picked(const GemmArgs& g, int num_sms, cudaStream_t s) {
   }
 }
 
+bool make_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
+                        uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                        CUtensorMapSwizzle swz) {
+  return make_map_2d(map, dt, base, inner, outer, row_stride_bytes, box_inner, box_outer, swz);
+}
+
 cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, cudaStream_t s) {
   if (g.M == 0 || g.N == 0) return cudaSuccess;
   if (g.dots) return launch_cfg<4, 128, kModeDump>(g, num_sms, s);
@@ -712,3 +718,6 @@ cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, cudaStream_t s) {
 }
 
 }  // namespace b2q
+
+// The Q4_K kernel shares this translation unit (and g_device_status).
+#include "b2q_gemm_q4k.cuh"

@@ -26,10 +26,20 @@ constexpr int kTypeQ8_0 = 8;
 constexpr int kTypeQ4_K = 12;  // ggml's k-quant, 256-value super-blocks (144 bytes)
 constexpr int kQKK = 256;
 constexpr int kQ4KBytes = 144;
-// Q4_K weights run on the same GEMM over K' = 2K: each 32-value sub-block
-// becomes a block of quants and a block of ones (the min term), against the
-// Q8_K activation sub-block duplicated (b2q_quantize.cu).
-inline int64_t packed_k(int wtype, int64_t k) { return wtype == kTypeQ4_K ? 2 * k : k; }
+// Q4_K packed ("planes") layout, base 256-byte aligned:
+//   codes int8 [3][n][k] | d fp32 [k/256][scale_ld(n)] | dmin fp32 [k/256][scale_ld(n)]
+// Q8_K prepared activations: codes int8 [m][k] | d fp32 [k/256][scale_ld(m)].
+struct Q4kWeight {
+  int8_t* codes;
+  float* d;
+  float* dmin;
+  int64_t ld;
+};
+struct Q8kAct {
+  int8_t* codes;
+  float* d;
+  int64_t ld;
+};
 
 inline int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 
@@ -53,6 +63,27 @@ inline int64_t scale_ld(int64_t rows) { return round_up(rows, 4); }
 inline size_t split_bytes(int64_t rows, int64_t k) {
   return static_cast<size_t>(round_up(rows * k, 256) + round_up((k / kQK) * scale_ld(rows) * 4, 256));
 }
+inline size_t q4k_bytes(int64_t n, int64_t k) {
+  return static_cast<size_t>(round_up(3 * n * k, 256) + 2 * round_up((k / kQKK) * scale_ld(n) * 4, 256));
+}
+inline size_t q8k_bytes(int64_t m, int64_t k) {
+  return static_cast<size_t>(round_up(m * k, 256) + round_up((k / kQKK) * scale_ld(m) * 4, 256));
+}
+inline Q4kWeight q4k_at(uint8_t* base, int64_t n, int64_t k) {
+  Q4kWeight w;
+  w.codes = reinterpret_cast<int8_t*>(base);
+  w.d = reinterpret_cast<float*>(base + round_up(3 * n * k, 256));
+  w.dmin = reinterpret_cast<float*>(base + round_up(3 * n * k, 256) + round_up((k / kQKK) * scale_ld(n) * 4, 256));
+  w.ld = scale_ld(n);
+  return w;
+}
+inline Q8kAct q8k_at(uint8_t* base, int64_t m, int64_t k) {
+  Q8kAct a;
+  a.codes = reinterpret_cast<int8_t*>(base);
+  a.d = reinterpret_cast<float*>(base + round_up(m * k, 256));
+  a.ld = scale_ld(m);
+  return a;
+}
 
 // The current device and its SM count, cached per device after the first
 // query (the launch paths call this on every call).  Returns the SM count;
@@ -66,8 +97,10 @@ cudaError_t launch_quantize_q8_0_blocks(const float* x, int64_t m, int64_t k, in
 cudaError_t launch_quantize_q8_0_split(const float* x, int64_t m, int64_t k, int64_t ldx_floats,
                                        int8_t* codes, float* scales, int64_t ld, int variant,
                                        bool vec4, cudaStream_t s);
-cudaError_t launch_quantize_q8_k_split(const float* x, int64_t m, int64_t k, int64_t ldx_floats, int8_t* codes,
-                                       float* scales, int64_t ld, bool vec4, cudaStream_t s);
+cudaError_t launch_quantize_q8_k(const float* x, int64_t m, int64_t k, int64_t ldx_floats, int8_t* codes,
+                                 float* dq, int64_t ld, bool vec4, cudaStream_t s);
+cudaError_t launch_pack_q4k(const uint8_t* w, int64_t n, int64_t k, int64_t ldw_bytes, int8_t* codes,
+                            int64_t plane_stride, float* dsc, float* dmn, int64_t ld, cudaStream_t s);
 cudaError_t launch_pack_weights(int wtype, const uint8_t* w, int64_t n, int64_t k,
                                 int64_t ldw_bytes, int8_t* codes, float* scales, int64_t ld,
                                 cudaStream_t s);
@@ -112,6 +145,33 @@ struct GemmArgs {
   int64_t ldr = 0;
 };
 cudaError_t launch_gemm_tc(const GemmArgs& args, int num_sms, cudaStream_t s);
+// 2-D tensor map (cuTensorMapEncodeTiled through the runtime's driver entry point).
+bool make_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
+                        uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                        CUtensorMapSwizzle swz);
+
+// Q4_K x Q8_K GEMM on the three-plane layout (b2q_gemm_q4k.cu):
+//   weight: int8 planes [3][N][K] (q4*(sc&7), q4*(sc>>3), m), fp32 d and dmin [K/256][ldw];
+//   activations: int8 Q8_K codes [M][K], fp32 d [K/256][lda].
+// y = w.x (+ bias), or resid + gate * (w.x + bias) when resid is set.
+struct Q4kArgs {
+  const int8_t* w_codes;
+  const float* w_d;
+  const float* w_dmin;
+  int64_t ldw;
+  const int8_t* a_codes;
+  const float* a_d;
+  int64_t lda;
+  int64_t M, N, K;
+  float* y;
+  int64_t ldy;
+  const float* bias = nullptr;
+  const float* gate = nullptr;
+  const float* resid = nullptr;
+  int64_t ldr = 0;
+};
+cudaError_t launch_gemm_q4k(const Q4kArgs& args, int num_sms, cudaStream_t s);
+
 // CUDA-core kernel for M <= kGemvMaxM tokens (plain, bias, gate + residual);
 // bit-identical to the tensor-core kernel (b2q_gemv.cu).
 constexpr int64_t kGemvMaxM = 8;

@@ -66,7 +66,8 @@ extern "C" int b2q_mul_mat_packed_noalloc(const void* packed, int64_t n, int64_t
                                           void* stream) {
   if (n < 0 || m < 0 || k <= 0 || k % kQK != 0) return B2Q_ERR_INVALID_ARG;
   if (n > INT_MAX || m > INT_MAX || k > INT_MAX) return B2Q_ERR_TOO_LARGE;
-  if (split_bytes(m, variant == B2Q_ACT_Q8_K ? 2 * k : k) > kScratchBytes) return B2Q_ERR_TOO_LARGE;
+  if (variant == B2Q_ACT_Q8_K && k % kQKK != 0) return B2Q_ERR_INVALID_ARG;
+  if ((variant == B2Q_ACT_Q8_K ? q8k_bytes(m, k) : split_bytes(m, k)) > kScratchBytes) return B2Q_ERR_TOO_LARGE;
   uint8_t* scratch = nullptr;
   if (m > 0 && n > 0) {
     if (int rc = scratch_on_current_device(&scratch)) return rc;

@@ -196,28 +196,24 @@ cudaError_t launch_gelu(const float* x, int64_t rows, int64_t cols, int64_t ldx_
 }
 
 // ------------------------------------------------------------------- Q4_K
-// Q4_K rows -> the split layout over K' = 2K.  Sub-block j (32 values) of a
-// row becomes two 32-value blocks of K':
-//   block 2j:   the 4-bit quants q (0..15), scale  d * sc_j
-//   block 2j+1: 32 ones,                    scale -(dmin * m_j)
-// so that against the Q8_K activation block a (duplicated into both) the
-// ordinary per-block fold gives d*sc_j*sum(q*a) - dmin*m_j*sum(a): the Q4_K
-// dot's two terms (value = d*sc_j*q - dmin*m_j).  Block layout and the 6-bit
-// scale/min unpacking are ggml's block_q4_K (see oracle/b2q_oracle_k.c).
-// One thread per (row, sub-block); byte loads (a raw row only needs 2-byte
-// alignment), 16-byte stores.
+// Q4_K rows -> the three-plane layout of the Q4_K GEMM (b2q_gemm_q4k.cuh):
+//   plane 0: q * (sc_j & 7), plane 1: q * (sc_j >> 3), plane 2: m_j   (int8 [N][K] each)
+//   d, dmin of each super-block as fp32 [K/256][ld]
+// for quants q (0..15) and the 6-bit scale sc_j and min m_j of sub-block j.
+// Block layout and scale/min unpacking are ggml's block_q4_K (see
+// oracle/b2q_oracle_k.c).  One thread per (row, sub-block); byte loads (a raw
+// row only needs 2-byte alignment), 16-byte stores.
 __global__ void __launch_bounds__(256) pack_q4k_kernel(const uint8_t* __restrict__ w, int64_t n, int64_t k,
                                                        int64_t ldw, int8_t* __restrict__ codes,
-                                                       float* __restrict__ scales, int64_t ld) {
-  const int64_t nsub = k / kQK, kp = 2 * k;
+                                                       int64_t plane_stride, float* __restrict__ dsc,
+                                                       float* __restrict__ dmn, int64_t ld) {
+  const int64_t nsub = k / kQK;
   const int64_t total = n * nsub;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t row = i / nsub, js = i - row * nsub;
     const int j = static_cast<int>(js & 7);
     const uint8_t* b = w + row * ldw + (js >> 3) * kQ4KBytes;
-    const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(b[0] | (b[1] << 8))));
-    const float dmin = __half2float(__ushort_as_half(static_cast<unsigned short>(b[2] | (b[3] << 8))));
     const uint8_t* sm = b + 4;
     int sc, mn;
     if (j < 4) {
@@ -227,41 +223,52 @@ __global__ void __launch_bounds__(256) pack_q4k_kernel(const uint8_t* __restrict
       sc = (sm[j + 4] & 15) | ((sm[j - 4] >> 6) << 4);
       mn = (sm[j + 4] >> 4) | ((sm[j] >> 6) << 4);
     }
+    const uint32_t lo = static_cast<uint32_t>(sc & 7), hi = static_cast<uint32_t>(sc >> 3);
     const uint8_t* q = b + 16 + 32 * (j >> 1);
-    uint32_t word[8];
+    uint32_t w1[8], w2[8];
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
-      uint32_t v = 0;
+      uint32_t v1 = 0, v2 = 0;
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const uint32_t byte = q[4 * t + u];
-        v |= ((j & 1) ? (byte >> 4) : (byte & 15u)) << (8 * u);
+        const uint32_t qq = (j & 1) ? (byte >> 4) : (byte & 15u);
+        v1 |= (qq * lo) << (8 * u);
+        v2 |= (qq * hi) << (8 * u);
       }
-      word[t] = v;
+      w1[t] = v1;
+      w2[t] = v2;
     }
-    uint4* dst = reinterpret_cast<uint4*>(codes + row * kp + 64 * js);
-    dst[0] = make_uint4(word[0], word[1], word[2], word[3]);
-    dst[1] = make_uint4(word[4], word[5], word[6], word[7]);
-    dst[2] = make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u);
-    dst[3] = dst[2];
-    scales[(2 * js) * ld + row] = __fmul_rn(d, static_cast<float>(sc)) * kWeightScaleMul;
-    scales[(2 * js + 1) * ld + row] = -__fmul_rn(dmin, static_cast<float>(mn)) * kWeightScaleMul;
+    const uint32_t m4 = static_cast<uint32_t>(mn) * 0x01010101u;
+    int8_t* base = codes + row * k + 32 * js;
+    uint4* d0 = reinterpret_cast<uint4*>(base);
+    uint4* d1 = reinterpret_cast<uint4*>(base + plane_stride);
+    uint4* d2 = reinterpret_cast<uint4*>(base + 2 * plane_stride);
+    d0[0] = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+    d0[1] = make_uint4(w1[4], w1[5], w1[6], w1[7]);
+    d1[0] = make_uint4(w2[0], w2[1], w2[2], w2[3]);
+    d1[1] = make_uint4(w2[4], w2[5], w2[6], w2[7]);
+    d2[0] = make_uint4(m4, m4, m4, m4);
+    d2[1] = d2[0];
+    if (j == 0) {
+      dsc[(js >> 3) * ld + row] = __half2float(__ushort_as_half(static_cast<unsigned short>(b[0] | (b[1] << 8))));
+      dmn[(js >> 3) * ld + row] = __half2float(__ushort_as_half(static_cast<unsigned short>(b[2] | (b[3] << 8))));
+    }
   }
 }
 
 // fp32 activations -> Q8_K (ggml's reference quantizer, per 256 values: the
 // value of largest |x|, first in scan order, sets iscale = -127/max; codes
 // min(127, round-half-even(iscale * x)); d = 1/iscale; all-zero blocks give
-// d = 0 and zero codes) in the split layout over K' = 2K: each 32-value
-// sub-block's codes twice (blocks 2j and 2j+1, matching pack_q4k_kernel), the
-// fp32 d (not fp16-rounded: Q8_K stores fp32) times 2^49 for both.
-// One warp per (row, 256-value block), 8 consecutive values per lane.
+// d = 0 and zero codes): codes int8 [M][K], d fp32 [K/256][ld].  The block
+// sums of block_q8_K are not stored: the Q4_K GEMM gets them from its third
+// weight plane.  One warp per (row, 256-value block), 8 values per lane.
 template <bool VEC4>
 __global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restrict__ x, int64_t m, int64_t k,
                                                            int64_t ldx, int8_t* __restrict__ codes,
-                                                           float* __restrict__ scales, int64_t ld) {
+                                                           float* __restrict__ dq, int64_t ld) {
   const int lane = threadIdx.x & 31;
-  const int64_t nsb = k / kQKK, kp = 2 * k;
+  const int64_t nsb = k / kQKK;
   const int64_t units = m * nsb;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
   for (int64_t u = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32; u < units; u += warps) {
@@ -312,15 +319,13 @@ __global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restri
       }
       d = __fdiv_rn(1.0f, iscale);
     }
-    int8_t* dst = codes + row * kp + 64 * (sb * 8 + lane / 4) + 8 * (lane % 4);
-    *reinterpret_cast<uint2*>(dst) = make_uint2(q0, q1);
-    *reinterpret_cast<uint2*>(dst + 32) = make_uint2(q0, q1);
-    if (lane < 16) scales[(16 * sb + lane) * ld + row] = d * kActScaleMul;
+    *reinterpret_cast<uint2*>(codes + row * k + sb * kQKK + 8 * lane) = make_uint2(q0, q1);
+    if (lane == 0) dq[sb * ld + row] = d;
   }
 }
 
-cudaError_t launch_quantize_q8_k_split(const float* x, int64_t m, int64_t k, int64_t ldx_floats, int8_t* codes,
-                                       float* scales, int64_t ld, bool vec4, cudaStream_t s) {
+cudaError_t launch_quantize_q8_k(const float* x, int64_t m, int64_t k, int64_t ldx_floats, int8_t* codes,
+                                 float* dq, int64_t ld, bool vec4, cudaStream_t s) {
   const int64_t units = m * (k / kQKK);
   if (units == 0) return cudaSuccess;
   int sms = current_device_sms();
@@ -328,9 +333,19 @@ cudaError_t launch_quantize_q8_k_split(const float* x, int64_t m, int64_t k, int
   const int64_t blocks = (units + 7) / 8;
   const int grid = static_cast<int>(blocks < sms * 8 ? blocks : sms * 8);
   if (vec4)
-    quantize_q8k_kernel<true><<<grid, 256, 0, s>>>(x, m, k, ldx_floats, codes, scales, ld);
+    quantize_q8k_kernel<true><<<grid, 256, 0, s>>>(x, m, k, ldx_floats, codes, dq, ld);
   else
-    quantize_q8k_kernel<false><<<grid, 256, 0, s>>>(x, m, k, ldx_floats, codes, scales, ld);
+    quantize_q8k_kernel<false><<<grid, 256, 0, s>>>(x, m, k, ldx_floats, codes, dq, ld);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pack_q4k(const uint8_t* w, int64_t n, int64_t k, int64_t ldw_bytes, int8_t* codes,
+                            int64_t plane_stride, float* dsc, float* dmn, int64_t ld, cudaStream_t s) {
+  const int64_t total = n * (k / kQK);
+  if (total == 0) return cudaSuccess;
+  const int64_t blocks = (total + 255) / 256;
+  const int grid = static_cast<int>(blocks < 65535 ? blocks : 65535);
+  pack_q4k_kernel<<<grid, 256, 0, s>>>(w, n, k, ldw_bytes, codes, plane_stride, dsc, dmn, ld);
   return cudaGetLastError();
 }
 
@@ -341,10 +356,6 @@ cudaError_t launch_pack_weights(int wtype, const uint8_t* w, int64_t n, int64_t 
   if (total == 0) return cudaSuccess;
   const int64_t blocks = (total + 255) / 256;
   const int grid = static_cast<int>(blocks < 65535 ? blocks : 65535);
-  if (wtype == kTypeQ4_K) {
-    pack_q4k_kernel<<<grid, 256, 0, s>>>(w, n, k, ldw_bytes, codes, scales, ld);
-    return cudaGetLastError();
-  }
   if (wtype == kTypeQ8_0)
     pack_weights_kernel<kTypeQ8_0><<<grid, 256, 0, s>>>(w, n, k, ldw_bytes, codes, scales, ld);
   else

@@ -179,16 +179,27 @@ def test_header_compiles_as_c(tmp_path):
 
 def test_q4_k_validation(b2q_mod):
     L = b2q.lib()
-    assert L.b2q_packed_k(12, 1024) == 2048 and L.b2q_packed_k(8, 1024) == 1024
-    assert L.b2q_packed_k(12, 96) == 0 and L.b2q_packed_k(3, 1024) == 0
+    # typed sizes: Q4_K packs three int8 planes plus two fp32 scale arrays; Q8_K one plane plus one
+    assert L.b2q_weight_packed_bytes(12, 64, 1024) == 3 * 64 * 1024 + 2 * 4 * 64 * 4
+    assert L.b2q_weight_packed_bytes(8, 64, 1024) == L.b2q_weight_packed_size(64, 1024)
+    assert L.b2q_weight_packed_bytes(12, 64, 96) == 0 and L.b2q_weight_packed_bytes(3, 64, 1024) == 0
+    assert L.b2q_act_prepared_bytes(2, 5, 512) == 5 * 512 + 256            # codes, then d [2][8] padded to 256
+    assert L.b2q_act_prepared_bytes(2, 4, 96) == 0 and L.b2q_act_prepared_bytes(0, 4, 96) == L.b2q_act_prepared_size(4, 96)
+    assert L.b2q_mul_mat_workspace_bytes(12, 4, 64, 1024, 1) == L.b2q_act_prepared_bytes(2, 4, 1024)
     big = 1 << 30
     # raw Q4_K: k % 256, the variant must be Q8_K and Q8_K only goes with Q4_K
     assert L.b2q_mul_mat(12, FAKE, 144 * 4, 64, 288, FAKE, 4, 4096, None, FAKE, 256, 2, FAKE, big, None) == 1
     assert L.b2q_mul_mat(12, FAKE, 144 * 4, 64, 1024, FAKE, 4, 4096, None, FAKE, 256, 0, FAKE, big, None) == 1
     assert L.b2q_mul_mat(8, FAKE, 1088, 64, 1024, FAKE, 4, 4096, None, FAKE, 256, 2, FAKE, big, None) == 1
     assert L.b2q_mul_mat(12, FAKE, 144 * 3, 64, 1024, FAKE, 4, 4096, None, FAKE, 256, 2, FAKE, big, None) == 1
-    # pack: the buffer must hold the K' = 2K layout
+    # pack: the buffer must hold the three-plane layout
     assert L.b2q_weight_pack(12, FAKE, 64, 1024, 576, FAKE, L.b2q_weight_packed_size(64, 1024), None) == 4
+    f = L.b2q_mul_mat_prepared_q4_k
+    assert f(FAKE, 64, 1000, FAKE, 4, None, None, None, 0, FAKE, 256, None) == 1   # k % 256
+    assert f(FAKE, 64, 1024, FAKE, 4, None, None, None, 0, FAKE, 128, None) == 1   # y stride
+    assert f(FAKE, 64, 1024, FAKE + 16, 4, None, None, None, 0, FAKE, 256, None) == 3
+    assert f(FAKE, 64, 1024, FAKE, 4, None, None, FAKE, 512, FAKE, 256, None) == 1  # aliased, strides differ
+    assert f(FAKE, 64, 1024, FAKE, 0, None, None, None, 0, FAKE, 256, None) == 0
     # debug check paths are for the 32-value block types
     assert L.b2q_block_dots(12, FAKE, 576, 64, 1024, FAKE, 4, 1088, FAKE, FAKE, big, None) == 2
     assert L.b2q_mul_mat_q_simt(12, FAKE, 576, 64, 1024, FAKE, 4, 1088, FAKE, 256, None) == 2
