@@ -352,6 +352,7 @@ def run_gpu(args, rank, world, local_rank):
     }
     if not args.only and not args.no_mlp:
         result["mlp_branch"] = mlp_branch(b2q, gemms, flush, stream, dev)
+        result["q4_k"] = q4_k_side(b2q, gemms, flush, stream, dev)
     if args.only:
         result["config"]["workload"] = f"single GEMM {args.only} (profiling case)"
         result["config"]["l2"] = "not flushed (profiling case)"
@@ -463,6 +464,46 @@ def mlp_branch(b2q, gemms, flush, stream, dev, iters=10):
             "path": "unfused: norm_modulate -> act_prepare -> mul_mat_prepared(+b1) -> gelu -> act_prepare -> "
                     "mul_mat_prepared(+b2) -> mul(gate) -> add(residual); fused: norm_modulate_q8 -> "
                     "mul_mat_prepared_gelu_q8(+b1) -> mul_mat_prepared_gate_residual(+b2, gate, in place)"}
+
+
+# ------------------------------------------------ Q4_K (the shipped format)
+def q4_k_side(b2q, gemms, flush, stream, dev, iters=10):
+    """The fc1 and fc2 GEMMs of the workload with Q4_K weights (the 4-bit
+    format the reference ships, cpp_ggml/models/MODEL_CARD.md:54-74) against
+    Q8_K activations: GEMM and quantize time with the L2 flushed, beside the
+    headline (not part of `value`).  Weights are seeded random valid Q4_K
+    blocks."""
+    import torch
+    import oracle as O
+    out = []
+    for g in gemms:
+        if g["name"] not in ("fc1_q4_0", "fc2_q4_0") or g["K"] % 256:
+            continue
+        M, N, K = g["M"], g["N"], g["K"]
+        packed = b2q.weight_pack(b2q.TYPE_Q4_K, torch.from_numpy(O.random_q4_k(N, K, seed=N + K)).to(dev), K)
+        act = b2q.act_prepare(g["x_dev"], b2q.ACT_Q8_K, stream=stream)
+        y = torch.empty((M, N), dtype=torch.float32, device=dev)
+
+        def timed(fn):
+            for _ in range(3):
+                fn()
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(iters)]
+            for e0, e1 in evs:
+                flush.zero_()
+                e0.record(stream)
+                fn()
+                e1.record(stream)
+            torch.cuda.synchronize()
+            return statistics.median(e0.elapsed_time(e1) * 1e3 for e0, e1 in evs)
+
+        gu = timed(lambda: b2q.mul_mat_prepared_q4_k(packed, N, K, act, M, out=y, stream=stream))
+        qu = timed(lambda: b2q.act_prepare(g["x_dev"], b2q.ACT_Q8_K, out=act, stream=stream))
+        o = ops_of(M, N, K)
+        out.append({"name": g["name"].replace("q4_0", "q4_k"), "M": M, "N": N, "K": K,
+                    "gemm_us_median": round(gu, 2), "quantize_us_median": round(qu, 2),
+                    "gemm_tops": round(o / (gu * 1e-6) / 1e12, 1)})
+    return {"kernel": "gemm_q4k_kernel (three int8 planes, per-super-block fold)", "gemms": out}
 
 
 # ------------------------------------------------- column-parallel (multi-GPU)
