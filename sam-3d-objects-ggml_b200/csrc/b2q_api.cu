@@ -100,10 +100,8 @@ int mul_mat_split(const SplitOperand& w, int64_t n, int64_t k, const float* x, i
 int run_q4k(const Q4kWeight& w, const Q8kAct& a, int64_t m, int64_t n, int64_t k, const float* bias,
             const float* gate, const float* resid, int64_t ldr, float* y, int64_t ldy, int sms, cudaStream_t s) {
   Q4kArgs g;
-  g.w_codes = w.codes;
-  g.w_d = w.d;
-  g.w_dmin = w.dmin;
-  g.ldw = w.ld;
+  g.w_raw = w.raw;
+  g.ldw_bytes = w.row_bytes;
   g.a_codes = a.codes;
   g.a_d = a.d;
   g.lda = a.ld;
@@ -259,10 +257,10 @@ int b2q_weight_pack(int wtype, const void* w, int64_t n, int64_t k, int64_t w_ro
   if (packed_bytes < (wtype == B2Q_TYPE_Q4_K ? q4k_bytes(n, k) : split_bytes(n, k))) return B2Q_ERR_WORKSPACE;
   if (!aligned(packed, 256)) return B2Q_ERR_MISALIGNED;
   if (int rc = check_device(nullptr)) return rc;
-  if (wtype == B2Q_TYPE_Q4_K) {
-    const Q4kWeight q = q4k_at(static_cast<uint8_t*>(packed), n, k);
-    return from_cuda(launch_pack_q4k(static_cast<const uint8_t*>(w), n, k, w_row_stride_bytes, q.codes, n * k, q.d,
-                                     q.dmin, q.ld, static_cast<cudaStream_t>(stream)));
+  if (wtype == B2Q_TYPE_Q4_K) {  // the packed form is the rows themselves, contiguous and aligned
+    const int64_t rb = raw_row_bytes(wtype, k);
+    return from_cuda(cudaMemcpy2DAsync(packed, rb, w, w_row_stride_bytes, rb, n, cudaMemcpyDeviceToDevice,
+                                       static_cast<cudaStream_t>(stream)));
   }
   SplitOperand s = split_at(static_cast<uint8_t*>(packed), n, k);
   return from_cuda(launch_pack_weights(wtype, static_cast<const uint8_t*>(w), n, k, w_row_stride_bytes,
@@ -283,21 +281,20 @@ int b2q_weight_upload(int wtype, const void* host_w, int64_t n, int64_t k, int64
   if (int rc = check_device(nullptr)) return rc;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   const SplitOperand out = split_at(static_cast<uint8_t*>(packed), n, k);
-  const Q4kWeight q = q4k_at(static_cast<uint8_t*>(packed), n, k);
-  const int64_t chunk = static_cast<int64_t>(staging_bytes / static_cast<size_t>(row_bytes));
   const uint8_t* src = static_cast<const uint8_t*>(host_w);
+  if (kq)  // the packed form is the rows themselves: straight into place, no staging needed
+    return from_cuda(cudaMemcpy2DAsync(packed, row_bytes, src, w_row_stride_bytes, row_bytes, n,
+                                       cudaMemcpyHostToDevice, s));
+  const int64_t chunk = static_cast<int64_t>(staging_bytes / static_cast<size_t>(row_bytes));
   for (int64_t r0 = 0; r0 < n; r0 += chunk) {
     const int64_t rows = n - r0 < chunk ? n - r0 : chunk;
     if (cudaMemcpy2DAsync(staging, row_bytes, src + r0 * w_row_stride_bytes, w_row_stride_bytes, row_bytes, rows,
                           cudaMemcpyHostToDevice, s) != cudaSuccess)
       return B2Q_ERR_CUDA;
-    const cudaError_t e =
-        kq ? launch_pack_q4k(static_cast<const uint8_t*>(staging), rows, k, row_bytes, q.codes + r0 * k, n * k,
-                             q.d + r0, q.dmin + r0, q.ld, s)
-           : launch_pack_weights(wtype, static_cast<const uint8_t*>(staging), rows, k, row_bytes,
-                                 const_cast<int8_t*>(out.codes) + r0 * k, const_cast<float*>(out.scales) + r0, out.ld,
-                                 s);
-    if (e != cudaSuccess) return B2Q_ERR_CUDA;
+    if (launch_pack_weights(wtype, static_cast<const uint8_t*>(staging), rows, k, row_bytes,
+                            const_cast<int8_t*>(out.codes) + r0 * k, const_cast<float*>(out.scales) + r0, out.ld,
+                            s) != cudaSuccess)
+      return B2Q_ERR_CUDA;
   }
   return B2Q_OK;
 }
@@ -345,12 +342,18 @@ int b2q_mul_mat(int wtype, const void* w, int64_t w_row_stride_bytes, int64_t n,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   Carve ws{static_cast<uint8_t*>(workspace), workspace_bytes};
   if (wtype == B2Q_TYPE_Q4_K) {
+    // The GEMM reads the rows with the TMA: in place when 16-byte aligned,
+    // else from a contiguous copy in the workspace.
     uint8_t* qbuf = ws.take(q4k_bytes(n, k));
     if (!qbuf) return B2Q_ERR_WORKSPACE;
-    const Q4kWeight q = q4k_at(qbuf, n, k);
-    if (launch_pack_q4k(static_cast<const uint8_t*>(w), n, k, w_row_stride_bytes, q.codes, n * k, q.d, q.dmin, q.ld,
-                        s) != cudaSuccess)
+    Q4kWeight q = q4k_at(qbuf, n, k);
+    if (aligned(w, 16) && w_row_stride_bytes % 16 == 0) {
+      q.raw = static_cast<const uint8_t*>(w);
+      q.row_bytes = w_row_stride_bytes;
+    } else if (cudaMemcpy2DAsync(qbuf, q.row_bytes, w, w_row_stride_bytes, q.row_bytes, n, cudaMemcpyDeviceToDevice,
+                                 s) != cudaSuccess) {
       return B2Q_ERR_CUDA;
+    }
     return mul_mat_q4k(q, n, k, x, m, x_row_stride_bytes, bias, y, y_row_stride_bytes, ws, sms, s);
   }
   uint8_t* wbuf = ws.take(split_bytes(n, k));

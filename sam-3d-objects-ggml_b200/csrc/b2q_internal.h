@@ -26,14 +26,12 @@ constexpr int kTypeQ8_0 = 8;
 constexpr int kTypeQ4_K = 12;  // ggml's k-quant, 256-value super-blocks (144 bytes)
 constexpr int kQKK = 256;
 constexpr int kQ4KBytes = 144;
-// Q4_K packed ("planes") layout, base 256-byte aligned:
-//   codes int8 [3][n][k] | d fp32 [k/256][scale_ld(n)] | dmin fp32 [k/256][scale_ld(n)]
-// Q8_K prepared activations: codes int8 [m][k] | d fp32 [k/256][scale_ld(m)].
+// Q4_K packed layout: the GGUF block_q4_K rows themselves, contiguous
+// (k/256 * 144 bytes per row), base 256-byte aligned; the GEMM unpacks them on
+// chip.  Q8_K prepared activations: codes int8 [m][k] | d fp32 [k/256][scale_ld(m)].
 struct Q4kWeight {
-  int8_t* codes;
-  float* d;
-  float* dmin;
-  int64_t ld;
+  const uint8_t* raw;
+  int64_t row_bytes;
 };
 struct Q8kAct {
   int8_t* codes;
@@ -63,18 +61,15 @@ inline int64_t scale_ld(int64_t rows) { return round_up(rows, 4); }
 inline size_t split_bytes(int64_t rows, int64_t k) {
   return static_cast<size_t>(round_up(rows * k, 256) + round_up((k / kQK) * scale_ld(rows) * 4, 256));
 }
-inline size_t q4k_bytes(int64_t n, int64_t k) {
-  return static_cast<size_t>(round_up(3 * n * k, 256) + 2 * round_up((k / kQKK) * scale_ld(n) * 4, 256));
-}
+inline size_t q4k_bytes(int64_t n, int64_t k) { return static_cast<size_t>(round_up(n * (k / kQKK) * kQ4KBytes, 256)); }
 inline size_t q8k_bytes(int64_t m, int64_t k) {
   return static_cast<size_t>(round_up(m * k, 256) + round_up((k / kQKK) * scale_ld(m) * 4, 256));
 }
-inline Q4kWeight q4k_at(uint8_t* base, int64_t n, int64_t k) {
+inline Q4kWeight q4k_at(const uint8_t* base, int64_t n, int64_t k) {
+  (void)n;
   Q4kWeight w;
-  w.codes = reinterpret_cast<int8_t*>(base);
-  w.d = reinterpret_cast<float*>(base + round_up(3 * n * k, 256));
-  w.dmin = reinterpret_cast<float*>(base + round_up(3 * n * k, 256) + round_up((k / kQKK) * scale_ld(n) * 4, 256));
-  w.ld = scale_ld(n);
+  w.raw = base;
+  w.row_bytes = (k / kQKK) * kQ4KBytes;
   return w;
 }
 inline Q8kAct q8k_at(uint8_t* base, int64_t m, int64_t k) {
@@ -99,8 +94,7 @@ cudaError_t launch_quantize_q8_0_split(const float* x, int64_t m, int64_t k, int
                                        bool vec4, cudaStream_t s);
 cudaError_t launch_quantize_q8_k(const float* x, int64_t m, int64_t k, int64_t ldx_floats, int8_t* codes,
                                  float* dq, int64_t ld, bool vec4, cudaStream_t s);
-cudaError_t launch_pack_q4k(const uint8_t* w, int64_t n, int64_t k, int64_t ldw_bytes, int8_t* codes,
-                            int64_t plane_stride, float* dsc, float* dmn, int64_t ld, cudaStream_t s);
+
 cudaError_t launch_pack_weights(int wtype, const uint8_t* w, int64_t n, int64_t k,
                                 int64_t ldw_bytes, int8_t* codes, float* scales, int64_t ld,
                                 cudaStream_t s);
@@ -150,15 +144,13 @@ bool make_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* ba
                         uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                         CUtensorMapSwizzle swz);
 
-// Q4_K x Q8_K GEMM on the three-plane layout (b2q_gemm_q4k.cu):
-//   weight: int8 planes [3][N][K] (q4*(sc&7), q4*(sc>>3), m), fp32 d and dmin [K/256][ldw];
+// Q4_K x Q8_K GEMM (b2q_gemm_q4k.cuh):
+//   weight: block_q4_K rows, ldw_bytes apart (16-byte aligned base and stride);
 //   activations: int8 Q8_K codes [M][K], fp32 d [K/256][lda].
 // y = w.x (+ bias), or resid + gate * (w.x + bias) when resid is set.
 struct Q4kArgs {
-  const int8_t* w_codes;
-  const float* w_d;
-  const float* w_dmin;
-  int64_t ldw;
+  const uint8_t* w_raw;
+  int64_t ldw_bytes;
   const int8_t* a_codes;
   const float* a_d;
   int64_t lda;

@@ -196,67 +196,6 @@ cudaError_t launch_gelu(const float* x, int64_t rows, int64_t cols, int64_t ldx_
 }
 
 // ------------------------------------------------------------------- Q4_K
-// Q4_K rows -> the three-plane layout of the Q4_K GEMM (b2q_gemm_q4k.cuh):
-//   plane 0: q * (sc_j & 7), plane 1: q * (sc_j >> 3), plane 2: m_j   (int8 [N][K] each)
-//   d, dmin of each super-block as fp32 [K/256][ld]
-// for quants q (0..15) and the 6-bit scale sc_j and min m_j of sub-block j.
-// Block layout and scale/min unpacking are ggml's block_q4_K (see
-// oracle/b2q_oracle_k.c).  One thread per (row, sub-block); byte loads (a raw
-// row only needs 2-byte alignment), 16-byte stores.
-__global__ void __launch_bounds__(256) pack_q4k_kernel(const uint8_t* __restrict__ w, int64_t n, int64_t k,
-                                                       int64_t ldw, int8_t* __restrict__ codes,
-                                                       int64_t plane_stride, float* __restrict__ dsc,
-                                                       float* __restrict__ dmn, int64_t ld) {
-  const int64_t nsub = k / kQK;
-  const int64_t total = n * nsub;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t row = i / nsub, js = i - row * nsub;
-    const int j = static_cast<int>(js & 7);
-    const uint8_t* b = w + row * ldw + (js >> 3) * kQ4KBytes;
-    const uint8_t* sm = b + 4;
-    int sc, mn;
-    if (j < 4) {
-      sc = sm[j] & 63;
-      mn = sm[j + 4] & 63;
-    } else {
-      sc = (sm[j + 4] & 15) | ((sm[j - 4] >> 6) << 4);
-      mn = (sm[j + 4] >> 4) | ((sm[j] >> 6) << 4);
-    }
-    const uint32_t lo = static_cast<uint32_t>(sc & 7), hi = static_cast<uint32_t>(sc >> 3);
-    const uint8_t* q = b + 16 + 32 * (j >> 1);
-    uint32_t w1[8], w2[8];
-#pragma unroll
-    for (int t = 0; t < 8; ++t) {
-      uint32_t v1 = 0, v2 = 0;
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const uint32_t byte = q[4 * t + u];
-        const uint32_t qq = (j & 1) ? (byte >> 4) : (byte & 15u);
-        v1 |= (qq * lo) << (8 * u);
-        v2 |= (qq * hi) << (8 * u);
-      }
-      w1[t] = v1;
-      w2[t] = v2;
-    }
-    const uint32_t m4 = static_cast<uint32_t>(mn) * 0x01010101u;
-    int8_t* base = codes + row * k + 32 * js;
-    uint4* d0 = reinterpret_cast<uint4*>(base);
-    uint4* d1 = reinterpret_cast<uint4*>(base + plane_stride);
-    uint4* d2 = reinterpret_cast<uint4*>(base + 2 * plane_stride);
-    d0[0] = make_uint4(w1[0], w1[1], w1[2], w1[3]);
-    d0[1] = make_uint4(w1[4], w1[5], w1[6], w1[7]);
-    d1[0] = make_uint4(w2[0], w2[1], w2[2], w2[3]);
-    d1[1] = make_uint4(w2[4], w2[5], w2[6], w2[7]);
-    d2[0] = make_uint4(m4, m4, m4, m4);
-    d2[1] = d2[0];
-    if (j == 0) {
-      dsc[(js >> 3) * ld + row] = __half2float(__ushort_as_half(static_cast<unsigned short>(b[0] | (b[1] << 8))));
-      dmn[(js >> 3) * ld + row] = __half2float(__ushort_as_half(static_cast<unsigned short>(b[2] | (b[3] << 8))));
-    }
-  }
-}
-
 // fp32 activations -> Q8_K (ggml's reference quantizer, per 256 values: the
 // value of largest |x|, first in scan order, sets iscale = -127/max; codes
 // min(127, round-half-even(iscale * x)); d = 1/iscale; all-zero blocks give
@@ -336,16 +275,6 @@ cudaError_t launch_quantize_q8_k(const float* x, int64_t m, int64_t k, int64_t l
     quantize_q8k_kernel<true><<<grid, 256, 0, s>>>(x, m, k, ldx_floats, codes, dq, ld);
   else
     quantize_q8k_kernel<false><<<grid, 256, 0, s>>>(x, m, k, ldx_floats, codes, dq, ld);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_pack_q4k(const uint8_t* w, int64_t n, int64_t k, int64_t ldw_bytes, int8_t* codes,
-                            int64_t plane_stride, float* dsc, float* dmn, int64_t ld, cudaStream_t s) {
-  const int64_t total = n * (k / kQK);
-  if (total == 0) return cudaSuccess;
-  const int64_t blocks = (total + 255) / 256;
-  const int grid = static_cast<int>(blocks < 65535 ? blocks : 65535);
-  pack_q4k_kernel<<<grid, 256, 0, s>>>(w, n, k, ldw_bytes, codes, plane_stride, dsc, dmn, ld);
   return cudaGetLastError();
 }
 

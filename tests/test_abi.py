@@ -179,8 +179,8 @@ def test_header_compiles_as_c(tmp_path):
 
 def test_q4_k_validation(b2q_mod):
     L = b2q.lib()
-    # typed sizes: Q4_K packs three int8 planes plus two fp32 scale arrays; Q8_K one plane plus one
-    assert L.b2q_weight_packed_bytes(12, 64, 1024) == 3 * 64 * 1024 + 2 * 4 * 64 * 4
+    # typed sizes: Q4_K packs as its own rows; Q8_K is the codes plus one fp32 scale per 256 values
+    assert L.b2q_weight_packed_bytes(12, 64, 1024) == 64 * 4 * 144                 # the rows themselves
     assert L.b2q_weight_packed_bytes(8, 64, 1024) == L.b2q_weight_packed_size(64, 1024)
     assert L.b2q_weight_packed_bytes(12, 64, 96) == 0 and L.b2q_weight_packed_bytes(3, 64, 1024) == 0
     assert L.b2q_act_prepared_bytes(2, 5, 512) == 5 * 512 + 256            # codes, then d [2][8] padded to 256
@@ -192,8 +192,8 @@ def test_q4_k_validation(b2q_mod):
     assert L.b2q_mul_mat(12, FAKE, 144 * 4, 64, 1024, FAKE, 4, 4096, None, FAKE, 256, 0, FAKE, big, None) == 1
     assert L.b2q_mul_mat(8, FAKE, 1088, 64, 1024, FAKE, 4, 4096, None, FAKE, 256, 2, FAKE, big, None) == 1
     assert L.b2q_mul_mat(12, FAKE, 144 * 3, 64, 1024, FAKE, 4, 4096, None, FAKE, 256, 2, FAKE, big, None) == 1
-    # pack: the buffer must hold the three-plane layout
-    assert L.b2q_weight_pack(12, FAKE, 64, 1024, 576, FAKE, L.b2q_weight_packed_size(64, 1024), None) == 4
+    # pack: the buffer must hold the rows
+    assert L.b2q_weight_pack(12, FAKE, 64, 1024, 576, FAKE, L.b2q_weight_packed_bytes(12, 64, 1024) - 1, None) == 4
     f = L.b2q_mul_mat_prepared_q4_k
     assert f(FAKE, 64, 1000, FAKE, 4, None, None, None, 0, FAKE, 256, None) == 1   # k % 256
     assert f(FAKE, 64, 1024, FAKE, 4, None, None, None, 0, FAKE, 128, None) == 1   # y stride
