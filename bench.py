@@ -72,8 +72,41 @@ def config_dict():
     }
 
 
+def synth_blocks(wtype: int, w: np.ndarray | None, n: int, k: int, seed: int = 0) -> np.ndarray:
+    """Synthetic GGUF weight rows (uint8 [n, row bytes]).  Q8_0 / Q4_0: the
+    fp32 matrix w quantized blockwise here in numpy (scale amax/127, or the
+    signed max / -8 for Q4_0; round to nearest); Q4_K: seeded random blocks
+    with finite fp16 d / dmin, since any such bytes are a valid weight.  The
+    bytes only need to be valid and realistic: the benchmark measures speed,
+    and the parity tests use the ggml quantizers' own bytes."""
+    if wtype == 12:  # Q4_K
+        rng = np.random.default_rng(seed)
+        nb = k // 256
+        b = rng.integers(0, 256, size=(n, nb, 144), dtype=np.uint8)
+        b[:, :, 0:2] = np.abs(rng.standard_normal((n, nb)) * 0.01).astype(np.float16).view(np.uint8).reshape(n, nb, 2)
+        b[:, :, 2:4] = np.abs(rng.standard_normal((n, nb)) * 0.01).astype(np.float16).view(np.uint8).reshape(n, nb, 2)
+        return b.reshape(n, nb * 144)
+    blk = w.reshape(n, k // 32, 32).astype(np.float32)
+    if wtype == 8:  # Q8_0
+        d = np.abs(blk).max(-1) / np.float32(127)
+        inv = np.where(d > 0, 1 / np.where(d > 0, d, 1), 0).astype(np.float32)
+        q = np.clip(np.rint(blk * inv[..., None]), -127, 127).astype(np.int8)
+        out = np.empty((n, k // 32, 34), np.uint8)
+        out[:, :, :2] = d.astype(np.float16).view(np.uint8).reshape(n, k // 32, 2)
+        out[:, :, 2:] = q.view(np.uint8)
+        return out.reshape(n, -1)
+    idx = np.abs(blk).argmax(-1)
+    mx = np.take_along_axis(blk, idx[..., None], -1)[..., 0]
+    d = mx / np.float32(-8)
+    inv = np.where(d != 0, 1 / np.where(d != 0, d, 1), 0).astype(np.float32)
+    q = np.clip(np.rint(blk * inv[..., None]) + 8, 0, 15).astype(np.uint8)
+    out = np.empty((n, k // 32, 18), np.uint8)
+    out[:, :, :2] = d.astype(np.float16).view(np.uint8).reshape(n, k // 32, 2)
+    out[:, :, 2:] = q[:, :, :16] | (q[:, :, 16:] << 4)
+    return out.reshape(n, -1)
+
+
 def make_inputs(seed=1234):
-    import oracle as O
     from_gelu = None
     rng = np.random.default_rng(seed)
     out = []
@@ -83,7 +116,7 @@ def make_inputs(seed=1234):
         if gelu:
             x64 = x.astype(np.float64)
             x = (0.5 * x64 * (1.0 + np.tanh(0.7978845608028654 * (x64 + 0.044715 * x64 ** 3)))).astype(np.float32)
-        out.append((name, wtype, M, N, K, O.quantize(w, wtype), x))
+        out.append((name, wtype, M, N, K, synth_blocks(wtype, w, N, K), x))
     del from_gelu
     return out
 
@@ -353,6 +386,8 @@ def run_gpu(args, rank, world, local_rank):
     if not args.only and not args.no_mlp:
         result["mlp_branch"] = mlp_branch(b2q, gemms, flush, stream, dev)
         result["q4_k"] = q4_k_side(b2q, gemms, flush, stream, dev)
+        result["ss_block"] = ss_block_side(b2q, flush, stream, dev,
+                                           cpu=(rank == 0 and world == 1 and not args.no_cpu_baseline))
     if args.only:
         result["config"]["workload"] = f"single GEMM {args.only} (profiling case)"
         result["config"]["l2"] = "not flushed (profiling case)"
@@ -474,13 +509,12 @@ def q4_k_side(b2q, gemms, flush, stream, dev, iters=10):
     headline (not part of `value`).  Weights are seeded random valid Q4_K
     blocks."""
     import torch
-    import oracle as O
     out = []
     for g in gemms:
         if g["name"] not in ("fc1_q4_0", "fc2_q4_0") or g["K"] % 256:
             continue
         M, N, K = g["M"], g["N"], g["K"]
-        packed = b2q.weight_pack(b2q.TYPE_Q4_K, torch.from_numpy(O.random_q4_k(N, K, seed=N + K)).to(dev), K)
+        packed = b2q.weight_pack(b2q.TYPE_Q4_K, torch.from_numpy(synth_blocks(12, None, N, K, seed=N + K)).to(dev), K)
         act = b2q.act_prepare(g["x_dev"], b2q.ACT_Q8_K, stream=stream)
         y = torch.empty((M, N), dtype=torch.float32, device=dev)
 
@@ -506,6 +540,76 @@ def q4_k_side(b2q, gemms, flush, stream, dev, iters=10):
     return {"kernel": "gemm_q4k_kernel (three int8 planes, per-super-block fold)", "gemms": out}
 
 
+# ------------------------------------------------- SS-flow DiT block step
+SS_BLOCK = dict(B=2, T=4096, C=1024, H=16)  # one block, 16 heads, 4096 tokens, CFG batch 2
+
+
+def ss_block_side(b2q, flush, stream, dev, cpu=False, iters=10):
+    """One SS-flow DiT block (sam-3d-objects-ggml_b200/ss_block.py) at the
+    BASELINE block config: pre-norms, qkv, RMS-norm heads, attention, output
+    projection with gate + residual, fused MLP; Q8_0 weights.  The attention
+    core is torch's SDPA (fp16), a library kernel; everything else is
+    libb2q.  Reported beside the headline.  With cpu=True the same block's
+    CPU time is estimated from the oracle port's quantized mul_mats (all host
+    threads) plus torch's CPU attention, each at full size."""
+    import torch
+    import ss_block
+    B, T, C, H = SS_BLOCK["B"], SS_BLOCK["T"], SS_BLOCK["C"], SS_BLOCK["H"]
+    rng = np.random.default_rng(99)
+    weights = {name: synth_blocks(8, (rng.standard_normal(sh) * 0.02).astype(np.float32), *sh)
+               for name, sh in ss_block.SsBlock.shapes(C, 4 * C).items()}
+    blk = ss_block.SsBlock(dev, weights, C=C, heads=H, wtype=8, seed=5)
+    x0 = torch.randn(B * T, C, device=dev, generator=torch.Generator(device=dev).manual_seed(5))
+    x = x0.clone()
+    for _ in range(3):
+        x.copy_(x0)
+        blk.forward(x, B, T)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    for e0, e1 in evs:
+        x.copy_(x0)
+        flush.zero_()
+        e0.record(stream)
+        blk.forward(x, B, T)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in evs)
+    M = B * T
+    lin_ops = sum(ops_of(M, n, k) for n, k in ss_block.SsBlock.shapes(C, 4 * C).values())
+    attn_flops = 4 * B * H * T * T * (C // H)
+    out = {"config": dict(SS_BLOCK, weights="Q8_0", mlp_ratio=4), "block_ms": round(ms, 4),
+           "linear_int_ops": lin_ops, "attention_flops": attn_flops,
+           "path": "libb2q: norm_modulate_q8, mul_mat_prepared, qkv_heads, heads_act_prepare, "
+                   "mul_mat_prepared_gate_residual, mul_mat_prepared_gelu_q8; attention core: torch SDPA fp16",
+           "not_included": "cross-attention to the condition tokens, the 4-token pose group, adaLN projection"}
+    if cpu:
+        out["cpu"] = cpu_block_seconds(weights, B, T, C, H)
+        out["speedup_vs_cpu"] = round(out["cpu"]["seconds"] * 1e3 / ms, 1)
+    return out
+
+
+def cpu_block_seconds(weights, B, T, C, H):
+    """CPU time of the same block's heavy parts: the oracle port's quantized
+    mul_mats (ggml CPU semantics, vectorised, all host threads) on the full
+    token count, and torch's fp32 CPU attention.  Norms and elementwise steps
+    are not timed (a lower bound)."""
+    import torch
+    import oracle as O
+    thr = host_threads()
+    torch.set_num_threads(thr)
+    rng = np.random.default_rng(7)
+    M = B * T
+    t0 = time.perf_counter()
+    for name, w in weights.items():
+        k = {"qkv": C, "out": C, "fc1": C, "fc2": 4 * C}[name]
+        O.mul_mat(8, w, rng.standard_normal((M, k)).astype(np.float32), O.ACT_X86, nthreads=thr, fast=True)
+    t1 = time.perf_counter()
+    q = torch.randn(B, H, T, C // H)
+    torch.nn.functional.scaled_dot_product_attention(q, q, q)
+    t2 = time.perf_counter()
+    return {"seconds": round(t2 - t0, 3), "linears_s": round(t1 - t0, 3), "attention_s": round(t2 - t1, 3),
+            "threads": thr, "kind": "port (linears) + torch CPU attention"}
+
+
 # ------------------------------------------------- column-parallel (multi-GPU)
 COLPAR_SHAPE = ("slat_qkv_q4_0", 2, 20480, 3072, 1024)  # name, wtype, M tokens, N out, K in
 
@@ -522,7 +626,6 @@ def run_colpar(args, rank, world, local_rank):
     import torch.distributed as dist
     import b2q
     import colpar
-    import oracle as O
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -532,7 +635,7 @@ def run_colpar(args, rank, world, local_rank):
     rng = np.random.default_rng(4321)  # same weights and inputs on every rank
     w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
     x = rng.standard_normal((M, K)).astype(np.float32)
-    wq = O.quantize(w, wtype)
+    wq = synth_blocks(wtype, w, N, K)
     start, stop = colpar.slices(N, world)[rank]
     n = stop - start
     stream = torch.cuda.current_stream()

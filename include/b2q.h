@@ -246,6 +246,28 @@ B2Q_API int b2q_norm_modulate_q8(const float* x, int64_t m, int64_t c, int64_t x
                                  const float* mod_scale, const float* mod_shift, int variant, void* act,
                                  size_t act_bytes, void* stream);
 
+/* ------------------------------------------ DiT self-attention in and out
+ * The tensors on either side of the attention core of an SS-flow block
+ * (cpp_ggml/src/ss_flow_graph.cpp:206-290; graph_builder.cpp:70-175).
+ *
+ * b2q_qkv_heads: the fused qkv projection output, fp32 rows [B*T][3C] (C =
+ * H*D, row stride qkv_row_stride_bytes) -> q, k, v as fp16 [B][H][T][D]
+ * (IEEE half, round to nearest even).  q and k go through the per-head RMS
+ * norm of gb_rms_norm_head (ggml_rms_norm with eps, then times gamma[h][d];
+ * gamma may be NULL); v is only converted.  fp16 is the K/V form of the
+ * reference's flash-attention path.  D in {32, 64, 128}.
+ *
+ * b2q_heads_act_prepare: an attention output o[b][h][t][d] (fp16, element
+ * strides stride_b / stride_h / stride_t, d contiguous) -> the Q8_0 prepared
+ * activations (b2q_act_prepare layout) of the output projection for rows
+ * b*T + t and K = H*D.  D % 32 == 0. */
+B2Q_API int b2q_qkv_heads(const float* qkv, int64_t B, int64_t T, int64_t H, int64_t D,
+                          int64_t qkv_row_stride_bytes, const float* gamma_q, const float* gamma_k, float eps,
+                          void* q16, void* k16, void* v16, void* stream);
+B2Q_API int b2q_heads_act_prepare(const void* o16, int64_t B, int64_t T, int64_t H, int64_t D, int64_t stride_b,
+                                  int64_t stride_h, int64_t stride_t, int variant, void* act, size_t act_bytes,
+                                  void* stream);
+
 /* ------------------------------------------- column-parallel form (multi-GPU)
  * One rank of a tensor-parallel group for a single large mul_mat (the SLat
  * flow transformer's linears at 8k-20k tokens): the weight is split by output

@@ -74,6 +74,8 @@ def _lib_obj():
             "b2q_mul_mat_prepared": (I, [P, I64, I64, P, I64, P, P, I64, P]),
             "b2q_mul_mat_prepared_gelu_q8": (I, [P, I64, I64, P, I64, P, P, SZ, I, P]),
             "b2q_gelu": (I, [P, I64, I64, I64, P, I64, P]),
+            "b2q_qkv_heads": (I, [P, I64, I64, I64, I64, I64, P, P, ctypes.c_float, P, P, P, P]),
+            "b2q_heads_act_prepare": (I, [P, I64, I64, I64, I64, I64, I64, I64, I, P, SZ, P]),
             "b2q_mul_mat_prepared_gate_residual": (I, [P, I64, I64, P, I64, P, P, P, I64, P, I64, P]),
             "b2q_norm_modulate": (I, [P, I64, I64, I64, ctypes.c_float, P, P, P, I64, P]),
             "b2q_norm_modulate_q8": (I, [P, I64, I64, I64, ctypes.c_float, P, P, I, P, SZ, P]),
@@ -330,6 +332,30 @@ def mul_mat_prepared_q4_k(packed, n: int, k: int, act, m: int, bias=None, gate=N
                                          resid.stride(0) * 4 if resid is not None else 0, _ptr(out),
                                          out.stride(0) * 4, _stream(stream))
     _check("b2q_mul_mat_prepared_q4_k", rc)
+    return out
+
+
+def qkv_heads(qkv, B: int, T: int, H: int, D: int, gamma_q=None, gamma_k=None, eps: float = 1e-6, stream=None):
+    """fused qkv rows fp32 [B*T, 3*H*D] -> (q, k, v) fp16 [B, H, T, D] (q, k RMS-normed per head)."""
+    torch = _torch()
+    q, k, v = (torch.empty((B, H, T, D), dtype=torch.float16, device=qkv.device) for _ in range(3))
+    rc = lib().b2q_qkv_heads(_ptr(qkv), B, T, H, D, qkv.stride(0) * 4, _ptr(gamma_q), _ptr(gamma_k), eps,
+                             _ptr(q), _ptr(k), _ptr(v), _stream(stream))
+    _check("b2q_qkv_heads", rc)
+    return q, k, v
+
+
+def heads_act_prepare(o, variant: int = ACT_X86, out=None, stream=None):
+    """attention output fp16 [B, H, T, D] (any strides, d contiguous) -> Q8_0
+    prepared activations for rows (b, t), K = H*D."""
+    B, H, T, D = o.shape
+    assert o.stride(3) == 1
+    size = act_prepared_size(B * T, H * D)
+    if out is None:
+        out = _empty_aligned(size, o.device)
+    rc = lib().b2q_heads_act_prepare(_ptr(o), B, T, H, D, o.stride(0), o.stride(1), o.stride(2), variant,
+                                     _ptr(out), out.numel(), _stream(stream))
+    _check("b2q_heads_act_prepare", rc)
     return out
 
 

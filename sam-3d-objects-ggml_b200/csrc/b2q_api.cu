@@ -523,6 +523,40 @@ int b2q_norm_modulate_q8(const float* x, int64_t m, int64_t c, int64_t x_row_str
                                         variant, static_cast<cudaStream_t>(stream)));
 }
 
+int b2q_qkv_heads(const float* qkv, int64_t B, int64_t T, int64_t H, int64_t D, int64_t qkv_row_stride_bytes,
+                  const float* gamma_q, const float* gamma_k, float eps, void* q16, void* k16, void* v16,
+                  void* stream) {
+  if (B < 0 || T < 0 || H <= 0 || (D != 32 && D != 64 && D != 128) || !(eps >= 0.0f)) return B2Q_ERR_INVALID_ARG;
+  if (B * T > INT_MAX || H > 4096) return B2Q_ERR_TOO_LARGE;
+  if (B * T > 0 && (!qkv || !q16 || !k16 || !v16)) return B2Q_ERR_INVALID_ARG;
+  if (qkv_row_stride_bytes < 3 * H * D * 4) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(qkv, 4) || qkv_row_stride_bytes % 4 != 0 || !aligned(q16, 2) || !aligned(k16, 2) ||
+      !aligned(v16, 2) || (gamma_q && !aligned(gamma_q, 4)) || (gamma_k && !aligned(gamma_k, 4)))
+    return B2Q_ERR_MISALIGNED;
+  if (B * T == 0) return B2Q_OK;
+  if (int rc = check_device(nullptr)) return rc;
+  return from_cuda(launch_qkv_heads(qkv, B, T, static_cast<int>(H), static_cast<int>(D), qkv_row_stride_bytes / 4,
+                                    gamma_q, gamma_k, eps, q16, k16, v16, static_cast<cudaStream_t>(stream)));
+}
+
+int b2q_heads_act_prepare(const void* o16, int64_t B, int64_t T, int64_t H, int64_t D, int64_t stride_b,
+                          int64_t stride_h, int64_t stride_t, int variant, void* act, size_t act_bytes,
+                          void* stream) {
+  if (B < 0 || T < 0 || H <= 0 || D <= 0 || D % kQK != 0) return B2Q_ERR_INVALID_ARG;
+  if (variant != B2Q_ACT_X86 && variant != B2Q_ACT_REF) return B2Q_ERR_INVALID_ARG;
+  if (B * T > INT_MAX || H * D > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (B * T > 0 && (!o16 || !act)) return B2Q_ERR_INVALID_ARG;
+  if (stride_b < 0 || stride_h < 0 || stride_t < 0) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(o16, 2) || !aligned(act, 256)) return B2Q_ERR_MISALIGNED;
+  if (act_bytes < split_bytes(B * T, H * D)) return B2Q_ERR_WORKSPACE;
+  if (B * T == 0) return B2Q_OK;
+  if (int rc = check_device(nullptr)) return rc;
+  const SplitOperand a = split_at(static_cast<uint8_t*>(act), B * T, H * D);
+  return from_cuda(launch_heads_q8(o16, B, T, static_cast<int>(H), static_cast<int>(D), stride_b, stride_h, stride_t,
+                                   const_cast<int8_t*>(a.codes), const_cast<float*>(a.scales), a.ld, variant,
+                                   static_cast<cudaStream_t>(stream)));
+}
+
 int b2q_mul_mat_prepared_peers(const void* packed, int64_t n, int64_t k, const void* act, int64_t m,
                                const float* bias, float* const* y_peers, int n_peers, int64_t y_col0,
                                int64_t y_row_stride_bytes, void* stream) {

@@ -1,0 +1,157 @@
+// b2q_attn_io.cu -- the tensors on either side of the DiT self-attention core
+// (cpp_ggml/src/ss_flow_graph.cpp:206-290, graph_builder.cpp:70-175):
+//
+//   qkv_heads:  the fused qkv projection output fp32 [B*T][3C] (C = H*D) ->
+//               q, k, v as fp16 [B][H][T][D]; q and k go through the
+//               per-head RMS norm with gamma first (gb_rms_norm_head:
+//               ggml_rms_norm then ggml_mul by gamma[h][d]).  fp16 is the K/V
+//               representation of the reference's flash-attention path
+//               (gb_attention casts K and V to F16; the CPU kernel takes Q to
+//               F16 for its K dots).
+//   heads_q8:   the attention output o[b][h][t][d] (fp16, any strides) ->
+//               the Q8_0 prepared activations of the output projection, rows
+//               (b, t), K = H*D.  Every 32-value block lies inside one head
+//               (D % 32 == 0), so a block is 32 contiguous d of one (b, h, t).
+//
+// RMS norm arithmetic (ggml_rms_norm, CPU backend): sum of x*x in double, mean
+// = sum / D, scale = 1 / sqrtf(mean + eps) in float, y = x * scale, then
+// y * gamma (ggml_mul), each one IEEE fp32 operation; fp16 conversion rounds
+// to nearest even.  The double sums are exact for ordinary data, so the
+// warp's order gives the sequential loop's value.
+#include <cuda_fp16.h>
+
+#include "b2q_internal.h"
+#include "b2q_q8.cuh"
+
+namespace b2q {
+
+namespace {
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// One warp per (row, head); lane l holds d = l + 32 i (i < D / 32).
+template <int DPL>  // values per lane = D / 32
+__global__ void __launch_bounds__(256) qkv_heads_kernel(const float* __restrict__ qkv, int64_t rows, int64_t T,
+                                                        int H, int64_t ldq, const float* __restrict__ gq,
+                                                        const float* __restrict__ gk, float eps,
+                                                        __half* __restrict__ q16, __half* __restrict__ k16,
+                                                        __half* __restrict__ v16) {
+  const int lane = threadIdx.x & 31;
+  constexpr int D = DPL * 32;
+  const int64_t C = static_cast<int64_t>(H) * D;
+  const int64_t units = rows * H;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+  for (int64_t u = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32; u < units; u += warps) {
+    const int64_t r = u / H;
+    const int h = static_cast<int>(u - r * H);
+    const int64_t b = r / T, t = r - b * T;
+    const int64_t dst = ((b * H + h) * T + t) * D;
+    const float* src = qkv + r * ldq + static_cast<int64_t>(h) * D;
+#pragma unroll
+    for (int part = 0; part < 3; ++part) {  // q, k, v
+      float x[DPL];
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) x[i] = __ldg(src + part * C + lane + 32 * i);
+      __half* out = part == 0 ? q16 : part == 1 ? k16 : v16;
+      if (part < 2) {
+        double s = 0.0;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) s += static_cast<double>(__fmul_rn(x[i], x[i]));
+        s = warp_sum_d(s);
+        const float mean = __double2float_rn(__ddiv_rn(s, static_cast<double>(D)));
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+        const float* g = (part == 0 ? gq : gk) + static_cast<int64_t>(h) * D;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) {
+          float y = __fmul_rn(x[i], scale);
+          if (g) y = __fmul_rn(y, __ldg(g + lane + 32 * i));
+          x[i] = y;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) out[dst + lane + 32 * i] = __float2half_rn(x[i]);
+    }
+  }
+}
+
+// One lane per (row, block): 32 contiguous fp16 of one head -> one Q8_0 block
+// (the stand-alone quantizer's arithmetic on their fp32 values).
+template <int VARIANT>
+__global__ void __launch_bounds__(256) heads_q8_kernel(const __half* __restrict__ o, int64_t rows, int64_t T,
+                                                       int H, int D, int64_t sb, int64_t sh, int64_t st,
+                                                       int8_t* __restrict__ codes, float* __restrict__ scales,
+                                                       int64_t ld) {
+  const int64_t kb = static_cast<int64_t>(H) * D / kQK;
+  const int64_t units = rows * kb;
+  for (int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < units;
+       u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = u / kb, j = u - r * kb;
+    const int64_t b = r / T, t = r - b * T;
+    const int64_t c0 = j * kQK;
+    const int h = static_cast<int>(c0 / D), d0 = static_cast<int>(c0 - static_cast<int64_t>(h) * D);
+    const __half* src = o + b * sb + h * sh + t * st + d0;
+    float v[kQK];
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kQK; ++i) {
+      v[i] = __half2float(src[i]);
+      amax = fmaxf(amax, fabsf(v[i]));
+    }
+    float d, inv;
+    q8_scale<VARIANT>(amax, d, inv);
+    uint32_t q[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      q[i] = quantize_code<VARIANT>(v[4 * i], inv) | (quantize_code<VARIANT>(v[4 * i + 1], inv) << 8) |
+             (quantize_code<VARIANT>(v[4 * i + 2], inv) << 16) | (quantize_code<VARIANT>(v[4 * i + 3], inv) << 24);
+    uint4* dst = reinterpret_cast<uint4*>(codes + r * (kb * kQK) + c0);
+    dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
+    dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
+    scales[j * ld + r] = q8_split_scale(d);
+  }
+}
+
+int grid_for(int64_t work_items, int per_block, int cap_per_sm) {
+  int sms = current_device_sms();
+  if (sms <= 0) sms = 148;
+  const int64_t blocks = (work_items + per_block - 1) / per_block;
+  const int64_t cap = static_cast<int64_t>(sms) * cap_per_sm;
+  return static_cast<int>(blocks < cap ? blocks : cap);
+}
+
+}  // namespace
+
+cudaError_t launch_qkv_heads(const float* qkv, int64_t B, int64_t T, int H, int D, int64_t ldq_floats,
+                             const float* gq, const float* gk, float eps, void* q16, void* k16, void* v16,
+                             cudaStream_t s) {
+  const int64_t rows = B * T;
+  if (rows == 0) return cudaSuccess;
+  const int grid = grid_for(rows * H, 8, 16);
+  __half *q = static_cast<__half*>(q16), *k = static_cast<__half*>(k16), *v = static_cast<__half*>(v16);
+  switch (D) {
+    case 32: qkv_heads_kernel<1><<<grid, 256, 0, s>>>(qkv, rows, T, H, ldq_floats, gq, gk, eps, q, k, v); break;
+    case 64: qkv_heads_kernel<2><<<grid, 256, 0, s>>>(qkv, rows, T, H, ldq_floats, gq, gk, eps, q, k, v); break;
+    case 128: qkv_heads_kernel<4><<<grid, 256, 0, s>>>(qkv, rows, T, H, ldq_floats, gq, gk, eps, q, k, v); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_heads_q8(const void* o16, int64_t B, int64_t T, int H, int D, int64_t sb, int64_t sh,
+                            int64_t st, int8_t* codes, float* scales, int64_t ld, int variant, cudaStream_t s) {
+  const int64_t rows = B * T;
+  if (rows == 0) return cudaSuccess;
+  const int grid = grid_for(rows * H * D / kQK, 256, 8);
+  const __half* o = static_cast<const __half*>(o16);
+  if (variant == 0)
+    heads_q8_kernel<0><<<grid, 256, 0, s>>>(o, rows, T, H, D, sb, sh, st, codes, scales, ld);
+  else
+    heads_q8_kernel<1><<<grid, 256, 0, s>>>(o, rows, T, H, D, sb, sh, st, codes, scales, ld);
+  return cudaGetLastError();
+}
+
+}  // namespace b2q

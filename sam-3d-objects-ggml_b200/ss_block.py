@@ -1,0 +1,75 @@
+"""One sparse-structure flow DiT block on the device (the shape group of
+cpp_ggml/src/ss_flow_graph.cpp:180-388), built from libb2q's entry points:
+
+    h = modulate(norm(x), scale_msa, shift_msa)          b2q_norm_modulate_q8
+    qkv = h . W_qkv + b_qkv                               b2q_mul_mat_prepared
+    q, k = rms_norm_head(q) * gq, rms_norm_head(k) * gk   b2q_qkv_heads (fp16 q, k, v)
+    o = softmax(q k^T / sqrt(D)) v                        attention core (see below)
+    x = x + gate_msa * (o . W_out + b_out)               b2q_heads_act_prepare + _gate_residual
+    h = modulate(norm(x), scale_mlp, shift_mlp)          b2q_norm_modulate_q8
+    x = x + gate_mlp * (gelu(h . W1 + b1) . W2 + b2)     _gelu_q8 + _gate_residual
+
+Every linear, norm, quantize and epilogue is libb2q's.  The attention core is
+torch's scaled_dot_product_attention on the fp16 q, k, v: a library kernel,
+outside the path this repository rebuilds.  Modulation vectors are shared by
+the batch (the CFG branches of one step share the timestep embedding).  The
+block's cross-attention to the condition tokens and the 4-token pose group
+are not part of this step (the BASELINE block config lists qkv, proj, fc1
+and fc2 only).
+"""
+from __future__ import annotations
+
+import b2q
+
+
+class SsBlock:
+    """Packed weights of one block and its forward pass on fp32 [B*T, C] x."""
+
+    # (out, in) of each linear for width C and hidden width Hd
+    @staticmethod
+    def shapes(C: int, hidden: int) -> dict:
+        return {"qkv": (3 * C, C), "out": (C, C), "fc1": (hidden, C), "fc2": (C, hidden)}
+
+    def __init__(self, dev, weights: dict, C: int = 1024, heads: int = 16, mlp_ratio: int = 4,
+                 wtype: int = b2q.TYPE_Q8_0, seed: int = 0):
+        """weights: GGUF rows (uint8 numpy [out, row bytes]) of "qkv", "out",
+        "fc1", "fc2"; the biases, gammas and modulation vectors are seeded."""
+        import numpy as np
+        import torch
+        self.C, self.H, self.D, self.hidden = C, heads, C // heads, C * mlp_ratio
+        self.wtype = wtype
+        rng = np.random.default_rng(seed)
+        self.raw = {}
+        self.packed = {}
+        for name, (n, k) in self.shapes(C, self.hidden).items():
+            w = weights[name]
+            assert w.shape[0] == n
+            self.raw[name] = w
+            self.packed[name] = b2q.weight_pack(wtype, torch.from_numpy(w).to(dev), k)
+        f = lambda n, s=1.0: torch.from_numpy((rng.standard_normal(n) * s).astype(np.float32)).to(dev)  # noqa: E731
+        self.vec = {"b_qkv": f(3 * C, 0.1), "b_out": f(C, 0.1), "b1": f(self.hidden, 0.1), "b2": f(C, 0.1),
+                    "gq": 1.0 + f(C, 0.1), "gk": 1.0 + f(C, 0.1),
+                    "shift_msa": f(C, 0.1), "scale_msa": f(C, 0.1), "gate_msa": f(C, 0.5),
+                    "shift_mlp": f(C, 0.1), "scale_mlp": f(C, 0.1), "gate_mlp": f(C, 0.5)}
+        self.dev = dev
+
+    def forward(self, x, B: int, T: int, stream=None):
+        """x: fp32 [B*T, C] residual stream, updated in place and returned.
+        The attention core runs on torch's current stream: pass that stream
+        (or None) as `stream`."""
+        import torch.nn.functional as F
+        C, H, D, v = self.C, self.H, self.D, self.vec
+        M = B * T
+        act = b2q.norm_modulate_q8(x, 1e-6, v["scale_msa"], v["shift_msa"], stream=stream)
+        qkv = b2q.mul_mat_prepared(self.packed["qkv"], 3 * C, C, act, M, bias=v["b_qkv"], stream=stream)
+        q, k, vv = b2q.qkv_heads(qkv, B, T, H, D, v["gq"], v["gk"], 1e-6, stream=stream)
+        o = F.scaled_dot_product_attention(q, k, vv)  # [B, H, T, D] fp16
+        act_o = b2q.heads_act_prepare(o, stream=stream)
+        b2q.mul_mat_prepared_gate_residual(self.packed["out"], C, C, act_o, M, x, bias=v["b_out"],
+                                           gate=v["gate_msa"], out=x, stream=stream)
+        act2 = b2q.norm_modulate_q8(x, 1e-6, v["scale_mlp"], v["shift_mlp"], stream=stream)
+        act3 = b2q.mul_mat_prepared_gelu_q8(self.packed["fc1"], self.hidden, C, act2, M, bias=v["b1"],
+                                            stream=stream)
+        b2q.mul_mat_prepared_gate_residual(self.packed["fc2"], C, self.hidden, act3, M, x, bias=v["b2"],
+                                           gate=v["gate_mlp"], out=x, stream=stream)
+        return x

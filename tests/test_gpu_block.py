@@ -1,0 +1,119 @@
+"""GPU check of one SS-flow DiT block (sam-3d-objects-ggml_b200/ss_block.py)
+against its CPU composition from the oracle (reference_forward), and of the
+attention I/O kernels (b2q_qkv_heads, b2q_heads_act_prepare) on their own.
+
+Bars: the fp16 q, k, v equal their CPU restatement bit for bit except where the
+fp32 RMS scale's last bit differs (< 0.1% of values, one fp16 step); the Q8_0
+output-projection activations equal act_prepare of the same fp32 values bit for
+bit; the whole block within BLOCK_RTOL of the CPU composition (the attention
+core runs in fp16 through a library kernel, and every mul_mat's 1e-5 passes
+through the next quantize)."""
+import numpy as np
+import pytest
+
+import b2q
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+BLOCK_RTOL = 2e-3
+
+
+def to_dev(a, dev):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+@pytest.fixture(autouse=True)
+def _no_device_errors(b2q_mod, dev):
+    yield
+    assert b2q.device_status(clear=True) == 0
+
+
+def test_qkv_heads_matches_cpu(dev):
+    import torch
+    B, T, H, D = 2, 37, 4, 64
+    C = H * D
+    rng = np.random.default_rng(1)
+    qkv = (rng.standard_normal((B * T, 3 * C + 8)) * 2).astype(np.float32)   # padded rows
+    gq = (1 + 0.1 * rng.standard_normal(C)).astype(np.float32)
+    gk = (1 + 0.1 * rng.standard_normal(C)).astype(np.float32)
+    d = to_dev(qkv, dev)
+    q, k, v = b2q.qkv_heads(d[:, :3 * C], B, T, H, D, to_dev(gq, dev), to_dev(gk, dev))
+    torch.cuda.synchronize()
+
+    def ref(t, g):
+        t = t.reshape(B, T, H, D)
+        if g is None:
+            return t.astype(np.float16).transpose(0, 2, 1, 3)
+        ms = ((t.astype(np.float64) ** 2).sum(-1, keepdims=True) / D).astype(np.float32)
+        sc = np.float32(1.0) / np.sqrt(ms + np.float32(1e-6))
+        return ((t * sc) * g.reshape(H, D)).astype(np.float16).transpose(0, 2, 1, 3)
+
+    for got, want in ((q, ref(qkv[:, :C], gq)), (k, ref(qkv[:, C:2 * C], gk)), (v, ref(qkv[:, 2 * C:3 * C], None))):
+        g = got.cpu().numpy()
+        diff = g.astype(np.float32) != want.astype(np.float32)
+        assert diff.mean() < 1e-3
+        assert np.all(np.abs(g.astype(np.float32) - want.astype(np.float32)) <= np.abs(np.spacing(want)).astype(np.float32) + 1e-12)
+
+
+def test_heads_act_prepare_equals_act_prepare(dev):
+    import torch
+    B, T, H, D = 2, 50, 4, 64
+    o = torch.randn(B, T, H, D, device=dev).half().permute(0, 2, 1, 3)   # [B, H, T, D] view, t-major memory
+    act = b2q.heads_act_prepare(o)
+    rows = o.permute(0, 2, 1, 3).reshape(B * T, H * D).float().contiguous()
+    ref = b2q.act_prepare(rows)
+    torch.cuda.synchronize()
+    M, K = B * T, H * D
+    a, r = act.cpu().numpy(), ref.cpu().numpy()
+    off, ld = (M * K + 255) // 256 * 256, (M + 3) // 4 * 4
+    assert np.array_equal(a[:M * K], r[:M * K])
+    sa = a[off:off + (K // 32) * ld * 4].view(np.float32).reshape(K // 32, ld)[:, :M]
+    sr = r[off:off + (K // 32) * ld * 4].view(np.float32).reshape(K // 32, ld)[:, :M]
+    assert np.array_equal(sa.view(np.uint32), sr.view(np.uint32))
+
+
+def reference_forward(blk, x, B: int, T: int):
+    """The block on the CPU from the oracle's ggml restatements (norm, quantized
+    mul_mat, GELU) and an fp64 softmax attention on the fp16-rounded q, k, v."""
+    v = {k: t.cpu().numpy() for k, t in blk.vec.items()}
+    C, H, D, wt = blk.C, blk.H, blk.D, blk.wtype
+    h = O.norm_modulate(x, 1e-6, v["scale_msa"], v["shift_msa"])
+    qkv = O.mul_mat(wt, blk.raw["qkv"], h, O.ACT_X86) + v["b_qkv"]
+
+    def heads(t, g):
+        t = t.reshape(B, T, H, D).astype(np.float32)
+        if g is not None:
+            ms = ((t.astype(np.float64) ** 2).sum(-1, keepdims=True) / D).astype(np.float32)
+            t = (t * (np.float32(1.0) / np.sqrt(ms + np.float32(1e-6)))) * g.reshape(H, D)
+        return t.astype(np.float16).astype(np.float64).transpose(0, 2, 1, 3)  # [B, H, T, D]
+
+    q, k, vv = heads(qkv[:, :C], v["gq"]), heads(qkv[:, C:2 * C], v["gk"]), heads(qkv[:, 2 * C:], None)
+    s = q @ k.transpose(0, 1, 3, 2) / np.sqrt(D)
+    s = np.exp(s - s.max(-1, keepdims=True))
+    o = (s / s.sum(-1, keepdims=True)) @ vv
+    o = o.astype(np.float16).astype(np.float32).transpose(0, 2, 1, 3).reshape(B * T, C)
+    x = x + (O.mul_mat(wt, blk.raw["out"], o, O.ACT_X86) + v["b_out"]) * v["gate_msa"]
+    h = O.norm_modulate(x, 1e-6, v["scale_mlp"], v["shift_mlp"])
+    h = O.gelu(O.mul_mat(wt, blk.raw["fc1"], h, O.ACT_X86) + v["b1"])
+    return x + (O.mul_mat(wt, blk.raw["fc2"], h, O.ACT_X86) + v["b2"]) * v["gate_mlp"]
+
+
+@pytest.mark.parametrize("wtype", [O.TYPE_Q8_0, O.TYPE_Q4_0])
+def test_ss_block_matches_cpu_composition(dev, wtype):
+    import torch
+    import ss_block
+    B, T, C, H = 2, 128, 256, 4
+    rng = np.random.default_rng(3)
+    weights = {name: O.quantize((rng.standard_normal(sh) * 0.02).astype(np.float32), wtype)
+               for name, sh in ss_block.SsBlock.shapes(C, 4 * C).items()}
+    blk = ss_block.SsBlock(dev, weights, C=C, heads=H, wtype=wtype, seed=3)
+    x = np.random.default_rng(4).standard_normal((B * T, C)).astype(np.float32)
+    xd = to_dev(x, dev)
+    blk.forward(xd, B, T)
+    torch.cuda.synchronize()
+    y = xd.cpu().numpy()
+    ref = reference_forward(blk, x, B, T)
+    err = np.linalg.norm((y - ref).astype(np.float64)) / np.linalg.norm(ref.astype(np.float64))
+    assert err <= BLOCK_RTOL, err
