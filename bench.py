@@ -541,7 +541,7 @@ def q4_k_side(b2q, gemms, flush, stream, dev, iters=10):
 
 
 # ------------------------------------------------- SS-flow DiT block step
-SS_BLOCK = dict(B=2, T=4096, C=1024, H=16)  # one block, 16 heads, 4096 tokens, CFG batch 2
+SS_BLOCK = dict(B=2, T=4096, C=1024, H=16, n_cond=1374)  # BASELINE configs[2] and the 1374 condition tokens
 
 
 def ss_block_side(b2q, flush, stream, dev, cpu=False, iters=10):
@@ -559,35 +559,40 @@ def ss_block_side(b2q, flush, stream, dev, cpu=False, iters=10):
     weights = {name: synth_blocks(8, (rng.standard_normal(sh) * 0.02).astype(np.float32), *sh)
                for name, sh in ss_block.SsBlock.shapes(C, 4 * C).items()}
     blk = ss_block.SsBlock(dev, weights, C=C, heads=H, wtype=8, seed=5)
-    x0 = torch.randn(B * T, C, device=dev, generator=torch.Generator(device=dev).manual_seed(5))
+    gen = torch.Generator(device=dev).manual_seed(5)
+    x0 = torch.randn(B * T, C, device=dev, generator=gen)
+    nc = SS_BLOCK["n_cond"]
+    cond = torch.randn(B * nc, C, device=dev, generator=gen)
     x = x0.clone()
     for _ in range(3):
         x.copy_(x0)
-        blk.forward(x, B, T)
+        blk.forward(x, B, T, cond, nc)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
     for e0, e1 in evs:
         x.copy_(x0)
         flush.zero_()
         e0.record(stream)
-        blk.forward(x, B, T)
+        blk.forward(x, B, T, cond, nc)
         e1.record(stream)
     torch.cuda.synchronize()
     ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in evs)
     M = B * T
-    lin_ops = sum(ops_of(M, n, k) for n, k in ss_block.SsBlock.shapes(C, 4 * C).values())
-    attn_flops = 4 * B * H * T * T * (C // H)
+    lin_ops = sum(ops_of(B * nc if name == "xkv" else M, n, k)
+                  for name, (n, k) in ss_block.SsBlock.shapes(C, 4 * C).items())
+    attn_flops = 4 * B * H * T * (T + nc) * (C // H)
     out = {"config": dict(SS_BLOCK, weights="Q8_0", mlp_ratio=4), "block_ms": round(ms, 4),
            "linear_int_ops": lin_ops, "attention_flops": attn_flops,
-           "path": "libb2q: norm_modulate_q8, mul_mat_prepared, qkv_heads, heads_act_prepare, "
-                   "mul_mat_prepared_gate_residual, mul_mat_prepared_gelu_q8; attention core: torch SDPA fp16",
-           "not_included": "cross-attention to the condition tokens, the 4-token pose group, adaLN projection"}
+           "path": "libb2q: norm_modulate_q8, layer_norm_q8, act_prepare, mul_mat_prepared, qkv_heads, "
+                   "rows_to_heads, heads_act_prepare, mul_mat_prepared_gate_residual, mul_mat_prepared_gelu_q8; "
+                   "attention cores (self and cross): torch SDPA fp16",
+           "not_included": "the 4-token pose group, the adaLN projection"}
     if cpu:
-        out["cpu"] = cpu_block_seconds(weights, B, T, C, H)
+        out["cpu"] = cpu_block_seconds(weights, B, T, C, H, nc)
         out["speedup_vs_cpu"] = round(out["cpu"]["seconds"] * 1e3 / ms, 1)
     return out
 
 
-def cpu_block_seconds(weights, B, T, C, H):
+def cpu_block_seconds(weights, B, T, C, H, n_cond):
     """CPU time of the same block's heavy parts: the oracle port's quantized
     mul_mats (ggml CPU semantics, vectorised, all host threads) on the full
     token count, and torch's fp32 CPU attention.  Norms and elementwise steps
@@ -600,11 +605,14 @@ def cpu_block_seconds(weights, B, T, C, H):
     M = B * T
     t0 = time.perf_counter()
     for name, w in weights.items():
-        k = {"qkv": C, "out": C, "fc1": C, "fc2": 4 * C}[name]
-        O.mul_mat(8, w, rng.standard_normal((M, k)).astype(np.float32), O.ACT_X86, nthreads=thr, fast=True)
+        k = 4 * C if name == "fc2" else C
+        rows = B * n_cond if name == "xkv" else M
+        O.mul_mat(8, w, rng.standard_normal((rows, k)).astype(np.float32), O.ACT_X86, nthreads=thr, fast=True)
     t1 = time.perf_counter()
     q = torch.randn(B, H, T, C // H)
+    kc = torch.randn(B, H, n_cond, C // H)
     torch.nn.functional.scaled_dot_product_attention(q, q, q)
+    torch.nn.functional.scaled_dot_product_attention(q, kc, kc)
     t2 = time.perf_counter()
     return {"seconds": round(t2 - t0, 3), "linears_s": round(t1 - t0, 3), "attention_s": round(t2 - t1, 3),
             "threads": thr, "kind": "port (linears) + torch CPU attention"}

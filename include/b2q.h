@@ -242,6 +242,13 @@ B2Q_API int b2q_gelu(const float* x, int64_t rows, int64_t cols, int64_t x_row_s
 B2Q_API int b2q_norm_modulate(const float* x, int64_t m, int64_t c, int64_t x_row_stride_bytes, float eps,
                               const float* mod_scale, const float* mod_shift, float* y,
                               int64_t y_row_stride_bytes, void* stream);
+/* gb_layer_norm with an affine weight and bias (the cross-attention's norm2,
+ * cpp_ggml/src/ss_flow_graph.cpp:310-312): ggml_norm, then h * weight
+ * (ggml_mul), then + bias (ggml_add), into Q8_0 prepared activations; same
+ * requirements as b2q_norm_modulate_q8. */
+B2Q_API int b2q_layer_norm_q8(const float* x, int64_t m, int64_t c, int64_t x_row_stride_bytes, float eps,
+                              const float* weight, const float* bias, int variant, void* act, size_t act_bytes,
+                              void* stream);
 B2Q_API int b2q_norm_modulate_q8(const float* x, int64_t m, int64_t c, int64_t x_row_stride_bytes, float eps,
                                  const float* mod_scale, const float* mod_shift, int variant, void* act,
                                  size_t act_bytes, void* stream);
@@ -264,6 +271,12 @@ B2Q_API int b2q_norm_modulate_q8(const float* x, int64_t m, int64_t c, int64_t x
 B2Q_API int b2q_qkv_heads(const float* qkv, int64_t B, int64_t T, int64_t H, int64_t D,
                           int64_t qkv_row_stride_bytes, const float* gamma_q, const float* gamma_k, float eps,
                           void* q16, void* k16, void* v16, void* stream);
+/* The same conversion for projections without the RMS norm (the
+ * cross-attention's q, and its k | v computed from the condition tokens as
+ * one 2C-wide projection): `parts` (1 or 2) C-wide fp32 tensors per row ->
+ * fp16 [B][H][T][D] each (out1 used when parts == 2). */
+B2Q_API int b2q_rows_to_heads(const float* src, int64_t B, int64_t T, int64_t H, int64_t D, int parts,
+                              int64_t src_row_stride_bytes, void* out0, void* out1, void* stream);
 B2Q_API int b2q_heads_act_prepare(const void* o16, int64_t B, int64_t T, int64_t H, int64_t D, int64_t stride_b,
                                   int64_t stride_h, int64_t stride_t, int variant, void* act, size_t act_bytes,
                                   void* stream);

@@ -76,6 +76,8 @@ def _lib_obj():
             "b2q_gelu": (I, [P, I64, I64, I64, P, I64, P]),
             "b2q_qkv_heads": (I, [P, I64, I64, I64, I64, I64, P, P, ctypes.c_float, P, P, P, P]),
             "b2q_heads_act_prepare": (I, [P, I64, I64, I64, I64, I64, I64, I64, I, P, SZ, P]),
+            "b2q_rows_to_heads": (I, [P, I64, I64, I64, I64, I, I64, P, P, P]),
+            "b2q_layer_norm_q8": (I, [P, I64, I64, I64, ctypes.c_float, P, P, I, P, SZ, P]),
             "b2q_mul_mat_prepared_gate_residual": (I, [P, I64, I64, P, I64, P, P, P, I64, P, I64, P]),
             "b2q_norm_modulate": (I, [P, I64, I64, I64, ctypes.c_float, P, P, P, I64, P]),
             "b2q_norm_modulate_q8": (I, [P, I64, I64, I64, ctypes.c_float, P, P, I, P, SZ, P]),
@@ -343,6 +345,28 @@ def qkv_heads(qkv, B: int, T: int, H: int, D: int, gamma_q=None, gamma_k=None, e
                              _ptr(q), _ptr(k), _ptr(v), _stream(stream))
     _check("b2q_qkv_heads", rc)
     return q, k, v
+
+
+def rows_to_heads(src, B: int, T: int, H: int, D: int, parts: int = 1, stream=None):
+    """fp32 rows [B*T, parts*H*D] -> parts fp16 tensors [B, H, T, D] (no norm)."""
+    torch = _torch()
+    outs = [torch.empty((B, H, T, D), dtype=torch.float16, device=src.device) for _ in range(parts)]
+    rc = lib().b2q_rows_to_heads(_ptr(src), B, T, H, D, parts, src.stride(0) * 4, _ptr(outs[0]),
+                                 _ptr(outs[1]) if parts == 2 else None, _stream(stream))
+    _check("b2q_rows_to_heads", rc)
+    return outs
+
+
+def layer_norm_q8(x, eps: float = 1e-6, weight=None, bias=None, variant: int = ACT_X86, out=None, stream=None):
+    """gb_layer_norm (affine weight, bias) straight into Q8_0 prepared activations."""
+    m, c = x.shape
+    size = act_prepared_size(m, c)
+    if out is None:
+        out = _empty_aligned(size, x.device)
+    rc = lib().b2q_layer_norm_q8(_ptr(x), m, c, x.stride(0) * 4, eps, _ptr(weight), _ptr(bias), variant, _ptr(out),
+                                 out.numel(), _stream(stream))
+    _check("b2q_layer_norm_q8", rc)
+    return out
 
 
 def heads_act_prepare(o, variant: int = ACT_X86, out=None, stream=None):

@@ -535,8 +535,39 @@ int b2q_qkv_heads(const float* qkv, int64_t B, int64_t T, int64_t H, int64_t D, 
     return B2Q_ERR_MISALIGNED;
   if (B * T == 0) return B2Q_OK;
   if (int rc = check_device(nullptr)) return rc;
-  return from_cuda(launch_qkv_heads(qkv, B, T, static_cast<int>(H), static_cast<int>(D), qkv_row_stride_bytes / 4,
-                                    gamma_q, gamma_k, eps, q16, k16, v16, static_cast<cudaStream_t>(stream)));
+  return from_cuda(launch_rows_to_heads(qkv, B, T, static_cast<int>(H), static_cast<int>(D), qkv_row_stride_bytes / 4,
+                                        3, 3u, gamma_q, gamma_k, eps, q16, k16, v16, static_cast<cudaStream_t>(stream)));
+}
+
+int b2q_rows_to_heads(const float* src, int64_t B, int64_t T, int64_t H, int64_t D, int parts,
+                      int64_t src_row_stride_bytes, void* out0, void* out1, void* stream) {
+  if (B < 0 || T < 0 || H <= 0 || (D != 32 && D != 64 && D != 128) || parts < 1 || parts > 2)
+    return B2Q_ERR_INVALID_ARG;
+  if (B * T > INT_MAX || H > 4096) return B2Q_ERR_TOO_LARGE;
+  if (B * T > 0 && (!src || !out0 || (parts == 2 && !out1))) return B2Q_ERR_INVALID_ARG;
+  if (src_row_stride_bytes < parts * H * D * 4) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(src, 4) || src_row_stride_bytes % 4 != 0 || !aligned(out0, 2) || (out1 && !aligned(out1, 2)))
+    return B2Q_ERR_MISALIGNED;
+  if (B * T == 0) return B2Q_OK;
+  if (int rc = check_device(nullptr)) return rc;
+  return from_cuda(launch_rows_to_heads(src, B, T, static_cast<int>(H), static_cast<int>(D), src_row_stride_bytes / 4,
+                                        parts, 0u, nullptr, nullptr, 0.0f, out0, out1, nullptr,
+                                        static_cast<cudaStream_t>(stream)));
+}
+
+int b2q_layer_norm_q8(const float* x, int64_t m, int64_t c, int64_t x_row_stride_bytes, float eps, const float* weight,
+                      const float* bias, int variant, void* act, size_t act_bytes, void* stream) {
+  if (int rc = check_norm(x, m, c, x_row_stride_bytes, eps, weight, bias)) return rc;
+  if (variant != B2Q_ACT_X86 && variant != B2Q_ACT_REF) return B2Q_ERR_INVALID_ARG;
+  if (m > 0 && !act) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(act, 256)) return B2Q_ERR_MISALIGNED;
+  if (act_bytes < split_bytes(m, c)) return B2Q_ERR_WORKSPACE;
+  if (m == 0) return B2Q_OK;
+  if (int rc = check_device(nullptr)) return rc;
+  const SplitOperand a = split_at(static_cast<uint8_t*>(act), m, c);
+  return from_cuda(launch_norm_modulate(x, m, c, x_row_stride_bytes / 4, eps, weight, bias, nullptr, 0,
+                                        const_cast<int8_t*>(a.codes), const_cast<float*>(a.scales), a.ld, variant,
+                                        static_cast<cudaStream_t>(stream), true));
 }
 
 int b2q_heads_act_prepare(const void* o16, int64_t B, int64_t T, int64_t H, int64_t D, int64_t stride_b,

@@ -33,13 +33,17 @@ __device__ __forceinline__ double warp_sum_d(double v) {
   return v;
 }
 
-// One warp per (row, head); lane l holds d = l + 32 i (i < D / 32).
+// One warp per (row, head); lane l holds d = l + 32 i (i < D / 32).  The row
+// holds `parts` C-wide tensors (q, k, v of a fused projection, or fewer);
+// part p goes to out[p] as fp16 [B][H][T][D], RMS-normed first when bit p of
+// norm_mask is set (times gamma[p] when that is not null).
 template <int DPL>  // values per lane = D / 32
-__global__ void __launch_bounds__(256) qkv_heads_kernel(const float* __restrict__ qkv, int64_t rows, int64_t T,
-                                                        int H, int64_t ldq, const float* __restrict__ gq,
-                                                        const float* __restrict__ gk, float eps,
-                                                        __half* __restrict__ q16, __half* __restrict__ k16,
-                                                        __half* __restrict__ v16) {
+__global__ void __launch_bounds__(256) rows_to_heads_kernel(const float* __restrict__ qkv, int64_t rows, int64_t T,
+                                                            int H, int64_t ldq, int parts, unsigned norm_mask,
+                                                            const float* __restrict__ gq,
+                                                            const float* __restrict__ gk, float eps,
+                                                            __half* __restrict__ q16, __half* __restrict__ k16,
+                                                            __half* __restrict__ v16) {
   const int lane = threadIdx.x & 31;
   constexpr int D = DPL * 32;
   const int64_t C = static_cast<int64_t>(H) * D;
@@ -51,20 +55,20 @@ __global__ void __launch_bounds__(256) qkv_heads_kernel(const float* __restrict_
     const int64_t b = r / T, t = r - b * T;
     const int64_t dst = ((b * H + h) * T + t) * D;
     const float* src = qkv + r * ldq + static_cast<int64_t>(h) * D;
-#pragma unroll
-    for (int part = 0; part < 3; ++part) {  // q, k, v
+    for (int part = 0; part < parts; ++part) {  // q, k, v
       float x[DPL];
 #pragma unroll
       for (int i = 0; i < DPL; ++i) x[i] = __ldg(src + part * C + lane + 32 * i);
       __half* out = part == 0 ? q16 : part == 1 ? k16 : v16;
-      if (part < 2) {
+      if ((norm_mask >> part) & 1u) {
         double s = 0.0;
 #pragma unroll
         for (int i = 0; i < DPL; ++i) s += static_cast<double>(__fmul_rn(x[i], x[i]));
         s = warp_sum_d(s);
         const float mean = __double2float_rn(__ddiv_rn(s, static_cast<double>(D)));
         const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-        const float* g = (part == 0 ? gq : gk) + static_cast<int64_t>(h) * D;
+        const float* g0 = part == 0 ? gq : gk;
+        const float* g = g0 ? g0 + static_cast<int64_t>(h) * D : nullptr;
 #pragma unroll
         for (int i = 0; i < DPL; ++i) {
           float y = __fmul_rn(x[i], scale);
@@ -125,17 +129,24 @@ int grid_for(int64_t work_items, int per_block, int cap_per_sm) {
 
 }  // namespace
 
-cudaError_t launch_qkv_heads(const float* qkv, int64_t B, int64_t T, int H, int D, int64_t ldq_floats,
-                             const float* gq, const float* gk, float eps, void* q16, void* k16, void* v16,
-                             cudaStream_t s) {
+cudaError_t launch_rows_to_heads(const float* src, int64_t B, int64_t T, int H, int D, int64_t ld_floats, int parts,
+                                 unsigned norm_mask, const float* g0, const float* g1, float eps, void* o0, void* o1,
+                                 void* o2, cudaStream_t s) {
   const int64_t rows = B * T;
   if (rows == 0) return cudaSuccess;
+  if (parts < 1 || parts > 3 || (norm_mask >> 2) != 0) return cudaErrorInvalidValue;  // v is never normed
   const int grid = grid_for(rows * H, 8, 16);
-  __half *q = static_cast<__half*>(q16), *k = static_cast<__half*>(k16), *v = static_cast<__half*>(v16);
+  __half *a = static_cast<__half*>(o0), *b = static_cast<__half*>(o1), *c = static_cast<__half*>(o2);
   switch (D) {
-    case 32: qkv_heads_kernel<1><<<grid, 256, 0, s>>>(qkv, rows, T, H, ldq_floats, gq, gk, eps, q, k, v); break;
-    case 64: qkv_heads_kernel<2><<<grid, 256, 0, s>>>(qkv, rows, T, H, ldq_floats, gq, gk, eps, q, k, v); break;
-    case 128: qkv_heads_kernel<4><<<grid, 256, 0, s>>>(qkv, rows, T, H, ldq_floats, gq, gk, eps, q, k, v); break;
+    case 32:
+      rows_to_heads_kernel<1><<<grid, 256, 0, s>>>(src, rows, T, H, ld_floats, parts, norm_mask, g0, g1, eps, a, b, c);
+      break;
+    case 64:
+      rows_to_heads_kernel<2><<<grid, 256, 0, s>>>(src, rows, T, H, ld_floats, parts, norm_mask, g0, g1, eps, a, b, c);
+      break;
+    case 128:
+      rows_to_heads_kernel<4><<<grid, 256, 0, s>>>(src, rows, T, H, ld_floats, parts, norm_mask, g0, g1, eps, a, b, c);
+      break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

@@ -106,12 +106,13 @@ cudaError_t launch_gemm_simt(int wtype, const uint8_t* w, int64_t ldw_bytes, int
 constexpr int64_t kNormMaxC = 4096;
 cudaError_t launch_norm_modulate(const float* x, int64_t m, int64_t c, int64_t ldx_floats, float eps,
                                  const float* mscale, const float* mshift, float* y, int64_t ldy_floats,
-                                 int8_t* codes, float* qscales, int64_t qld, int variant, cudaStream_t s);
+                                 int8_t* codes, float* qscales, int64_t qld, int variant, cudaStream_t s,
+                                 bool affine = false);
 
 // DiT attention I/O (b2q_attn_io.cu).
-cudaError_t launch_qkv_heads(const float* qkv, int64_t B, int64_t T, int H, int D, int64_t ldq_floats,
-                             const float* gq, const float* gk, float eps, void* q16, void* k16, void* v16,
-                             cudaStream_t s);
+cudaError_t launch_rows_to_heads(const float* src, int64_t B, int64_t T, int H, int D, int64_t ld_floats, int parts,
+                                 unsigned norm_mask, const float* g0, const float* g1, float eps, void* o0, void* o1,
+                                 void* o2, cudaStream_t s);
 cudaError_t launch_heads_q8(const void* o16, int64_t B, int64_t T, int H, int D, int64_t sb, int64_t sh,
                             int64_t st, int8_t* codes, float* scales, int64_t ld, int variant, cudaStream_t s);
 

@@ -14,6 +14,8 @@
 //   scale = 1 / sqrtf(var + eps)
 //   h     = v * scale
 //   h     = (h * mod_scale + h) + mod_shift        (ggml_add(ggml_mul(h, s), h), then ggml_add(., shift))
+//   or, as gb_layer_norm with affine weight and bias (the cross-attention's norm2),
+//   h     = (h * weight) + bias                    (ggml_mul, then ggml_add)
 // The double sums are exact for ordinary data (their terms span far fewer than
 // 53 bits), so the warp's tree order gives the same value as a sequential loop.
 //
@@ -45,7 +47,8 @@ __global__ void __launch_bounds__(256) norm_modulate_kernel(const float* __restr
                                                             const float* __restrict__ mshift,
                                                             float* __restrict__ y, int64_t ldy,
                                                             int8_t* __restrict__ codes,
-                                                            float* __restrict__ qscales, int64_t qld) {
+                                                            float* __restrict__ qscales, int64_t qld,
+                                                            bool affine) {
   const int lane = threadIdx.x & 31;
   const int ng = c / 4;  // float4 groups per row
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
@@ -89,10 +92,17 @@ __global__ void __launch_bounds__(256) norm_modulate_kernel(const float* __restr
       float h[4] = {__fmul_rn(v[j].x, rs), __fmul_rn(v[j].y, rs), __fmul_rn(v[j].z, rs), __fmul_rn(v[j].w, rs)};
       if (mscale && in) {
         const float4 t = __ldg(reinterpret_cast<const float4*>(mscale) + g);
-        h[0] = __fadd_rn(__fmul_rn(h[0], t.x), h[0]);
-        h[1] = __fadd_rn(__fmul_rn(h[1], t.y), h[1]);
-        h[2] = __fadd_rn(__fmul_rn(h[2], t.z), h[2]);
-        h[3] = __fadd_rn(__fmul_rn(h[3], t.w), h[3]);
+        if (affine) {  // gb_layer_norm's weight: ggml_mul
+          h[0] = __fmul_rn(h[0], t.x);
+          h[1] = __fmul_rn(h[1], t.y);
+          h[2] = __fmul_rn(h[2], t.z);
+          h[3] = __fmul_rn(h[3], t.w);
+        } else {       // modulate: ggml_add(ggml_mul(h, scale), h)
+          h[0] = __fadd_rn(__fmul_rn(h[0], t.x), h[0]);
+          h[1] = __fadd_rn(__fmul_rn(h[1], t.y), h[1]);
+          h[2] = __fadd_rn(__fmul_rn(h[2], t.z), h[2]);
+          h[3] = __fadd_rn(__fmul_rn(h[3], t.w), h[3]);
+        }
       }
       if (mshift && in) {
         const float4 t = __ldg(reinterpret_cast<const float4*>(mshift) + g);
@@ -122,36 +132,39 @@ __global__ void __launch_bounds__(256) norm_modulate_kernel(const float* __restr
 
 template <int NJ, bool Q8, int VARIANT>
 cudaError_t launch_kb(const float* x, int64_t m, int c, int64_t ldx, float eps, const float* ms, const float* sh,
-                      float* y, int64_t ldy, int8_t* codes, float* qs, int64_t qld, cudaStream_t s) {
+                      float* y, int64_t ldy, int8_t* codes, float* qs, int64_t qld, bool affine, cudaStream_t s) {
   int sms = current_device_sms();
   if (sms <= 0) sms = 148;
   const int64_t blocks = (m + 7) / 8;  // 8 rows (warps) per block
   const int cap = sms * (NJ <= 8 ? 8 : NJ <= 16 ? 4 : 2);
   const int grid = static_cast<int>(blocks < cap ? blocks : cap);
-  norm_modulate_kernel<NJ, Q8, VARIANT><<<grid, 256, 0, s>>>(x, m, c, ldx, eps, ms, sh, y, ldy, codes, qs, qld);
+  norm_modulate_kernel<NJ, Q8, VARIANT><<<grid, 256, 0, s>>>(x, m, c, ldx, eps, ms, sh, y, ldy, codes, qs, qld,
+                                                              affine);
   return cudaGetLastError();
 }
 
 template <bool Q8, int VARIANT>
 cudaError_t launch_q(const float* x, int64_t m, int c, int64_t ldx, float eps, const float* ms, const float* sh,
-                     float* y, int64_t ldy, int8_t* codes, float* qs, int64_t qld, cudaStream_t s) {
-  if (c <= 1024) return launch_kb<8, Q8, VARIANT>(x, m, c, ldx, eps, ms, sh, y, ldy, codes, qs, qld, s);
-  if (c <= 2048) return launch_kb<16, Q8, VARIANT>(x, m, c, ldx, eps, ms, sh, y, ldy, codes, qs, qld, s);
-  return launch_kb<32, Q8, VARIANT>(x, m, c, ldx, eps, ms, sh, y, ldy, codes, qs, qld, s);
+                     float* y, int64_t ldy, int8_t* codes, float* qs, int64_t qld, bool affine, cudaStream_t s) {
+  if (c <= 1024) return launch_kb<8, Q8, VARIANT>(x, m, c, ldx, eps, ms, sh, y, ldy, codes, qs, qld, affine, s);
+  if (c <= 2048) return launch_kb<16, Q8, VARIANT>(x, m, c, ldx, eps, ms, sh, y, ldy, codes, qs, qld, affine, s);
+  return launch_kb<32, Q8, VARIANT>(x, m, c, ldx, eps, ms, sh, y, ldy, codes, qs, qld, affine, s);
 }
 
 }  // namespace
 
 cudaError_t launch_norm_modulate(const float* x, int64_t m, int64_t c, int64_t ldx_floats, float eps,
                                  const float* mscale, const float* mshift, float* y, int64_t ldy_floats,
-                                 int8_t* codes, float* qscales, int64_t qld, int variant, cudaStream_t s) {
+                                 int8_t* codes, float* qscales, int64_t qld, int variant, cudaStream_t s,
+                                 bool affine) {
   if (m == 0) return cudaSuccess;
   if (c <= 0 || c % kQK != 0 || c > kNormMaxC) return cudaErrorInvalidValue;
   const int ci = static_cast<int>(c);
-  if (!codes) return launch_q<false, 0>(x, m, ci, ldx_floats, eps, mscale, mshift, y, ldy_floats, nullptr, nullptr, 0, s);
+  if (!codes)
+    return launch_q<false, 0>(x, m, ci, ldx_floats, eps, mscale, mshift, y, ldy_floats, nullptr, nullptr, 0, affine, s);
   if (variant == 0)
-    return launch_q<true, 0>(x, m, ci, ldx_floats, eps, mscale, mshift, nullptr, 0, codes, qscales, qld, s);
-  return launch_q<true, 1>(x, m, ci, ldx_floats, eps, mscale, mshift, nullptr, 0, codes, qscales, qld, s);
+    return launch_q<true, 0>(x, m, ci, ldx_floats, eps, mscale, mshift, nullptr, 0, codes, qscales, qld, affine, s);
+  return launch_q<true, 1>(x, m, ci, ldx_floats, eps, mscale, mshift, nullptr, 0, codes, qscales, qld, affine, s);
 }
 
 }  // namespace b2q

@@ -6,6 +6,10 @@ cpp_ggml/src/ss_flow_graph.cpp:180-388), built from libb2q's entry points:
     q, k = rms_norm_head(q) * gq, rms_norm_head(k) * gk   b2q_qkv_heads (fp16 q, k, v)
     o = softmax(q k^T / sqrt(D)) v                        attention core (see below)
     x = x + gate_msa * (o . W_out + b_out)               b2q_heads_act_prepare + _gate_residual
+    h = norm(x) * w2 + b2n                                b2q_layer_norm_q8           (cross-attention,
+    q = h . W_xq + b_xq;  k | v = cond . W_xkv + b_xkv    b2q_mul_mat_prepared         :308-352)
+    o = softmax(q k^T / sqrt(D)) v                        b2q_rows_to_heads, attention core
+    x = x + (o . W_xout + b_xout)                         b2q_heads_act_prepare + _gate_residual
     h = modulate(norm(x), scale_mlp, shift_mlp)          b2q_norm_modulate_q8
     x = x + gate_mlp * (gelu(h . W1 + b1) . W2 + b2)     _gelu_q8 + _gate_residual
 
@@ -13,9 +17,8 @@ Every linear, norm, quantize and epilogue is libb2q's.  The attention core is
 torch's scaled_dot_product_attention on the fp16 q, k, v: a library kernel,
 outside the path this repository rebuilds.  Modulation vectors are shared by
 the batch (the CFG branches of one step share the timestep embedding).  The
-block's cross-attention to the condition tokens and the 4-token pose group
-are not part of this step (the BASELINE block config lists qkv, proj, fc1
-and fc2 only).
+4-token pose group (whose tiny linears run on the few-token kernel) and the
+adaLN projection are not part of this step.
 """
 from __future__ import annotations
 
@@ -28,12 +31,13 @@ class SsBlock:
     # (out, in) of each linear for width C and hidden width Hd
     @staticmethod
     def shapes(C: int, hidden: int) -> dict:
-        return {"qkv": (3 * C, C), "out": (C, C), "fc1": (hidden, C), "fc2": (C, hidden)}
+        return {"qkv": (3 * C, C), "out": (C, C), "xq": (C, C), "xkv": (2 * C, C), "xout": (C, C),
+                "fc1": (hidden, C), "fc2": (C, hidden)}
 
     def __init__(self, dev, weights: dict, C: int = 1024, heads: int = 16, mlp_ratio: int = 4,
                  wtype: int = b2q.TYPE_Q8_0, seed: int = 0):
-        """weights: GGUF rows (uint8 numpy [out, row bytes]) of "qkv", "out",
-        "fc1", "fc2"; the biases, gammas and modulation vectors are seeded."""
+        """weights: GGUF rows (uint8 numpy [out, row bytes]) of every linear in
+        shapes(); the biases, gammas, norm2 affine and modulation vectors are seeded."""
         import numpy as np
         import torch
         self.C, self.H, self.D, self.hidden = C, heads, C // heads, C * mlp_ratio
@@ -50,13 +54,15 @@ class SsBlock:
         self.vec = {"b_qkv": f(3 * C, 0.1), "b_out": f(C, 0.1), "b1": f(self.hidden, 0.1), "b2": f(C, 0.1),
                     "gq": 1.0 + f(C, 0.1), "gk": 1.0 + f(C, 0.1),
                     "shift_msa": f(C, 0.1), "scale_msa": f(C, 0.1), "gate_msa": f(C, 0.5),
-                    "shift_mlp": f(C, 0.1), "scale_mlp": f(C, 0.1), "gate_mlp": f(C, 0.5)}
+                    "shift_mlp": f(C, 0.1), "scale_mlp": f(C, 0.1), "gate_mlp": f(C, 0.5),
+                    "n2w": 1.0 + f(C, 0.1), "n2b": f(C, 0.1), "b_xq": f(C, 0.1), "b_xkv": f(2 * C, 0.1),
+                    "b_xout": f(C, 0.1)}
         self.dev = dev
 
-    def forward(self, x, B: int, T: int, stream=None):
-        """x: fp32 [B*T, C] residual stream, updated in place and returned.
-        The attention core runs on torch's current stream: pass that stream
-        (or None) as `stream`."""
+    def forward(self, x, B: int, T: int, cond, n_cond: int, stream=None):
+        """x: fp32 [B*T, C] residual stream, updated in place and returned;
+        cond: fp32 [B*n_cond, C] condition tokens.  The attention core runs on
+        torch's current stream: pass that stream (or None) as `stream`."""
         import torch.nn.functional as F
         C, H, D, v = self.C, self.H, self.D, self.vec
         M = B * T
@@ -67,6 +73,17 @@ class SsBlock:
         act_o = b2q.heads_act_prepare(o, stream=stream)
         b2q.mul_mat_prepared_gate_residual(self.packed["out"], C, C, act_o, M, x, bias=v["b_out"],
                                            gate=v["gate_msa"], out=x, stream=stream)
+        # cross-attention to the condition tokens
+        act = b2q.layer_norm_q8(x, 1e-6, v["n2w"], v["n2b"], stream=stream)
+        xq = b2q.mul_mat_prepared(self.packed["xq"], C, C, act, M, bias=v["b_xq"], stream=stream)
+        act_c = b2q.act_prepare(cond, stream=stream)
+        xkv = b2q.mul_mat_prepared(self.packed["xkv"], 2 * C, C, act_c, B * n_cond, bias=v["b_xkv"], stream=stream)
+        (q,) = b2q.rows_to_heads(xq, B, T, H, D, 1, stream=stream)
+        k, vv = b2q.rows_to_heads(xkv, B, n_cond, H, D, 2, stream=stream)
+        o = F.scaled_dot_product_attention(q, k, vv)
+        act_o = b2q.heads_act_prepare(o, stream=stream)
+        b2q.mul_mat_prepared_gate_residual(self.packed["xout"], C, C, act_o, M, x, bias=v["b_xout"], out=x,
+                                           stream=stream)
         act2 = b2q.norm_modulate_q8(x, 1e-6, v["scale_mlp"], v["shift_mlp"], stream=stream)
         act3 = b2q.mul_mat_prepared_gelu_q8(self.packed["fc1"], self.hidden, C, act2, M, bias=v["b1"],
                                             stream=stream)

@@ -206,3 +206,29 @@ def test_q4_k_validation(b2q_mod):
     # Q8_K activations: k % 256; the fused GELU quantize does not produce Q8_K
     assert L.b2q_act_prepare(FAKE, 4, 96, 384, 2, FAKE, big, None) == 1
     assert L.b2q_mul_mat_prepared_gelu_q8(FAKE, 256, 1024, FAKE, 4, None, FAKE, big, 2, None) == 1
+
+
+def test_attention_io_validation(b2q_mod):
+    L = b2q.lib()
+    qkv, r2h, hq, ln = L.b2q_qkv_heads, L.b2q_rows_to_heads, L.b2q_heads_act_prepare, L.b2q_layer_norm_q8
+    st = 3 * 4 * 64 * 4
+    assert qkv(FAKE, 2, 8, 4, 48, st, None, None, 1e-6, FAKE, FAKE, FAKE, None) == 1     # D not 32/64/128
+    assert qkv(FAKE, 2, 8, 4, 64, st - 4, None, None, 1e-6, FAKE, FAKE, FAKE, None) == 1  # stride < 3C
+    assert qkv(FAKE, 0, 8, 4, 64, st, None, None, 1e-6, FAKE, FAKE, FAKE, None) == 0     # empty: no-op
+    assert r2h(FAKE, 2, 8, 4, 64, 3, 4 * 64 * 8, FAKE, FAKE, None) == 1                  # parts > 2
+    assert r2h(FAKE, 2, 8, 4, 64, 2, 4 * 64 * 8, FAKE, None, None) == 1                  # parts 2, null out1
+    assert r2h(FAKE, 2, 8, 4, 64, 2, 4 * 64 * 8 - 4, FAKE, FAKE, None) == 1              # stride < 2C
+    assert r2h(FAKE + 2, 2, 8, 4, 64, 1, 4 * 64 * 4, FAKE, None, None) == 3              # src alignment
+    assert r2h(FAKE, 2, 8, 4, 64, 1, 4 * 64 * 4, FAKE + 1, None, None) == 3              # out alignment
+    assert r2h(FAKE, 0, 8, 4, 64, 1, 4 * 64 * 4, FAKE, None, None) == 0                  # empty: no-op
+    need = L.b2q_act_prepared_size(16, 256)
+    assert hq(FAKE, 2, 8, 4, 48, 0, 0, 0, 0, FAKE, need, None) == 1                       # D % 32
+    assert hq(FAKE, 2, 8, 4, 64, -1, 0, 0, 0, FAKE, need, None) == 1                      # negative stride
+    assert hq(FAKE, 2, 8, 4, 64, 0, 0, 0, 0, FAKE + 16, need, None) == 3                  # act alignment
+    assert hq(FAKE, 2, 8, 4, 64, 0, 0, 0, 0, FAKE, need - 1, None) == 4                   # act too small
+    need = L.b2q_act_prepared_size(4, 64)
+    assert ln(FAKE, 4, 48, 192, 1e-6, None, None, 0, FAKE, need, None) == 1              # c % 32
+    assert ln(FAKE, 4, 64, 256, 1e-6, FAKE + 4, None, 0, FAKE, need, None) == 3          # weight alignment
+    assert ln(FAKE, 4, 64, 256, 1e-6, None, None, 2, FAKE, need, None) == 1              # variant
+    assert ln(FAKE, 4, 64, 256, 1e-6, None, None, 0, FAKE, need - 1, None) == 4          # act too small
+    assert ln(FAKE, 0, 64, 256, 1e-6, None, None, 0, FAKE, 0, None) == 0                 # empty: no-op

@@ -57,6 +57,42 @@ def test_qkv_heads_matches_cpu(dev):
         assert np.all(np.abs(g.astype(np.float32) - want.astype(np.float32)) <= np.abs(np.spacing(want)).astype(np.float32) + 1e-12)
 
 
+@pytest.mark.parametrize("parts", [1, 2])
+def test_rows_to_heads_is_fp16_transpose(dev, parts):
+    """The cross-attention's q (parts 1) and k | v (parts 2) rows -> fp16
+    heads: a plain round-to-nearest conversion and a transpose, bit-exact."""
+    B, T, H, D = 2, 45, 8, 32
+    C = H * D
+    rng = np.random.default_rng(7 + parts)
+    rows = (rng.standard_normal((B * T, parts * C + 4)) * 3).astype(np.float32)
+    outs = b2q.rows_to_heads(to_dev(rows, dev)[:, :parts * C], B, T, H, D, parts)
+    assert len(outs) == parts
+    for p, got in enumerate(outs):
+        want = rows[:, p * C:(p + 1) * C].reshape(B, T, H, D).astype(np.float16).transpose(0, 2, 1, 3)
+        assert tuple(got.shape) == (B, H, T, D)
+        assert np.array_equal(got.cpu().numpy().view(np.uint16), np.ascontiguousarray(want).view(np.uint16))
+
+
+@pytest.mark.parametrize("variant", [0, 1])
+def test_layer_norm_q8_matches_oracle(dev, variant):
+    """gb_layer_norm (ggml_norm, * weight, + bias) with the Q8_0 quantize of
+    the next mul_mat fused in: the same bytes as the oracle's."""
+    M, C = 300, 1024
+    rng = np.random.default_rng(11)
+    x = (rng.standard_normal((M, C)) * 2).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(C)).astype(np.float32)
+    bb = (0.1 * rng.standard_normal(C)).astype(np.float32)
+    act = b2q.layer_norm_q8(to_dev(x, dev), 1e-6, to_dev(w, dev), to_dev(bb, dev), variant=variant)
+    a = act.cpu().numpy()
+    h = O.norm_modulate(x, 1e-6) * w + bb
+    ref = O.quantize(h.astype(np.float32), O.TYPE_Q8_0, variant).reshape(M, C // 32, 34)
+    assert np.array_equal(a[:M * C].view(np.int8).reshape(M, C // 32, 32), ref[:, :, 2:].view(np.int8))
+    off, ld = (M * C + 255) // 256 * 256, (M + 3) // 4 * 4
+    sc = a[off:off + (C // 32) * ld * 4].view(np.float32).reshape(C // 32, ld)[:, :M]
+    d16 = ref[:, :, :2].copy().view(np.float16).reshape(M, C // 32).astype(np.float32)
+    assert np.array_equal(sc.T, d16 * np.float32(2.0 ** 49))
+
+
 def test_heads_act_prepare_equals_act_prepare(dev):
     import torch
     B, T, H, D = 2, 50, 4, 64
@@ -74,7 +110,7 @@ def test_heads_act_prepare_equals_act_prepare(dev):
     assert np.array_equal(sa.view(np.uint32), sr.view(np.uint32))
 
 
-def reference_forward(blk, x, B: int, T: int):
+def reference_forward(blk, x, B: int, T: int, cond, n_cond: int):
     """The block on the CPU from the oracle's ggml restatements (norm, quantized
     mul_mat, GELU) and an fp64 softmax attention on the fp16-rounded q, k, v."""
     v = {k: t.cpu().numpy() for k, t in blk.vec.items()}
@@ -89,12 +125,22 @@ def reference_forward(blk, x, B: int, T: int):
             t = (t * (np.float32(1.0) / np.sqrt(ms + np.float32(1e-6)))) * g.reshape(H, D)
         return t.astype(np.float16).astype(np.float64).transpose(0, 2, 1, 3)  # [B, H, T, D]
 
+    def attend(q, k, vv):
+        s = q @ k.transpose(0, 1, 3, 2) / np.sqrt(D)
+        s = np.exp(s - s.max(-1, keepdims=True))
+        o = (s / s.sum(-1, keepdims=True)) @ vv
+        return o.astype(np.float16).astype(np.float32).transpose(0, 2, 1, 3).reshape(-1, C)
+
     q, k, vv = heads(qkv[:, :C], v["gq"]), heads(qkv[:, C:2 * C], v["gk"]), heads(qkv[:, 2 * C:], None)
-    s = q @ k.transpose(0, 1, 3, 2) / np.sqrt(D)
-    s = np.exp(s - s.max(-1, keepdims=True))
-    o = (s / s.sum(-1, keepdims=True)) @ vv
-    o = o.astype(np.float16).astype(np.float32).transpose(0, 2, 1, 3).reshape(B * T, C)
+    o = attend(q, k, vv)
     x = x + (O.mul_mat(wt, blk.raw["out"], o, O.ACT_X86) + v["b_out"]) * v["gate_msa"]
+    # cross-attention: affine LayerNorm, q from x, k | v from cond, residual without gate
+    h = O.norm_modulate(x) * v["n2w"] + v["n2b"]
+    xq = O.mul_mat(wt, blk.raw["xq"], h, O.ACT_X86) + v["b_xq"]
+    xkv = O.mul_mat(wt, blk.raw["xkv"], cond, O.ACT_X86) + v["b_xkv"]
+    ch = lambda t, n: t.reshape(B, n, H, D).astype(np.float16).astype(np.float64).transpose(0, 2, 1, 3)  # noqa: E731
+    o = attend(ch(xq, T), ch(xkv[:, :C], n_cond), ch(xkv[:, C:], n_cond))
+    x = x + (O.mul_mat(wt, blk.raw["xout"], o, O.ACT_X86) + v["b_xout"])
     h = O.norm_modulate(x, 1e-6, v["scale_mlp"], v["shift_mlp"])
     h = O.gelu(O.mul_mat(wt, blk.raw["fc1"], h, O.ACT_X86) + v["b1"])
     return x + (O.mul_mat(wt, blk.raw["fc2"], h, O.ACT_X86) + v["b2"]) * v["gate_mlp"]
@@ -110,10 +156,12 @@ def test_ss_block_matches_cpu_composition(dev, wtype):
                for name, sh in ss_block.SsBlock.shapes(C, 4 * C).items()}
     blk = ss_block.SsBlock(dev, weights, C=C, heads=H, wtype=wtype, seed=3)
     x = np.random.default_rng(4).standard_normal((B * T, C)).astype(np.float32)
+    n_cond = 77
+    cond = np.random.default_rng(5).standard_normal((B * n_cond, C)).astype(np.float32)
     xd = to_dev(x, dev)
-    blk.forward(xd, B, T)
+    blk.forward(xd, B, T, to_dev(cond, dev), n_cond)
     torch.cuda.synchronize()
     y = xd.cpu().numpy()
-    ref = reference_forward(blk, x, B, T)
+    ref = reference_forward(blk, x, B, T, cond, n_cond)
     err = np.linalg.norm((y - ref).astype(np.float64)) / np.linalg.norm(ref.astype(np.float64))
     assert err <= BLOCK_RTOL, err
