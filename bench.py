@@ -388,6 +388,8 @@ def run_gpu(args, rank, world, local_rank):
         result["q4_k"] = q4_k_side(b2q, gemms, flush, stream, dev)
         result["ss_block"] = ss_block_side(b2q, flush, stream, dev,
                                            cpu=(rank == 0 and world == 1 and not args.no_cpu_baseline))
+        result["ss_step"] = ss_step_side(b2q, stream, dev, result["ss_block"].get("cpu"))
+        result["slat_linears"] = slat_side(b2q, stream, dev)
     if args.only:
         result["config"]["workload"] = f"single GEMM {args.only} (profiling case)"
         result["config"]["l2"] = "not flushed (profiling case)"
@@ -585,7 +587,7 @@ def ss_block_side(b2q, flush, stream, dev, cpu=False, iters=10):
            "path": "libb2q: norm_modulate_q8, layer_norm_q8, act_prepare, mul_mat_prepared, qkv_heads, "
                    "rows_to_heads, heads_act_prepare, mul_mat_prepared_gate_residual, mul_mat_prepared_gelu_q8; "
                    "attention cores (self and cross): torch SDPA fp16",
-           "not_included": "the 4-token pose group, the adaLN projection"}
+           "not_included": "the 4-token pose group, the adaLN projection (both are in ss_step)"}
     if cpu:
         out["cpu"] = cpu_block_seconds(weights, B, T, C, H, nc)
         out["speedup_vs_cpu"] = round(out["cpu"]["seconds"] * 1e3 / ms, 1)
@@ -616,6 +618,140 @@ def cpu_block_seconds(weights, B, T, C, H, n_cond):
     t2 = time.perf_counter()
     return {"seconds": round(t2 - t0, 3), "linears_s": round(t1 - t0, 3), "attention_s": round(t2 - t1, 3),
             "threads": thr, "kind": "port (linears) + torch CPU attention"}
+
+
+SS_FLOW = dict(C=1024, heads=16, n_blocks=24, n_shape=4096, in_ch=8, mlp_ratio=4)
+
+
+def ss_step_side(b2q, stream, dev, cpu_block=None, iters=5):
+    """One Euler / CFG sampling step of the full 24-block SS-flow DiT
+    (sam-3d-objects-ggml_b200/ss_flow.py) at BASELINE configs[4]: 4096 shape
+    tokens + 4 pose tokens, 1374 condition tokens, C 1024, Q8_0 random-init
+    weights generated on the device, both CFG branches in one batched pass.
+    Timed as a CUDA-graph replay (and eagerly, for the launch overhead) with
+    CUDA events; the step streams ~1 GB of weights, far above L2, so no flush.
+    The CPU figure is 24 x the measured CPU time of one block's heavy parts
+    (the pose group, adaLN and embeddings are not in it: a lower bound)."""
+    import torch
+    import ss_flow
+    cfg = SS_FLOW
+    C, nc = cfg["C"], SS_BLOCK["n_cond"]
+    specs = ss_flow.param_specs(C, cfg["n_blocks"], cfg["n_shape"], cfg["in_ch"], cfg["mlp_ratio"])
+    params = ss_flow.random_params(specs, dev, b2q.TYPE_Q8_0, seed=11)
+    wbytes = sum(int(v.numel()) for n, v in params.items() if v.dtype == torch.uint8)
+    flow = ss_flow.SsFlow(dev, params, **cfg)
+    del params
+    gen = torch.Generator(device=dev).manual_seed(13)
+    smp = ss_flow.SsSampler(flow, torch.randn(nc, C, device=dev, generator=gen), nc, seed=12)
+    t, dt = ss_flow.euler_schedule()[0]
+    t_model = t * 1000.0
+
+    def timed(n):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for e0, e1 in evs:
+            e0.record(stream)
+            smp.step(t_model, dt)
+            e1.record(stream)
+        torch.cuda.synchronize()
+        return statistics.median(e0.elapsed_time(e1) for e0, e1 in evs)
+
+    smp.step(t_model, dt)
+    eager_ms = timed(3)
+    smp.capture(cfg=True)
+    for _ in range(2):
+        smp.step(t_model, dt)
+    graph_ms = timed(iters)
+    finite = bool(torch.isfinite(smp.xs).all().item())
+    B, T, M = 2, cfg["n_shape"], 2 * cfg["n_shape"]
+    hid = C * cfg["mlp_ratio"]
+    per_group = lambda m: (ops_of(m, 3 * C, C) + 3 * ops_of(m, C, C) + ops_of(m, hid, C)  # noqa: E731
+                           + ops_of(m, C, hid))
+    lin_ops = cfg["n_blocks"] * (per_group(M) + per_group(B * 4) + 2 * ops_of(B * nc, 2 * C, C))
+    out = {"config": dict(cfg, n_cond=nc, cfg_branches=B, weights="Q8_0 (random codes and fp16 scales)",
+                          graph="whole step (forward + CFG blend + Euler update) in one CUDA graph"),
+           "step_ms": round(graph_ms, 3), "step_ms_eager": round(eager_ms, 3),
+           "weights_bytes": wbytes, "linear_int_ops": lin_ops,
+           "linear_tops_effective": round(lin_ops / (graph_ms * 1e-3) / 1e12, 1),
+           "state_finite": finite,
+           "path": "ss_flow.SsSampler: libb2q for every quantized linear, norm, quantize, head layout and "
+                   "fused epilogue; torch SDPA (fp16) attention cores; torch for the K<=8 F32 input layers, "
+                   "timestep cos/sin/SiLU and the Euler update"}
+    if cpu_block:
+        cpu_s = cpu_block["seconds"] * cfg["n_blocks"]
+        out["cpu_estimate_s"] = round(cpu_s, 2)
+        out["cpu_estimate"] = f"{cfg['n_blocks']} x one block's measured CPU time ({cpu_block['kind']})"
+        out["speedup_vs_cpu"] = round(cpu_s * 1e3 / graph_ms, 1)
+    del smp, flow
+    torch.cuda.empty_cache()
+    return out
+
+
+SLAT = dict(C=1024, n_blocks=24, grid=64, occupancy=0.03, n_cond=1374, fixed_tokens=(8192, 20480))
+
+
+def slat_tokens(seed: int = 3):
+    """BASELINE configs[3] token count: 3% of the 64^3 cells sampled without
+    replacement, downsampled to 32^3 (coarse = unique(coord // 2))."""
+    g = SLAT["grid"]
+    rng = np.random.default_rng(seed)
+    n_fine = int(round(SLAT["occupancy"] * g ** 3))
+    idx = rng.choice(g ** 3, n_fine, replace=False)
+    x, y, z = idx // (g * g), (idx // g) % g, idx % g
+    return n_fine, int(np.unique((x // 2) * 1024 + (y // 2) * 32 + z // 2).size)
+
+
+def slat_side(b2q, stream, dev, iters=3):
+    """the SLat flow transformer's linears over 24 blocks
+    with Q4_0 weights (random codes and fp16 scales generated on the device)
+    at the sampled sparse token count and at 8192 / 20480 tokens.  One pass =
+    for every block: qkv, out, cross q, cross kv (on the condition tokens),
+    cross out, fc1, fc2, each with its activation quantize (ggml mul_mat
+    semantics: every mul_mat quantizes its fp32 input).  The weights (216 MB)
+    and activations exceed L2, so no flush."""
+    import torch
+    import ss_flow
+    C, nbk, nc = SLAT["C"], SLAT["n_blocks"], SLAT["n_cond"]
+    shapes = ss_flow.linear_shapes(C, 4 * C)
+    specs = [(f"b{i}.{name}", "q", shp, (0.0, 0.02)) for i in range(nbk) for name, shp in shapes.items()]
+    raw = ss_flow.random_params(specs, dev, b2q.TYPE_Q4_0, seed=21)
+    W = {name: b2q.weight_pack(b2q.TYPE_Q4_0, raw[name], shp[1]) for name, _, shp, _ in specs}
+    del raw
+    n_fine, n_coarse = slat_tokens()
+    gen = torch.Generator(device=dev).manual_seed(22)
+    cond = torch.randn(nc, C, device=dev, generator=gen)
+    out = {"config": dict(SLAT, weights="Q4_0 (random codes and fp16 scales)", sampled_fine_cells=n_fine),
+           "runs": []}
+    for M in (n_coarse,) + SLAT["fixed_tokens"]:
+        x = torch.randn(M, C, device=dev, generator=gen)
+        xh = torch.randn(M, 4 * C, device=dev, generator=gen)
+        y = torch.empty(M * 4 * C, device=dev)
+        act = b2q._empty_aligned(b2q.act_prepared_size(M, 4 * C), dev)
+        act_c = b2q._empty_aligned(b2q.act_prepared_size(nc, C), dev)
+
+        def one_pass():
+            for i in range(nbk):
+                for name, (n, k) in shapes.items():
+                    src, m = (cond, nc) if name == "xkv" else ((xh, M) if name == "fc2" else (x, M))
+                    a = act_c if name == "xkv" else act
+                    b2q.act_prepare(src, out=a, stream=stream)
+                    b2q.mul_mat_prepared(W[f"b{i}.{name}"], n, k, a, m, out=y[:m * n].view(m, n), stream=stream)
+
+        one_pass()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+        for e0, e1 in evs:
+            e0.record(stream)
+            one_pass()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in evs)
+        ops = nbk * sum(ops_of(nc if name == "xkv" else M, n, k) for name, (n, k) in shapes.items())
+        out["runs"].append({"tokens": M, "source": "sampled" if M == n_coarse else "fixed",
+                            "ms_24_blocks": round(ms, 3), "int_ops": ops,
+                            "tops_incl_quantize": round(ops / (ms * 1e-3) / 1e12, 1),
+                            "launches": nbk * len(shapes) * 2})
+    del W
+    torch.cuda.empty_cache()
+    return out
 
 
 # ------------------------------------------------- column-parallel (multi-GPU)
