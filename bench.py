@@ -390,6 +390,7 @@ def run_gpu(args, rank, world, local_rank):
                                            cpu=(rank == 0 and world == 1 and not args.no_cpu_baseline))
         result["ss_step"] = ss_step_side(b2q, stream, dev, result["ss_block"].get("cpu"))
         result["slat_linears"] = slat_side(b2q, stream, dev)
+        result["f16"] = f16_side(b2q, flush, stream, dev, peaks)
     if args.only:
         result["config"]["workload"] = f"single GEMM {args.only} (profiling case)"
         result["config"]["l2"] = "not flushed (profiling case)"
@@ -683,6 +684,39 @@ def ss_step_side(b2q, stream, dev, cpu_block=None, iters=5):
         out["speedup_vs_cpu"] = round(cpu_s * 1e3 / graph_ms, 1)
     del smp, flow
     torch.cuda.empty_cache()
+    return out
+
+
+def f16_side(b2q, flush, stream, dev, peaks, iters=10):
+    """F16-weight mul_mat (b2q_mul_mat with B2Q_TYPE_F16: fp16 rounding of the
+    activations + the tcgen05 kind::f16 GEMM) at the fc1 / fc2 shapes, L2
+    flushed between runs.  Tensor-bound: reported against the measured dense
+    bf16 rate (fp16 runs at the same rate on the tensor cores)."""
+    import torch
+    gen = torch.Generator(device=dev).manual_seed(31)
+    out = {"kernel": "gemm_f16_kernel (tcgen05 kind::f16, fp32 TMEM accumulators)", "gemms": []}
+    peak = peaks.get("bf16_tflops")
+    for name, M, N, K in (("fc1_f16", 4096, 4096, 1024), ("fc2_f16", 4096, 1024, 4096)):
+        w = (torch.randn(N, K, device=dev, generator=gen) * 0.02).half()
+        x = torch.randn(M, K, device=dev, generator=gen)
+        y = torch.empty(M, N, device=dev)
+        ws = b2q._empty_aligned(b2q.lib().b2q_mul_mat_workspace_bytes(b2q.TYPE_F16, M, N, K, 0), dev)
+        for _ in range(3):
+            b2q.mul_mat(b2q.TYPE_F16, w, x, out=y, ws=ws, stream=stream)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record(stream)
+            b2q.mul_mat(b2q.TYPE_F16, w, x, out=y, ws=ws, stream=stream)
+            e1.record(stream)
+        torch.cuda.synchronize()
+        us = statistics.median(e0.elapsed_time(e1) for e0, e1 in evs) * 1e3
+        tflops = ops_of(M, N, K) / (us * 1e-6) / 1e12
+        row = {"name": name, "M": M, "N": N, "K": K, "us_incl_fp16_rounding": round(us, 2),
+               "tflops": round(tflops, 1)}
+        if peak:
+            row["frac_of_measured_bf16"] = round(tflops / peak, 4)
+        out["gemms"].append(row)
     return out
 
 

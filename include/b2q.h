@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-enum b2q_type { B2Q_TYPE_F32 = 0, B2Q_TYPE_Q4_0 = 2, B2Q_TYPE_Q8_0 = 8, B2Q_TYPE_Q4_K = 12 };
+enum b2q_type { B2Q_TYPE_F32 = 0, B2Q_TYPE_F16 = 1, B2Q_TYPE_Q4_0 = 2, B2Q_TYPE_Q8_0 = 8, B2Q_TYPE_Q4_K = 12 };
 
 /* Activation-quantizer variant (fp32 -> Q8_0 rounding).
  *   B2Q_ACT_X86: the from_float of ggml's CPU backend on x86 (the host the
@@ -135,6 +135,12 @@ B2Q_API int b2q_mul_mat(int wtype, const void* w, int64_t w_row_stride_bytes, in
                 const float* x, int64_t m, int64_t x_row_stride_bytes, const float* bias,
                 float* y, int64_t y_row_stride_bytes, int variant, void* workspace,
                 size_t workspace_bytes, void* stream);
+/* With wtype = B2Q_TYPE_F16 (src0 F16, ggml_mul_mat's path for F16 GGUF
+ * tensors): x is rounded to fp16 (ggml's vec_dot_type for F16, round to nearest
+ * even) into the workspace, then a tcgen05 kind::f16 GEMM with fp32
+ * accumulation reads the weight rows in place.  k % 8 == 0; w and its row
+ * stride 16-byte aligned; variant must be B2Q_ACT_X86 or B2Q_ACT_REF and is
+ * not used; workspace = b2q_mul_mat_workspace_bytes(B2Q_TYPE_F16, m, n, k, 0). */
 
 /* Same with a weight packed once by b2q_weight_pack (the production path). */
 B2Q_API int b2q_mul_mat_packed(const void* packed, int64_t n, int64_t k, const float* x, int64_t m,

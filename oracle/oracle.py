@@ -23,7 +23,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "libb2q_oracle.so")
 
 QK = 32
-TYPE_F32, TYPE_Q4_0, TYPE_Q8_0, TYPE_Q4_K = 0, 2, 8, 12
+TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q8_0, TYPE_Q4_K = 0, 1, 2, 8, 12
 QK_K, Q4_K_BYTES, Q8_K_BYTES = 256, 144, 292
 ACT_X86, ACT_REF = 0, 1
 BLOCK_BYTES = {TYPE_Q8_0: 34, TYPE_Q4_0: 18}
@@ -150,6 +150,19 @@ def mul_mat(wtype: int, w: np.ndarray, x: np.ndarray, act_variant: int = ACT_X86
     if rc < 0:
         raise MemoryError("oracle mul_mat failed to allocate")
     return y
+
+
+def mul_mat_f16(w16: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """GGML_OP_MUL_MAT with src0 F16 on ggml's CPU backend (the F16 GGUF
+    tensors and the autocast linears, cpp_ggml/src/slat_flow_graph.cpp:29-40;
+    exercised by cpp_ggml/src/matmul_backend_test.cpp:177-183): src1 is rounded
+    to fp16 (vec_dot_type F16, round to nearest even), and each output is one
+    dot of fp16 x fp16 products (exact in fp32) summed in wide precision
+    (ggml_vec_dot_f16 accumulates in fp32 SIMD lanes and a double; this fp64
+    sum differs from it by far less than the 1e-5 parity bar) -> fp32."""
+    x16 = np.asarray(x, dtype=np.float32).astype(np.float16)
+    w = np.asarray(w16, dtype=np.float16)
+    return (x16.astype(np.float64) @ w.astype(np.float64).T).astype(np.float32)
 
 
 def mul_mat_f64(wtype: int, w: np.ndarray, a: np.ndarray, K: int) -> np.ndarray:

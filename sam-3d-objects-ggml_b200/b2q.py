@@ -21,7 +21,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libb2q.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "b2q.h")
 
-TYPE_F32, TYPE_Q4_0, TYPE_Q8_0, TYPE_Q4_K = 0, 2, 8, 12
+TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q8_0, TYPE_Q4_K = 0, 1, 2, 8, 12
 ACT_X86, ACT_REF, ACT_Q8_K = 0, 1, 2
 QK, QK_K = 32, 256
 BLOCK_BYTES = {TYPE_Q8_0: 34, TYPE_Q4_0: 18}
@@ -206,8 +206,9 @@ def workspace(m: int, n: int, k: int, packed_weight: bool, device):
 
 def mul_mat(wtype: int, w, x, k: int | None = None, bias=None, variant: int | None = None,
             out=None, ws=None, stream=None):
-    """ggml_mul_mat(w, x) (+ bias): w raw blocks uint8 [N, >=row_bytes], x fp32 [M, K] -> [M, N].
-    variant defaults to ACT_X86 (ACT_Q8_K for Q4_K weights)."""
+    """ggml_mul_mat(w, x) (+ bias): w raw blocks uint8 [N, >=row_bytes] (TYPE_F16:
+    float16 [N, >=K]), x fp32 [M, K] -> [M, N].  variant defaults to ACT_X86
+    (ACT_Q8_K for Q4_K weights)."""
     torch = _torch()
     m, kk = x.shape
     k = kk if k is None else k
@@ -218,7 +219,7 @@ def mul_mat(wtype: int, w, x, k: int | None = None, bias=None, variant: int | No
         out = torch.empty((m, n), dtype=torch.float32, device=x.device)
     if ws is None:
         ws = _empty_aligned(lib().b2q_mul_mat_workspace_bytes(wtype, m, n, k, 0), x.device)
-    rc = lib().b2q_mul_mat(wtype, _ptr(w), w.stride(0), n, k, _ptr(x), m, x.stride(0) * 4,
+    rc = lib().b2q_mul_mat(wtype, _ptr(w), w.stride(0) * w.element_size(), n, k, _ptr(x), m, x.stride(0) * 4,
                            _ptr(bias), _ptr(out), out.stride(0) * 4, variant, _ptr(ws), ws.numel(),
                            _stream(stream))
     _check("b2q_mul_mat", rc)

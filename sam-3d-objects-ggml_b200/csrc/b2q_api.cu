@@ -219,7 +219,34 @@ size_t b2q_act_prepared_bytes(int variant, int64_t m, int64_t k) {
   return variant == B2Q_ACT_X86 || variant == B2Q_ACT_REF ? split_bytes(m, k) : 0;
 }
 
+// fp16 copy of the activations for F16 weights.
+size_t f16_act_bytes(int64_t m, int64_t k) { return round_up(m * k * 2, 256); }
+
+// ggml_mul_mat with F16 weights: x -> fp16 (round to nearest even) in the
+// workspace, then the kind::f16 GEMM on the weight rows in place.
+int mul_mat_f16(const void* w, int64_t ldw, int64_t n, int64_t k, const float* x, int64_t m, int64_t ldx,
+                const float* bias, float* y, int64_t ldy, int variant, void* workspace, size_t workspace_bytes,
+                void* stream) {
+  if (n < 0 || k <= 0 || k % 8 != 0) return B2Q_ERR_INVALID_ARG;
+  if (n > INT_MAX || k > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (n > 0 && !w) return B2Q_ERR_INVALID_ARG;
+  if (ldw < 2 * k) return B2Q_ERR_INVALID_ARG;
+  if (variant != B2Q_ACT_X86 && variant != B2Q_ACT_REF) return B2Q_ERR_INVALID_ARG;
+  if (int rc = check_x_y(x, m, k, ldx, y, n, ldy, variant)) return rc;
+  if (!aligned(w, 16) || ldw % 16 != 0 || !aligned(workspace, 256) || (bias && !aligned(bias, 4)))
+    return B2Q_ERR_MISALIGNED;
+  if (m == 0 || n == 0) return B2Q_OK;
+  if (!workspace || workspace_bytes < f16_act_bytes(m, k)) return B2Q_ERR_WORKSPACE;
+  int sms = 0;
+  if (int rc = check_device(&sms)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool vec4 = aligned(x, 16) && ldx % 16 == 0;
+  if (launch_to_f16(x, m, k, ldx / 4, workspace, k, vec4, s) != cudaSuccess) return B2Q_ERR_CUDA;
+  return from_cuda(launch_gemm_f16(w, ldw, workspace, k * 2, m, n, k, y, ldy / 4, bias, sms, s));
+}
+
 size_t b2q_mul_mat_workspace_bytes(int wtype, int64_t m, int64_t n, int64_t k, int packed_weight) {
+  if (wtype == B2Q_TYPE_F16) return (m < 0 || n < 0 || k <= 0 || k % 8 != 0) ? 0 : f16_act_bytes(m, k);
   if (wtype != B2Q_TYPE_Q4_K) return valid_wtype(wtype) ? b2q_mul_mat_workspace_size(m, n, k, packed_weight) : 0;
   if (m < 0 || n < 0 || k <= 0 || k % kQKK != 0) return 0;
   return q8k_bytes(m, k) + (packed_weight ? 0 : q4k_bytes(n, k));
@@ -331,6 +358,9 @@ int b2q_mul_mat(int wtype, const void* w, int64_t w_row_stride_bytes, int64_t n,
                 const float* x, int64_t m, int64_t x_row_stride_bytes, const float* bias,
                 float* y, int64_t y_row_stride_bytes, int variant, void* workspace,
                 size_t workspace_bytes, void* stream) {
+  if (wtype == B2Q_TYPE_F16)
+    return mul_mat_f16(w, w_row_stride_bytes, n, k, x, m, x_row_stride_bytes, bias, y, y_row_stride_bytes, variant,
+                       workspace, workspace_bytes, stream);
   if (int rc = check_raw_weight(wtype, w, w_row_stride_bytes, n, k)) return rc;
   if (int rc = check_x_y(x, m, k, x_row_stride_bytes, y, n, y_row_stride_bytes, variant)) return rc;
   if ((wtype == B2Q_TYPE_Q4_K) != (variant == B2Q_ACT_Q8_K)) return B2Q_ERR_INVALID_ARG;

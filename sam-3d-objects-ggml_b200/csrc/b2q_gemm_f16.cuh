@@ -1,0 +1,245 @@
+// b2q_gemm_f16.cuh -- F16 weights x F32 activations (GGML_OP_MUL_MAT with
+// src0 F16): the activations are rounded to fp16 first (ggml's CPU backend
+// converts src1 to its vec_dot_type, F16, with round-to-nearest-even), then
+//   y[m][n] = sum_k w16[n][k] * x16[m][k]   (fp32 accumulation)
+// on the tensor cores: tcgen05.mma kind::f16 (A = B = F16, never BF16), fp32
+// accumulators in TMEM carried over all of K.  No per-block scales, so this is
+// a plain GEMM: the epilogue runs once per tile, not once per 32 values.
+//
+// Structure (persistent, one CTA per SM, 192 threads):
+//   warp 0      TMA producer: weight tile [128 rows x 64 K] and activation
+//               tile [256 tokens x 64 K] per stage (one 128-byte swizzle row
+//               of fp16 each), 4 stages of 48 KB
+//   warp 1      TMEM allocator (512 columns) + single-thread MMA issuer:
+//               4 MMAs (M 128, N 256, K 16) per stage into one of two
+//               256-column accumulators, so a tile's epilogue overlaps the
+//               next tile's MMAs
+//   warps 2..5  epilogue: thread t of warp w owns weight row 32*(w%4) + t (its
+//               TMEM lane) and all 256 token columns; 32-column TMEM loads,
+//               double-buffered, bias add, 128-byte coalesced stores
+// Tiles run weight-row-fastest, so the CTAs of one wave share activation tiles
+// in L2.  Every wait is bounded; no TMA multicast.
+//
+// Included by b2q_gemm_tc.cu (same device status word, one translation unit).
+#pragma once
+
+namespace b2q {
+
+namespace f16 {
+
+constexpr int kBM = 128;             // weight rows per tile (MMA M, TMEM lanes)
+constexpr int kBN = 256;             // tokens per tile (MMA N)
+constexpr int kStageK = 64;          // fp16 values of K per stage (128 bytes)
+constexpr int kMmaK = 16;            // K per kind::f16 MMA (32 bytes)
+constexpr int kStages = 4;
+constexpr int kAccs = 2;             // TMEM accumulators of kBN columns
+constexpr uint32_t kTmemColsF = kAccs * kBN;
+constexpr int kEpiWarp0 = 2, kEpiWarps = 4;
+constexpr int kThreadsF = (kEpiWarp0 + kEpiWarps) * 32;
+constexpr int kABytes = kBM * kStageK * 2;  // 16 KB
+constexpr int kBBytes = kBN * kStageK * 2;  // 32 KB
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kOffBars = kStages * kStageBytes;
+constexpr int kNBars = 2 * kStages + 2 * kAccs + 1;  // full, empty, acc_full, acc_empty, done
+constexpr int kSmemF = kOffBars + kNBars * 8 + 16 + 1024;  // + alignment slack
+static_assert(kSmemF <= 227 * 1024, "shared memory per CTA");
+static_assert(kStageBytes % 1024 == 0 && kABytes % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
+static_assert(kTmemColsF <= 512, "TMEM columns");
+
+struct F16Params {
+  int M, N, kst, n_tiles, num_tiles;
+  float* y;
+  int64_t ldy;
+  const float* bias;
+};
+
+__global__ void __launch_bounds__(kThreadsF, 1)
+    gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                    const F16Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBars);
+  uint64_t* empty = full + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint64_t* acc_empty = acc_full + kAccs;
+  uint64_t* mma_done = acc_empty + kAccs;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < kAccs; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], kEpiWarps);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, kTmemColsF);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      uint32_t stage = 0, phase = 0, issued_mask = 0, issued_par = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        const int n0 = (tile % p.n_tiles) * kBM;
+        const int m0 = (tile / p.n_tiles) * kBN;
+        for (int ks = 0; ks < p.kst; ++ks) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, &g_device_status, kDevWaitProducer, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sb = smem + stage * kStageBytes;
+          mbar_arrive_expect_tx(&full[stage], kStageBytes);
+          tma_load_2d(sb, &tm_w, &full[stage], ks * kStageK, n0);            // x * 2 bytes = 128 * ks
+          tma_load_2d(sb + kABytes, &tm_x, &full[stage], ks * kStageK, m0);
+          issued_mask |= 1u << stage;
+          issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      for (int s = 0; s < kStages; ++s)  // every issued copy lands before the CTA may exit
+        if ((issued_mask >> s) & 1u)
+          mbar_wait(&full[s], (issued_par >> s) & 1u, &g_device_status, kDevWaitDrain, nullptr);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idesc = idesc_f16(kBM, kBN);
+      uint32_t stage = 0, phase = 0, t = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++t) {
+        const uint32_t a = t & (kAccs - 1), apar = (t / kAccs) & 1u;
+        if (!mbar_wait(&acc_empty[a], apar ^ 1u, &g_device_status, kDevWaitMma, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + a * kBN;
+        for (int ks = 0; ks < p.kst; ++ks) {
+          if (!mbar_wait(&full[stage], phase, &g_device_status, kDevWaitMma, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + stage * kStageBytes);
+          const uint32_t b_base = a_base + kABytes;
+#pragma unroll
+          for (int j = 0; j < kStageK / kMmaK; ++j)
+            mma_f16(d, smem_desc_k_sw128(a_base + j * kMmaK * 2), smem_desc_k_sw128(b_base + j * kMmaK * 2), idesc,
+                    (ks | j) != 0 ? 1u : 0u);
+          mma_commit(&empty[stage]);  // the stage goes back once its MMAs have read it
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) mma_commit(&acc_full[a]);
+      }
+      mma_commit(mma_done);  // all issued MMAs complete before TMEM is released
+      mbar_wait(mma_done, 0, &g_device_status, kDevWaitDrain, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;
+    const uint32_t tlane = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+    uint32_t t = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++t) {
+      const uint32_t a = t & (kAccs - 1), apar = (t / kAccs) & 1u;
+      if (!mbar_wait(&acc_full[a], apar, &g_device_status, kDevWaitEpilogue, abort_flag)) break;
+      tc_fence_after();
+      const int64_t n = static_cast<int64_t>(tile % p.n_tiles) * kBM + row;
+      const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * kBN;
+      const bool nv = n < p.N;
+      const float bv = (p.bias && nv) ? p.bias[n] : 0.0f;
+      float* yp = p.y + m0 * p.ldy + n;
+      uint32_t buf[2][32];
+      tmem_ld_32x32b_x32(tlane + a * kBN, buf[0]);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) {
+        if (c + 1 < kBN / 32) tmem_ld_32x32b_x32(tlane + a * kBN + (c + 1) * 32, buf[(c + 1) & 1]);
+        if (nv) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int64_t m = m0 + c * 32 + i;
+            const float v = __uint_as_float(buf[c & 1][i]);
+            if (m < p.M) yp[(c * 32 + i) * p.ldy] = p.bias ? __fadd_rn(v, bv) : v;  // gb_linear's ggml_add
+          }
+        }
+        tmem_wait_ld();
+        if (c == kBN / 32 - 2) {  // the last chunk is in registers: the accumulator goes back
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[a]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemColsF);
+  }
+}
+
+}  // namespace f16
+
+cudaError_t launch_gemm_f16(const void* w, int64_t ldw_bytes, const void* x16, int64_t ldx_bytes, int64_t M,
+                            int64_t N, int64_t K, float* y, int64_t ldy, const float* bias, int num_sms,
+                            cudaStream_t s) {
+  if (M == 0 || N == 0) return cudaSuccess;
+  if (K <= 0 || K % 8 != 0 || M > INT32_MAX || N > INT32_MAX) return cudaErrorInvalidValue;
+  CUtensorMap tm_w, tm_x;
+  if (!make_tensor_map_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, w, K, N, ldw_bytes, f16::kStageK, f16::kBM,
+                          CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tensor_map_2d(&tm_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x16, K, M, ldx_bytes, f16::kStageK, f16::kBN,
+                          CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  f16::F16Params p;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.kst = static_cast<int>((K + f16::kStageK - 1) / f16::kStageK);
+  p.n_tiles = static_cast<int>((N + f16::kBM - 1) / f16::kBM);
+  const int64_t tiles = static_cast<int64_t>(p.n_tiles) * ((M + f16::kBN - 1) / f16::kBN);
+  if (tiles > INT32_MAX) return cudaErrorInvalidValue;
+  p.num_tiles = static_cast<int>(tiles);
+  p.y = y;
+  p.ldy = ldy;
+  p.bias = bias;
+  static std::atomic<uint64_t> ready{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
+  const uint64_t bit = dev < 64 ? (uint64_t{1} << dev) : 0;
+  if (!bit || !(ready.load(std::memory_order_acquire) & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(f16::gemm_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, f16::kSmemF);
+    if (e != cudaSuccess) return e;
+    ready.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  const int grid = p.num_tiles < num_sms ? p.num_tiles : num_sms;
+  f16::gemm_f16_kernel<<<grid, f16::kThreadsF, f16::kSmemF, s>>>(tm_w, tm_x, p);
+  return cudaGetLastError();
+}
+
+}  // namespace b2q

@@ -719,5 +719,6 @@ cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, cudaStream_t s) {
 
 }  // namespace b2q
 
-// The Q4_K kernel shares this translation unit (and g_device_status).
+// The Q4_K and F16 kernels share this translation unit (and g_device_status).
 #include "b2q_gemm_q4k.cuh"
+#include "b2q_gemm_f16.cuh"

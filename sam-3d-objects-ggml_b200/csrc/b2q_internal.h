@@ -172,6 +172,16 @@ struct Q4kArgs {
 };
 cudaError_t launch_gemm_q4k(const Q4kArgs& args, int num_sms, cudaStream_t s);
 
+// F16 weights (b2q_gemm_f16.cuh): w fp16 [N][K] rows ldw_bytes apart, x16 fp16
+// [M][K] rows ldx_bytes apart (both 16-byte aligned, K % 8 == 0);
+// y[m][n] = sum_k w[n][k] x16[m][k] (+ bias[n]), fp32, ldy floats.
+cudaError_t launch_gemm_f16(const void* w, int64_t ldw_bytes, const void* x16, int64_t ldx_bytes, int64_t M,
+                            int64_t N, int64_t K, float* y, int64_t ldy, const float* bias, int num_sms,
+                            cudaStream_t s);
+// fp32 rows -> fp16 rows [m][ldy] (round to nearest even), k % 8 == 0.
+cudaError_t launch_to_f16(const float* x, int64_t m, int64_t k, int64_t ldx_floats, void* y, int64_t ldy,
+                          bool vec4, cudaStream_t s);
+
 // CUDA-core kernel for M <= kGemvMaxM tokens (plain, bias, gate + residual);
 // bit-identical to the tensor-core kernel (b2q_gemv.cu).
 constexpr int64_t kGemvMaxM = 8;

@@ -147,6 +147,18 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T, f16 x f16 -> fp32 (kind::f16; A and B
+// both f16 -- the descriptor never mixes f16 with bf16).
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on `bar` once all previously issued tcgen05 async ops of this thread completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile(
@@ -229,6 +241,16 @@ __host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
   return (2u << 4)                               // D = S32
          | (1u << 7)                             // A = signed 8-bit
          | (1u << 10)                            // B = signed 8-bit
+         | (static_cast<uint32_t>(n >> 3) << 17) // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);  // M / 16
+}
+
+// Instruction descriptor: kind::f16 with A = B = F16 (never BF16), fp32 D,
+// both K-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
+  return (1u << 4)                               // D = F32
+         | (0u << 7)                             // A = F16
+         | (0u << 10)                            // B = F16
          | (static_cast<uint32_t>(n >> 3) << 17) // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);  // M / 16
 }

@@ -278,6 +278,57 @@ cudaError_t launch_quantize_q8_k(const float* x, int64_t m, int64_t k, int64_t l
   return cudaGetLastError();
 }
 
+// fp32 -> fp16 rows, round to nearest even: the src1 conversion of ggml's
+// mul_mat against F16 weights (vec_dot_type F16; the CPU backend's F16C
+// conversion with rounding mode 0).  Eight values per thread, one 16-byte store.
+template <bool VEC4>
+__global__ void __launch_bounds__(256) to_f16_kernel(const float* __restrict__ x, int64_t m, int64_t k, int64_t ldx,
+                                                     __half* __restrict__ y, int64_t ldy) {
+  const int64_t per_row = k / 8;
+  const int64_t units = m * per_row;
+  for (int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < units;
+       u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = u / per_row, c = (u - r * per_row) * 8;
+    const float* src = x + r * ldx + c;
+    float v[8];
+    if (VEC4) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+      v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = __ldg(src + i);
+    }
+    uint4 o;
+    __half2 h;
+    h = __floats2half2_rn(v[0], v[1]);
+    o.x = *reinterpret_cast<uint32_t*>(&h);
+    h = __floats2half2_rn(v[2], v[3]);
+    o.y = *reinterpret_cast<uint32_t*>(&h);
+    h = __floats2half2_rn(v[4], v[5]);
+    o.z = *reinterpret_cast<uint32_t*>(&h);
+    h = __floats2half2_rn(v[6], v[7]);
+    o.w = *reinterpret_cast<uint32_t*>(&h);
+    *reinterpret_cast<uint4*>(y + r * ldy + c) = o;
+  }
+}
+
+cudaError_t launch_to_f16(const float* x, int64_t m, int64_t k, int64_t ldx_floats, void* y, int64_t ldy,
+                          bool vec4, cudaStream_t s) {
+  const int64_t units = m * (k / 8);
+  if (units == 0) return cudaSuccess;
+  int sms = current_device_sms();
+  if (sms <= 0) sms = 148;
+  const int64_t blocks = (units + 255) / 256;
+  const int grid = static_cast<int>(blocks < sms * 8 ? blocks : sms * 8);
+  __half* yh = static_cast<__half*>(y);
+  if (vec4)
+    to_f16_kernel<true><<<grid, 256, 0, s>>>(x, m, k, ldx_floats, yh, ldy);
+  else
+    to_f16_kernel<false><<<grid, 256, 0, s>>>(x, m, k, ldx_floats, yh, ldy);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_pack_weights(int wtype, const uint8_t* w, int64_t n, int64_t k,
                                 int64_t ldw_bytes, int8_t* codes, float* scales, int64_t ld,
                                 cudaStream_t s) {

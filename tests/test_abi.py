@@ -232,3 +232,18 @@ def test_attention_io_validation(b2q_mod):
     assert ln(FAKE, 4, 64, 256, 1e-6, None, None, 2, FAKE, need, None) == 1              # variant
     assert ln(FAKE, 4, 64, 256, 1e-6, None, None, 0, FAKE, need - 1, None) == 4          # act too small
     assert ln(FAKE, 0, 64, 256, 1e-6, None, None, 0, FAKE, 0, None) == 0                 # empty: no-op
+
+
+def test_f16_validation(b2q_mod):
+    L = b2q.lib()
+    f = L.b2q_mul_mat
+    ws = 1 << 22
+    assert L.b2q_mul_mat_workspace_bytes(1, 33, 65, 256, 0) == (33 * 256 * 2 + 255) // 256 * 256
+    assert L.b2q_mul_mat_workspace_bytes(1, 33, 65, 252, 0) == 0                              # k % 8
+    assert f(1, FAKE, 2016, 64, 1004, FAKE, 4, 4016, None, FAKE, 256, 0, FAKE, ws, None) == 1  # k % 8
+    assert f(1, FAKE, 1024, 64, 1024, FAKE, 4, 4096, None, FAKE, 256, 0, FAKE, ws, None) == 1  # row stride < 2k
+    assert f(1, FAKE + 2, 2048, 64, 1024, FAKE, 4, 4096, None, FAKE, 256, 0, FAKE, ws, None) == 3  # w alignment
+    assert f(1, FAKE, 2056, 64, 1024, FAKE, 4, 4096, None, FAKE, 256, 0, FAKE, ws, None) == 3  # stride % 16
+    assert f(1, FAKE, 2048, 64, 1024, FAKE, 4, 4096, None, FAKE, 256, 2, FAKE, ws, None) == 1  # Q8_K variant
+    assert f(1, FAKE, 2048, 64, 1024, FAKE, 4, 4096, None, FAKE, 256, 0, FAKE, 100, None) == 4  # workspace
+    assert f(1, FAKE, 2048, 64, 1024, FAKE, 0, 4096, None, FAKE, 256, 0, FAKE, 0, None) == 0    # m == 0
