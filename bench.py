@@ -687,6 +687,35 @@ def ss_step_side(b2q, stream, dev, cpu_block=None, iters=5):
     return out
 
 
+F16_CASES = {"f16_fc1": (4096, 4096, 1024), "f16_fc2": (4096, 1024, 4096)}
+
+
+def run_f16_case(args):
+    """Profiling case: --steps F16 mul_mats of one shape (after --warmup), no
+    side measurements; prints the median CUDA-event time per call."""
+    import torch
+    import b2q
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    M, N, K = F16_CASES[args.only]
+    gen = torch.Generator(device=dev).manual_seed(31)
+    w = (torch.randn(N, K, device=dev, generator=gen) * 0.02).half()
+    x = torch.randn(M, K, device=dev, generator=gen)
+    y = torch.empty(M, N, device=dev)
+    ws = b2q._empty_aligned(b2q.lib().b2q_mul_mat_workspace_bytes(b2q.TYPE_F16, M, N, K, 0), dev)
+    for _ in range(args.warmup):
+        b2q.mul_mat(b2q.TYPE_F16, w, x, out=y, ws=ws)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for e0, e1 in evs:
+        e0.record()
+        b2q.mul_mat(b2q.TYPE_F16, w, x, out=y, ws=ws)
+        e1.record()
+    torch.cuda.synchronize()
+    us = statistics.median(e0.elapsed_time(e1) for e0, e1 in evs) * 1e3
+    return {"case": args.only, "M": M, "N": N, "K": K, "us_median_hot_l2": round(us, 2),
+            "tflops": round(ops_of(M, N, K) / (us * 1e-6) / 1e12, 1), "launches_per_call": 2}
+
+
 def f16_side(b2q, flush, stream, dev, peaks, iters=10):
     """F16-weight mul_mat (b2q_mul_mat with B2Q_TYPE_F16: fp16 rounding of the
     activations + the tcgen05 kind::f16 GEMM) at the fc1 / fc2 shapes, L2
@@ -992,7 +1021,10 @@ def main():
         if rank == 0:
             print(json.dumps(run_reference(args)), flush=True)
         return
-    res = run_colpar(args, rank, world, local_rank) if args.colpar else run_gpu(args, rank, world, local_rank)
+    if args.only in F16_CASES:
+        res = run_f16_case(args)
+    else:
+        res = run_colpar(args, rank, world, local_rank) if args.colpar else run_gpu(args, rank, world, local_rank)
     if rank == 0:
         print(json.dumps(res), flush=True)
 
