@@ -391,6 +391,7 @@ def run_gpu(args, rank, world, local_rank):
         result["ss_step"] = ss_step_side(b2q, stream, dev, result["ss_block"].get("cpu"))
         result["slat_linears"] = slat_side(b2q, stream, dev)
         result["f16"] = f16_side(b2q, flush, stream, dev, peaks)
+        result["slat_sparse"] = slat_sparse_side(b2q, flush, stream, dev, peaks)
     if args.only:
         result["config"]["workload"] = f"single GEMM {args.only} (profiling case)"
         result["config"]["l2"] = "not flushed (profiling case)"
@@ -761,6 +762,92 @@ def slat_tokens(seed: int = 3):
     idx = rng.choice(g ** 3, n_fine, replace=False)
     x, y, z = idx // (g * g), (idx // g) % g, idx % g
     return n_fine, int(np.unique((x // 2) * 1024 + (y // 2) * 32 + z // 2).size)
+
+
+def neighbour_table(keys: np.ndarray, g: int) -> np.ndarray:
+    """27-neighbour table (offset-major, -1 = missing) of the sorted cell keys
+    (x * g + y) * g + z of a g^3 grid."""
+    n = keys.size
+    xyz = np.stack([keys // (g * g), (keys // g) % g, keys % g], 1)
+    idx = np.full((27, n), -1, np.int32)
+    o = 0
+    for dx in (-1, 0, 1):
+        for dy in (-1, 0, 1):
+            for dz in (-1, 0, 1):
+                q = xyz + np.array([dx, dy, dz])
+                inside = np.all((q >= 0) & (q < g), 1)
+                qk = (q[:, 0] * g + q[:, 1]) * g + q[:, 2]
+                pos = np.clip(np.searchsorted(keys, qk), 0, n - 1)
+                hit = inside & (keys[pos] == qk)
+                idx[o, hit] = pos[hit]
+                o += 1
+    return idx
+
+
+def slat_grid_tables(seed: int = 3):
+    """The configs[3] sparse grid (3% of 64^3 sampled without replacement):
+    the 27-neighbour tables of the fine cells and of their 2x-downsampled
+    coarse cells, and the downsample mapping (coarse row per fine cell,
+    divisors |children| + 1)."""
+    g = SLAT["grid"]
+    rng = np.random.default_rng(seed)
+    n = int(round(SLAT["occupancy"] * g ** 3))
+    keys = np.sort(rng.choice(g ** 3, n, replace=False))
+    x, y, z = keys // (g * g), (keys // g) % g, keys % g
+    ck = ((x // 2) * (g // 2) + y // 2) * (g // 2) + z // 2
+    ckeys, rows = np.unique(ck, return_inverse=True)
+    counts = (np.bincount(rows, minlength=ckeys.size) + 1).astype(np.float32)
+    return neighbour_table(keys, g), neighbour_table(ckeys, g // 2), rows.astype(np.int32), counts
+
+
+def slat_sparse_side(b2q, flush, stream, dev, peaks, iters=10):
+    """The SLat sparse stages at the configs[3] grid: the F16 submanifold
+    convolution (gather of the 27 neighbour rows + kind::f16 GEMM) on the fine
+    cells at 128 -> 128 channels and on the coarse cells at 256 -> 256, and
+    the F16 scatter-mean (2x downsample) of 128 channels.  L2 flushed between
+    runs; CUDA events."""
+    import torch
+    idx, cidx, rows, counts = slat_grid_tables()
+    fine, coarse = idx.shape[1], cidx.shape[1]
+    gen = torch.Generator(device=dev).manual_seed(41)
+
+    def timed(fn):
+        fn()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        return statistics.median(e0.elapsed_time(e1) for e0, e1 in evs) * 1e3
+
+    out = {"grid": f"{SLAT['grid']}^3 at {SLAT['occupancy']:.0%}", "fine_cells": fine, "coarse_cells": coarse,
+           "conv": []}
+    idx_d = torch.from_numpy(idx).to(dev)
+    for name, tokens, C, cout, table in (("fine_128_128", fine, 128, 128, idx_d),
+                                         ("coarse_256_256", coarse, 256, 256, torch.from_numpy(cidx).to(dev))):
+        x16 = torch.randn(tokens, C, device=dev, generator=gen).half()
+        w16 = (torch.randn(cout, 27 * C, device=dev, generator=gen) / (27 * C) ** 0.5).half()
+        b16 = (torch.randn(cout, device=dev, generator=gen) * 0.1).half()
+        y16 = torch.empty(tokens, cout, device=dev, dtype=torch.float16)
+        ws = b2q._empty_aligned(b2q.lib().b2q_sparse_conv_f16_workspace_bytes(tokens, C, cout), dev)
+        us = timed(lambda: b2q.sparse_conv_f16(x16, w16, b16, table, out=y16, ws=ws, stream=stream))
+        flops = 2.0 * tokens * cout * 27 * C
+        valid = int((table >= 0).sum().item())
+        row = {"name": name, "tokens": tokens, "C": C, "Cout": cout, "us": round(us, 2),
+               "tflops_dense_27": round(flops / (us * 1e-6) / 1e12, 1),
+               "valid_neighbour_fraction": round(valid / (27 * tokens), 3),
+               "gather_bytes": tokens * 27 * C * 2, "launches": 3}
+        out["conv"].append(row)
+    x16 = torch.randn(fine, 128, device=dev, generator=gen).half()
+    rows_d, counts_d = torch.from_numpy(rows).to(dev), torch.from_numpy(counts).to(dev)
+    o16 = torch.empty(coarse, 128, device=dev, dtype=torch.float16)
+    ws = b2q._empty_aligned(b2q.lib().b2q_sparse_scatter_mean_workspace_bytes(fine, coarse), dev)
+    us = timed(lambda: b2q.sparse_scatter_mean_f16(x16, rows_d, counts_d, coarse, out=o16, ws=ws, stream=stream))
+    out["scatter_mean"] = {"fine": fine, "coarse": coarse, "C": 128, "us": round(us, 2),
+                           "bytes": fine * 256 + coarse * 256 + fine * 8, "launches": 6}
+    return out
 
 
 def slat_side(b2q, stream, dev, iters=3):

@@ -327,6 +327,37 @@ B2Q_API int b2q_mul_mat_q_simt(int wtype, const void* w, int64_t w_row_stride_by
                        int64_t k, const void* a, int64_t m, int64_t a_row_stride_bytes,
                        float* y, int64_t y_row_stride_bytes, void* stream);
 
+/* ------------------------------------------------------ SLat sparse stages
+ * b2q_sparse_conv_f16: the F16 submanifold convolution of the SLat flow
+ * transformer, ggml_sam3d_sparse_conv_f16 (ggml patch
+ * 0001-sam3d-ggml-combined.patch:65-76 declaration, :217-272 CPU semantics;
+ * called at cpp_ggml/src/slat_flow_graph.cpp:168-221):
+ *   y16[t][n] = fp16(bias[n] + sum_{o<27} sum_{c<C} w16[n][o*C + c] * x16[idx[o*tokens + t]][c])
+ * with fp32 accumulation; a neighbour index < 0 or >= tokens contributes
+ * nothing (the reference's -1 / sentinel row).  x16 fp16 [tokens][C]; w16 fp16
+ * [Cout][27*C] (the converter's row format); bias16 fp16 [Cout] or NULL; idx
+ * int32 [27][tokens], offset-major; y16 fp16 [tokens][Cout].  Runs a gather of
+ * the 27 neighbour rows into the workspace, then the kind::f16 tensor-core
+ * GEMM with K = 27*C and an fp16 epilogue.  C % 8 == 0; x16 and w16 16-byte
+ * aligned; workspace 256-byte aligned, b2q_sparse_conv_f16_workspace_bytes.
+ *
+ * b2q_sparse_scatter_mean_f16: the SLat 2x downsample,
+ * ggml_sam3d_sparse_scatter_mean (patch :55-63 declaration, :151-215 CPU
+ * semantics; slat_flow_graph.cpp:223-236): out16 [coarse][C] = every fine row i
+ * with 0 <= rows[i] < coarse added into out16[rows[i]] in ascending i, each
+ * partial sum rounded to fp16, starting from zero; then each value divided in
+ * fp32 by counts[c] (|children| + 1 in the reference) and rounded to fp16.
+ * Bit-exact with that CPU path.  C % 8 == 0; features16 and out16 16-byte
+ * aligned; workspace b2q_sparse_scatter_mean_workspace_bytes. */
+B2Q_API size_t b2q_sparse_conv_f16_workspace_bytes(int64_t tokens, int64_t channels, int64_t out_channels);
+B2Q_API int b2q_sparse_conv_f16(const void* x16, int64_t tokens, int64_t channels, const void* w16,
+                                int64_t out_channels, const void* bias16, const int32_t* indices, void* y16,
+                                void* workspace, size_t workspace_bytes, void* stream);
+B2Q_API size_t b2q_sparse_scatter_mean_workspace_bytes(int64_t fine_rows, int64_t coarse_rows);
+B2Q_API int b2q_sparse_scatter_mean_f16(const void* features16, int64_t fine_rows, int64_t channels,
+                                        const int32_t* row_indices, const float* counts, int64_t coarse_rows,
+                                        void* out16, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Fault-free test of the failure path: launches the GEMM of
  * b2q_mul_mat_prepared with its TMA producer withholding every stage, so the
  * MMA and epilogue waits run out (after ~2 s), the kernel drains, frees its

@@ -165,6 +165,47 @@ def mul_mat_f16(w16: np.ndarray, x: np.ndarray) -> np.ndarray:
     return (x16.astype(np.float64) @ w.astype(np.float64).T).astype(np.float32)
 
 
+def sparse_scatter_mean_f16(x16: np.ndarray, rows: np.ndarray, counts: np.ndarray, coarse: int) -> np.ndarray:
+    """ggml_sam3d_sparse_scatter_mean on ggml's CPU backend (ggml patch
+    0001-sam3d-ggml-combined.patch:151-215): out starts at fp16 zero; fine rows
+    in ascending order add into their coarse row, each partial sum
+    fp16(fp32(acc) + fp32(x)); rows outside [0, coarse) are skipped; finally
+    fp16(fp32(acc) / counts[c])."""
+    x16 = np.asarray(x16, dtype=np.float16)
+    out = np.zeros((coarse, x16.shape[1]), dtype=np.float16)
+    with np.errstate(over="ignore"):  # fp16 partial sums may saturate to inf, as in the reference
+        for i, c in enumerate(np.asarray(rows)):
+            if 0 <= c < coarse:
+                out[c] = (out[c].astype(np.float32) + x16[i].astype(np.float32)).astype(np.float16)
+    return (out.astype(np.float32) / np.asarray(counts, np.float32)[:, None]).astype(np.float16)
+
+
+def sparse_conv_f16(x16: np.ndarray, w16: np.ndarray, b16, idx: np.ndarray) -> np.ndarray:
+    """ggml_sam3d_sparse_conv_f16 on ggml's CPU backend (patch :217-272): per
+    token and output channel, acc = fp32(bias), then for offset o = 0..26 and
+    channel c in order acc += fp32(w[n][o*C + c]) * fp32(x[idx[o][t]][c]) in
+    fp32 (the product of two fp16 values is exact in fp32, so a fused or
+    separate multiply-add gives the same sum), skipping indices outside
+    [0, tokens); result fp16(acc).  Vectorised over tokens and outputs, in the
+    reference's summation order."""
+    x16 = np.asarray(x16, dtype=np.float16)
+    w16 = np.asarray(w16, dtype=np.float16)
+    tokens, C = x16.shape
+    cout = w16.shape[0]
+    w = w16.astype(np.float32).reshape(cout, 27, C)
+    x = x16.astype(np.float32)
+    acc = np.zeros((tokens, cout), np.float32) if b16 is None else np.tile(
+        np.asarray(b16, np.float16).astype(np.float32), (tokens, 1))
+    for o in range(27):
+        src = np.asarray(idx)[o]
+        ok = (src >= 0) & (src < tokens)
+        xs = np.zeros((tokens, C), np.float32)
+        xs[ok] = x[src[ok]]
+        for c in range(C):
+            acc += (xs[:, c][:, None] * w[:, o, c][None, :]).astype(np.float32)
+    return acc.astype(np.float16)
+
+
 def mul_mat_f64(wtype: int, w: np.ndarray, a: np.ndarray, K: int) -> np.ndarray:
     w = np.ascontiguousarray(w)
     a = np.ascontiguousarray(a)

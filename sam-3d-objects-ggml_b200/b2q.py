@@ -88,6 +88,10 @@ def _lib_obj():
             "b2q_mul_mat_q_simt": (I, [I, P, I64, I64, I64, P, I64, I64, P, I64, P]),
             "b2q_device_status": (I, [ctypes.POINTER(ctypes.c_uint), I]),
             "b2q_selftest_stalled_mul_mat": (I, [P, I64, I64, P, I64, P, I64, P]),
+            "b2q_sparse_conv_f16_workspace_bytes": (SZ, [I64, I64, I64]),
+            "b2q_sparse_conv_f16": (I, [P, I64, I64, P, I64, P, P, P, P, SZ, P]),
+            "b2q_sparse_scatter_mean_workspace_bytes": (SZ, [I64, I64]),
+            "b2q_sparse_scatter_mean_f16": (I, [P, I64, I64, P, P, I64, P, P, SZ, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -367,6 +371,39 @@ def layer_norm_q8(x, eps: float = 1e-6, weight=None, bias=None, variant: int = A
     rc = lib().b2q_layer_norm_q8(_ptr(x), m, c, x.stride(0) * 4, eps, _ptr(weight), _ptr(bias), variant, _ptr(out),
                                  out.numel(), _stream(stream))
     _check("b2q_layer_norm_q8", rc)
+    return out
+
+
+def sparse_conv_f16(x16, w16, bias16, indices, out=None, ws=None, stream=None):
+    """F16 submanifold convolution: x16 [tokens, C] fp16, w16 [Cout, 27*C] fp16,
+    bias16 [Cout] fp16 or None, indices int32 [27, tokens] (offset-major, -1 =
+    missing) -> fp16 [tokens, Cout]."""
+    torch = _torch()
+    tokens, C = x16.shape
+    cout = w16.shape[0]
+    assert w16.shape[1] == 27 * C and indices.shape == (27, tokens)
+    if out is None:
+        out = torch.empty((tokens, cout), dtype=torch.float16, device=x16.device)
+    if ws is None:
+        ws = _empty_aligned(max(lib().b2q_sparse_conv_f16_workspace_bytes(tokens, C, cout), 256), x16.device)
+    rc = lib().b2q_sparse_conv_f16(_ptr(x16), tokens, C, _ptr(w16), cout, _ptr(bias16), _ptr(indices), _ptr(out),
+                                   _ptr(ws), ws.numel(), _stream(stream))
+    _check("b2q_sparse_conv_f16", rc)
+    return out
+
+
+def sparse_scatter_mean_f16(x16, rows, counts, coarse: int, out=None, ws=None, stream=None):
+    """F16 scatter-mean: x16 [fine, C] fp16, rows int32 [fine] (target coarse
+    row), counts fp32 [coarse] (divisors) -> fp16 [coarse, C]."""
+    torch = _torch()
+    fine, C = x16.shape
+    if out is None:
+        out = torch.empty((coarse, C), dtype=torch.float16, device=x16.device)
+    if ws is None:
+        ws = _empty_aligned(max(lib().b2q_sparse_scatter_mean_workspace_bytes(fine, coarse), 256), x16.device)
+    rc = lib().b2q_sparse_scatter_mean_f16(_ptr(x16), fine, C, _ptr(rows), _ptr(counts), coarse, _ptr(out),
+                                           _ptr(ws), ws.numel(), _stream(stream))
+    _check("b2q_sparse_scatter_mean_f16", rc)
     return out
 
 

@@ -245,6 +245,59 @@ int mul_mat_f16(const void* w, int64_t ldw, int64_t n, int64_t k, const float* x
   return from_cuda(launch_gemm_f16(w, ldw, workspace, k * 2, m, n, k, y, ldy / 4, bias, sms, s));
 }
 
+// ------------------------------------------------------------ sparse stages
+size_t b2q_sparse_conv_f16_workspace_bytes(int64_t tokens, int64_t channels, int64_t out_channels) {
+  if (tokens < 0 || channels <= 0 || channels % 8 != 0 || out_channels <= 0) return 0;
+  return round_up(tokens * 27 * channels * 2, 256) + round_up(out_channels * 4, 256);
+}
+
+int b2q_sparse_conv_f16(const void* x16, int64_t tokens, int64_t channels, const void* w16, int64_t out_channels,
+                        const void* bias16, const int32_t* indices, void* y16, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  if (tokens < 0 || channels <= 0 || channels % 8 != 0 || out_channels <= 0) return B2Q_ERR_INVALID_ARG;
+  if (tokens > INT_MAX || 27 * channels > INT_MAX || out_channels > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (tokens > 0 && (!x16 || !w16 || !indices || !y16)) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(x16, 16) || !aligned(w16, 16) || !aligned(y16, 2) || !aligned(bias16, 2) || !aligned(indices, 4) ||
+      !aligned(workspace, 256))
+    return B2Q_ERR_MISALIGNED;
+  if (tokens == 0) return B2Q_OK;
+  if (!workspace || workspace_bytes < b2q_sparse_conv_f16_workspace_bytes(tokens, channels, out_channels))
+    return B2Q_ERR_WORKSPACE;
+  int sms = 0;
+  if (int rc = check_device(&sms)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* g = static_cast<uint8_t*>(workspace);
+  float* bias = reinterpret_cast<float*>(g + round_up(tokens * 27 * channels * 2, 256));
+  const int64_t K = 27 * channels;
+  if (launch_gather27(x16, tokens, channels, indices, g, s) != cudaSuccess) return B2Q_ERR_CUDA;
+  if (bias16 && launch_half_to_float(bias16, out_channels, bias, s) != cudaSuccess) return B2Q_ERR_CUDA;
+  return from_cuda(launch_gemm_f16(w16, K * 2, g, K * 2, tokens, out_channels, K, nullptr, out_channels,
+                                   bias16 ? bias : nullptr, sms, s, y16));
+}
+
+size_t b2q_sparse_scatter_mean_workspace_bytes(int64_t fine_rows, int64_t coarse_rows) {
+  if (fine_rows < 0 || coarse_rows < 0) return 0;
+  return round_up((3 * coarse_rows + 1 + fine_rows) * 4, 256);
+}
+
+int b2q_sparse_scatter_mean_f16(const void* features16, int64_t fine_rows, int64_t channels,
+                                const int32_t* row_indices, const float* counts, int64_t coarse_rows, void* out16,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+  if (fine_rows < 0 || coarse_rows < 0 || channels <= 0 || channels % 8 != 0) return B2Q_ERR_INVALID_ARG;
+  if (fine_rows > INT_MAX || coarse_rows > INT_MAX / 4 || channels > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (coarse_rows > 0 && (!counts || !out16 || (fine_rows > 0 && (!features16 || !row_indices))))
+    return B2Q_ERR_INVALID_ARG;
+  if (!aligned(features16, 16) || !aligned(out16, 16) || !aligned(row_indices, 4) || !aligned(counts, 4) ||
+      !aligned(workspace, 4))
+    return B2Q_ERR_MISALIGNED;
+  if (coarse_rows == 0) return B2Q_OK;
+  if (!workspace || workspace_bytes < b2q_sparse_scatter_mean_workspace_bytes(fine_rows, coarse_rows))
+    return B2Q_ERR_WORKSPACE;
+  if (int rc = check_device(nullptr)) return rc;
+  return from_cuda(launch_scatter_mean_f16(features16, fine_rows, channels, row_indices, counts, coarse_rows, out16,
+                                           static_cast<int32_t*>(workspace), static_cast<cudaStream_t>(stream)));
+}
+
 size_t b2q_mul_mat_workspace_bytes(int wtype, int64_t m, int64_t n, int64_t k, int packed_weight) {
   if (wtype == B2Q_TYPE_F16) return (m < 0 || n < 0 || k <= 0 || k % 8 != 0) ? 0 : f16_act_bytes(m, k);
   if (wtype != B2Q_TYPE_Q4_K) return valid_wtype(wtype) ? b2q_mul_mat_workspace_size(m, n, k, packed_weight) : 0;

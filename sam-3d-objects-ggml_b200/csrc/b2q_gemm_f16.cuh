@@ -48,11 +48,15 @@ static_assert(kTmemColsF <= 512, "TMEM columns");
 
 struct F16Params {
   int M, N, kst, n_tiles, num_tiles;
-  float* y;
+  float* y;           // fp32 output [M][ldy], or
+  __half* y16;        // fp16 output [M][ldy] (round to nearest even) when not null
   int64_t ldy;
   const float* bias;
 };
 
+// OUT16: fp16 output (y16), else fp32 (y); one instantiation each, so the
+// store loop carries no per-element branch on the output type.
+template <bool OUT16>
 __global__ void __launch_bounds__(kThreadsF, 1)
     gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                     const F16Params p) {
@@ -172,6 +176,7 @@ __global__ void __launch_bounds__(kThreadsF, 1)
       const bool nv = n < p.N;
       const float bv = (p.bias && nv) ? p.bias[n] : 0.0f;
       float* yp = p.y + m0 * p.ldy + n;
+      __half* yp16 = p.y16 + m0 * p.ldy + n;
       uint32_t buf[2][32];
       tmem_ld_32x32b_x32(tlane + a * kBN, buf[0]);
       tmem_wait_ld();
@@ -183,7 +188,13 @@ __global__ void __launch_bounds__(kThreadsF, 1)
           for (int i = 0; i < 32; ++i) {
             const int64_t m = m0 + c * 32 + i;
             const float v = __uint_as_float(buf[c & 1][i]);
-            if (m < p.M) yp[(c * 32 + i) * p.ldy] = p.bias ? __fadd_rn(v, bv) : v;  // gb_linear's ggml_add
+            const float o = p.bias ? __fadd_rn(v, bv) : v;  // gb_linear's ggml_add
+            if (m < p.M) {
+              if constexpr (OUT16)
+                yp16[(c * 32 + i) * p.ldy] = __float2half_rn(o);
+              else
+                yp[(c * 32 + i) * p.ldy] = o;
+            }
           }
         }
         tmem_wait_ld();
@@ -208,7 +219,7 @@ __global__ void __launch_bounds__(kThreadsF, 1)
 
 cudaError_t launch_gemm_f16(const void* w, int64_t ldw_bytes, const void* x16, int64_t ldx_bytes, int64_t M,
                             int64_t N, int64_t K, float* y, int64_t ldy, const float* bias, int num_sms,
-                            cudaStream_t s) {
+                            cudaStream_t s, void* y16) {
   if (M == 0 || N == 0) return cudaSuccess;
   if (K <= 0 || K % 8 != 0 || M > INT32_MAX || N > INT32_MAX) return cudaErrorInvalidValue;
   CUtensorMap tm_w, tm_x;
@@ -226,6 +237,7 @@ cudaError_t launch_gemm_f16(const void* w, int64_t ldw_bytes, const void* x16, i
   if (tiles > INT32_MAX) return cudaErrorInvalidValue;
   p.num_tiles = static_cast<int>(tiles);
   p.y = y;
+  p.y16 = static_cast<__half*>(y16);
   p.ldy = ldy;
   p.bias = bias;
   static std::atomic<uint64_t> ready{0};
@@ -233,12 +245,18 @@ cudaError_t launch_gemm_f16(const void* w, int64_t ldw_bytes, const void* x16, i
   if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
   const uint64_t bit = dev < 64 ? (uint64_t{1} << dev) : 0;
   if (!bit || !(ready.load(std::memory_order_acquire) & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(f16::gemm_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, f16::kSmemF);
+    cudaError_t e = cudaFuncSetAttribute(f16::gemm_f16_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         f16::kSmemF);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(f16::gemm_f16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, f16::kSmemF);
     if (e != cudaSuccess) return e;
     ready.fetch_or(bit, std::memory_order_acq_rel);
   }
   const int grid = p.num_tiles < num_sms ? p.num_tiles : num_sms;
-  f16::gemm_f16_kernel<<<grid, f16::kThreadsF, f16::kSmemF, s>>>(tm_w, tm_x, p);
+  if (p.y16)
+    f16::gemm_f16_kernel<true><<<grid, f16::kThreadsF, f16::kSmemF, s>>>(tm_w, tm_x, p);
+  else
+    f16::gemm_f16_kernel<false><<<grid, f16::kThreadsF, f16::kSmemF, s>>>(tm_w, tm_x, p);
   return cudaGetLastError();
 }
 

@@ -174,10 +174,23 @@ cudaError_t launch_gemm_q4k(const Q4kArgs& args, int num_sms, cudaStream_t s);
 
 // F16 weights (b2q_gemm_f16.cuh): w fp16 [N][K] rows ldw_bytes apart, x16 fp16
 // [M][K] rows ldx_bytes apart (both 16-byte aligned, K % 8 == 0);
-// y[m][n] = sum_k w[n][k] x16[m][k] (+ bias[n]), fp32, ldy floats.
+// y[m][n] = sum_k w[n][k] x16[m][k] (+ bias[n]), fp32, ldy floats -- or, when
+// y16 is not null, rounded to fp16 into y16 (ldy halves) instead of y.
 cudaError_t launch_gemm_f16(const void* w, int64_t ldw_bytes, const void* x16, int64_t ldx_bytes, int64_t M,
                             int64_t N, int64_t K, float* y, int64_t ldy, const float* bias, int num_sms,
+                            cudaStream_t s, void* y16 = nullptr);
+// SLat sparse stages (b2q_sparse.cu).
+// Submanifold-conv gather: g[t][o*C + c] = x16[idx[o*tokens + t]][c] for the
+// 27 offsets o, zero where the index is < 0 or >= tokens.  C % 8 == 0.
+cudaError_t launch_gather27(const void* x16, int64_t tokens, int64_t C, const int32_t* idx, void* g,
                             cudaStream_t s);
+// fp16 -> fp32 of n values.
+cudaError_t launch_half_to_float(const void* h, int64_t n, float* f, cudaStream_t s);
+// Scatter-mean with fp16 partial sums in fine-row order (see b2q_sparse.cu);
+// ws holds 3 * coarse + 1 + fine int32 (hist, cursor, offsets, child lists).
+cudaError_t launch_scatter_mean_f16(const void* x16, int64_t fine, int64_t C, const int32_t* rows,
+                                    const float* counts, int64_t coarse, void* out16, int32_t* ws,
+                                    cudaStream_t s);
 // fp32 rows -> fp16 rows [m][ldy] (round to nearest even), k % 8 == 0.
 cudaError_t launch_to_f16(const float* x, int64_t m, int64_t k, int64_t ldx_floats, void* y, int64_t ldy,
                           bool vec4, cudaStream_t s);

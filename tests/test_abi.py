@@ -247,3 +247,21 @@ def test_f16_validation(b2q_mod):
     assert f(1, FAKE, 2048, 64, 1024, FAKE, 4, 4096, None, FAKE, 256, 2, FAKE, ws, None) == 1  # Q8_K variant
     assert f(1, FAKE, 2048, 64, 1024, FAKE, 4, 4096, None, FAKE, 256, 0, FAKE, 100, None) == 4  # workspace
     assert f(1, FAKE, 2048, 64, 1024, FAKE, 0, 4096, None, FAKE, 256, 0, FAKE, 0, None) == 0    # m == 0
+
+
+def test_sparse_validation(b2q_mod):
+    L = b2q.lib()
+    conv, sm = L.b2q_sparse_conv_f16, L.b2q_sparse_scatter_mean_f16
+    ws = 1 << 24
+    assert L.b2q_sparse_conv_f16_workspace_bytes(10, 12, 16) == 0                          # C % 8
+    assert L.b2q_sparse_conv_f16_workspace_bytes(10, 8, 16) == 4352 + 256                  # 10*27*8*2 -> 4352
+    assert conv(FAKE, 10, 12, FAKE, 16, None, FAKE, FAKE, FAKE, ws, None) == 1             # C % 8
+    assert conv(FAKE + 8, 10, 8, FAKE, 16, None, FAKE, FAKE, FAKE, ws, None) == 3          # x alignment
+    assert conv(FAKE, 10, 8, FAKE, 16, FAKE + 1, FAKE, FAKE, FAKE, ws, None) == 3          # bias alignment
+    assert conv(FAKE, 10, 8, FAKE, 16, None, FAKE, FAKE, FAKE, 100, None) == 4             # workspace
+    assert conv(FAKE, 0, 8, FAKE, 16, None, FAKE, FAKE, FAKE, 0, None) == 0                # no tokens
+    assert L.b2q_sparse_scatter_mean_workspace_bytes(100, 10) == 768                       # (31 + 100) * 4 -> 768
+    assert sm(FAKE, 100, 12, FAKE, FAKE, 10, FAKE, FAKE, ws, None) == 1                    # C % 8
+    assert sm(FAKE, 100, 8, FAKE, FAKE, 10, FAKE + 4, FAKE, ws, None) == 3                 # out alignment
+    assert sm(FAKE, 100, 8, FAKE, FAKE, 10, FAKE, FAKE, 100, None) == 4                    # workspace
+    assert sm(FAKE, 100, 8, FAKE, FAKE, 0, FAKE, FAKE, 0, None) == 0                       # no coarse rows

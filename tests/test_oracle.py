@@ -216,3 +216,26 @@ def test_q4_k_dot_matches_fp64_of_dequantized():
     xa = (qa * da[:, :, None]).reshape(9, 1024)
     y64 = xa @ O.dequantize_q4_k(w, 1024).astype(np.float64).T
     assert rel_frobenius(y, y64) < 1e-6
+
+
+def test_sparse_oracles_small_cases():
+    """The scatter-mean restatement on a hand case (fp16 partial sums, zero
+    start, fp32 division) and the conv restatement against an fp64 dense sum."""
+    x16 = np.array([[1.0, 2048.0], [1.0, 1.0], [3.0, 1.0], [5.0, 0.5]], np.float16)
+    rows = np.array([0, 0, 1, 3], np.int32)   # row 3 is outside coarse = 2: skipped
+    out = O.sparse_scatter_mean_f16(x16, rows, np.array([3.0, 2.0], np.float32), 2)
+    # 2048 + 1 = 2049 rounds to 2048 in fp16 (ties to even), then / 3
+    assert out.tolist() == [[np.float16(2.0 / 3.0), np.float16(2048.0 / 3.0)], [1.5, 0.5]]
+    rng = np.random.default_rng(0)
+    t, C, cout = 20, 8, 4
+    xs = rng.standard_normal((t, C)).astype(np.float16)
+    w = rng.standard_normal((cout, 27 * C)).astype(np.float16)
+    b = rng.standard_normal(cout).astype(np.float16)
+    idx = rng.integers(-1, t, (27, t)).astype(np.int32)
+    g = np.zeros((t, 27, C))
+    for o in range(27):
+        ok = idx[o] >= 0
+        g[ok, o] = xs[idx[o][ok]]
+    dense = g.reshape(t, -1) @ w.astype(np.float64).T + b
+    got = O.sparse_conv_f16(xs, w, b, idx).astype(np.float64)
+    assert np.max(np.abs(got - dense) / np.maximum(np.abs(dense), 1e-3)) < 2e-3
