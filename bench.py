@@ -845,8 +845,12 @@ def slat_sparse_side(b2q, flush, stream, dev, peaks, iters=10):
     o16 = torch.empty(coarse, 128, device=dev, dtype=torch.float16)
     ws = b2q._empty_aligned(b2q.lib().b2q_sparse_scatter_mean_workspace_bytes(fine, coarse), dev)
     us = timed(lambda: b2q.sparse_scatter_mean_f16(x16, rows_d, counts_d, coarse, out=o16, ws=ws, stream=stream))
-    out["scatter_mean"] = {"fine": fine, "coarse": coarse, "C": 128, "us": round(us, 2),
-                           "bytes": fine * 256 + coarse * 256 + fine * 8, "launches": 6}
+    plan = b2q.sparse_scatter_plan(rows_d, coarse, stream=stream)
+    us_planned = timed(lambda: b2q.sparse_scatter_mean_f16_planned(x16, plan, counts_d, coarse, out=o16,
+                                                                   stream=stream))
+    out["scatter_mean"] = {"fine": fine, "coarse": coarse, "C": 128, "us": round(us, 2), "launches": 6,
+                           "us_planned": round(us_planned, 2), "launches_planned": 1,
+                           "bytes": fine * 256 + coarse * 256 + fine * 8}
     return out
 
 

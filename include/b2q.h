@@ -357,6 +357,19 @@ B2Q_API size_t b2q_sparse_scatter_mean_workspace_bytes(int64_t fine_rows, int64_
 B2Q_API int b2q_sparse_scatter_mean_f16(const void* features16, int64_t fine_rows, int64_t channels,
                                         const int32_t* row_indices, const float* counts, int64_t coarse_rows,
                                         void* out16, void* workspace, size_t workspace_bytes, void* stream);
+/* The same in two parts, for a mapping that serves many calls (the SLat
+ * downsample table is fixed per object, cpp_ggml/src/slat_flow_graph.cpp:
+ * 223-236, and reused by every sampling step): b2q_sparse_scatter_plan lists the
+ * fine rows of every coarse row in ascending order into `plan`
+ * (b2q_sparse_scatter_mean_workspace_bytes(fine, coarse) bytes, 4-byte
+ * aligned); b2q_sparse_scatter_mean_f16_planned then runs the accumulation
+ * alone, one launch, bit-identical to b2q_sparse_scatter_mean_f16.  The plan
+ * stays valid while row_indices, fine_rows and coarse_rows do not change. */
+B2Q_API int b2q_sparse_scatter_plan(const int32_t* row_indices, int64_t fine_rows, int64_t coarse_rows, void* plan,
+                                    size_t plan_bytes, void* stream);
+B2Q_API int b2q_sparse_scatter_mean_f16_planned(const void* features16, int64_t fine_rows, int64_t channels,
+                                                const void* plan, const float* counts, int64_t coarse_rows,
+                                                void* out16, void* stream);
 
 /* Fault-free test of the failure path: launches the GEMM of
  * b2q_mul_mat_prepared with its TMA producer withholding every stage, so the

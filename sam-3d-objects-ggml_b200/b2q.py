@@ -92,6 +92,8 @@ def _lib_obj():
             "b2q_sparse_conv_f16": (I, [P, I64, I64, P, I64, P, P, P, P, SZ, P]),
             "b2q_sparse_scatter_mean_workspace_bytes": (SZ, [I64, I64]),
             "b2q_sparse_scatter_mean_f16": (I, [P, I64, I64, P, P, I64, P, P, SZ, P]),
+            "b2q_sparse_scatter_plan": (I, [P, I64, I64, P, SZ, P]),
+            "b2q_sparse_scatter_mean_f16_planned": (I, [P, I64, I64, P, P, I64, P, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -404,6 +406,27 @@ def sparse_scatter_mean_f16(x16, rows, counts, coarse: int, out=None, ws=None, s
     rc = lib().b2q_sparse_scatter_mean_f16(_ptr(x16), fine, C, _ptr(rows), _ptr(counts), coarse, _ptr(out),
                                            _ptr(ws), ws.numel(), _stream(stream))
     _check("b2q_sparse_scatter_mean_f16", rc)
+    return out
+
+
+def sparse_scatter_plan(rows, coarse: int, stream=None):
+    """Child lists of every coarse row for sparse_scatter_mean_f16_planned
+    (reusable while rows does not change)."""
+    fine = rows.shape[0]
+    plan = _empty_aligned(max(lib().b2q_sparse_scatter_mean_workspace_bytes(fine, coarse), 256), rows.device)
+    rc = lib().b2q_sparse_scatter_plan(_ptr(rows), fine, coarse, _ptr(plan), plan.numel(), _stream(stream))
+    _check("b2q_sparse_scatter_plan", rc)
+    return plan
+
+
+def sparse_scatter_mean_f16_planned(x16, plan, counts, coarse: int, out=None, stream=None):
+    torch = _torch()
+    fine, C = x16.shape
+    if out is None:
+        out = torch.empty((coarse, C), dtype=torch.float16, device=x16.device)
+    rc = lib().b2q_sparse_scatter_mean_f16_planned(_ptr(x16), fine, C, _ptr(plan), _ptr(counts), coarse, _ptr(out),
+                                                   _stream(stream))
+    _check("b2q_sparse_scatter_mean_f16_planned", rc)
     return out
 
 

@@ -298,6 +298,34 @@ int b2q_sparse_scatter_mean_f16(const void* features16, int64_t fine_rows, int64
                                            static_cast<int32_t*>(workspace), static_cast<cudaStream_t>(stream)));
 }
 
+int b2q_sparse_scatter_plan(const int32_t* row_indices, int64_t fine_rows, int64_t coarse_rows, void* plan,
+                            size_t plan_bytes, void* stream) {
+  if (fine_rows < 0 || coarse_rows < 0) return B2Q_ERR_INVALID_ARG;
+  if (fine_rows > INT_MAX || coarse_rows > INT_MAX / 4) return B2Q_ERR_TOO_LARGE;
+  if (coarse_rows > 0 && (!plan || (fine_rows > 0 && !row_indices))) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(row_indices, 4) || !aligned(plan, 4)) return B2Q_ERR_MISALIGNED;
+  if (coarse_rows == 0) return B2Q_OK;
+  if (plan_bytes < b2q_sparse_scatter_mean_workspace_bytes(fine_rows, coarse_rows)) return B2Q_ERR_WORKSPACE;
+  if (int rc = check_device(nullptr)) return rc;
+  return from_cuda(launch_scatter_plan(row_indices, fine_rows, coarse_rows, static_cast<int32_t*>(plan),
+                                       static_cast<cudaStream_t>(stream)));
+}
+
+int b2q_sparse_scatter_mean_f16_planned(const void* features16, int64_t fine_rows, int64_t channels,
+                                        const void* plan, const float* counts, int64_t coarse_rows, void* out16,
+                                        void* stream) {
+  if (fine_rows < 0 || coarse_rows < 0 || channels <= 0 || channels % 8 != 0) return B2Q_ERR_INVALID_ARG;
+  if (fine_rows > INT_MAX || coarse_rows > INT_MAX / 4 || channels > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (coarse_rows > 0 && (!counts || !out16 || !plan || (fine_rows > 0 && !features16)))
+    return B2Q_ERR_INVALID_ARG;
+  if (!aligned(features16, 16) || !aligned(out16, 16) || !aligned(plan, 4) || !aligned(counts, 4))
+    return B2Q_ERR_MISALIGNED;
+  if (coarse_rows == 0) return B2Q_OK;
+  if (int rc = check_device(nullptr)) return rc;
+  return from_cuda(launch_scatter_mean_planned(features16, channels, static_cast<const int32_t*>(plan), counts,
+                                               coarse_rows, out16, static_cast<cudaStream_t>(stream)));
+}
+
 size_t b2q_mul_mat_workspace_bytes(int wtype, int64_t m, int64_t n, int64_t k, int packed_weight) {
   if (wtype == B2Q_TYPE_F16) return (m < 0 || n < 0 || k <= 0 || k % 8 != 0) ? 0 : f16_act_bytes(m, k);
   if (wtype != B2Q_TYPE_Q4_K) return valid_wtype(wtype) ? b2q_mul_mat_workspace_size(m, n, k, packed_weight) : 0;

@@ -191,6 +191,12 @@ cudaError_t launch_half_to_float(const void* h, int64_t n, float* f, cudaStream_
 cudaError_t launch_scatter_mean_f16(const void* x16, int64_t fine, int64_t C, const int32_t* rows,
                                     const float* counts, int64_t coarse, void* out16, int32_t* ws,
                                     cudaStream_t s);
+// The same in two parts: the child lists of every coarse row (a plan of
+// 3 * coarse + 1 + fine int32, reusable while rows does not change), then the
+// one-launch fp16 accumulation over a plan.
+cudaError_t launch_scatter_plan(const int32_t* rows, int64_t fine, int64_t coarse, int32_t* plan, cudaStream_t s);
+cudaError_t launch_scatter_mean_planned(const void* x16, int64_t C, const int32_t* plan, const float* counts,
+                                        int64_t coarse, void* out16, cudaStream_t s);
 // fp32 rows -> fp16 rows [m][ldy] (round to nearest even), k % 8 == 0.
 cudaError_t launch_to_f16(const float* x, int64_t m, int64_t k, int64_t ldx_floats, void* y, int64_t ldy,
                           bool vec4, cudaStream_t s);

@@ -169,14 +169,13 @@ cudaError_t launch_half_to_float(const void* h, int64_t n, float* f, cudaStream_
   return cudaGetLastError();
 }
 
-cudaError_t launch_scatter_mean_f16(const void* x16, int64_t fine, int64_t C, const int32_t* rows,
-                                    const float* counts, int64_t coarse, void* out16, int32_t* ws,
-                                    cudaStream_t s) {
+// Plan layout (int32): hist[coarse], cursor[coarse], off[coarse + 1], list[fine].
+cudaError_t launch_scatter_plan(const int32_t* rows, int64_t fine, int64_t coarse, int32_t* plan, cudaStream_t s) {
   if (coarse == 0) return cudaSuccess;
-  int32_t* hist = ws;
-  int32_t* cursor = ws + coarse;
-  int32_t* off = ws + 2 * coarse;         // coarse + 1 entries
-  int32_t* list = ws + 3 * coarse + 1;    // fine entries
+  int32_t* hist = plan;
+  int32_t* cursor = plan + coarse;
+  int32_t* off = plan + 2 * coarse;
+  int32_t* list = plan + 3 * coarse + 1;
   cudaError_t e = cudaMemsetAsync(hist, 0, 2 * coarse * sizeof(int32_t), s);
   if (e != cudaSuccess) return e;
   if (fine > 0) count_children_kernel<<<grid_cap(fine, 256, 8), 256, 0, s>>>(rows, fine, coarse, hist);
@@ -184,10 +183,26 @@ cudaError_t launch_scatter_mean_f16(const void* x16, int64_t fine, int64_t C, co
   if (fine > 0)
     fill_children_kernel<<<grid_cap(fine, 256, 8), 256, 0, s>>>(rows, fine, coarse, off, cursor, list);
   sort_children_kernel<<<grid_cap(coarse, 256, 8), 256, 0, s>>>(off, coarse, list);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scatter_mean_planned(const void* x16, int64_t C, const int32_t* plan, const float* counts,
+                                        int64_t coarse, void* out16, cudaStream_t s) {
+  if (coarse == 0) return cudaSuccess;
+  const int32_t* off = plan + 2 * coarse;
+  const int32_t* list = plan + 3 * coarse + 1;
   const int64_t c8 = C / 8;
   scatter_mean_kernel<<<grid_cap(coarse * c8, 256, 16), 256, 0, s>>>(
       static_cast<const uint4*>(x16), c8, off, list, counts, coarse, static_cast<uint4*>(out16));
   return cudaGetLastError();
+}
+
+cudaError_t launch_scatter_mean_f16(const void* x16, int64_t fine, int64_t C, const int32_t* rows,
+                                    const float* counts, int64_t coarse, void* out16, int32_t* ws,
+                                    cudaStream_t s) {
+  cudaError_t e = launch_scatter_plan(rows, fine, coarse, ws, s);
+  if (e != cudaSuccess) return e;
+  return launch_scatter_mean_planned(x16, C, ws, counts, coarse, out16, s);
 }
 
 }  // namespace b2q

@@ -276,7 +276,7 @@ class SsSampler:
         torch.cuda.current_stream().wait_stream(s)
         self.dt.copy_(dt)
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
+        with torch.cuda.graph(g, capture_error_mode="thread_local"):  # other threads (e.g. a NCCL watchdog) may query events
             self._step(cfg)
         self.graphs[cfg] = g
         return g

@@ -265,3 +265,9 @@ def test_sparse_validation(b2q_mod):
     assert sm(FAKE, 100, 8, FAKE, FAKE, 10, FAKE + 4, FAKE, ws, None) == 3                 # out alignment
     assert sm(FAKE, 100, 8, FAKE, FAKE, 10, FAKE, FAKE, 100, None) == 4                    # workspace
     assert sm(FAKE, 100, 8, FAKE, FAKE, 0, FAKE, FAKE, 0, None) == 0                       # no coarse rows
+    plan, run = L.b2q_sparse_scatter_plan, L.b2q_sparse_scatter_mean_f16_planned
+    assert plan(FAKE, 100, 10, FAKE, 100, None) == 4                                       # plan too small
+    assert plan(FAKE + 2, 100, 10, FAKE, ws, None) == 3                                    # rows alignment
+    assert plan(FAKE, 100, 0, FAKE, 0, None) == 0                                          # no coarse rows
+    assert run(FAKE, 100, 12, FAKE, FAKE, 10, FAKE, None) == 1                             # C % 8
+    assert run(FAKE, 100, 8, None, FAKE, 10, FAKE, None) == 1                              # no plan

@@ -81,6 +81,20 @@ def test_scatter_mean_order_fanin_skips_and_overflow(dev):
     assert np.array_equal(again.cpu().numpy().view(np.uint16), want.view(np.uint16))
 
 
+def test_scatter_plan_reused_across_calls(dev):
+    """One plan serves several feature sets (the mapping is fixed per object):
+    the planned accumulation equals the one-shot operator bit for bit."""
+    _, rows, counts, coarse = sparse_grid(32, 0.04, 7)
+    rows_d, counts_d = to_dev(rows, dev), to_dev(counts, dev)
+    plan = b2q.sparse_scatter_plan(rows_d, coarse)
+    rng = np.random.default_rng(9)
+    for _ in range(2):
+        x16 = (rng.standard_normal((rows.size, 64)) * 2).astype(np.float16)
+        got = b2q.sparse_scatter_mean_f16_planned(to_dev(x16, dev), plan, counts_d, coarse)
+        want = O.sparse_scatter_mean_f16(x16, rows, counts, coarse)
+        assert np.array_equal(got.cpu().numpy().view(np.uint16), want.view(np.uint16))
+
+
 def _conv_bound(x16, w16, idx, want):
     """Largest allowed |GPU - CPU| per output: one fp16 step of the CPU value
     (both round their fp32 sum to fp16) plus twice the worst-case fp32
