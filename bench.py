@@ -833,12 +833,17 @@ def slat_sparse_side(b2q, flush, stream, dev, peaks, iters=10):
         y16 = torch.empty(tokens, cout, device=dev, dtype=torch.float16)
         ws = b2q._empty_aligned(b2q.lib().b2q_sparse_conv_f16_workspace_bytes(tokens, C, cout), dev)
         us = timed(lambda: b2q.sparse_conv_f16(x16, w16, b16, table, out=y16, ws=ws, stream=stream))
+        plan = b2q.sparse_conv_plan(table, stream=stream)
+        wsp = b2q._empty_aligned(b2q.lib().b2q_sparse_conv_f16_planned_workspace_bytes(tokens, C, cout), dev)
+        us_p = timed(lambda: b2q.sparse_conv_f16_planned(x16, w16, b16, plan, out=y16, ws=wsp, stream=stream))
         flops = 2.0 * tokens * cout * 27 * C
         valid = int((table >= 0).sum().item())
         row = {"name": name, "tokens": tokens, "C": C, "Cout": cout, "us": round(us, 2),
                "tflops_dense_27": round(flops / (us * 1e-6) / 1e12, 1),
                "valid_neighbour_fraction": round(valid / (27 * tokens), 3),
-               "gather_bytes": tokens * 27 * C * 2, "launches": 3}
+               "gather_bytes": tokens * 27 * C * 2, "launches": 3,
+               "us_planned": round(us_p, 2), "launches_planned": 4,
+               "tflops_useful_planned": round(2.0 * valid * cout * C / (us_p * 1e-6) / 1e12, 1)}
         out["conv"].append(row)
     x16 = torch.randn(fine, 128, device=dev, generator=gen).half()
     rows_d, counts_d = torch.from_numpy(rows).to(dev), torch.from_numpy(counts).to(dev)

@@ -353,6 +353,27 @@ B2Q_API size_t b2q_sparse_conv_f16_workspace_bytes(int64_t tokens, int64_t chann
 B2Q_API int b2q_sparse_conv_f16(const void* x16, int64_t tokens, int64_t channels, const void* w16,
                                 int64_t out_channels, const void* bias16, const int32_t* indices, void* y16,
                                 void* workspace, size_t workspace_bytes, void* stream);
+/* Planned form of b2q_sparse_conv_f16 for a neighbour table that serves many
+ * calls (the SLat tables are built once per object and reused by every
+ * sampling step).  The dense form multiplies all 27 neighbour slots, empty
+ * ones included, as the reference's get_rows + GEMM does; at the sparse
+ * occupancies of SLat most slots are empty.  b2q_sparse_conv_plan lists the
+ * occupied (output token, input token) pairs of every offset, in token order,
+ * padded per offset to 256-row tiles (plan of b2q_sparse_conv_plan_bytes(tokens)
+ * bytes, 16-byte aligned).  b2q_sparse_conv_f16_planned then gathers only those
+ * rows, runs one grouped kind::f16 GEMM in which every tile multiplies its
+ * offset's weight slice W_o, and sums each token's partials in fp32 in offset
+ * order onto the bias before the fp16 rounding: the same result as
+ * b2q_sparse_conv_f16 within fp32 summation order.  channels % 64 == 0,
+ * out_channels % 8 == 0; x16, w16, y16 16-byte aligned; workspace
+ * b2q_sparse_conv_f16_planned_workspace_bytes (sized for any table of that
+ * many tokens).  The plan stays valid while the table does not change. */
+B2Q_API size_t b2q_sparse_conv_plan_bytes(int64_t tokens);
+B2Q_API int b2q_sparse_conv_plan(const int32_t* indices, int64_t tokens, void* plan, size_t plan_bytes, void* stream);
+B2Q_API size_t b2q_sparse_conv_f16_planned_workspace_bytes(int64_t tokens, int64_t channels, int64_t out_channels);
+B2Q_API int b2q_sparse_conv_f16_planned(const void* x16, int64_t tokens, int64_t channels, const void* w16,
+                                        int64_t out_channels, const void* bias16, const void* plan, void* y16,
+                                        void* workspace, size_t workspace_bytes, void* stream);
 B2Q_API size_t b2q_sparse_scatter_mean_workspace_bytes(int64_t fine_rows, int64_t coarse_rows);
 B2Q_API int b2q_sparse_scatter_mean_f16(const void* features16, int64_t fine_rows, int64_t channels,
                                         const int32_t* row_indices, const float* counts, int64_t coarse_rows,

@@ -93,6 +93,10 @@ def _lib_obj():
             "b2q_sparse_scatter_mean_workspace_bytes": (SZ, [I64, I64]),
             "b2q_sparse_scatter_mean_f16": (I, [P, I64, I64, P, P, I64, P, P, SZ, P]),
             "b2q_sparse_scatter_plan": (I, [P, I64, I64, P, SZ, P]),
+            "b2q_sparse_conv_plan_bytes": (SZ, [I64]),
+            "b2q_sparse_conv_plan": (I, [P, I64, P, SZ, P]),
+            "b2q_sparse_conv_f16_planned_workspace_bytes": (SZ, [I64, I64, I64]),
+            "b2q_sparse_conv_f16_planned": (I, [P, I64, I64, P, I64, P, P, P, P, SZ, P]),
             "b2q_sparse_scatter_mean_f16_planned": (I, [P, I64, I64, P, P, I64, P, P]),
         }
         for name, (res, args) in sig.items():
@@ -406,6 +410,31 @@ def sparse_scatter_mean_f16(x16, rows, counts, coarse: int, out=None, ws=None, s
     rc = lib().b2q_sparse_scatter_mean_f16(_ptr(x16), fine, C, _ptr(rows), _ptr(counts), coarse, _ptr(out),
                                            _ptr(ws), ws.numel(), _stream(stream))
     _check("b2q_sparse_scatter_mean_f16", rc)
+    return out
+
+
+def sparse_conv_plan(indices, stream=None):
+    """Occupied (token, neighbour) pairs of a 27-neighbour table int32 [27, tokens],
+    for sparse_conv_f16_planned (reusable while the table does not change)."""
+    tokens = indices.shape[1]
+    plan = _empty_aligned(lib().b2q_sparse_conv_plan_bytes(tokens), indices.device)
+    rc = lib().b2q_sparse_conv_plan(_ptr(indices), tokens, _ptr(plan), plan.numel(), _stream(stream))
+    _check("b2q_sparse_conv_plan", rc)
+    return plan
+
+
+def sparse_conv_f16_planned(x16, w16, bias16, plan, out=None, ws=None, stream=None):
+    """sparse_conv_f16 over the occupied pairs of a plan (C % 64 == 0, Cout % 8 == 0)."""
+    torch = _torch()
+    tokens, C = x16.shape
+    cout = w16.shape[0]
+    if out is None:
+        out = torch.empty((tokens, cout), dtype=torch.float16, device=x16.device)
+    if ws is None:
+        ws = _empty_aligned(max(lib().b2q_sparse_conv_f16_planned_workspace_bytes(tokens, C, cout), 256), x16.device)
+    rc = lib().b2q_sparse_conv_f16_planned(_ptr(x16), tokens, C, _ptr(w16), cout, _ptr(bias16), _ptr(plan), _ptr(out),
+                                           _ptr(ws), ws.numel(), _stream(stream))
+    _check("b2q_sparse_conv_f16_planned", rc)
     return out
 
 

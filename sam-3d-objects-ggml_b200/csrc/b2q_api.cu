@@ -275,6 +275,54 @@ int b2q_sparse_conv_f16(const void* x16, int64_t tokens, int64_t channels, const
                                    bias16 ? bias : nullptr, sms, s, y16));
 }
 
+size_t b2q_sparse_conv_plan_bytes(int64_t tokens) {
+  if (tokens < 0 || tokens > INT_MAX / 32) return 0;
+  return round_up(conv_plan_ints(tokens) * 4, 256);
+}
+
+int b2q_sparse_conv_plan(const int32_t* indices, int64_t tokens, void* plan, size_t plan_bytes, void* stream) {
+  if (tokens < 0) return B2Q_ERR_INVALID_ARG;
+  if (tokens > INT_MAX / 32) return B2Q_ERR_TOO_LARGE;
+  if (!plan || (tokens > 0 && !indices)) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(indices, 4) || !aligned(plan, 16)) return B2Q_ERR_MISALIGNED;
+  if (plan_bytes < b2q_sparse_conv_plan_bytes(tokens)) return B2Q_ERR_WORKSPACE;
+  if (int rc = check_device(nullptr)) return rc;
+  return from_cuda(launch_conv_plan(indices, tokens, static_cast<int32_t*>(plan), static_cast<cudaStream_t>(stream)));
+}
+
+size_t b2q_sparse_conv_f16_planned_workspace_bytes(int64_t tokens, int64_t channels, int64_t out_channels) {
+  if (tokens < 0 || tokens > INT_MAX / 32 || channels <= 0 || channels % 64 != 0 || out_channels <= 0 ||
+      out_channels % 8 != 0)
+    return 0;
+  const int64_t P = conv_plan_rows(tokens);
+  return round_up(P * channels * 2, 256) + round_up(P * out_channels * 4, 256) + round_up(out_channels * 4, 256);
+}
+
+int b2q_sparse_conv_f16_planned(const void* x16, int64_t tokens, int64_t channels, const void* w16,
+                                int64_t out_channels, const void* bias16, const void* plan, void* y16,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+  if (tokens < 0 || channels <= 0 || channels % 64 != 0 || out_channels <= 0 || out_channels % 8 != 0)
+    return B2Q_ERR_INVALID_ARG;
+  if (tokens > INT_MAX / 32 || 27 * channels > INT_MAX || out_channels > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (tokens > 0 && (!x16 || !w16 || !plan || !y16)) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(x16, 16) || !aligned(w16, 16) || !aligned(y16, 16) || !aligned(bias16, 2) || !aligned(plan, 16) ||
+      !aligned(workspace, 256))
+    return B2Q_ERR_MISALIGNED;
+  if (tokens == 0) return B2Q_OK;
+  if (!workspace || workspace_bytes < b2q_sparse_conv_f16_planned_workspace_bytes(tokens, channels, out_channels))
+    return B2Q_ERR_WORKSPACE;
+  int sms = 0;
+  if (int rc = check_device(&sms)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t P = conv_plan_rows(tokens);
+  uint8_t* g = static_cast<uint8_t*>(workspace);
+  float* part = reinterpret_cast<float*>(g + round_up(P * channels * 2, 256));
+  float* bias = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(part) + round_up(P * out_channels * 4, 256));
+  if (bias16 && launch_half_to_float(bias16, out_channels, bias, s) != cudaSuccess) return B2Q_ERR_CUDA;
+  return from_cuda(launch_conv_planned(x16, tokens, channels, w16, out_channels, bias16 ? bias : nullptr,
+                                       static_cast<const int32_t*>(plan), g, part, y16, sms, s));
+}
+
 size_t b2q_sparse_scatter_mean_workspace_bytes(int64_t fine_rows, int64_t coarse_rows) {
   if (fine_rows < 0 || coarse_rows < 0) return 0;
   return round_up((3 * coarse_rows + 1 + fine_rows) * 4, 256);

@@ -52,11 +52,17 @@ struct F16Params {
   __half* y16;        // fp16 output [M][ldy] (round to nearest even) when not null
   int64_t ldy;
   const float* bias;
+  // Grouped form only (the planned sparse convolution): the number of
+  // 256-row tiles of x is read from device memory (*m_tiles_dev), and tile j's
+  // rows multiply the weight's K slice [k_group[j] * K, (k_group[j] + 1) * K).
+  const int32_t* m_tiles_dev;
+  const int32_t* k_group;
 };
 
 // OUT16: fp16 output (y16), else fp32 (y); one instantiation each, so the
-// store loop carries no per-element branch on the output type.
-template <bool OUT16>
+// store loop carries no per-element branch on the output type.  GROUPED: the
+// tile count and each token tile's weight K slice come from device memory.
+template <bool OUT16, bool GROUPED = false>
 __global__ void __launch_bounds__(kThreadsF, 1)
     gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                     const F16Params p) {
@@ -97,15 +103,23 @@ __global__ void __launch_bounds__(kThreadsF, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  int num_tiles = p.num_tiles, M = p.M;
+  if constexpr (GROUPED) {  // written by an earlier kernel on this stream; clamped to the buffers' capacity
+    const int cap = p.num_tiles / p.n_tiles;
+    const int mt = min(max(__ldg(p.m_tiles_dev), 0), cap);
+    num_tiles = p.n_tiles * mt;
+    M = mt * kBN;
+  }
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (elect_one()) {
       uint32_t stage = 0, phase = 0, issued_mask = 0, issued_par = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
         const int n0 = (tile % p.n_tiles) * kBM;
         const int m0 = (tile / p.n_tiles) * kBN;
+        const int kw0 = GROUPED ? min(max(__ldg(p.k_group + tile / p.n_tiles), 0), 26) * p.kst * kStageK : 0;
         for (int ks = 0; ks < p.kst; ++ks) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, &g_device_status, kDevWaitProducer, abort_flag)) {
             ok = false;
@@ -113,7 +127,7 @@ __global__ void __launch_bounds__(kThreadsF, 1)
           }
           uint8_t* sb = smem + stage * kStageBytes;
           mbar_arrive_expect_tx(&full[stage], kStageBytes);
-          tma_load_2d(sb, &tm_w, &full[stage], ks * kStageK, n0);            // x * 2 bytes = 128 * ks
+          tma_load_2d(sb, &tm_w, &full[stage], kw0 + ks * kStageK, n0);      // x * 2 bytes = 128 * (..)
           tma_load_2d(sb + kABytes, &tm_x, &full[stage], ks * kStageK, m0);
           issued_mask |= 1u << stage;
           issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
@@ -133,7 +147,7 @@ __global__ void __launch_bounds__(kThreadsF, 1)
       constexpr uint32_t idesc = idesc_f16(kBM, kBN);
       uint32_t stage = 0, phase = 0, t = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++t) {
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++t) {
         const uint32_t a = t & (kAccs - 1), apar = (t / kAccs) & 1u;
         if (!mbar_wait(&acc_empty[a], apar ^ 1u, &g_device_status, kDevWaitMma, abort_flag)) break;
         tc_fence_after();
@@ -167,7 +181,7 @@ __global__ void __launch_bounds__(kThreadsF, 1)
     const int row = quarter * 32 + lane;
     const uint32_t tlane = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
     uint32_t t = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++t) {
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
       const uint32_t a = t & (kAccs - 1), apar = (t / kAccs) & 1u;
       if (!mbar_wait(&acc_full[a], apar, &g_device_status, kDevWaitEpilogue, abort_flag)) break;
       tc_fence_after();
@@ -189,7 +203,7 @@ __global__ void __launch_bounds__(kThreadsF, 1)
             const int64_t m = m0 + c * 32 + i;
             const float v = __uint_as_float(buf[c & 1][i]);
             const float o = p.bias ? __fadd_rn(v, bv) : v;  // gb_linear's ggml_add
-            if (m < p.M) {
+            if (m < M) {
               if constexpr (OUT16)
                 yp16[(c * 32 + i) * p.ldy] = __float2half_rn(o);
               else
@@ -257,6 +271,50 @@ cudaError_t launch_gemm_f16(const void* w, int64_t ldw_bytes, const void* x16, i
     f16::gemm_f16_kernel<true><<<grid, f16::kThreadsF, f16::kSmemF, s>>>(tm_w, tm_x, p);
   else
     f16::gemm_f16_kernel<false><<<grid, f16::kThreadsF, f16::kSmemF, s>>>(tm_w, tm_x, p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_f16_grouped(const void* w, int64_t ldw_bytes, int64_t Kw, const void* x16, int64_t ldx_bytes,
+                                    int64_t M_cap, int64_t N, int64_t K, float* y, int64_t ldy,
+                                    const int32_t* m_tiles_dev, const int32_t* k_group, int64_t max_m_tiles,
+                                    int num_sms, cudaStream_t s) {
+  if (N == 0 || max_m_tiles == 0) return cudaSuccess;
+  // Every group's K slice must be whole stages, so a tile never reads into the next slice.
+  if (K <= 0 || K % f16::kStageK != 0 || Kw % K != 0 || M_cap < max_m_tiles * f16::kBN || N > INT32_MAX ||
+      M_cap > INT32_MAX)
+    return cudaErrorInvalidValue;
+  CUtensorMap tm_w, tm_x;
+  if (!make_tensor_map_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, w, Kw, N, ldw_bytes, f16::kStageK, f16::kBM,
+                          CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tensor_map_2d(&tm_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x16, K, M_cap, ldx_bytes, f16::kStageK, f16::kBN,
+                          CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  f16::F16Params p{};
+  p.M = static_cast<int>(M_cap);
+  p.N = static_cast<int>(N);
+  p.kst = static_cast<int>(K / f16::kStageK);
+  p.n_tiles = static_cast<int>((N + f16::kBM - 1) / f16::kBM);
+  const int64_t tiles = static_cast<int64_t>(p.n_tiles) * max_m_tiles;
+  if (tiles > INT32_MAX) return cudaErrorInvalidValue;
+  p.num_tiles = static_cast<int>(tiles);  // upper bound; the kernel reads the real count
+  p.y = y;
+  p.y16 = nullptr;
+  p.ldy = ldy;
+  p.bias = nullptr;
+  p.m_tiles_dev = m_tiles_dev;
+  p.k_group = k_group;
+  static std::atomic<uint64_t> ready{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
+  const uint64_t bit = dev < 64 ? (uint64_t{1} << dev) : 0;
+  if (!bit || !(ready.load(std::memory_order_acquire) & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(f16::gemm_f16_kernel<false, true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, f16::kSmemF);
+    if (e != cudaSuccess) return e;
+    ready.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  const int grid = p.num_tiles < num_sms ? p.num_tiles : num_sms;
+  f16::gemm_f16_kernel<false, true><<<grid, f16::kThreadsF, f16::kSmemF, s>>>(tm_w, tm_x, p);
   return cudaGetLastError();
 }
 

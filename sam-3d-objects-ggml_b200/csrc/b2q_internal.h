@@ -194,6 +194,23 @@ cudaError_t launch_scatter_mean_f16(const void* x16, int64_t fine, int64_t C, co
 // The same in two parts: the child lists of every coarse row (a plan of
 // 3 * coarse + 1 + fine int32, reusable while rows does not change), then the
 // one-launch fp16 accumulation over a plan.
+// Grouped F16 GEMM for the planned sparse convolution (b2q_gemm_f16.cuh):
+// x16 [M_cap][K] in 256-row tiles, *m_tiles_dev of them valid; tile j uses the
+// weight columns [k_group[j] * K, (k_group[j] + 1) * K) of w [N][Kw];
+// fp32 y [M_cap][ldy].  K % 64 == 0.
+cudaError_t launch_gemm_f16_grouped(const void* w, int64_t ldw_bytes, int64_t Kw, const void* x16, int64_t ldx_bytes,
+                                    int64_t M_cap, int64_t N, int64_t K, float* y, int64_t ldy,
+                                    const int32_t* m_tiles_dev, const int32_t* k_group, int64_t max_m_tiles,
+                                    int num_sms, cudaStream_t s);
+// Planned sparse convolution (b2q_sparse.cu): plan rows and size, plan build,
+// and the run (pair gather into g [rows][C] fp16, grouped GEMM into part
+// [rows][cout] fp32, ordered reduce into y16).  C % 64 == 0, cout % 8 == 0.
+int64_t conv_plan_rows(int64_t tokens);
+int64_t conv_plan_ints(int64_t tokens);
+cudaError_t launch_conv_plan(const int32_t* idx, int64_t tokens, int32_t* plan, cudaStream_t s);
+cudaError_t launch_conv_planned(const void* x16, int64_t tokens, int64_t C, const void* w16, int64_t cout,
+                                const float* bias, const int32_t* plan, void* g, float* part, void* y16, int num_sms,
+                                cudaStream_t s);
 cudaError_t launch_scatter_plan(const int32_t* rows, int64_t fine, int64_t coarse, int32_t* plan, cudaStream_t s);
 cudaError_t launch_scatter_mean_planned(const void* x16, int64_t C, const int32_t* plan, const float* counts,
                                         int64_t coarse, void* out16, cudaStream_t s);

@@ -151,7 +151,186 @@ __global__ void __launch_bounds__(256) scatter_mean_kernel(const uint4* __restri
   }
 }
 
+// ------------------------------------------------- planned sparse convolution
+// Plan (int32), built once per neighbour table:
+//   cnt[27] valid pairs per offset | goff[28] row start of each offset's group,
+//   groups padded to 256-row tiles | m_tiles[1] | pair_src[P] source token of
+//   each padded row (-1: padding) | pair_of[27][tokens] row of (offset, token)
+//   or -1 | tile_off[P / 256] offset of each tile.
+// P = plan_rows(tokens) bounds the padded row count of any table.
+constexpr int kPlanHead = 27 + 28 + 1;
+
+__global__ void __launch_bounds__(256) conv_count_kernel(const int32_t* __restrict__ idx, int64_t tokens,
+                                                         int32_t* __restrict__ cnt) {
+  __shared__ int32_t local[27];
+  if (threadIdx.x < 27) local[threadIdx.x] = 0;
+  __syncthreads();
+  const int64_t units = 27 * tokens;
+  for (int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < units;
+       u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t s = idx[u];
+    if (s >= 0 && s < tokens) atomicAdd(local + u / tokens, 1);
+  }
+  __syncthreads();
+  if (threadIdx.x < 27 && local[threadIdx.x]) atomicAdd(cnt + threadIdx.x, local[threadIdx.x]);
+}
+
+// One block: group starts (each group rounded up to whole 256-row tiles), the
+// tile count and every tile's offset.
+__global__ void __launch_bounds__(256) conv_layout_kernel(int32_t* __restrict__ plan, int64_t max_tiles,
+                                                          int32_t* __restrict__ tile_off) {
+  const int32_t* cnt = plan;
+  int32_t* goff = plan + 27;
+  __shared__ int32_t g[28];
+  if (threadIdx.x == 0) {
+    g[0] = 0;
+    for (int o = 0; o < 27; ++o) g[o + 1] = g[o] + (cnt[o] + 255) / 256 * 256;
+    plan[27 + 28] = g[27] / 256;
+  }
+  __syncthreads();
+  if (threadIdx.x < 28) goff[threadIdx.x] = g[threadIdx.x];
+  for (int o = 0; o < 27; ++o)
+    for (int32_t j = g[o] / 256 + threadIdx.x; j < g[o + 1] / 256 && j < max_tiles; j += blockDim.x) tile_off[j] = o;
+}
+
+// One block per offset: a block-wide scan of the valid flags over the tokens
+// (in token order, so the layout is deterministic) places every pair.
+__global__ void __launch_bounds__(1024) conv_fill_kernel(const int32_t* __restrict__ idx, int64_t tokens,
+                                                         const int32_t* __restrict__ plan,
+                                                         int32_t* __restrict__ pair_src,
+                                                         int32_t* __restrict__ pair_of) {
+  __shared__ int32_t warp_sums[32];
+  __shared__ int32_t base_s;
+  const int o = blockIdx.x;
+  const int32_t g0 = plan[27 + o], g1 = plan[27 + o + 1], n_valid = plan[o];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (threadIdx.x == 0) base_s = 0;
+  __syncthreads();
+  for (int64_t t0 = 0; t0 < tokens; t0 += blockDim.x) {
+    const int64_t t = t0 + threadIdx.x;
+    const int32_t s = t < tokens ? idx[o * tokens + t] : -1;
+    const bool v = s >= 0 && s < tokens;
+    const unsigned bal = __ballot_sync(0xffffffffu, v);
+    if (lane == 0) warp_sums[wid] = __popc(bal);
+    __syncthreads();
+    if (wid == 0) {
+      int32_t x = warp_sums[lane];
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int32_t y = __shfl_up_sync(0xffffffffu, x, d);
+        if (lane >= d) x += y;
+      }
+      warp_sums[lane] = x;  // inclusive
+    }
+    __syncthreads();
+    const int32_t before = (wid ? warp_sums[wid - 1] : 0) + __popc(bal & ((1u << lane) - 1u));
+    const int32_t base = base_s;
+    if (t < tokens) {
+      const int32_t r = g0 + base + before;
+      pair_of[o * tokens + t] = v ? r : -1;
+      if (v) pair_src[r] = s;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) base_s = base + warp_sums[31];
+    __syncthreads();
+  }
+  for (int32_t r = g0 + n_valid + threadIdx.x; r < g1; r += blockDim.x) pair_src[r] = -1;  // padding rows
+}
+
+// Rows of the padded pair matrix: g[r] = x[pair_src[r]] (zero for padding),
+// for r below the plan's row count.
+__global__ void __launch_bounds__(256) gather_pairs_kernel(const uint4* __restrict__ x, int64_t tokens, int64_t c8,
+                                                           const int32_t* __restrict__ plan, int64_t max_rows,
+                                                           const int32_t* __restrict__ pair_src,
+                                                           uint4* __restrict__ g) {
+  int64_t rows = static_cast<int64_t>(plan[27 + 28]) * 256;
+  rows = rows < 0 ? 0 : (rows > max_rows ? max_rows : rows);  // a plan never exceeds its own capacity
+  const int64_t units = rows * c8;
+  for (int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < units;
+       u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = u / c8, ch = u - r * c8;
+    const int32_t s = pair_src[r];
+    g[u] = (s >= 0 && s < tokens) ? __ldg(x + s * c8 + ch) : make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+// y16[t][8 outputs] = fp16(bias + sum over offsets o = 0..26 of the pair
+// partials), fp32, offsets in ascending order.
+__global__ void __launch_bounds__(256) conv_reduce_kernel(const float4* __restrict__ part, int64_t cout8,
+                                                          int64_t part_rows, const int32_t* __restrict__ pair_of,
+                                                          int64_t tokens, const float* __restrict__ bias,
+                                                          uint4* __restrict__ y) {
+  const int64_t units = tokens * cout8;
+  for (int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < units;
+       u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = u / cout8, c = u - t * cout8;
+    float a[8];
+    if (bias) {
+      const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias) + 2 * c);
+      const float4 b1 = __ldg(reinterpret_cast<const float4*>(bias) + 2 * c + 1);
+      a[0] = b0.x, a[1] = b0.y, a[2] = b0.z, a[3] = b0.w, a[4] = b1.x, a[5] = b1.y, a[6] = b1.z, a[7] = b1.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a[i] = 0.0f;
+    }
+    for (int o = 0; o < 27; ++o) {
+      const int32_t r = pair_of[o * tokens + t];
+      if (r < 0 || r >= part_rows) continue;
+      const float4 p0 = __ldg(part + (static_cast<int64_t>(r) * cout8 + c) * 2);
+      const float4 p1 = __ldg(part + (static_cast<int64_t>(r) * cout8 + c) * 2 + 1);
+      a[0] = __fadd_rn(a[0], p0.x), a[1] = __fadd_rn(a[1], p0.y), a[2] = __fadd_rn(a[2], p0.z);
+      a[3] = __fadd_rn(a[3], p0.w), a[4] = __fadd_rn(a[4], p1.x), a[5] = __fadd_rn(a[5], p1.y);
+      a[6] = __fadd_rn(a[6], p1.z), a[7] = __fadd_rn(a[7], p1.w);
+    }
+    uint4 o16;
+    __half* h = reinterpret_cast<__half*>(&o16);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) h[i] = __float2half_rn(a[i]);
+    y[u] = o16;
+  }
+}
+
 }  // namespace
+
+int64_t conv_plan_rows(int64_t tokens) { return round_up(27 * tokens + 27 * 255, 256); }
+int64_t conv_plan_ints(int64_t tokens) {
+  return kPlanHead + conv_plan_rows(tokens) + 27 * tokens + conv_plan_rows(tokens) / 256;
+}
+
+cudaError_t launch_conv_plan(const int32_t* idx, int64_t tokens, int32_t* plan, cudaStream_t s) {
+  const int64_t P = conv_plan_rows(tokens);
+  int32_t* pair_src = plan + kPlanHead;
+  int32_t* pair_of = pair_src + P;
+  int32_t* tile_off = pair_of + 27 * tokens;
+  cudaError_t e = cudaMemsetAsync(plan, 0, kPlanHead * sizeof(int32_t), s);
+  if (e != cudaSuccess) return e;
+  if (tokens > 0) conv_count_kernel<<<grid_cap(27 * tokens, 256, 8), 256, 0, s>>>(idx, tokens, plan);
+  conv_layout_kernel<<<1, 256, 0, s>>>(plan, P / 256, tile_off);
+  if (tokens > 0) conv_fill_kernel<<<27, 1024, 0, s>>>(idx, tokens, plan, pair_src, pair_of);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_conv_planned(const void* x16, int64_t tokens, int64_t C, const void* w16, int64_t cout,
+                                const float* bias, const int32_t* plan, void* g, float* part, void* y16, int num_sms,
+                                cudaStream_t s) {
+  if (tokens == 0) return cudaSuccess;
+  const int64_t P = conv_plan_rows(tokens);
+  const int32_t* pair_src = plan + kPlanHead;
+  const int32_t* pair_of = pair_src + P;
+  const int32_t* tile_off = pair_of + 27 * tokens;
+  const int64_t c8 = C / 8;
+  gather_pairs_kernel<<<grid_cap(P * c8, 256, 16), 256, 0, s>>>(static_cast<const uint4*>(x16), tokens, c8, plan, P,
+                                                                pair_src, static_cast<uint4*>(g));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  e = launch_gemm_f16_grouped(w16, 27 * C * 2, 27 * C, g, C * 2, P, cout, C, part, cout, plan + 27 + 28, tile_off,
+                              P / 256, num_sms, s);
+  if (e != cudaSuccess) return e;
+  const int64_t cout8 = cout / 8;
+  conv_reduce_kernel<<<grid_cap(tokens * cout8, 256, 16), 256, 0, s>>>(
+      reinterpret_cast<const float4*>(part), cout8, P, pair_of, tokens, bias, static_cast<uint4*>(y16));
+  return cudaGetLastError();
+}
 
 cudaError_t launch_gather27(const void* x16, int64_t tokens, int64_t C, const int32_t* idx, void* g,
                             cudaStream_t s) {

@@ -271,3 +271,19 @@ def test_sparse_validation(b2q_mod):
     assert plan(FAKE, 100, 0, FAKE, 0, None) == 0                                          # no coarse rows
     assert run(FAKE, 100, 12, FAKE, FAKE, 10, FAKE, None) == 1                             # C % 8
     assert run(FAKE, 100, 8, None, FAKE, 10, FAKE, None) == 1                              # no plan
+
+
+def test_sparse_conv_plan_validation(b2q_mod):
+    L = b2q.lib()
+    plan, run = L.b2q_sparse_conv_plan, L.b2q_sparse_conv_f16_planned
+    ws = 1 << 26
+    assert L.b2q_sparse_conv_plan_bytes(100) > 27 * 100 * 4
+    assert L.b2q_sparse_conv_f16_planned_workspace_bytes(100, 96, 64) == 0                 # C % 64
+    assert L.b2q_sparse_conv_f16_planned_workspace_bytes(100, 64, 60) == 0                 # Cout % 8
+    assert plan(FAKE, 100, FAKE, 100, None) == 4                                           # plan too small
+    assert plan(FAKE + 2, 100, FAKE, ws, None) == 3                                        # index alignment
+    assert run(FAKE, 100, 96, FAKE, 64, None, FAKE, FAKE, FAKE, ws, None) == 1             # C % 64
+    assert run(FAKE, 100, 64, FAKE, 60, None, FAKE, FAKE, FAKE, ws, None) == 1             # Cout % 8
+    assert run(FAKE, 100, 64, FAKE, 64, None, FAKE, FAKE + 8, FAKE, ws, None) == 3         # y alignment
+    assert run(FAKE, 100, 64, FAKE, 64, None, FAKE, FAKE, FAKE, 100, None) == 4            # workspace
+    assert run(FAKE, 0, 64, FAKE, 64, None, FAKE, FAKE, FAKE, 0, None) == 0                # no tokens

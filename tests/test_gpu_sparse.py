@@ -142,3 +142,49 @@ def test_sparse_conv_missing_neighbours_and_out_of_range(dev):
     assert np.array_equal(got[0], b16) and np.array_equal(got[1], b16)
     err = np.abs(got.astype(np.float64) - want.astype(np.float64))
     assert np.all(err <= _conv_bound(x16, w16, idx, want))
+
+
+@pytest.mark.parametrize("grid,occ,C,cout,bias", [(24, 0.05, 64, 96, True), (20, 0.3, 128, 128, False),
+                                                  (16, 0.02, 256, 64, True)])
+def test_planned_conv_matches_cpu_operator(dev, grid, occ, C, cout, bias):
+    """The planned convolution (only occupied neighbour pairs, grouped GEMM,
+    ordered fp32 reduce) against the CPU operator, with the same bound as the
+    dense form, and one plan reused for two inputs."""
+    idx, _, _, _ = sparse_grid(grid, occ, C + cout)
+    tokens = idx.shape[1]
+    rng = np.random.default_rng(C * 3 + cout)
+    w16 = (rng.standard_normal((cout, 27 * C)) / np.sqrt(27 * C)).astype(np.float16)
+    b16 = (rng.standard_normal(cout) * 0.1).astype(np.float16) if bias else None
+    idx_d = to_dev(idx, dev)
+    plan = b2q.sparse_conv_plan(idx_d)
+    for _ in range(2):
+        x16 = rng.standard_normal((tokens, C)).astype(np.float16)
+        got = b2q.sparse_conv_f16_planned(to_dev(x16, dev), to_dev(w16, dev), to_dev(b16, dev) if bias else None,
+                                          plan).cpu().numpy()
+        want = O.sparse_conv_f16(x16, w16, b16, idx)
+        err = np.abs(got.astype(np.float64) - want.astype(np.float64))
+        assert np.all(np.isfinite(got))
+        assert np.all(err <= _conv_bound(x16, w16, idx, want))
+        assert np.mean(err == 0) >= 0.97
+
+
+def test_planned_conv_isolated_tokens_and_out_of_range(dev):
+    """Tokens with no valid neighbour return the bias; indices >= tokens are
+    missing; a table with every slot empty gives the bias everywhere."""
+    C, cout, tokens = 64, 32, 300
+    rng = np.random.default_rng(12)
+    x16 = rng.standard_normal((tokens, C)).astype(np.float16)
+    w16 = (rng.standard_normal((cout, 27 * C)) * 0.05).astype(np.float16)
+    b16 = rng.standard_normal(cout).astype(np.float16)
+    idx = np.where(rng.random((27, tokens)) < 0.1, rng.integers(0, tokens + 5, (27, tokens)), -1).astype(np.int32)
+    idx[:, :3] = -1
+    got = b2q.sparse_conv_f16_planned(to_dev(x16, dev), to_dev(w16, dev), to_dev(b16, dev),
+                                      b2q.sparse_conv_plan(to_dev(idx, dev))).cpu().numpy()
+    want = O.sparse_conv_f16(x16, w16, b16, idx)
+    assert np.array_equal(got[:3], np.tile(b16, (3, 1)))
+    err = np.abs(got.astype(np.float64) - want.astype(np.float64))
+    assert np.all(err <= _conv_bound(x16, w16, idx, want))
+    empty = np.full((27, tokens), -1, np.int32)
+    got = b2q.sparse_conv_f16_planned(to_dev(x16, dev), to_dev(w16, dev), to_dev(b16, dev),
+                                      b2q.sparse_conv_plan(to_dev(empty, dev))).cpu().numpy()
+    assert np.array_equal(got, np.tile(b16, (tokens, 1)))
