@@ -800,6 +800,47 @@ def slat_grid_tables(seed: int = 3):
     return neighbour_table(keys, g), neighbour_table(ckeys, g // 2), rows.astype(np.int32), counts
 
 
+SPARSE_CASES = ("sparse_conv_fine", "sparse_conv_fine_planned")
+
+
+def run_sparse_case(args):
+    """Profiling case: --steps sparse convolutions (128 -> 128 channels on the
+    configs[3] fine cells), dense or planned, after --warmup; hot L2."""
+    import torch
+    import b2q
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    idx, _, _, _ = slat_grid_tables()
+    tokens, C, cout = idx.shape[1], 128, 128
+    gen = torch.Generator(device=dev).manual_seed(41)
+    x16 = torch.randn(tokens, C, device=dev, generator=gen).half()
+    w16 = (torch.randn(cout, 27 * C, device=dev, generator=gen) / (27 * C) ** 0.5).half()
+    b16 = (torch.randn(cout, device=dev, generator=gen) * 0.1).half()
+    y16 = torch.empty(tokens, cout, device=dev, dtype=torch.float16)
+    table = torch.from_numpy(idx).to(dev)
+    if args.only.endswith("planned"):
+        plan = b2q.sparse_conv_plan(table)
+        ws = b2q._empty_aligned(b2q.lib().b2q_sparse_conv_f16_planned_workspace_bytes(tokens, C, cout), dev)
+        fn = lambda: b2q.sparse_conv_f16_planned(x16, w16, b16, plan, out=y16, ws=ws)  # noqa: E731
+    else:
+        ws = b2q._empty_aligned(b2q.lib().b2q_sparse_conv_f16_workspace_bytes(tokens, C, cout), dev)
+        fn = lambda: b2q.sparse_conv_f16(x16, w16, b16, table, out=y16, ws=ws)  # noqa: E731
+    for _ in range(args.warmup):
+        fn()
+    # Ten calls per event pair: a single call of a few microseconds would time
+    # the host's submission, not the device.
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for e0, e1 in evs:
+        e0.record()
+        for _ in range(10):
+            fn()
+        e1.record()
+    torch.cuda.synchronize()
+    us = statistics.median(e0.elapsed_time(e1) for e0, e1 in evs) * 1e3 / 10
+    return {"case": args.only, "tokens": tokens, "C": C, "Cout": cout, "us_per_call_hot_l2": round(us, 2),
+            "calls_per_event_pair": 10}
+
+
 def slat_sparse_side(b2q, flush, stream, dev, peaks, iters=10):
     """The SLat sparse stages at the configs[3] grid: the F16 submanifold
     convolution (gather of the 27 neighbour rows + kind::f16 GEMM) on the fine
@@ -1119,6 +1160,8 @@ def main():
         return
     if args.only in F16_CASES:
         res = run_f16_case(args)
+    elif args.only in SPARSE_CASES:
+        res = run_sparse_case(args)
     else:
         res = run_colpar(args, rank, world, local_rank) if args.colpar else run_gpu(args, rank, world, local_rank)
     if rank == 0:

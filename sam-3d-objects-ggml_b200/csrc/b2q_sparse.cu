@@ -273,8 +273,14 @@ __global__ void __launch_bounds__(256) conv_reduce_kernel(const float4* __restri
 #pragma unroll
       for (int i = 0; i < 8; ++i) a[i] = 0.0f;
     }
+    // All 27 pair rows first (independent loads), then the partials; the adds
+    // stay in offset order.
+    int32_t rr[27];
+#pragma unroll
+    for (int o = 0; o < 27; ++o) rr[o] = __ldg(pair_of + o * tokens + t);
+#pragma unroll
     for (int o = 0; o < 27; ++o) {
-      const int32_t r = pair_of[o * tokens + t];
+      const int32_t r = rr[o];
       if (r < 0 || r >= part_rows) continue;
       const float4 p0 = __ldg(part + (static_cast<int64_t>(r) * cout8 + c) * 2);
       const float4 p1 = __ldg(part + (static_cast<int64_t>(r) * cout8 + c) * 2 + 1);
