@@ -959,8 +959,9 @@ COLPAR_SHAPE = ("slat_qkv_q4_0", 2, 20480, 3072, 1024)  # name, wtype, M tokens,
 
 
 def run_colpar(args, rank, world, local_rank):
-    """One large SLat linear split by output rows over the ranks (survey §8(e)):
-    every rank needs the whole [M][N] output.  Times the fused kernel (GEMM
+    """One large SLat linear split by output rows over the ranks (the
+    column-parallel variant of BASELINE configs[4]): every rank needs the whole
+    [M][N] output.  Times the fused kernel (GEMM
     epilogue storing each tile into every rank's buffer over NVLink) against
     GEMM + NCCL all-gather + transpose.  Each iteration ends with a one-element
     all-reduce so that every rank's work of the iteration is complete; both
