@@ -282,30 +282,39 @@ def run_gpu(args, rank, world, local_rank):
 
     # Copies run on their own streams so that the upload of one GEMM's input,
     # another GEMM's compute and the download of a third GEMM's output overlap
-    # (the H2D and D2H copy engines and the SMs are separate); events keep each
-    # buffer's reuse ordered across steps.
+    # (the H2D and D2H copy engines and the SMs are separate).  The device
+    # input and output buffers are doubled and alternate by step, so a step's
+    # uploads need not wait for the previous step's GEMMs; events keep each
+    # buffer's reuse ordered.
     h2d_stream, d2h_stream = torch.cuda.Stream(), torch.cuda.Stream()
     ev = lambda: torch.cuda.Event()  # noqa: E731
     for g in gemms:
-        g["uploaded"], g["computed"], g["downloaded"] = ev(), ev(), ev()
-        g["computed"].record(stream)
-        g["downloaded"].record(stream)
+        g["x_devs"] = [g["x_dev"], torch.empty_like(g["x_dev"])]
+        g["y_devs"] = [g["y_dev"], torch.empty_like(g["y_dev"])]
+        g["uploaded"] = ev()
+        g["computed"], g["downloaded"] = [ev(), ev()], [ev(), ev()]
+        for b in range(2):
+            g["computed"][b].record(stream)
+            g["downloaded"][b].record(stream)
+    e2e_parity = [0]
 
     def e2e_step():
+        b = e2e_parity[0]
+        e2e_parity[0] ^= 1
         for g in gemms:
-            h2d_stream.wait_event(g["computed"])  # the previous step's GEMM has read x_dev
+            h2d_stream.wait_event(g["computed"][b])  # the GEMM two steps back has read this x buffer
             with torch.cuda.stream(h2d_stream):
-                g["x_dev"].copy_(g["x_host"], non_blocking=True)
+                g["x_devs"][b].copy_(g["x_host"], non_blocking=True)
             g["uploaded"].record(h2d_stream)
             stream.wait_event(g["uploaded"])
-            stream.wait_event(g["downloaded"])  # the previous step's y has left y_dev
-            b2q.mul_mat_packed(g["packed"], g["N"], g["K"], g["x_dev"], out=g["y_dev"], ws=g["ws"],
+            stream.wait_event(g["downloaded"][b])  # this y buffer's previous result has left
+            b2q.mul_mat_packed(g["packed"], g["N"], g["K"], g["x_devs"][b], out=g["y_devs"][b], ws=g["ws"],
                                stream=stream)
-            g["computed"].record(stream)
-            d2h_stream.wait_event(g["computed"])
+            g["computed"][b].record(stream)
+            d2h_stream.wait_event(g["computed"][b])
             with torch.cuda.stream(d2h_stream):
-                g["y_host"].copy_(g["y_dev"], non_blocking=True)
-            g["downloaded"].record(d2h_stream)
+                g["y_host"].copy_(g["y_devs"][b], non_blocking=True)
+            g["downloaded"][b].record(d2h_stream)
 
     for _ in range(min(args.warmup, 3) if e2e_steps else 0):
         e2e_step()
@@ -318,7 +327,8 @@ def run_gpu(args, rank, world, local_rank):
     for _ in range(e2e_steps):
         e2e_step()
     for g in gemms:  # the timed region ends when every download has landed
-        stream.wait_event(g["downloaded"])
+        for b in range(2):
+            stream.wait_event(g["downloaded"][b])
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
@@ -379,7 +389,8 @@ def run_gpu(args, rank, world, local_rank):
         "e2e": {"value": round(e2e_value, 2) if e2e_value else None, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "path": "b2q_mul_mat_packed per GEMM; pinned host x -> device -> pinned host y, uploads and "
-                        "downloads on their own streams, overlapped with other GEMMs' compute"},
+                        "downloads on their own streams, overlapped with other GEMMs' compute; device x / y "
+                        "buffers doubled and alternated by step"},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(), "breakdown": breakdown,
     }
