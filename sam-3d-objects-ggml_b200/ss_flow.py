@@ -25,7 +25,8 @@ B200-first choices: the CFG branches share one pass (twice the tokens per
 GEMM); the adaLN weights of all blocks are stacked into one [blocks*6C, C]
 mul_mat (its input SiLU(mod) is the same for every block); the condition
 tokens are quantized once per forward for all blocks and both groups; the
-whole step is captured into one CUDA graph (`capture`).  Library pieces, not
+pose group runs on a second stream beside the shape group; the whole step is
+captured into one CUDA graph (`capture`), both streams included.  Library pieces, not
 the mul_mat path: the attention cores (torch SDPA, fp16), the F32 input layers
 (K <= 8, not block-quantizable: torch matmul), the timestep embedding's cos /
 sin and SiLU on 256 / 1024 values, and the Euler update (torch elementwise).
@@ -185,6 +186,10 @@ class SsFlow:
         import torch.nn.functional as F
         C, T, nb = self.C, self.T, self.nb
         n_cond = cond.shape[0] // B
+        main = torch.cuda.current_stream(self.dev)
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream(device=self.dev)
+        side = self._side
         mod = self._embed("t", t) + self._embed("d", d)
         six_all = b2q.mul_mat_packed(self.W_adaln, nb * 6 * C, C, F.silu(mod), bias=self.b_adaln)
         act_c = b2q.act_prepare(cond)  # one quantize of the condition tokens for every block and group
@@ -193,20 +198,38 @@ class SsFlow:
         hs = (hs + self.V["pe.shape"]).view(B * T, C).contiguous()
         hp = torch.stack([xp[m] @ self.V[f"in.{m}"].t() + self.V[f"in.{m}.b"] + self.V[f"pe.{m}"][0]
                           for m, _ in POSE], 1).reshape(B * 4, C).contiguous()  # row b*4 + j
+        # The 4-token pose group runs on a second stream: its kernels are small
+        # and latency-bound, and only its self-attention needs the shape
+        # group's keys and values (one event per block).  The shape group keeps
+        # the main stream; both join before the output layers.
+        forked = torch.cuda.Event()
+        forked.record(main)
+        side.wait_event(forked)
+        for t_ in (six_all, act_c, hp):
+            t_.record_stream(side)
         for i in range(nb):
             six = six_all[0, i * 6 * C:(i + 1) * 6 * C]
             shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = (six[j * C:(j + 1) * C]
                                                                               for j in range(6))
             qs, ks, vs = self._qkv("s", i, hs, B, T, scale_msa, shift_msa)
-            qp, kp, vp = self._qkv("p", i, hp, B, 4, scale_msa, shift_msa)
+            kv_ready = torch.cuda.Event()
+            kv_ready.record(main)
+            with torch.cuda.stream(side):
+                qp, kp, vp = self._qkv("p", i, hp, B, 4, scale_msa, shift_msa)
+                side.wait_event(kv_ready)
+                ks.record_stream(side)
+                vs.record_stream(side)
+                o_p = F.scaled_dot_product_attention(qp, torch.cat([kp, ks], 2), torch.cat([vp, vs], 2))
+                self._attn_out("p", i, o_p, hp, gate_msa)
+                self._cross("p", i, hp, B, 4, act_c, n_cond)
+                self._mlp("p", i, hp, scale_mlp, shift_mlp, gate_mlp)
             o_s = F.scaled_dot_product_attention(qs, ks, vs)
-            o_p = F.scaled_dot_product_attention(qp, torch.cat([kp, ks], 2), torch.cat([vp, vs], 2))
             self._attn_out("s", i, o_s, hs, gate_msa)
-            self._attn_out("p", i, o_p, hp, gate_msa)
             self._cross("s", i, hs, B, T, act_c, n_cond)
-            self._cross("p", i, hp, B, 4, act_c, n_cond)
             self._mlp("s", i, hs, scale_mlp, shift_mlp, gate_mlp)
-            self._mlp("p", i, hp, scale_mlp, shift_mlp, gate_mlp)
+        joined = torch.cuda.Event()
+        joined.record(side)
+        main.wait_event(joined)
         act = b2q.norm_modulate_q8(hs, EPS)
         v_shape = b2q.mul_mat_prepared(self.W["out.shape"], self.in_ch, C, act, B * T, bias=self.V["out.shape.b"])
         hpn = b2q.norm_modulate(hp, EPS)
