@@ -172,3 +172,31 @@ def test_euler_schedule_matches_reference_formula():
     u = 0.52
     assert abs(np.float32(u / (1 + 2 * (1 - u))) - ss_flow.euler_schedule(50, 3.0)[26][0]) < 1e-7
     assert abs(sum(dt for _, dt in s) - 1.0) < 1e-5
+
+
+@pytest.mark.gpu
+def test_sampler_step_without_cfg(b2q_mod, dev):
+    """A step past the CFG window (model time > 500) runs the conditional
+    branch alone (B = 1) and integrates x + dt * vc; its captured graph
+    replays bit-identically."""
+    import torch
+    wtype = O.TYPE_Q8_0
+    p = make_params(wtype, seed=2)
+    flow = ss_flow.SsFlow(dev, p, wtype=wtype, **CFG)
+    _, _, cond, _ = inputs(1, seed=6)
+    eager = ss_flow.SsSampler(flow, torch.from_numpy(cond).to(dev), N_COND, seed=4)
+    graph = ss_flow.SsSampler(flow, torch.from_numpy(cond).to(dev), N_COND, seed=4)
+    graph.capture(cfg=False)
+    t, dt = ss_flow.euler_schedule()[20]
+    assert t * 1000.0 > ss_flow.CFG_END
+    x0 = eager.xs.clone()
+    vs, vp = flow.forward(x0, {m: v.clone() for m, v in eager.xp.items()}, torch.tensor([t * 1000.0], device=dev),
+                          torch.zeros(1, device=dev), eager.cond2[:N_COND], 1)
+    eager.step(t * 1000.0, dt)
+    graph.step(t * 1000.0, dt)
+    torch.cuda.synchronize()
+    assert torch.equal(eager.xs, x0 + torch.tensor([dt], device=dev) * vs)
+    assert torch.equal(graph.xs, eager.xs)
+    for m in eager.xp:
+        assert torch.equal(graph.xp[m], eager.xp[m])
+    assert b2q.device_status() == 0
