@@ -811,6 +811,37 @@ def slat_grid_tables(seed: int = 3):
     return neighbour_table(keys, g), neighbour_table(ckeys, g // 2), rows.astype(np.int32), counts
 
 
+def run_ss_step_case(args):
+    """Profiling case: the configs[4] SS-flow step run eagerly (no graph, so a
+    profiler sees every kernel), --warmup steps, then --steps steps inside the
+    NVTX range "ss_step"; prints the median CUDA-event time per step."""
+    import torch
+    import b2q
+    import ss_flow
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = SS_FLOW
+    C, nc = cfg["C"], SS_BLOCK["n_cond"]
+    specs = ss_flow.param_specs(C, cfg["n_blocks"], cfg["n_shape"], cfg["in_ch"], cfg["mlp_ratio"])
+    flow = ss_flow.SsFlow(dev, ss_flow.random_params(specs, dev, b2q.TYPE_Q8_0, seed=11), **cfg)
+    gen = torch.Generator(device=dev).manual_seed(13)
+    smp = ss_flow.SsSampler(flow, torch.randn(nc, C, device=dev, generator=gen), nc, seed=12)
+    t, dt = ss_flow.euler_schedule()[0]
+    for _ in range(args.warmup):
+        smp.step(t * 1000.0, dt)
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    torch.cuda.nvtx.range_push("ss_step")
+    for e0, e1 in evs:
+        e0.record()
+        smp.step(t * 1000.0, dt)
+        e1.record()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in evs)
+    return {"case": "ss_step", "step_ms_eager": round(ms, 3), "steps": args.steps}
+
+
 SPARSE_CASES = ("sparse_conv_fine", "sparse_conv_fine_planned")
 
 
@@ -1174,6 +1205,8 @@ def main():
         res = run_f16_case(args)
     elif args.only in SPARSE_CASES:
         res = run_sparse_case(args)
+    elif args.only == "ss_step":
+        res = run_ss_step_case(args)
     else:
         res = run_colpar(args, rank, world, local_rank) if args.colpar else run_gpu(args, rank, world, local_rank)
     if rank == 0:

@@ -82,18 +82,74 @@ __global__ void __launch_bounds__(256) rows_to_heads_kernel(const float* __restr
   }
 }
 
+// D = 64 (16 heads of C 1024): a warp takes two heads of one row, 16 lanes
+// each, lane holding d = 4 (l % 16) .. + 3: one 512-byte float4 load per part
+// and 8-byte fp16 stores (each head's 128-byte output row contiguous).  The
+// double sum of squares is exact for ordinary data, so the 16-lane tree gives
+// the same value as the 32-lane layout above.  Index math in 32 bits.
+__global__ void __launch_bounds__(256) rows_to_heads64_kernel(const float* __restrict__ qkv, uint32_t rows, uint32_t T,
+                                                              uint32_t H, int64_t ldq, int parts, unsigned norm_mask,
+                                                              const float* __restrict__ gq,
+                                                              const float* __restrict__ gk, float eps,
+                                                              __half* __restrict__ q16, __half* __restrict__ k16,
+                                                              __half* __restrict__ v16) {
+  constexpr int D = 64;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane >> 4, l16 = lane & 15;
+  const int64_t C = static_cast<int64_t>(H) * D;
+  const uint32_t hpairs = H / 2;
+  const uint32_t units = rows * hpairs;
+  const uint32_t warps = gridDim.x * (blockDim.x / 32);
+  for (uint32_t u = (blockIdx.x * blockDim.x + threadIdx.x) / 32; u < units; u += warps) {
+    const uint32_t r = u / hpairs;
+    const uint32_t h = (u - r * hpairs) * 2 + sub;
+    const uint32_t b = r / T, t = r - b * T;
+    const int64_t dst = ((static_cast<int64_t>(b) * H + h) * T + t) * D + 4 * l16;
+    const float* src = qkv + static_cast<int64_t>(r) * ldq + static_cast<int64_t>(h) * D + 4 * l16;
+    for (int part = 0; part < parts; ++part) {  // q, k, v
+      float4 x = __ldg(reinterpret_cast<const float4*>(src + part * C));
+      __half* out = part == 0 ? q16 : part == 1 ? k16 : v16;
+      if ((norm_mask >> part) & 1u) {
+        double s = static_cast<double>(__fmul_rn(x.x, x.x)) + static_cast<double>(__fmul_rn(x.y, x.y)) +
+                   static_cast<double>(__fmul_rn(x.z, x.z)) + static_cast<double>(__fmul_rn(x.w, x.w));
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);  // within the 16 lanes
+        const float mean = __double2float_rn(__ddiv_rn(s, static_cast<double>(D)));
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+        x.x = __fmul_rn(x.x, scale), x.y = __fmul_rn(x.y, scale), x.z = __fmul_rn(x.z, scale);
+        x.w = __fmul_rn(x.w, scale);
+        const float* g0 = part == 0 ? gq : gk;
+        if (g0) {
+          const float4 g = __ldg(reinterpret_cast<const float4*>(g0 + static_cast<int64_t>(h) * D + 4 * l16));
+          x.x = __fmul_rn(x.x, g.x), x.y = __fmul_rn(x.y, g.y), x.z = __fmul_rn(x.z, g.z), x.w = __fmul_rn(x.w, g.w);
+        }
+      }
+      __half2 lo = __floats2half2_rn(x.x, x.y), hi = __floats2half2_rn(x.z, x.w);
+      uint2 pk;
+      pk.x = *reinterpret_cast<uint32_t*>(&lo);
+      pk.y = *reinterpret_cast<uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(out + dst) = pk;
+    }
+  }
+}
+
 // One lane per (row, block): 32 contiguous fp16 of one head -> one Q8_0 block
 // (the stand-alone quantizer's arithmetic on their fp32 values).
+// Lane i of a warp takes row 32 * rg + i and block j (the stand-alone
+// quantizer's mapping): the 32 scales of a warp are one 128-byte store.
 template <int VARIANT>
 __global__ void __launch_bounds__(256) heads_q8_kernel(const __half* __restrict__ o, int64_t rows, int64_t T,
                                                        int H, int D, int64_t sb, int64_t sh, int64_t st,
                                                        int8_t* __restrict__ codes, float* __restrict__ scales,
                                                        int64_t ld) {
   const int64_t kb = static_cast<int64_t>(H) * D / kQK;
-  const int64_t units = rows * kb;
-  for (int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < units;
-       u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t r = u / kb, j = u - r * kb;
+  const int64_t units = (rows + 31) / 32 * kb;  // (row group, block)
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32; w < units; w += warps) {
+    const int64_t rg = w / kb, j = w - rg * kb;
+    const int64_t r = rg * 32 + lane;
+    if (r >= rows) continue;
     const int64_t b = r / T, t = r - b * T;
     const int64_t c0 = j * kQK;
     const int h = static_cast<int>(c0 / D), d0 = static_cast<int>(c0 - static_cast<int64_t>(h) * D);
@@ -142,7 +198,15 @@ cudaError_t launch_rows_to_heads(const float* src, int64_t B, int64_t T, int H, 
       rows_to_heads_kernel<1><<<grid, 256, 0, s>>>(src, rows, T, H, ld_floats, parts, norm_mask, g0, g1, eps, a, b, c);
       break;
     case 64:
-      rows_to_heads_kernel<2><<<grid, 256, 0, s>>>(src, rows, T, H, ld_floats, parts, norm_mask, g0, g1, eps, a, b, c);
+      if (H % 2 == 0 && ld_floats % 4 == 0 && reinterpret_cast<uintptr_t>(src) % 16 == 0 &&
+          (!g0 || reinterpret_cast<uintptr_t>(g0) % 16 == 0) && (!g1 || reinterpret_cast<uintptr_t>(g1) % 16 == 0) &&
+          rows * H <= 0xffffffffLL)
+        rows_to_heads64_kernel<<<grid_for(rows * H / 2, 8, 16), 256, 0, s>>>(
+            src, static_cast<uint32_t>(rows), static_cast<uint32_t>(T), static_cast<uint32_t>(H), ld_floats, parts,
+            norm_mask, g0, g1, eps, a, b, c);
+      else
+        rows_to_heads_kernel<2><<<grid, 256, 0, s>>>(src, rows, T, H, ld_floats, parts, norm_mask, g0, g1, eps, a, b,
+                                                     c);
       break;
     case 128:
       rows_to_heads_kernel<4><<<grid, 256, 0, s>>>(src, rows, T, H, ld_floats, parts, norm_mask, g0, g1, eps, a, b, c);
@@ -156,7 +220,7 @@ cudaError_t launch_heads_q8(const void* o16, int64_t B, int64_t T, int H, int D,
                             int64_t st, int8_t* codes, float* scales, int64_t ld, int variant, cudaStream_t s) {
   const int64_t rows = B * T;
   if (rows == 0) return cudaSuccess;
-  const int grid = grid_for(rows * H * D / kQK, 256, 8);
+  const int grid = grid_for((rows + 31) / 32 * (H * D / kQK) * 32, 256, 8);
   const __half* o = static_cast<const __half*>(o16);
   if (variant == 0)
     heads_q8_kernel<0><<<grid, 256, 0, s>>>(o, rows, T, H, D, sb, sh, st, codes, scales, ld);

@@ -30,9 +30,10 @@ def _no_device_errors(b2q_mod, dev):
     assert b2q.device_status(clear=True) == 0
 
 
-def test_qkv_heads_matches_cpu(dev):
+@pytest.mark.parametrize("H", [4, 5])  # even H: the float4 kernel; odd H: the 32-lane kernel
+def test_qkv_heads_matches_cpu(dev, H):
     import torch
-    B, T, H, D = 2, 37, 4, 64
+    B, T, D = 2, 37, 64
     C = H * D
     rng = np.random.default_rng(1)
     qkv = (rng.standard_normal((B * T, 3 * C + 8)) * 2).astype(np.float32)   # padded rows
@@ -58,10 +59,12 @@ def test_qkv_heads_matches_cpu(dev):
 
 
 @pytest.mark.parametrize("parts", [1, 2])
-def test_rows_to_heads_is_fp16_transpose(dev, parts):
+@pytest.mark.parametrize("D", [32, 64])
+def test_rows_to_heads_is_fp16_transpose(dev, parts, D):
     """The cross-attention's q (parts 1) and k | v (parts 2) rows -> fp16
-    heads: a plain round-to-nearest conversion and a transpose, bit-exact."""
-    B, T, H, D = 2, 45, 8, 32
+    heads: a plain round-to-nearest conversion and a transpose, bit-exact
+    (D = 64 takes the two-heads-per-warp float4 kernel)."""
+    B, T, H = 2, 45, 8
     C = H * D
     rng = np.random.default_rng(7 + parts)
     rows = (rng.standard_normal((B * T, parts * C + 4)) * 3).astype(np.float32)
