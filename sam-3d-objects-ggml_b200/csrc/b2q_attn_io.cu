@@ -135,21 +135,19 @@ __global__ void __launch_bounds__(256) rows_to_heads64_kernel(const float* __res
 
 // One lane per (row, block): 32 contiguous fp16 of one head -> one Q8_0 block
 // (the stand-alone quantizer's arithmetic on their fp32 values).
-// Lane i of a warp takes row 32 * rg + i and block j (the stand-alone
-// quantizer's mapping): the 32 scales of a warp are one 128-byte store.
+// Consecutive lanes take consecutive blocks of one token row: the attention
+// output is token-major in memory, so a warp's loads are contiguous (a
+// row-group mapping, with coalesced scale stores instead, measured slower).
 template <int VARIANT>
 __global__ void __launch_bounds__(256) heads_q8_kernel(const __half* __restrict__ o, int64_t rows, int64_t T,
                                                        int H, int D, int64_t sb, int64_t sh, int64_t st,
                                                        int8_t* __restrict__ codes, float* __restrict__ scales,
                                                        int64_t ld) {
   const int64_t kb = static_cast<int64_t>(H) * D / kQK;
-  const int64_t units = (rows + 31) / 32 * kb;  // (row group, block)
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
-  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32; w < units; w += warps) {
-    const int64_t rg = w / kb, j = w - rg * kb;
-    const int64_t r = rg * 32 + lane;
-    if (r >= rows) continue;
+  const int64_t units = rows * kb;
+  for (int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < units;
+       u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = u / kb, j = u - r * kb;
     const int64_t b = r / T, t = r - b * T;
     const int64_t c0 = j * kQK;
     const int h = static_cast<int>(c0 / D), d0 = static_cast<int>(c0 - static_cast<int64_t>(h) * D);
@@ -220,7 +218,7 @@ cudaError_t launch_heads_q8(const void* o16, int64_t B, int64_t T, int H, int D,
                             int64_t st, int8_t* codes, float* scales, int64_t ld, int variant, cudaStream_t s) {
   const int64_t rows = B * T;
   if (rows == 0) return cudaSuccess;
-  const int grid = grid_for((rows + 31) / 32 * (H * D / kQK) * 32, 256, 8);
+  const int grid = grid_for(rows * H * D / kQK, 256, 8);
   const __half* o = static_cast<const __half*>(o16);
   if (variant == 0)
     heads_q8_kernel<0><<<grid, 256, 0, s>>>(o, rows, T, H, D, sb, sh, st, codes, scales, ld);
