@@ -200,3 +200,30 @@ def test_sampler_step_without_cfg(b2q_mod, dev):
     for m in eager.xp:
         assert torch.equal(graph.xp[m], eager.xp[m])
     assert b2q.device_status() == 0
+
+
+@pytest.mark.gpu
+def test_full_sampling_loop_graph_equals_eager(b2q_mod, dev):
+    """The reference's whole SS sampling loop (25 rescaled Euler steps, CFG on
+    the first half): replaying the two captured graphs gives bit for bit the
+    eager loop's final state, and the state stays finite."""
+    import torch
+    wtype = O.TYPE_Q8_0
+    p = make_params(wtype, seed=3)
+    flow = ss_flow.SsFlow(dev, p, wtype=wtype, **CFG)
+    _, _, cond, _ = inputs(1, seed=8)
+    eager = ss_flow.SsSampler(flow, torch.from_numpy(cond).to(dev), N_COND, seed=11)
+    graph = ss_flow.SsSampler(flow, torch.from_numpy(cond).to(dev), N_COND, seed=11)
+    graph.capture(cfg=True)
+    graph.capture(cfg=False)
+    sched = ss_flow.euler_schedule()
+    assert any(t * 1000.0 <= ss_flow.CFG_END for t, _ in sched) and any(t * 1000.0 > ss_flow.CFG_END for t, _ in sched)
+    for t, dt in sched:
+        eager.step(t * 1000.0, dt)
+        graph.step(t * 1000.0, dt)
+    torch.cuda.synchronize()
+    assert torch.isfinite(eager.xs).all()
+    assert torch.equal(graph.xs, eager.xs)
+    for m in eager.xp:
+        assert torch.equal(graph.xp[m], eager.xp[m])
+    assert b2q.device_status() == 0
