@@ -47,6 +47,69 @@ def test_weight_quantizer_matches_golden(golden, name, wtype):
     assert np.array_equal(O.dequantize(mine, wtype, K), golden[f"w_{name}_dequant"])
 
 
+REF_Q4 = os.path.join(os.path.dirname(__file__), "golden", "ref_q4_0.npz")
+
+
+def test_q4_0_quantizer_matches_reference_fixture(oracle_mod):
+    """Q4_0 bytes equal the reference's own quantizer (cpp_ggml/scripts/
+    gguf_schema.py:27-52, documented there as ggml's quantize_row_q4_0_ref
+    byte for byte), recorded by tests/golden/make_ref_q4_golden.py: edge blocks
+    in full, and the BASELINE fc1 / fc2 weight shapes by SHA-256."""
+    import hashlib
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(__file__), "golden"))
+    try:
+        import make_ref_q4_golden as G
+    finally:
+        sys.path.pop(0)
+    g = np.load(REF_Q4)
+    assert np.array_equal(O.quantize(g["w_small"], O.TYPE_Q4_0), g["q4_small"])
+    for name, n, k, seed in G.BIG:
+        assert [int(v) for v in g[f"{name}_shape"]] == [n, k, seed]
+        wb = O.quantize(G.big_matrix(n, k, seed), O.TYPE_Q4_0)
+        assert np.array_equal(wb[:16], g[f"{name}_head"])
+        assert hashlib.sha256(wb.tobytes()).hexdigest() == str(g[f"{name}_sha256"])
+
+
+def test_q4_0_quantizer_matches_reference_live(oracle_mod):
+    """The same pin run live against the reference checkout when it is present
+    (this container; the GPU box has none), on fresh seeds and odd scales."""
+    import sys
+    root = os.path.join(os.sep, "root", "reference", "cpp_ggml", "scripts")
+    if not os.path.exists(os.path.join(root, "gguf_schema.py")):
+        pytest.skip("reference checkout not present")
+    sys.path.insert(0, os.path.join(os.path.dirname(__file__), "golden"))
+    try:
+        import make_ref_q4_golden as G
+    finally:
+        sys.path.pop(0)
+    ref_q4 = G.load_reference_quantizer(os.path.join(os.sep, "root", "reference"))
+    rng = np.random.default_rng(99)
+    for scale in (1e-5, 0.02, 1.0, 1e4):
+        w = (rng.standard_normal((48, 512)) * scale).astype(np.float32)
+        w[0, :32] = np.round(w[0, :32] * 8) / 8  # many exact ties
+        assert np.array_equal(O.quantize(w, O.TYPE_Q4_0), ref_q4(w).reshape(48, -1))
+
+
+def test_bench_weights_use_the_ggml_reference_quantizers(oracle_mod):
+    """bench.py builds its synthetic GGUF weights in numpy; they must be the
+    bytes of the ggml reference quantizers the oracle restates (and, for Q4_0,
+    the reference's own quantizer pins)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        "bench_mod", os.path.join(os.path.dirname(os.path.dirname(__file__)), "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    rng = np.random.default_rng(5)
+    for scale in (0.02, 1.0):
+        w = (rng.standard_normal((64, 1024)) * scale).astype(np.float32)
+        w[0, :32] = 0.0
+        w[1, :32] = np.arange(32, dtype=np.float32) - 15.5
+        w[2, 32:64] = np.round(w[2, 32:64] * 127) / 127
+        for wtype in (O.TYPE_Q8_0, O.TYPE_Q4_0):
+            assert np.array_equal(bench.synth_blocks(wtype, w, 64, 1024), O.quantize(w, wtype))
+
+
 def test_activation_ref_variant_matches_golden(golden):
     assert np.array_equal(O.quantize(golden["x"], O.TYPE_Q8_0, O.ACT_REF), golden["a_q8_ref"])
 
