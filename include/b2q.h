@@ -157,14 +157,18 @@ B2Q_API int b2q_mul_mat_packed(const void* packed, int64_t n, int64_t k, const f
  * mul_mat takes its quantized-activation scratch from the work buffer that
  * ggml_graph_plan sizes and the caller provides.
  * The activations go to one fixed device array of B2Q_NOALLOC_SCRATCH_BYTES
- * (32 MiB per device, reserved when the library's CUDA module loads), so
- * b2q_act_prepared_size(m, k) must not exceed it (about 29.8 M values: m = 4096
- * rows up to k = 7168); larger sizes return B2Q_ERR_TOO_LARGE.  The first call on
- * each device sets up (looks up the array's address, with that device current);
- * make it before any stream capture begins.  Every call on a device shares the
- * array, which keeps the last call's contents: calls that can overlap on one
- * device (several streams or threads) race, so serialise them.
- * Arguments, alignment and results are those of b2q_mul_mat_packed. */
+ * (32 MiB per device, reserved no later than the first call on each device and
+ * held until the process exits), so b2q_act_prepared_bytes(variant, m, k) must
+ * not exceed it (Q8_0 activations: about 29.8 M values, e.g. m = 4096 rows up to
+ * k = 7168); larger sizes return B2Q_ERR_TOO_LARGE.  The first call on each
+ * device sets up (looks up the array's address, with that device current), and
+ * so does the first call after the device's CUDA context was replaced (after
+ * cudaDeviceReset); make those calls before any stream capture begins.  Every
+ * call on a device shares the array, which keeps the last call's contents:
+ * calls that can overlap on one device (several streams or threads) race, so
+ * serialise them.  Arguments, alignment and results are those of
+ * b2q_mul_mat_packed, with the same checks (an unknown variant is
+ * B2Q_ERR_INVALID_ARG whatever the size). */
 #define B2Q_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
 B2Q_API int b2q_mul_mat_packed_noalloc(const void* packed, int64_t n, int64_t k, const float* x,
                                        int64_t m, int64_t x_row_stride_bytes, const float* bias,

@@ -1,15 +1,19 @@
 // b2q_noalloc.cu -- b2q_mul_mat_packed_noalloc: the packed-weight mul_mat for
 // callers that may not allocate device memory and have no workspace to lend.
-// The Q8_0 activations (the one scratch buffer b2q_mul_mat_packed carves from
-// its caller's workspace) live instead in one file-scope device array of
+// The prepared activations (the one scratch buffer b2q_mul_mat_packed carves
+// from its caller's workspace) live instead in one file-scope device array of
 // B2Q_NOALLOC_SCRATCH_BYTES, and the call then runs exactly the kernels of
 // b2q_mul_mat_packed on it.
 //
 // Set-up: the first call on each device, with that device current, looks up
 // the array's device address with cudaGetSymbolAddress (which also makes the
-// CUDA runtime load this module, reserving the array on that device) and
-// caches it; later calls on that device only read the cache.  Make that first
-// call before any stream capture begins.
+// CUDA runtime load this module, so the array is reserved on that device no
+// later than that call) and caches it together with the CUDA context it
+// belongs to.  Later calls on that device compare the current context with the
+// cached one (one driver query) and reuse the address; if the context has
+// changed -- after cudaDeviceReset, or a release and re-creation of the primary
+// context, which reloads the module at a new address -- they redo the set-up.
+// Make the first call on a device before any stream capture begins.
 //
 // Sharing: every call on a device uses the same array, which keeps the last
 // call's contents.  Calls that can overlap on one device (several streams,
@@ -36,14 +40,39 @@ __device__ __align__(256) static uint8_t g_noalloc_scratch[kScratchBytes];
 
 std::mutex g_setup_mu;
 uint8_t* g_scratch_addr[kMaxDevices] = {};
+CUcontext g_scratch_ctx[kMaxDevices] = {};
 
-// Device address of g_noalloc_scratch on the current device (looked up once).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+// cuCtxGetCurrent through the runtime's driver entry point (the library links
+// the static runtime only); nullptr when the driver does not provide it.
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<CtxGetCurrentFn>(nullptr);
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  return fn;
+}
+
+CUcontext current_ctx() {
+  CUcontext ctx = nullptr;
+  if (CtxGetCurrentFn fn = ctx_get_current_fn()) fn(&ctx);
+  return ctx;
+}
+
+// Device address of g_noalloc_scratch on the current device: looked up once per
+// device and context, then read from the cache.
 int scratch_on_current_device(uint8_t** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return B2Q_ERR_CUDA;
   if (dev < 0 || dev >= kMaxDevices) return B2Q_ERR_UNSUPPORTED;
   std::lock_guard<std::mutex> lock(g_setup_mu);
-  if (!g_scratch_addr[dev]) {
+  const CUcontext ctx = current_ctx();
+  if (!g_scratch_addr[dev] || !ctx || ctx != g_scratch_ctx[dev]) {
     int major = 0, minor = 0;
     if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
@@ -53,6 +82,7 @@ int scratch_on_current_device(uint8_t** out) {
     if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return B2Q_ERR_CUDA;
     if (reinterpret_cast<uintptr_t>(p) % 256 != 0) return B2Q_ERR_MISALIGNED;
     g_scratch_addr[dev] = static_cast<uint8_t*>(p);
+    g_scratch_ctx[dev] = current_ctx();  // the runtime call above made the context current
   }
   *out = g_scratch_addr[dev];
   return B2Q_OK;
@@ -65,8 +95,10 @@ extern "C" int b2q_mul_mat_packed_noalloc(const void* packed, int64_t n, int64_t
                                           float* y, int64_t y_row_stride_bytes, int variant,
                                           void* stream) {
   if (n < 0 || m < 0 || k <= 0 || k % kQK != 0) return B2Q_ERR_INVALID_ARG;
-  if (n > INT_MAX || m > INT_MAX || k > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (variant != B2Q_ACT_X86 && variant != B2Q_ACT_REF && variant != B2Q_ACT_Q8_K) return B2Q_ERR_INVALID_ARG;
   if (variant == B2Q_ACT_Q8_K && k % kQKK != 0) return B2Q_ERR_INVALID_ARG;
+  if (n > INT_MAX || m > INT_MAX || k > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  // The same bound as b2q_act_prepared_bytes(variant, m, k).
   if ((variant == B2Q_ACT_Q8_K ? q8k_bytes(m, k) : split_bytes(m, k)) > kScratchBytes) return B2Q_ERR_TOO_LARGE;
   uint8_t* scratch = nullptr;
   if (m > 0 && n > 0) {
