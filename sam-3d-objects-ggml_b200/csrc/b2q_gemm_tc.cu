@@ -25,14 +25,16 @@
 // (its TMEM lane) and 64 of the 128 token columns, read with two
 // tcgen05.ld.32x32b.x32 (the widest-bandwidth load shape).  Its weight scale is
 // one scalar per block; the 64 activation scales are warp-uniform broadcast
-// loads.  The next block's 64 values are loaded into a second register buffer
-// while the current block is scaled (tcgen05.wait::ld covers all of a thread's
-// loads, so the double buffer is what keeps 64 KB of TMEM reads in flight per
-// SM).  The four slots are handed between MMA and epilogue in pairs of
-// consecutive blocks: one commit, one wait and one release per two blocks.
-// Every hand-off makes all eight epilogue warps meet, and each meeting costs
-// more than the latency of the barrier itself, so halving them pays; the loop
-// is specialised per half of a pair so the hot path carries no hand-off tests.
+// loads.  Hand-off per block and per slot: the MMA thread commits each block to
+// its slot's barrier; an epilogue warp waits for the block, loads it, scales it
+// into its accumulators and only then hands the slot back (one arrival per
+// warp).  What bounds this loop, measured on B200: a block's MMA result becomes
+// visible to a waiting thread ~1300 cycles after issue with 4 slots in flight
+// (a ping-pong with no epilogue work at all runs at ~330-400 cycles per block),
+// and TMEM holds only 4 blocks of int32 accumulators, so the chain, not the
+// FMA work (256 cycles per block), sets the pace.  Register double buffering
+// (loading block g+1 while scaling g) and releasing a slot before scaling both
+// measured slower than this single-buffered, release-after-scaling order.
 // K is padded to whole stages (the padding blocks read zero codes and scales
 // through the tensor maps' out-of-bounds fill and add exactly nothing).
 // Output stores: for each token, the 32 threads of a warp write 32 consecutive
@@ -80,8 +82,6 @@ constexpr int kRegsEpilogue = 232;
 static_assert(128 * kRegsControl + 256 * kRegsEpilogue <= kThreads * kLaunchRegs, "register split");
 constexpr uint32_t kTmemCols = 512;
 constexpr int kSlots = static_cast<int>(kTmemCols) / kSlotCols;  // accumulator slots (blocks in flight)
-constexpr int kPairs = kSlots / 2;  // slots are handed over in pairs of consecutive blocks
-static_assert(kKBS % 2 == 0, "a stage holds whole slot pairs");
 constexpr uint32_t kOffset = 1u << 20;        // added to every S by the constant MMA
 constexpr int kOffsetTileBytes = 4096;        // 128 rows x 32 bytes, every 16-byte chunk = P
 constexpr float kNegTwoPowM129 = -0x1p-129f;  // subnormal, exact
@@ -100,7 +100,7 @@ struct Cfg {
   static constexpr int STAGE_BYTES = (TX_BYTES + 1023) / 1024 * 1024;          // stage pitch in smem
   static constexpr int OFF_TILE = STAGES * STAGE_BYTES;
   static constexpr int BAR_OFF = OFF_TILE + kOffsetTileBytes;
-  static constexpr int NBARS = 2 * STAGES + 2 * kPairs + 1;
+  static constexpr int NBARS = 2 * STAGES + 2 * kSlots + 1;  // stage and slot barrier pairs, MMA drain
   static constexpr int SMEM = BAR_OFF + NBARS * 8 + 16 + 1024;  // + alignment slack
   // GELU + Q8_0 variant only: a 32 x 33 fp32 transpose buffer per epilogue warp.
   static constexpr int XPOSE_OFF = (BAR_OFF + NBARS * 8 + 16 + 127) / 128 * 128;
@@ -185,47 +185,26 @@ __device__ __forceinline__ void load_slot(uint32_t taddr, uint32_t (&r)[COLS]) {
   if (c + 8 <= COLS) tmem_ld_32x32b_x8(taddr + c, &r[c]);
 }
 
-// Where the epilogue of one CTA stands in its flat sequence of blocks.
-struct EpiState {
-  int g;  // block counter over all of this CTA's tiles (slot g % kSlots, pair g / 2)
-  uint32_t stage, phase;
-};
-
-// One block of the epilogue: scale and accumulate block g (already in `cur`)
-// while block g + 1 streams into `nxt`.  Blocks come in slot pairs, so the two
-// steps of a pair are specialised: the FIRST step (g even) loads the second
-// block of its own pair and then hands the pair back; the SECOND step (g odd)
-// waits for the next pair before loading its first block.  kb: block within
-// the tile (stage boundaries fall on even blocks).  Returns false when a
-// bounded wait gave up.
-template <int STAGES, int BN, bool DUMP, bool FIRST, int COLS = BN / 2>
-__device__ __forceinline__ bool epi_step(uint32_t (&cur)[COLS], uint32_t (&nxt)[COLS], float2 (&acc)[COLS / 2],
-                                         EpiState& st, int kb, int tile, const TcParams& p, int total,
-                                         uint8_t* smem, uint64_t* full, uint64_t* empty, uint64_t* acc_full,
-                                         uint64_t* acc_empty, volatile int* abort_flag, uint32_t tbase,
-                                         int row, int chalf, int lane) {
+// One block of the epilogue: wait for block g in accumulator slot `slot`,
+// load this thread's COLS columns, scale them into acc, then hand the slot
+// back.  j: block within the stage (selects the stage's scales).  Returns
+// false when a bounded wait gave up.
+template <int STAGES, int BN, bool DUMP, int COLS = BN / 2>
+__device__ __forceinline__ bool epi_block(uint32_t (&cur)[COLS], float2 (&acc)[COLS / 2], int slot, uint32_t sphase,
+                                          int j, int kb, int tile, const TcParams& p, const uint8_t* sb,
+                                          uint64_t* acc_full, uint64_t* acc_empty, volatile int* abort_flag,
+                                          uint32_t tbase, int row, int chalf, int lane) {
   using C = Cfg<STAGES, BN>;
-  const int j = kb & (kKBS - 1);
-  if (FIRST && j == 0 &&
-      !mbar_wait(&full[st.stage], st.phase, &g_device_status, kDevWaitEpilogue, abort_flag))
-    return false;
-  const uint32_t nb = static_cast<uint32_t>(st.g + 1);
-  const uint32_t npair = (nb >> 1) & (kPairs - 1);
-  const bool more = FIRST || st.g + 1 < total;  // a pair is never split
-  if (more) {
-    if (!FIRST &&
-        !mbar_wait(&acc_full[npair], (nb / kSlots) & 1u, &g_device_status, kDevWaitEpilogue, abort_flag))
-      return false;
-    tc_fence_after();
-    load_slot<COLS>(tbase + (nb & (kSlots - 1)) * kSlotCols, nxt);
-  }
-  const uint8_t* sb = smem + st.stage * C::STAGE_BYTES;
+  if (!mbar_wait(&acc_full[slot], sphase, &g_device_status, kDevWaitEpilogue, abort_flag)) return false;
+  tc_fence_after();
+  load_slot<COLS>(tbase + slot * kSlotCols, cur);
   const float* sw = reinterpret_cast<const float*>(sb + C::A_BYTES + C::B_BYTES);
   const float* sa = sw + kKBS * kBM;
   const float w = sw[j * kBM + row];
   const float2 w2 = make_float2(w, w);
   const float2 c2 = make_float2(w * kNegTwoPowM129, w * kNegTwoPowM129);
   const float4* da4 = reinterpret_cast<const float4*>(sa + j * BN + chalf * COLS);
+  tmem_wait_ld();
   if (DUMP && kb < p.KB_real) {
     const int64_t n = static_cast<int64_t>(tile % p.n_tiles) * kBM + row;
     const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * BN + chalf * COLS;
@@ -242,22 +221,9 @@ __device__ __forceinline__ bool epi_step(uint32_t (&cur)[COLS], uint32_t (&nxt)[
     acc[2 * i] = ffma2(t0, make_float2(d.x, d.y), acc[2 * i]);
     acc[2 * i + 1] = ffma2(t1, make_float2(d.z, d.w), acc[2 * i + 1]);
   }
-  if (more) {
-    tmem_wait_ld();
-    if (FIRST) {  // both blocks of the pair are in registers: hand the pair back
-      tc_fence_before();
-      mbar_arrive(&acc_empty[npair]);
-    }
-  }
-  if (!FIRST && j == kKBS - 1) {
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st.stage]);
-    if (++st.stage == STAGES) {
-      st.stage = 0;
-      st.phase ^= 1u;
-    }
-  }
-  ++st.g;
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&acc_empty[slot]);
   return true;
 }
 
@@ -324,8 +290,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
-  uint64_t* acc_empty = acc_full + kPairs;
-  uint64_t* mma_done = acc_empty + kPairs;
+  uint64_t* acc_empty = acc_full + kSlots;
+  uint64_t* mma_done = acc_empty + kSlots;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -337,9 +303,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kEpiWarps);
     }
-    for (int a = 0; a < kPairs; ++a) {
+    for (int a = 0; a < kSlots; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], kEpiWarps * 32);  // every epilogue thread arrives
+      mbar_init(&acc_empty[a], kEpiWarps);  // one arrival per epilogue warp
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -412,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr uint32_t idesc = idesc_i8(kBM, BN);
         constexpr uint32_t idesc_off = idesc_u8(kBM, BN);
         const uint64_t off_desc = smem_desc_k_noswz(smem_u32(smem + C::OFF_TILE));
-        uint32_t stage = 0, phase = 0, q = 0;  // q: pair counter; pair q fills slots 2(q % kPairs) + {0, 1}
+        uint32_t stage = 0, phase = 0, q = 0;  // q: block counter; block q fills slot q % kSlots
         bool ok = true;
         for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
           for (int ks = 0; ok && ks < n_ks; ++ks) {
@@ -423,20 +389,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const uint32_t a_base = smem_u32(smem + stage * C::STAGE_BYTES);
             const uint32_t b_base = a_base + C::A_BYTES;
-            for (int j2 = 0; j2 < kKBS; j2 += 2, ++q) {
-              const uint32_t pair = q & (kPairs - 1);
-              if (!mbar_wait(&acc_empty[pair], ((q / kPairs) & 1u) ^ 1u, &g_device_status, kDevWaitMma, abort_flag)) {
+            for (int j = 0; j < kKBS; ++j, ++q) {
+              const uint32_t slot = q & (kSlots - 1);
+              if (!mbar_wait(&acc_empty[slot], ((q / kSlots) & 1u) ^ 1u, &g_device_status, kDevWaitMma, abort_flag)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
-#pragma unroll
-              for (int j = j2; j < j2 + 2; ++j) {
-                const uint32_t d = tmem_base + (2 * pair + (j - j2)) * kSlotCols;
-                mma_i8(d, smem_desc_k_sw128(a_base + j * kQK), smem_desc_k_sw128(b_base + j * kQK), idesc, 0u);
-                mma_i8(d, off_desc, off_desc, idesc_off, 1u);
-              }
-              mma_commit(&acc_full[pair]);
+              const uint32_t d = tmem_base + slot * kSlotCols;
+              mma_i8(d, smem_desc_k_sw128(a_base + j * kQK), smem_desc_k_sw128(b_base + j * kQK), idesc, 0u);
+              mma_i8(d, off_desc, off_desc, idesc_off, 1u);
+              mma_commit(&acc_full[slot]);
             }
             if (++stage == STAGES) {
               stage = 0;
@@ -456,29 +419,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int chalf = (warp - kEpiWarp0) >> 2;  // which 64 of the 128 token columns
     const int row = quarter * 32 + lane;        // this thread's weight row (TMEM lane)
     const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + chalf * COLS;
-    const int my_tiles = (p.num_tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                         static_cast<int>(gridDim.x);
-    const int total = my_tiles * KB;
-    EpiState st{0, 0u, 0u};
-    uint32_t ra[COLS], rb[COLS];
+    uint32_t ra[COLS];
     float2 acc[COLS / 2];
-    bool ok = total > 0 && mbar_wait(&acc_full[0], 0, &g_device_status, kDevWaitEpilogue, abort_flag);
-    if (ok) {
-      // Block 0 of this CTA goes into buffer A before the pipelined loop.
-      tc_fence_after();
-      load_slot(tbase, ra);
-      tmem_wait_ld();
-    }
+    uint32_t stage = 0, phase = 0, q = 0;  // q: block counter, as the MMA issuer's
+    bool ok = true;
     for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
 #pragma unroll
       for (int c = 0; c < COLS / 2; ++c) acc[c] = make_float2(0.0f, 0.0f);
-      for (int kb = 0; kb < KB; kb += 2) {  // KB is a whole number of stages, so even
-        if (!epi_step<STAGES, BN, DUMP, true>(ra, rb, acc, st, kb, tile, p, total, smem, full, empty, acc_full,
-                                          acc_empty, abort_flag, tbase, row, chalf, lane) ||
-            !epi_step<STAGES, BN, DUMP, false>(rb, ra, acc, st, kb + 1, tile, p, total, smem, full, empty, acc_full,
-                                           acc_empty, abort_flag, tbase, row, chalf, lane)) {
+      for (int ks = 0; ks < n_ks; ++ks) {
+        // The stage's scales are read from shared memory: wait for its copies.
+        if (!mbar_wait(&full[stage], phase, &g_device_status, kDevWaitEpilogue, abort_flag)) {
           ok = false;
           break;
+        }
+        const uint8_t* sb = smem + stage * C::STAGE_BYTES;
+#pragma unroll
+        for (int j = 0; j < kKBS; ++j, ++q) {
+          if (!epi_block<STAGES, BN, DUMP>(ra, acc, static_cast<int>(q & (kSlots - 1)), (q / kSlots) & 1u, j,
+                                           ks * kKBS + j, tile, p, sb, acc_full, acc_empty, abort_flag, tbase, row,
+                                           chalf, lane)) {
+            ok = false;
+            break;
+          }
+        }
+        if (!ok) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
         }
       }
       if (!ok || (!GELUQ && !p.y)) continue;
