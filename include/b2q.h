@@ -291,6 +291,32 @@ B2Q_API int b2q_heads_act_prepare(const void* o16, int64_t B, int64_t T, int64_t
                                   int64_t stride_h, int64_t stride_t, int variant, void* act, size_t act_bytes,
                                   void* stream);
 
+/* ------------------------------------------------ attention, F32 contract
+ * The numeric-gate form of gb_attention (cpp_ggml/src/graph_builder.cpp:
+ * 139-175 with AttentionOptions.strict_kv: ggml_flash_attn_ext on F32 Q, K and
+ * V with GGML_PREC_F32), the form the reference keeps for parity diagnosis:
+ *   o[b*Tq + t][h*D + d] = sum_j p_j v[b][h][j][d] / sum_j p_j,
+ *   p_j = exp(s_j - max_j s_j),  s_j = scale * (q[b][h][t] . key_j)
+ * as a per-query online softmax with every product, sum and exp in IEEE fp32.
+ * q fp32 [B][H][Tq][D]; k, v fp32 [B][H][Tk][D]; an optional second key source
+ * k2, v2 fp32 [B][H][Tk2][D] supplies keys Tk .. Tk + Tk2 - 1 (the pose group
+ * attends its own keys followed by the shape group's,
+ * cpp_ggml/src/ss_flow_graph.cpp:262-275); both NULL for none.  o is written as
+ * fp32 rows [B*Tq] of o_row_stride_bytes, head h at columns h*D .. h*D+D-1: the
+ * [D, H, Tq, B] tensor the output projection reads (graph_builder.cpp:
+ * 146-149).  D in {32, 64, 128}; q, k, v, k2, v2 16-byte aligned.
+ * b2q_qkv_heads_f32 / b2q_rows_to_heads_f32 are b2q_qkv_heads /
+ * b2q_rows_to_heads with fp32 outputs (no fp16 rounding), the inputs of this
+ * form; outputs 16-byte aligned. */
+B2Q_API int b2q_qkv_heads_f32(const float* qkv, int64_t B, int64_t T, int64_t H, int64_t D,
+                              int64_t qkv_row_stride_bytes, const float* gamma_q, const float* gamma_k, float eps,
+                              float* q, float* k, float* v, void* stream);
+B2Q_API int b2q_rows_to_heads_f32(const float* src, int64_t B, int64_t T, int64_t H, int64_t D, int parts,
+                                  int64_t src_row_stride_bytes, float* out0, float* out1, void* stream);
+B2Q_API int b2q_attention_f32(const float* q, const float* k, const float* v, int64_t B, int64_t H, int64_t Tq,
+                              int64_t Tk, int64_t D, const float* k2, const float* v2, int64_t Tk2, float scale,
+                              float* o, int64_t o_row_stride_bytes, void* stream);
+
 /* ------------------------------------------- column-parallel form (multi-GPU)
  * One rank of a tensor-parallel group for a single large mul_mat (the SLat
  * flow transformer's linears at 8k-20k tokens): the weight is split by output

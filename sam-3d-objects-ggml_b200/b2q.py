@@ -77,6 +77,9 @@ def _lib_obj():
             "b2q_qkv_heads": (I, [P, I64, I64, I64, I64, I64, P, P, ctypes.c_float, P, P, P, P]),
             "b2q_heads_act_prepare": (I, [P, I64, I64, I64, I64, I64, I64, I64, I, P, SZ, P]),
             "b2q_rows_to_heads": (I, [P, I64, I64, I64, I64, I, I64, P, P, P]),
+            "b2q_qkv_heads_f32": (I, [P, I64, I64, I64, I64, I64, P, P, ctypes.c_float, P, P, P, P]),
+            "b2q_rows_to_heads_f32": (I, [P, I64, I64, I64, I64, I, I64, P, P, P]),
+            "b2q_attention_f32": (I, [P, P, P, I64, I64, I64, I64, I64, P, P, I64, ctypes.c_float, P, I64, P]),
             "b2q_layer_norm_q8": (I, [P, I64, I64, I64, ctypes.c_float, P, P, I, P, SZ, P]),
             "b2q_mul_mat_prepared_gate_residual": (I, [P, I64, I64, P, I64, P, P, P, I64, P, I64, P]),
             "b2q_norm_modulate": (I, [P, I64, I64, I64, ctypes.c_float, P, P, P, I64, P]),
@@ -366,6 +369,47 @@ def rows_to_heads(src, B: int, T: int, H: int, D: int, parts: int = 1, stream=No
                                  _ptr(outs[1]) if parts == 2 else None, _stream(stream))
     _check("b2q_rows_to_heads", rc)
     return outs
+
+
+def qkv_heads_f32(qkv, B: int, T: int, H: int, D: int, gamma_q=None, gamma_k=None, eps: float = 1e-6,
+                  stream=None):
+    """qkv_heads with fp32 outputs [B, H, T, D] (the F32 attention contract)."""
+    torch = _torch()
+    q, k, v = (torch.empty((B, H, T, D), dtype=torch.float32, device=qkv.device) for _ in range(3))
+    rc = lib().b2q_qkv_heads_f32(_ptr(qkv), B, T, H, D, qkv.stride(0) * 4, _ptr(gamma_q), _ptr(gamma_k), eps,
+                                 _ptr(q), _ptr(k), _ptr(v), _stream(stream))
+    _check("b2q_qkv_heads_f32", rc)
+    return q, k, v
+
+
+def rows_to_heads_f32(src, B: int, T: int, H: int, D: int, parts: int = 1, stream=None):
+    """rows_to_heads with fp32 outputs [B, H, T, D]."""
+    torch = _torch()
+    outs = [torch.empty((B, H, T, D), dtype=torch.float32, device=src.device) for _ in range(parts)]
+    rc = lib().b2q_rows_to_heads_f32(_ptr(src), B, T, H, D, parts, src.stride(0) * 4, _ptr(outs[0]),
+                                     _ptr(outs[1]) if parts == 2 else None, _stream(stream))
+    _check("b2q_rows_to_heads_f32", rc)
+    return outs
+
+
+def attention_f32(q, k, v, k2=None, v2=None, scale: float | None = None, out=None, stream=None):
+    """F32-contract attention: q [B, H, Tq, D], k, v [B, H, Tk, D] fp32 (plus an
+    optional second key source k2, v2 [B, H, Tk2, D]) -> fp32 rows [B*Tq, H*D]."""
+    import math
+    torch = _torch()
+    B, H, Tq, D = q.shape
+    Tk = k.shape[2]
+    Tk2 = k2.shape[2] if k2 is not None else 0
+    for t in (q, k, v, k2, v2):
+        assert t is None or (t.dtype == torch.float32 and t.is_contiguous())
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty((B * Tq, H * D), dtype=torch.float32, device=q.device)
+    rc = lib().b2q_attention_f32(_ptr(q), _ptr(k), _ptr(v), B, H, Tq, Tk, D, _ptr(k2), _ptr(v2), Tk2, scale,
+                                 _ptr(out), out.stride(0) * 4, _stream(stream))
+    _check("b2q_attention_f32", rc)
+    return out
 
 
 def layer_norm_q8(x, eps: float = 1e-6, weight=None, bias=None, variant: int = ACT_X86, out=None, stream=None):

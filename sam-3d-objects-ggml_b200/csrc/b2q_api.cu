@@ -7,6 +7,7 @@
 
 #include <atomic>
 #include <climits>
+#include <cmath>
 #include <cstdint>
 
 namespace {
@@ -711,6 +712,58 @@ int b2q_rows_to_heads(const float* src, int64_t B, int64_t T, int64_t H, int64_t
   if (int rc = check_device(nullptr)) return rc;
   return from_cuda(launch_rows_to_heads(src, B, T, static_cast<int>(H), static_cast<int>(D), src_row_stride_bytes / 4,
                                         parts, 0u, nullptr, nullptr, 0.0f, out0, out1, nullptr,
+                                        static_cast<cudaStream_t>(stream)));
+}
+
+int b2q_qkv_heads_f32(const float* qkv, int64_t B, int64_t T, int64_t H, int64_t D, int64_t qkv_row_stride_bytes,
+                      const float* gamma_q, const float* gamma_k, float eps, float* q, float* k, float* v,
+                      void* stream) {
+  if (B < 0 || T < 0 || H <= 0 || (D != 32 && D != 64 && D != 128) || !(eps >= 0.0f)) return B2Q_ERR_INVALID_ARG;
+  if (B * T > INT_MAX || H > 4096) return B2Q_ERR_TOO_LARGE;
+  if (B * T > 0 && (!qkv || !q || !k || !v)) return B2Q_ERR_INVALID_ARG;
+  if (qkv_row_stride_bytes < 3 * H * D * 4) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(qkv, 4) || qkv_row_stride_bytes % 4 != 0 || !aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) ||
+      (gamma_q && !aligned(gamma_q, 4)) || (gamma_k && !aligned(gamma_k, 4)))
+    return B2Q_ERR_MISALIGNED;
+  if (B * T == 0) return B2Q_OK;
+  if (int rc = check_device(nullptr)) return rc;
+  return from_cuda(launch_rows_to_heads(qkv, B, T, static_cast<int>(H), static_cast<int>(D), qkv_row_stride_bytes / 4,
+                                        3, 3u, gamma_q, gamma_k, eps, q, k, v, static_cast<cudaStream_t>(stream), true));
+}
+
+int b2q_rows_to_heads_f32(const float* src, int64_t B, int64_t T, int64_t H, int64_t D, int parts,
+                          int64_t src_row_stride_bytes, float* out0, float* out1, void* stream) {
+  if (B < 0 || T < 0 || H <= 0 || (D != 32 && D != 64 && D != 128) || parts < 1 || parts > 2)
+    return B2Q_ERR_INVALID_ARG;
+  if (B * T > INT_MAX || H > 4096) return B2Q_ERR_TOO_LARGE;
+  if (B * T > 0 && (!src || !out0 || (parts == 2 && !out1))) return B2Q_ERR_INVALID_ARG;
+  if (src_row_stride_bytes < parts * H * D * 4) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(src, 4) || src_row_stride_bytes % 4 != 0 || !aligned(out0, 16) || (out1 && !aligned(out1, 16)))
+    return B2Q_ERR_MISALIGNED;
+  if (B * T == 0) return B2Q_OK;
+  if (int rc = check_device(nullptr)) return rc;
+  return from_cuda(launch_rows_to_heads(src, B, T, static_cast<int>(H), static_cast<int>(D), src_row_stride_bytes / 4,
+                                        parts, 0u, nullptr, nullptr, 0.0f, out0, out1, nullptr,
+                                        static_cast<cudaStream_t>(stream), true));
+}
+
+int b2q_attention_f32(const float* q, const float* k, const float* v, int64_t B, int64_t H, int64_t Tq, int64_t Tk,
+                      int64_t D, const float* k2, const float* v2, int64_t Tk2, float scale, float* o,
+                      int64_t o_row_stride_bytes, void* stream) {
+  if (B < 0 || Tq < 0 || Tk < 0 || H <= 0 || (D != 32 && D != 64 && D != 128) || !std::isfinite(scale))
+    return B2Q_ERR_INVALID_ARG;
+  if ((k2 == nullptr) != (v2 == nullptr) || (k2 && Tk2 < 0)) return B2Q_ERR_INVALID_ARG;
+  const int64_t tk_all = Tk + (k2 ? Tk2 : 0);
+  if (B * Tq > 0 && (!q || !o || tk_all <= 0 || (Tk > 0 && (!k || !v)))) return B2Q_ERR_INVALID_ARG;
+  if (o_row_stride_bytes < H * D * 4 || o_row_stride_bytes % 4 != 0) return B2Q_ERR_INVALID_ARG;
+  if (B > 65535 || H > 65535 || (Tq + 63) / 64 > INT_MAX || B * H * (tk_all > Tq ? tk_all : Tq) * D > (int64_t{1} << 40))
+    return B2Q_ERR_TOO_LARGE;
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(k2, 16) || !aligned(v2, 16) || !aligned(o, 4))
+    return B2Q_ERR_MISALIGNED;
+  if (B * Tq == 0) return B2Q_OK;
+  if (int rc = check_device(nullptr)) return rc;
+  return from_cuda(launch_attention_f32(q, k, v, k2, v2, B, static_cast<int>(H), Tq, Tk, k2 ? Tk2 : 0,
+                                        static_cast<int>(D), scale, o, o_row_stride_bytes / 4,
                                         static_cast<cudaStream_t>(stream)));
 }
 

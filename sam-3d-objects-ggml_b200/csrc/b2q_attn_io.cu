@@ -37,13 +37,16 @@ __device__ __forceinline__ double warp_sum_d(double v) {
 // holds `parts` C-wide tensors (q, k, v of a fused projection, or fewer);
 // part p goes to out[p] as fp16 [B][H][T][D], RMS-normed first when bit p of
 // norm_mask is set (times gamma[p] when that is not null).
-template <int DPL>  // values per lane = D / 32
+__device__ __forceinline__ void store_out(__half* p, float v) { *p = __float2half_rn(v); }
+__device__ __forceinline__ void store_out(float* p, float v) { *p = v; }
+
+template <int DPL, typename OutT>  // values per lane = D / 32; OutT: __half (rounded) or float
 __global__ void __launch_bounds__(256) rows_to_heads_kernel(const float* __restrict__ qkv, int64_t rows, int64_t T,
                                                             int H, int64_t ldq, int parts, unsigned norm_mask,
                                                             const float* __restrict__ gq,
                                                             const float* __restrict__ gk, float eps,
-                                                            __half* __restrict__ q16, __half* __restrict__ k16,
-                                                            __half* __restrict__ v16) {
+                                                            OutT* __restrict__ q16, OutT* __restrict__ k16,
+                                                            OutT* __restrict__ v16) {
   const int lane = threadIdx.x & 31;
   constexpr int D = DPL * 32;
   const int64_t C = static_cast<int64_t>(H) * D;
@@ -59,7 +62,7 @@ __global__ void __launch_bounds__(256) rows_to_heads_kernel(const float* __restr
       float x[DPL];
 #pragma unroll
       for (int i = 0; i < DPL; ++i) x[i] = __ldg(src + part * C + lane + 32 * i);
-      __half* out = part == 0 ? q16 : part == 1 ? k16 : v16;
+      OutT* out = part == 0 ? q16 : part == 1 ? k16 : v16;
       if ((norm_mask >> part) & 1u) {
         double s = 0.0;
 #pragma unroll
@@ -77,7 +80,7 @@ __global__ void __launch_bounds__(256) rows_to_heads_kernel(const float* __restr
         }
       }
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) out[dst + lane + 32 * i] = __float2half_rn(x[i]);
+      for (int i = 0; i < DPL; ++i) store_out(out + dst + lane + 32 * i, x[i]);
     }
   }
 }
@@ -87,12 +90,13 @@ __global__ void __launch_bounds__(256) rows_to_heads_kernel(const float* __restr
 // and 8-byte fp16 stores (each head's 128-byte output row contiguous).  The
 // double sum of squares is exact for ordinary data, so the 16-lane tree gives
 // the same value as the 32-lane layout above.  Index math in 32 bits.
+template <typename OutT>
 __global__ void __launch_bounds__(256) rows_to_heads64_kernel(const float* __restrict__ qkv, uint32_t rows, uint32_t T,
                                                               uint32_t H, int64_t ldq, int parts, unsigned norm_mask,
                                                               const float* __restrict__ gq,
                                                               const float* __restrict__ gk, float eps,
-                                                              __half* __restrict__ q16, __half* __restrict__ k16,
-                                                              __half* __restrict__ v16) {
+                                                              OutT* __restrict__ q16, OutT* __restrict__ k16,
+                                                              OutT* __restrict__ v16) {
   constexpr int D = 64;
   const int lane = threadIdx.x & 31;
   const int sub = lane >> 4, l16 = lane & 15;
@@ -108,7 +112,7 @@ __global__ void __launch_bounds__(256) rows_to_heads64_kernel(const float* __res
     const float* src = qkv + static_cast<int64_t>(r) * ldq + static_cast<int64_t>(h) * D + 4 * l16;
     for (int part = 0; part < parts; ++part) {  // q, k, v
       float4 x = __ldg(reinterpret_cast<const float4*>(src + part * C));
-      __half* out = part == 0 ? q16 : part == 1 ? k16 : v16;
+      OutT* out = part == 0 ? q16 : part == 1 ? k16 : v16;
       if ((norm_mask >> part) & 1u) {
         double s = static_cast<double>(__fmul_rn(x.x, x.x)) + static_cast<double>(__fmul_rn(x.y, x.y)) +
                    static_cast<double>(__fmul_rn(x.z, x.z)) + static_cast<double>(__fmul_rn(x.w, x.w));
@@ -124,11 +128,15 @@ __global__ void __launch_bounds__(256) rows_to_heads64_kernel(const float* __res
           x.x = __fmul_rn(x.x, g.x), x.y = __fmul_rn(x.y, g.y), x.z = __fmul_rn(x.z, g.z), x.w = __fmul_rn(x.w, g.w);
         }
       }
-      __half2 lo = __floats2half2_rn(x.x, x.y), hi = __floats2half2_rn(x.z, x.w);
-      uint2 pk;
-      pk.x = *reinterpret_cast<uint32_t*>(&lo);
-      pk.y = *reinterpret_cast<uint32_t*>(&hi);
-      *reinterpret_cast<uint2*>(out + dst) = pk;
+      if constexpr (sizeof(OutT) == 4) {
+        *reinterpret_cast<float4*>(out + dst) = x;
+      } else {
+        __half2 lo = __floats2half2_rn(x.x, x.y), hi = __floats2half2_rn(x.z, x.w);
+        uint2 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&lo);
+        pk.y = *reinterpret_cast<uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(out + dst) = pk;
+      }
     }
   }
 }
@@ -181,37 +189,47 @@ int grid_for(int64_t work_items, int per_block, int cap_per_sm) {
   return static_cast<int>(blocks < cap ? blocks : cap);
 }
 
-}  // namespace
-
-cudaError_t launch_rows_to_heads(const float* src, int64_t B, int64_t T, int H, int D, int64_t ld_floats, int parts,
-                                 unsigned norm_mask, const float* g0, const float* g1, float eps, void* o0, void* o1,
-                                 void* o2, cudaStream_t s) {
+template <typename OutT>
+cudaError_t rows_to_heads_t(const float* src, int64_t B, int64_t T, int H, int D, int64_t ld_floats, int parts,
+                            unsigned norm_mask, const float* g0, const float* g1, float eps, void* o0, void* o1,
+                            void* o2, cudaStream_t s) {
   const int64_t rows = B * T;
   if (rows == 0) return cudaSuccess;
   if (parts < 1 || parts > 3 || (norm_mask >> 2) != 0) return cudaErrorInvalidValue;  // v is never normed
   const int grid = grid_for(rows * H, 8, 16);
-  __half *a = static_cast<__half*>(o0), *b = static_cast<__half*>(o1), *c = static_cast<__half*>(o2);
+  OutT *a = static_cast<OutT*>(o0), *b = static_cast<OutT*>(o1), *c = static_cast<OutT*>(o2);
   switch (D) {
     case 32:
-      rows_to_heads_kernel<1><<<grid, 256, 0, s>>>(src, rows, T, H, ld_floats, parts, norm_mask, g0, g1, eps, a, b, c);
+      rows_to_heads_kernel<1, OutT><<<grid, 256, 0, s>>>(src, rows, T, H, ld_floats, parts, norm_mask, g0, g1, eps, a,
+                                                         b, c);
       break;
     case 64:
       if (H % 2 == 0 && ld_floats % 4 == 0 && reinterpret_cast<uintptr_t>(src) % 16 == 0 &&
           (!g0 || reinterpret_cast<uintptr_t>(g0) % 16 == 0) && (!g1 || reinterpret_cast<uintptr_t>(g1) % 16 == 0) &&
           rows * H <= 0xffffffffLL)
-        rows_to_heads64_kernel<<<grid_for(rows * H / 2, 8, 16), 256, 0, s>>>(
+        rows_to_heads64_kernel<OutT><<<grid_for(rows * H / 2, 8, 16), 256, 0, s>>>(
             src, static_cast<uint32_t>(rows), static_cast<uint32_t>(T), static_cast<uint32_t>(H), ld_floats, parts,
             norm_mask, g0, g1, eps, a, b, c);
       else
-        rows_to_heads_kernel<2><<<grid, 256, 0, s>>>(src, rows, T, H, ld_floats, parts, norm_mask, g0, g1, eps, a, b,
-                                                     c);
+        rows_to_heads_kernel<2, OutT><<<grid, 256, 0, s>>>(src, rows, T, H, ld_floats, parts, norm_mask, g0, g1, eps,
+                                                           a, b, c);
       break;
     case 128:
-      rows_to_heads_kernel<4><<<grid, 256, 0, s>>>(src, rows, T, H, ld_floats, parts, norm_mask, g0, g1, eps, a, b, c);
+      rows_to_heads_kernel<4, OutT><<<grid, 256, 0, s>>>(src, rows, T, H, ld_floats, parts, norm_mask, g0, g1, eps, a,
+                                                         b, c);
       break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_rows_to_heads(const float* src, int64_t B, int64_t T, int H, int D, int64_t ld_floats, int parts,
+                                 unsigned norm_mask, const float* g0, const float* g1, float eps, void* o0, void* o1,
+                                 void* o2, cudaStream_t s, bool f32_out) {
+  return f32_out ? rows_to_heads_t<float>(src, B, T, H, D, ld_floats, parts, norm_mask, g0, g1, eps, o0, o1, o2, s)
+                 : rows_to_heads_t<__half>(src, B, T, H, D, ld_floats, parts, norm_mask, g0, g1, eps, o0, o1, o2, s);
 }
 
 cudaError_t launch_heads_q8(const void* o16, int64_t B, int64_t T, int H, int D, int64_t sb, int64_t sh,

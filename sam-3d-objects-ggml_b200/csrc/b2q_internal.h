@@ -112,9 +112,15 @@ cudaError_t launch_norm_modulate(const float* x, int64_t m, int64_t c, int64_t l
 // DiT attention I/O (b2q_attn_io.cu).
 cudaError_t launch_rows_to_heads(const float* src, int64_t B, int64_t T, int H, int D, int64_t ld_floats, int parts,
                                  unsigned norm_mask, const float* g0, const float* g1, float eps, void* o0, void* o1,
-                                 void* o2, cudaStream_t s);
+                                 void* o2, cudaStream_t s, bool f32_out = false);
 cudaError_t launch_heads_q8(const void* o16, int64_t B, int64_t T, int H, int D, int64_t sb, int64_t sh,
                             int64_t st, int8_t* codes, float* scales, int64_t ld, int variant, cudaStream_t s);
+
+// fp32 attention core, online softmax in IEEE fp32 (b2q_attention.cu): q [B][H][Tq][D],
+// k, v [B][H][Tk][D] (+ optional k2, v2 [B][H][Tk2][D]), o rows [B*Tq][ldo] at column h*D.
+cudaError_t launch_attention_f32(const float* q, const float* k, const float* v, const float* k2, const float* v2,
+                                 int64_t B, int H, int64_t Tq, int64_t Tk, int64_t Tk2, int D, float scale, float* o,
+                                 int64_t ldo_floats, cudaStream_t s);
 
 cudaError_t launch_gelu(const float* x, int64_t rows, int64_t cols, int64_t ldx_floats, float* y,
                         int64_t ldy_floats, cudaStream_t s);

@@ -108,11 +108,20 @@ class SsFlow:
     """Packed weights of the whole SS-flow DiT and its forward / sampling step."""
 
     def __init__(self, dev, params: dict, C: int = 1024, heads: int = 16, n_blocks: int = 24,
-                 n_shape: int = 4096, in_ch: int = 8, mlp_ratio: int = 4, wtype: int = b2q.TYPE_Q8_0):
+                 n_shape: int = 4096, in_ch: int = 8, mlp_ratio: int = 4, wtype: int = b2q.TYPE_Q8_0,
+                 attn: str = "f16"):
         """params: name -> tensor per param_specs (numpy or torch): "q" entries
-        GGUF rows of wtype, uint8 [out, row bytes]; "f" entries fp32."""
+        GGUF rows of wtype, uint8 [out, row bytes]; "f" entries fp32.
+        attn: "f16" -- the production attention (q, k, v and o in fp16, the
+        reference's flash-attention path with F16 K/V); "f32" -- the reference's
+        F32 numeric-gate contract (gb_attention with strict K/V,
+        cpp_ggml/src/graph_builder.cpp:139-175): fp32 heads, libb2q's fp32
+        online-softmax core, fp32 output into the projection."""
         import numpy as np
         import torch
+        if attn not in ("f16", "f32"):
+            raise ValueError("attn: 'f16' or 'f32'")
+        self.attn = attn
         self.dev, self.C, self.H, self.D = dev, C, heads, C // heads
         self.nb, self.T, self.in_ch, self.hidden, self.wtype = n_blocks, n_shape, in_ch, C * mlp_ratio, wtype
 
@@ -151,23 +160,36 @@ class SsFlow:
         C, H, D, p = self.C, self.H, self.D, f"b{i}.{g}."
         act = b2q.norm_modulate_q8(x, EPS, scale, shift)
         qkv = b2q.mul_mat_prepared(self.W[p + "qkv"], 3 * C, C, act, B * T, bias=self.V[p + "qkv.b"])
-        return b2q.qkv_heads(qkv, B, T, H, D, self.V[p + "gq"], self.V[p + "gk"], EPS)
+        heads = b2q.qkv_heads_f32 if self.attn == "f32" else b2q.qkv_heads
+        return heads(qkv, B, T, H, D, self.V[p + "gq"], self.V[p + "gk"], EPS)
+
+    def _attend(self, q, k, v, k2=None, v2=None):
+        """The attention core: fp16 heads -> fp16 o [B, H, T, D] (production), or
+        fp32 heads -> fp32 rows [B*T, C] (F32 contract).  k2 / v2: a second key
+        source appended after k / v."""
+        import torch
+        import torch.nn.functional as F
+        if self.attn == "f32":
+            return b2q.attention_f32(q, k, v, k2, v2)
+        if k2 is not None:
+            k, v = torch.cat([k, k2], 2), torch.cat([v, v2], 2)
+        return F.scaled_dot_product_attention(q, k, v)
 
     def _attn_out(self, g: str, i: int, o, x, gate, name: str = "out"):
         p = f"b{i}.{g}.{name}"
-        act = b2q.heads_act_prepare(o)
+        act = b2q.act_prepare(o) if self.attn == "f32" else b2q.heads_act_prepare(o)
         b2q.mul_mat_prepared_gate_residual(self.W[p], self.C, self.C, act, x.shape[0], x, bias=self.V[p + ".b"],
                                            gate=gate, out=x)
 
     def _cross(self, g: str, i: int, x, B: int, T: int, act_c, n_cond: int):
-        import torch.nn.functional as F
         C, H, D, p = self.C, self.H, self.D, f"b{i}.{g}."
         act = b2q.layer_norm_q8(x, EPS, self.V[p + "n2w"], self.V[p + "n2b"])
         xq = b2q.mul_mat_prepared(self.W[p + "xq"], C, C, act, B * T, bias=self.V[p + "xq.b"])
         xkv = b2q.mul_mat_prepared(self.W[p + "xkv"], 2 * C, C, act_c, B * n_cond, bias=self.V[p + "xkv.b"])
-        (q,) = b2q.rows_to_heads(xq, B, T, H, D, 1)
-        k, v = b2q.rows_to_heads(xkv, B, n_cond, H, D, 2)
-        self._attn_out(g, i, F.scaled_dot_product_attention(q, k, v), x, None, "xout")
+        heads = b2q.rows_to_heads_f32 if self.attn == "f32" else b2q.rows_to_heads
+        (q,) = heads(xq, B, T, H, D, 1)
+        k, v = heads(xkv, B, n_cond, H, D, 2)
+        self._attn_out(g, i, self._attend(q, k, v), x, None, "xout")
 
     def _mlp(self, g: str, i: int, x, scale, shift, gate):
         C, p = self.C, f"b{i}.{g}."
@@ -219,11 +241,11 @@ class SsFlow:
                 side.wait_event(kv_ready)
                 ks.record_stream(side)
                 vs.record_stream(side)
-                o_p = F.scaled_dot_product_attention(qp, torch.cat([kp, ks], 2), torch.cat([vp, vs], 2))
+                o_p = self._attend(qp, kp, vp, ks, vs)
                 self._attn_out("p", i, o_p, hp, gate_msa)
                 self._cross("p", i, hp, B, 4, act_c, n_cond)
                 self._mlp("p", i, hp, scale_mlp, shift_mlp, gate_mlp)
-            o_s = F.scaled_dot_product_attention(qs, ks, vs)
+            o_s = self._attend(qs, ks, vs)
             self._attn_out("s", i, o_s, hs, gate_msa)
             self._cross("s", i, hs, B, T, act_c, n_cond)
             self._mlp("s", i, hs, scale_mlp, shift_mlp, gate_mlp)

@@ -14,22 +14,28 @@ N_COND = 40
 TOL = 3e-3  # fp16 attention cores (both sides round q, k, v and o to fp16)
 
 
-def make_params(wtype, seed=0):
+def make_params(wtype, seed=0, cfg=None):
+    cfg = CFG if cfg is None else cfg
     rng = np.random.default_rng(seed)
     p = {}
-    specs = ss_flow.param_specs(CFG["C"], CFG["n_blocks"], CFG["n_shape"], CFG["in_ch"], CFG["mlp_ratio"])
+    specs = ss_flow.param_specs(cfg["C"], cfg["n_blocks"], cfg["n_shape"], cfg["in_ch"], cfg["mlp_ratio"])
     for name, kind, shape, (mean, std) in specs:
         v = (rng.standard_normal(shape) * std + mean).astype(np.float32)
         p[name] = O.quantize(v, wtype) if kind == "q" else v
     return p
 
 
-def cpu_forward(p, wtype, xs, xp, t, d, cond, B):
+def cpu_forward(p, wtype, xs, xp, t, d, cond, B, cfg=None, n_cond=None, attn="f16"):
     """The reference graph on the CPU: oracle mul_mat (x86 activation
-    quantizer) for every quantized linear, fp32 numpy elementwise, fp16 q / k /
-    v / o around an fp64 softmax attention."""
-    C, H, T, nb = CFG["C"], CFG["heads"], CFG["n_shape"], CFG["n_blocks"]
+    quantizer) for every quantized linear, fp32 numpy elementwise, and an fp64
+    softmax attention on q / k / v / o rounded to fp16 (attn "f16", the
+    production flash path) or kept in fp32 (attn "f32", the reference's F32
+    numeric-gate contract, cpp_ggml/src/graph_builder.cpp:139-175)."""
+    cfg = CFG if cfg is None else cfg
+    n_cond = N_COND if n_cond is None else n_cond
+    C, H, T, nb = cfg["C"], cfg["heads"], cfg["n_shape"], cfg["n_blocks"]
     D = C // H
+    rnd = (lambda a: a.astype(np.float16).astype(np.float64)) if attn == "f16" else (lambda a: a.astype(np.float64))  # noqa: E731
     f32 = np.float32
     lin = lambda name, x: O.mul_mat(wtype, p[name], np.ascontiguousarray(x, f32), O.ACT_X86) + p[name + ".b"]  # noqa: E731
     silu = lambda x: (x / (f32(1) + np.exp(-x))).astype(f32)  # noqa: E731
@@ -56,13 +62,13 @@ def cpu_forward(p, wtype, xs, xp, t, d, cond, B):
         if g is not None:
             ms = ((x.astype(np.float64) ** 2).sum(-1, keepdims=True) / D).astype(f32)
             x = (x * (f32(1) / np.sqrt(ms + f32(1e-6)))).astype(f32) * g.reshape(H, D)
-        return x.astype(np.float16).astype(np.float64).transpose(0, 2, 1, 3)
+        return rnd(x).transpose(0, 2, 1, 3)
 
     def attend(q, k, v):
         s = q @ k.transpose(0, 1, 3, 2) / np.sqrt(D)
         s = np.exp(s - s.max(-1, keepdims=True))
         o = (s / s.sum(-1, keepdims=True)) @ v
-        return o.astype(np.float16).astype(f32).transpose(0, 2, 1, 3).reshape(-1, C)
+        return rnd(o).astype(f32).transpose(0, 2, 1, 3).reshape(-1, C)
 
     for i in range(nb):
         six = (O.mul_mat(wtype, p[f"b{i}.adaln"], sm, O.ACT_X86) + p[f"b{i}.adaln.b"])[0]
@@ -83,7 +89,7 @@ def cpu_forward(p, wtype, xs, xp, t, d, cond, B):
             h = ln(x) * p[f"b{i}.{g}.n2w"] + p[f"b{i}.{g}.n2b"]
             q = heads(lin(f"b{i}.{g}.xq", h), n)
             kv = lin(f"b{i}.{g}.xkv", cond)
-            o = attend(q, heads(kv[:, :C], N_COND), heads(kv[:, C:], N_COND))
+            o = attend(q, heads(kv[:, :C], n_cond), heads(kv[:, C:], n_cond))
             x = x + lin(f"b{i}.{g}.xout", o)
             h = O.gelu(lin(f"b{i}.{g}.fc1", modulate(x, sc_mlp, sh_mlp)))
             out.append(x + lin(f"b{i}.{g}.fc2", h) * g_mlp)
@@ -98,13 +104,15 @@ def rel(a, b):
     return float(np.linalg.norm(a - b) / np.linalg.norm(b))
 
 
-def inputs(B, seed=3):
+def inputs(B, seed=3, cfg=None, n_cond=None):
+    cfg = CFG if cfg is None else cfg
+    n_cond = N_COND if n_cond is None else n_cond
     rng = np.random.default_rng(seed)
-    xs = np.repeat(rng.standard_normal((1, CFG["n_shape"], CFG["in_ch"])).astype(np.float32), B, 0)
-    xs = xs.reshape(B * CFG["n_shape"], CFG["in_ch"])
+    xs = np.repeat(rng.standard_normal((1, cfg["n_shape"], cfg["in_ch"])).astype(np.float32), B, 0)
+    xs = xs.reshape(B * cfg["n_shape"], cfg["in_ch"])
     xp = {m: np.repeat(rng.standard_normal((1, ch)).astype(np.float32), B, 0) for m, ch in ss_flow.POSE}
-    cond = rng.standard_normal((N_COND, CFG["C"])).astype(np.float32)
-    cond2 = np.concatenate([cond, np.zeros_like(cond)])[:B * N_COND]
+    cond = rng.standard_normal((n_cond, cfg["C"])).astype(np.float32)
+    cond2 = np.concatenate([cond, np.zeros_like(cond)])[:B * n_cond]
     return xs, xp, cond, cond2
 
 
