@@ -189,6 +189,33 @@ B2Q_API int b2q_mul_mat_prepared(const void* packed, int64_t n, int64_t k, const
                                  int64_t m, const float* bias, float* y,
                                  int64_t y_row_stride_bytes, void* stream);
 
+/* ------------------------------------------------- compact Q4_0 weights
+ * Q4_0 kept at its GGUF footprint (0.5625 bytes per value, against 1.125 for
+ * the int8 layout b2q_weight_pack builds): b2q_weight_pack_q4_0 moves each
+ * block's 16 nibble bytes to 16-byte-aligned rows and its fp16 scale to a
+ * block-major table (b2q_weight_packed_q4_0_bytes(n, k) bytes, 256-byte
+ * aligned; from GGUF Q4_0 rows as cpp_ggml/src/gguf_loader.cpp:113-133 loads
+ * them, w_row_stride_bytes apart, 2-byte aligned).  The GEMM widens the nibbles
+ * to int8 (value - 8) in shared memory before the MMA, so the result is the
+ * same, bit for bit, as b2q_mul_mat_prepared on the b2q_weight_pack layout of
+ * the same weight (ggml's CPU mul_mat semantics, Q8_0 activations from
+ * b2q_act_prepare):
+ *   b2q_mul_mat_prepared_q4_0: y = w.act + bias, or with resid != NULL
+ *     y = resid + gate * (w.act + bias) (gate may be NULL; resid and y the same
+ *     buffer with the same stride, or disjoint);
+ *   b2q_mul_mat_prepared_q4_0_gelu_q8: the fused GELU + Q8_0 tile end of
+ *     b2q_mul_mat_prepared_gelu_q8 (n % 32 == 0). */
+B2Q_API size_t b2q_weight_packed_q4_0_bytes(int64_t n, int64_t k);
+B2Q_API int b2q_weight_pack_q4_0(const void* w, int64_t n, int64_t k, int64_t w_row_stride_bytes, void* packed,
+                                 size_t packed_bytes, void* stream);
+B2Q_API int b2q_mul_mat_prepared_q4_0(const void* packed, int64_t n, int64_t k, const void* act, int64_t m,
+                                      const float* bias, const float* gate, const float* resid,
+                                      int64_t resid_row_stride_bytes, float* y, int64_t y_row_stride_bytes,
+                                      void* stream);
+B2Q_API int b2q_mul_mat_prepared_q4_0_gelu_q8(const void* packed, int64_t n, int64_t k, const void* act,
+                                              int64_t m, const float* bias, void* act_out, size_t act_out_bytes,
+                                              int variant, void* stream);
+
 /* Q4_K on prepared operands: the packed Q4_K weight (b2q_weight_pack /
  * b2q_weight_upload with B2Q_TYPE_Q4_K) against Q8_K activations
  * (b2q_act_prepare with B2Q_ACT_Q8_K):
@@ -308,6 +335,20 @@ B2Q_API int b2q_heads_act_prepare(const void* o16, int64_t B, int64_t T, int64_t
  * b2q_qkv_heads_f32 / b2q_rows_to_heads_f32 are b2q_qkv_heads /
  * b2q_rows_to_heads with fp32 outputs (no fp16 rounding), the inputs of this
  * form; outputs 16-byte aligned. */
+/* ------------------------------------------------- attention, F16 (production)
+ * gb_attention's production path (cpp_ggml/src/graph_builder.cpp:151-171:
+ * ggml_flash_attn_ext with K and V cast to F16) for D = 64, on the tensor cores:
+ * S = q k^T (fp16 x fp16, fp32 accumulation), softmax in fp32 (exp2 of the
+ * scores times scale * log2 e), P rounded to fp16, o = P v / sum P in fp32,
+ * o rounded to fp16.  q fp16 [B][H][Tq][64]; k, v fp16 [B][H][Tk][64]; optional
+ * k2, v2 [B][H][Tk2][64] append keys Tk .. Tk + Tk2 - 1 (both NULL for none).
+ * o is written as fp16 rows [B*Tq] of o_row_stride_bytes (a multiple of 16),
+ * head h at columns h*64 .. h*64+63 -- b2q_heads_act_prepare reads it with
+ * strides (Tq*row, 64, row).  All pointers 16-byte aligned.  D other than 64
+ * returns B2Q_ERR_UNSUPPORTED. */
+B2Q_API int b2q_attention_f16(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t Tq,
+                              int64_t Tk, int64_t D, const void* k2, const void* v2, int64_t Tk2, float scale,
+                              void* o, int64_t o_row_stride_bytes, void* stream);
 B2Q_API int b2q_qkv_heads_f32(const float* qkv, int64_t B, int64_t T, int64_t H, int64_t D,
                               int64_t qkv_row_stride_bytes, const float* gamma_q, const float* gamma_k, float eps,
                               float* q, float* k, float* v, void* stream);

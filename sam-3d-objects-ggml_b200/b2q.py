@@ -63,6 +63,10 @@ def _lib_obj():
             "b2q_act_prepared_bytes": (SZ, [I, I64, I64]),
             "b2q_mul_mat_workspace_bytes": (SZ, [I, I64, I64, I64, I]),
             "b2q_mul_mat_prepared_q4_k": (I, [P, I64, I64, P, I64, P, P, P, I64, P, I64, P]),
+            "b2q_weight_packed_q4_0_bytes": (SZ, [I64, I64]),
+            "b2q_weight_pack_q4_0": (I, [P, I64, I64, I64, P, SZ, P]),
+            "b2q_mul_mat_prepared_q4_0": (I, [P, I64, I64, P, I64, P, P, P, I64, P, I64, P]),
+            "b2q_mul_mat_prepared_q4_0_gelu_q8": (I, [P, I64, I64, P, I64, P, P, SZ, I, P]),
             "b2q_weight_pack": (I, [I, P, I64, I64, I64, P, SZ, P]),
             "b2q_weight_upload": (I, [I, P, I64, I64, I64, P, SZ, P, SZ, P]),
             "b2q_mul_mat_workspace_size": (SZ, [I64, I64, I64, I]),
@@ -80,6 +84,7 @@ def _lib_obj():
             "b2q_qkv_heads_f32": (I, [P, I64, I64, I64, I64, I64, P, P, ctypes.c_float, P, P, P, P]),
             "b2q_rows_to_heads_f32": (I, [P, I64, I64, I64, I64, I, I64, P, P, P]),
             "b2q_attention_f32": (I, [P, P, P, I64, I64, I64, I64, I64, P, P, I64, ctypes.c_float, P, I64, P]),
+            "b2q_attention_f16": (I, [P, P, P, I64, I64, I64, I64, I64, P, P, I64, ctypes.c_float, P, I64, P]),
             "b2q_layer_norm_q8": (I, [P, I64, I64, I64, ctypes.c_float, P, P, I, P, SZ, P]),
             "b2q_mul_mat_prepared_gate_residual": (I, [P, I64, I64, P, I64, P, P, P, I64, P, I64, P]),
             "b2q_norm_modulate": (I, [P, I64, I64, I64, ctypes.c_float, P, P, P, I64, P]),
@@ -189,6 +194,42 @@ def weight_pack(wtype: int, w, k: int, stream=None):
     rc = lib().b2q_weight_pack(wtype, _ptr(w), n, k, w.stride(0), _ptr(packed), size, _stream(stream))
     _check("b2q_weight_pack", rc)
     return packed
+
+
+def weight_pack_q4_0(w, k: int, stream=None):
+    """GGUF Q4_0 rows uint8 [N, >=K/32*18] (device) -> the compact Q4_0 layout
+    (GGUF footprint; the GEMM widens the nibbles on chip)."""
+    n = w.shape[0]
+    size = lib().b2q_weight_packed_q4_0_bytes(n, k)
+    packed = _empty_aligned(size, w.device)
+    rc = lib().b2q_weight_pack_q4_0(_ptr(w), n, k, w.stride(0), _ptr(packed), size, _stream(stream))
+    _check("b2q_weight_pack_q4_0", rc)
+    return packed
+
+
+def mul_mat_prepared_q4_0(packed, n: int, k: int, act, m: int, bias=None, gate=None, resid=None, out=None,
+                          stream=None):
+    """Compact Q4_0 weight x prepared Q8_0 activations -> fp32 [m, n]; with
+    resid: resid + gate * (w.act + bias) (out=resid updates in place)."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=act.device)
+    rc = lib().b2q_mul_mat_prepared_q4_0(_ptr(packed), n, k, _ptr(act), m, _ptr(bias), _ptr(gate), _ptr(resid),
+                                         resid.stride(0) * 4 if resid is not None else 0, _ptr(out),
+                                         out.stride(0) * 4, _stream(stream))
+    _check("b2q_mul_mat_prepared_q4_0", rc)
+    return out
+
+
+def mul_mat_prepared_q4_0_gelu_q8(packed, n: int, k: int, act, m: int, bias=None, variant: int = ACT_X86,
+                                  out=None, stream=None):
+    size = act_prepared_size(m, n)
+    if out is None:
+        out = _empty_aligned(size, act.device)
+    rc = lib().b2q_mul_mat_prepared_q4_0_gelu_q8(_ptr(packed), n, k, _ptr(act), m, _ptr(bias), _ptr(out),
+                                                 out.numel() * out.element_size(), variant, _stream(stream))
+    _check("b2q_mul_mat_prepared_q4_0_gelu_q8", rc)
+    return out
 
 
 def weight_upload(wtype: int, host_w, k: int, staging_bytes: int = 8 << 20, device=None, stream=None):
@@ -409,6 +450,26 @@ def attention_f32(q, k, v, k2=None, v2=None, scale: float | None = None, out=Non
     rc = lib().b2q_attention_f32(_ptr(q), _ptr(k), _ptr(v), B, H, Tq, Tk, D, _ptr(k2), _ptr(v2), Tk2, scale,
                                  _ptr(out), out.stride(0) * 4, _stream(stream))
     _check("b2q_attention_f32", rc)
+    return out
+
+
+def attention_f16(q, k, v, k2=None, v2=None, scale: float | None = None, out=None, stream=None):
+    """Tensor-core attention (D = 64): q [B, H, Tq, 64], k, v [B, H, Tk, 64] fp16
+    (plus an optional second key source k2, v2) -> fp16 rows [B*Tq, H*64]."""
+    import math
+    torch = _torch()
+    B, H, Tq, D = q.shape
+    Tk = k.shape[2]
+    Tk2 = k2.shape[2] if k2 is not None else 0
+    for t in (q, k, v, k2, v2):
+        assert t is None or (t.dtype == torch.float16 and t.is_contiguous())
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty((B * Tq, H * D), dtype=torch.float16, device=q.device)
+    rc = lib().b2q_attention_f16(_ptr(q), _ptr(k), _ptr(v), B, H, Tq, Tk, D, _ptr(k2), _ptr(v2), Tk2, scale,
+                                 _ptr(out), out.stride(0) * 2, _stream(stream))
+    _check("b2q_attention_f16", rc)
     return out
 
 

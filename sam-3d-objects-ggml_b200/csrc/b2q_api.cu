@@ -67,6 +67,18 @@ SplitOperand split_at(uint8_t* base, int64_t rows, int64_t k) {
   return s;
 }
 
+// The compact Q4_0 entries' weight and activation operands.
+int q4c_operands(const void* packed, int64_t n, int64_t k, const void* act, int64_t m, GemmArgs& g) {
+  g.q4c = q4c_at(static_cast<const uint8_t*>(packed), n, k);
+  g.a = split_at(static_cast<uint8_t*>(const_cast<void*>(act)), m, k);
+  g.w = g.a;  // unused by the compact path
+  g.M = m;
+  g.N = n;
+  g.K = k;
+  g.dots = nullptr;
+  return B2Q_OK;
+}
+
 int run_gemm(const SplitOperand& w, const SplitOperand& a, int64_t m, int64_t n, int64_t k,
              float* y, int64_t ldy_floats, const float* bias, int32_t* dots, int sms,
              cudaStream_t s) {
@@ -683,6 +695,79 @@ int b2q_norm_modulate_q8(const float* x, int64_t m, int64_t c, int64_t x_row_str
                                         variant, static_cast<cudaStream_t>(stream)));
 }
 
+size_t b2q_weight_packed_q4_0_bytes(int64_t n, int64_t k) {
+  if (n < 0 || k <= 0 || k % kQK != 0) return 0;
+  return q4c_bytes(n, k);
+}
+
+int b2q_weight_pack_q4_0(const void* w, int64_t n, int64_t k, int64_t w_row_stride_bytes, void* packed,
+                         size_t packed_bytes, void* stream) {
+  if (n < 0 || k <= 0 || k % kQK != 0) return B2Q_ERR_INVALID_ARG;
+  if (n > INT_MAX || k > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (n > 0 && (!w || !packed)) return B2Q_ERR_INVALID_ARG;
+  if (w_row_stride_bytes < (k / kQK) * kQ4Bytes) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(w, 2) || w_row_stride_bytes % 2 != 0 || !aligned(packed, 256)) return B2Q_ERR_MISALIGNED;
+  if (packed_bytes < q4c_bytes(n, k)) return B2Q_ERR_WORKSPACE;
+  if (n == 0) return B2Q_OK;
+  if (int rc = check_device(nullptr)) return rc;
+  const Q4cWeight c = q4c_at(static_cast<const uint8_t*>(packed), n, k);
+  return from_cuda(launch_pack_q4c(static_cast<const uint8_t*>(w), n, k, w_row_stride_bytes,
+                                   const_cast<uint8_t*>(c.nibbles), const_cast<uint16_t*>(c.scales), c.ld,
+                                   static_cast<cudaStream_t>(stream)));
+}
+
+int b2q_mul_mat_prepared_q4_0(const void* packed, int64_t n, int64_t k, const void* act, int64_t m,
+                              const float* bias, const float* gate, const float* resid,
+                              int64_t resid_row_stride_bytes, float* y, int64_t y_row_stride_bytes, void* stream) {
+  if (n < 0 || m < 0 || k <= 0 || k % kQK != 0) return B2Q_ERR_INVALID_ARG;
+  if (n > INT_MAX || m > INT_MAX || k > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (m > 0 && n > 0 && (!packed || !act || !y)) return B2Q_ERR_INVALID_ARG;
+  if (y_row_stride_bytes < n * 4 || (resid && resid_row_stride_bytes < n * 4)) return B2Q_ERR_INVALID_ARG;
+  if (resid == y && resid && resid_row_stride_bytes != y_row_stride_bytes) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(packed, 256) || !aligned(act, 256) || !aligned(y, 4) || y_row_stride_bytes % 4 != 0 ||
+      (resid && (!aligned(resid, 4) || resid_row_stride_bytes % 4 != 0)) || (bias && !aligned(bias, 4)) ||
+      (gate && !aligned(gate, 4)))
+    return B2Q_ERR_MISALIGNED;
+  if (m == 0 || n == 0) return B2Q_OK;
+  int sms = 0;
+  if (int rc = check_device(&sms)) return rc;
+  GemmArgs g;
+  q4c_operands(packed, n, k, act, m, g);
+  g.y = y;
+  g.ldy = y_row_stride_bytes / 4;
+  g.bias = bias;
+  g.gate = gate;
+  g.resid = resid;
+  g.ldr = resid ? resid_row_stride_bytes / 4 : 0;
+  return from_cuda(launch_gemm_tc(g, sms, static_cast<cudaStream_t>(stream)));
+}
+
+int b2q_mul_mat_prepared_q4_0_gelu_q8(const void* packed, int64_t n, int64_t k, const void* act, int64_t m,
+                                      const float* bias, void* act_out, size_t act_out_bytes, int variant,
+                                      void* stream) {
+  if (n < 0 || m < 0 || k <= 0 || k % kQK != 0 || n % kQK != 0) return B2Q_ERR_INVALID_ARG;
+  if (n > INT_MAX || m > INT_MAX || k > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (variant != B2Q_ACT_X86 && variant != B2Q_ACT_REF) return B2Q_ERR_INVALID_ARG;
+  if (m > 0 && n > 0 && (!packed || !act || !act_out)) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(packed, 256) || !aligned(act, 256) || !aligned(act_out, 256) || (bias && !aligned(bias, 4)))
+    return B2Q_ERR_MISALIGNED;
+  if (n > 0 && act_out_bytes < split_bytes(m, n)) return B2Q_ERR_WORKSPACE;
+  if (m == 0 || n == 0) return B2Q_OK;
+  int sms = 0;
+  if (int rc = check_device(&sms)) return rc;
+  const SplitOperand out = split_at(static_cast<uint8_t*>(act_out), m, n);
+  GemmArgs g;
+  q4c_operands(packed, n, k, act, m, g);
+  g.y = nullptr;
+  g.ldy = 0;
+  g.bias = bias;
+  g.q_codes = const_cast<int8_t*>(out.codes);
+  g.q_scales = const_cast<float*>(out.scales);
+  g.q_ld = out.ld;
+  g.q_variant = variant;
+  return from_cuda(launch_gemm_tc(g, sms, static_cast<cudaStream_t>(stream)));
+}
+
 int b2q_qkv_heads(const float* qkv, int64_t B, int64_t T, int64_t H, int64_t D, int64_t qkv_row_stride_bytes,
                   const float* gamma_q, const float* gamma_k, float eps, void* q16, void* k16, void* v16,
                   void* stream) {
@@ -765,6 +850,26 @@ int b2q_attention_f32(const float* q, const float* k, const float* v, int64_t B,
   return from_cuda(launch_attention_f32(q, k, v, k2, v2, B, static_cast<int>(H), Tq, Tk, k2 ? Tk2 : 0,
                                         static_cast<int>(D), scale, o, o_row_stride_bytes / 4,
                                         static_cast<cudaStream_t>(stream)));
+}
+
+int b2q_attention_f16(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t Tq, int64_t Tk,
+                      int64_t D, const void* k2, const void* v2, int64_t Tk2, float scale, void* o,
+                      int64_t o_row_stride_bytes, void* stream) {
+  if (B < 0 || Tq < 0 || Tk < 0 || H <= 0 || !std::isfinite(scale)) return B2Q_ERR_INVALID_ARG;
+  if (D != 64) return B2Q_ERR_UNSUPPORTED;
+  if ((k2 == nullptr) != (v2 == nullptr) || (k2 && Tk2 < 0)) return B2Q_ERR_INVALID_ARG;
+  const int64_t tk_all = Tk + (k2 ? Tk2 : 0);
+  if (B * Tq > 0 && (!q || !o || tk_all <= 0 || (Tk > 0 && (!k || !v)))) return B2Q_ERR_INVALID_ARG;
+  if (o_row_stride_bytes < H * D * 2) return B2Q_ERR_INVALID_ARG;
+  const int64_t rows = B * H * (Tq > tk_all ? Tq : tk_all);
+  if (B > 65535 || H > 65535 || rows + 128 > INT_MAX || (Tq + 127) / 128 > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(k2, 16) || !aligned(v2, 16) || !aligned(o, 16) ||
+      o_row_stride_bytes % 16 != 0)
+    return B2Q_ERR_MISALIGNED;
+  if (B * Tq == 0) return B2Q_OK;
+  if (int rc = check_device(nullptr)) return rc;
+  return from_cuda(launch_attention_f16(q, k, v, k2, v2, B, static_cast<int>(H), Tq, Tk, k2 ? Tk2 : 0, scale, o,
+                                        o_row_stride_bytes / 2, static_cast<cudaStream_t>(stream)));
 }
 
 int b2q_layer_norm_q8(const float* x, int64_t m, int64_t c, int64_t x_row_stride_bytes, float eps, const float* weight,
@@ -913,6 +1018,9 @@ int b2q_device_status(unsigned int* code, int clear) {
   if (int rc = check_device(nullptr)) return rc;
   if (cudaDeviceSynchronize() != cudaSuccess) return B2Q_ERR_CUDA;
   if (read_device_status(code, clear != 0) != cudaSuccess) return B2Q_ERR_CUDA;
+  unsigned int attn = 0;
+  if (read_attention_status(&attn, clear != 0) != cudaSuccess) return B2Q_ERR_CUDA;
+  if (!*code) *code = attn;
   return *code ? B2Q_ERR_DEVICE : B2Q_OK;
 }
 

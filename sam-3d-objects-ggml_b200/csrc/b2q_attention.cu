@@ -16,12 +16,18 @@
 //   o    fp32 rows [B*Tq][H*D]       row (b, t), columns h*D + d: the layout the
 //                                    output projection consumes
 //
-// Mapping: one CTA per 64 queries of one (b, h), 256 threads.  The CTA walks
+// F16 form (attention_f16_kernel below): the production path of gb_attention
+// (flash attention on F16 K/V), for D = 64, on the tensor cores.
+//
+// Mapping of the F32 kernel: one CTA per 64 queries of one (b, h), 256 threads.  The CTA walks
 // the keys in tiles of 64: K and V tiles in shared memory, each thread a 4 x 4
 // block of the score tile (4 queries x 4 keys) and a 4 x D/16 block of the
 // output.  A query row's 64 scores sit in 16 consecutive lanes, so the row max
 // and row sum are 16-lane shuffles.
 #include "b2q_internal.h"
+#include "b2q_ptx.cuh"
+
+#include <cuda_fp16.h>
 
 #include <cmath>
 
@@ -210,6 +216,368 @@ cudaError_t launch_attention_f32_d(const float* q, const float* k, const float* 
   return cudaGetLastError();
 }
 
+// ----------------------------------------------------------------- F16 form
+// Flash attention on the tensor cores for D = 64, fp16 q / k / v / o, fp32
+// softmax.  One CTA per 256 queries (two 128-query tiles) of one (b, h);
+// 384 threads = 3 warpgroups:
+//   warp 0       TMA producer: both Q tiles once, then K and V tiles of 128 keys
+//                (fp16, 128-byte swizzle) through a 3-stage ring shared by the
+//                two query tiles
+//   warp 1       TMEM allocator + MMA issuer: per key tile, S_i = Q_i K^T
+//                (kind::f16, M 128, N 128, K 64) for both query tiles, then
+//                (P V)_i of the previous key tile (M 128, N 64, K 128; V read as
+//                an MN-major operand straight from its TMA tile)
+//   warps 2, 3   idle (complete warpgroup 0, which runs on 40 registers)
+//   warpgroups 1 and 2: softmax of query tile 0 and 1 (232 registers each):
+//                thread t owns one query row (its TMEM lane) and reads the row's
+//                128 scores, so the row max and sum need no shuffles (eight
+//                independent chains each); writes P as fp16 into shared memory in
+//                the swizzled K-major layout the P V MMA reads; keeps the fp32
+//                output row in registers (o = o * alpha + P V per tile), so no
+//                TMEM rescale has to be ordered between MMAs.
+// The two warpgroups ping-pong: while one computes its softmax, the tensor core
+// works on the other's tile.  exp2 is the hardware ex2.approx (scores
+// pre-multiplied by scale * log2(e)).  Keys of a partial last tile of a source
+// are masked to -inf.  Every wait is bounded; on give-up the CTA drains and
+// frees TMEM.  A CTA whose second query tile lies wholly past Tq runs one tile.
+__device__ unsigned int g_attn_status = 0;
+
+constexpr int kFaBM = 128, kFaBN = 128, kFaD = 64, kFaStages = 3;
+constexpr int kFaThreads = 384;
+constexpr int kFaLaunchRegs = 168, kFaRegsControl = 40, kFaRegsSoftmax = 232;
+static_assert(128 * kFaRegsControl + 256 * kFaRegsSoftmax <= kFaThreads * kFaLaunchRegs, "register split");
+constexpr int kFaTile = 128 * 128;  // bytes of a 128-row x 64-fp16 tile
+constexpr uint32_t kFaTmemCols = 512;
+// TMEM columns: S_i at 128 i; (P V)_i at 256 + 96 i, 80 wide: o in 0..63, the row sum of P in 64
+constexpr int kFaSOff = 0, kFaPvOff = 256, kFaPvPitch = 96, kFaPvN = 80;
+struct FaSmem {
+  static constexpr int Q = 0;                            // Q_i at Q + i * tile
+  static constexpr int KV = Q + 2 * kFaTile;             // stage s: K at KV + 2s * tile, V next
+  static constexpr int P = KV + kFaStages * 2 * kFaTile;  // P_i: two 64-key panels at P + 2i * tile
+  static constexpr int ONES = P + 2 * 2 * kFaTile;       // V's 65th column: 1.0 for every key (MN-major atom)
+  static constexpr int BAR = ONES + kFaTile;
+  static constexpr int NBAR = 1 + 2 * kFaStages + 12 + 1;
+  static constexpr int BYTES = BAR + NBAR * 8 + 16 + 1024;
+};
+
+struct FaParams {
+  int n1, n2;          // key tiles of the first and second source
+  int64_t Tq, Tk, Tk2;
+  int H;
+  float c2;            // scale * log2(e)
+  __half* o;
+  int64_t ldo;         // halves
+};
+
+__device__ __forceinline__ float fa_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// The P V result of key tile u joins the output row: o = o * alpha_u + (P V)_u
+// for the 64 outputs and, in o[64], for the row sum of P (the ones column).
+__device__ __forceinline__ bool fa_o_update(float (&o)[kFaD + 1], int u, float alpha, uint32_t tpv, uint64_t* pv_full,
+                                            uint64_t* pv_empty, unsigned int* status, volatile int* abort_flag,
+                                            int lane) {
+  if (!mbar_wait(pv_full, u & 1u, status, kDevWaitEpilogue, abort_flag)) return false;
+  tc_fence_after();
+  uint32_t r[kFaD + 8];
+  tmem_ld_32x32b_x32(tpv, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+  tmem_ld_32x32b_x32(tpv + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+  tmem_ld_32x32b_x8(tpv + 64, &r[64]);
+  tmem_wait_ld();
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(pv_empty);
+#pragma unroll
+  for (int d = 0; d <= kFaD; ++d) o[d] = __fmaf_rn(o[d], alpha, __uint_as_float(r[d]));
+  return true;
+}
+
+// ex2 of two fp32 values as one fp16x2 MUFU operation: the inputs are rounded to
+// fp16 first (P is fp16 anyway; the largest p, at x - m near 0, keep their
+// precision), two results per instruction.
+__device__ __forceinline__ uint32_t fa_ex2_h2(float a, float b) {
+  const __half2 x = __floats2half2_rn(a, b);
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(*reinterpret_cast<const uint32_t*>(&x)));
+  return y;
+}
+
+// Shared-memory descriptor for an MN-major operand with the 128-byte swizzle
+// whose MN extent spans two 64-element atoms `lbo` bytes apart (V and the ones
+// column); 8-row K groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t addr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3fffu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3fffu) << 16;
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
+__global__ void __launch_bounds__(kFaThreads, 1)
+    attention_f16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_k2,
+                         const __grid_constant__ CUtensorMap tm_v2, const FaParams p) {
+  extern __shared__ uint8_t fa_smem_raw[];
+  uint8_t* smem = fa_smem_raw + ((1024u - (smem_u32(fa_smem_raw) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + FaSmem::BAR);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + kFaStages;
+  uint64_t* s_full = kv_empty + kFaStages;  // [2] per query tile
+  uint64_t* s_empty = s_full + 2;
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* p_empty = p_full + 2;
+  uint64_t* pv_full = p_empty + 2;
+  uint64_t* pv_empty = pv_full + 2;
+  uint64_t* done = pv_empty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  unsigned int* status = &g_attn_status;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t bh = static_cast<int64_t>(blockIdx.z) * p.H + blockIdx.y;
+  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * 2 * kFaBM;
+  const int nq = q0 + kFaBM < p.Tq ? 2 : 1;  // query tiles this CTA runs
+  const int ntiles = p.n1 + p.n2;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kFaStages; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 4);  // one arrival per softmax warp
+      mbar_init(&p_full[i], 4);
+      mbar_init(&p_empty[i], 1);
+      mbar_init(&pv_full[i], 1);
+      mbar_init(&pv_empty[i], 4);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  {
+    // The ones atom: MN element 0 (the row-sum column) is 1.0 in every key row;
+    // in the 128-byte swizzle, row r keeps its chunk 0 at chunk r % 8.
+    uint4* ones = reinterpret_cast<uint4*>(smem + FaSmem::ONES);
+    for (int c = threadIdx.x; c < kFaTile / 16; c += kFaThreads) {
+      const int r = c >> 3, chunk = c & 7;
+      ones[c] = make_uint4(chunk == (r & 7) ? 0x3C00u : 0u, 0u, 0u, 0u);  // fp16 1.0 in the low half
+    }
+    fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+    if (p.n2) {
+      tma_prefetch_desc(&tm_k2);
+      tma_prefetch_desc(&tm_v2);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, kFaTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp < 4) {
+    setmaxnreg_dec<kFaRegsControl>();
+    if (warp == 0) {
+      // ---------------------------------------------------------- producer
+      if (elect_one()) {
+        uint32_t issued = 0, issued_par = 0;
+        mbar_arrive_expect_tx(q_full, nq * kFaTile);
+        for (int i = 0; i < nq; ++i)
+          tma_load_2d(smem + FaSmem::Q + i * kFaTile, &tm_q, q_full, 0, static_cast<int32_t>(bh * p.Tq + q0 + i * kFaBM));
+        for (int t = 0; t < ntiles; ++t) {
+          const int st = t % kFaStages;
+          const uint32_t ph = (t / kFaStages) & 1u;
+          if (!mbar_wait(&kv_empty[st], ph ^ 1u, status, kDevWaitProducer, abort_flag)) break;
+          const bool second = t >= p.n1;
+          const int64_t row = second ? bh * p.Tk2 + static_cast<int64_t>(t - p.n1) * kFaBN
+                                     : bh * p.Tk + static_cast<int64_t>(t) * kFaBN;
+          uint8_t* kd = smem + FaSmem::KV + 2 * st * kFaTile;
+          mbar_arrive_expect_tx(&kv_full[st], 2 * kFaTile);
+          tma_load_2d(kd, second ? &tm_k2 : &tm_k, &kv_full[st], 0, static_cast<int32_t>(row));
+          tma_load_2d(kd + kFaTile, second ? &tm_v2 : &tm_v, &kv_full[st], 0, static_cast<int32_t>(row));
+          issued |= 1u << st;
+          issued_par = (issued_par & ~(1u << st)) | (ph << st);
+        }
+        // every issued copy lands before the CTA may exit
+        mbar_wait(q_full, 0, status, kDevWaitDrain, nullptr);
+        for (int st = 0; st < kFaStages; ++st)
+          if ((issued >> st) & 1u) mbar_wait(&kv_full[st], (issued_par >> st) & 1u, status, kDevWaitDrain, nullptr);
+      }
+    } else if (warp == 1) {
+      // -------------------------------------------------------- MMA issuer
+      if (elect_one()) {
+        constexpr uint32_t idesc_qk = idesc_f16(kFaBM, kFaBN);
+        constexpr uint32_t idesc_pv = idesc_f16(kFaBM, kFaPvN) | (1u << 16);  // B (V | ones) MN-major
+        bool ok = mbar_wait(q_full, 0, status, kDevWaitMma, abort_flag);
+        for (int t = 0; ok && t <= ntiles; ++t) {
+          if (t < ntiles) {
+            const int st = t % kFaStages;
+            if (!mbar_wait(&kv_full[st], (t / kFaStages) & 1u, status, kDevWaitMma, abort_flag)) {
+              ok = false;
+              break;
+            }
+            const uint32_t k_addr = smem_u32(smem + FaSmem::KV + 2 * st * kFaTile);
+            for (int i = 0; ok && i < nq; ++i) {
+              if (!mbar_wait(&s_empty[i], (t & 1u) ^ 1u, status, kDevWaitMma, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t q_addr = smem_u32(smem + FaSmem::Q + i * kFaTile);
+#pragma unroll
+              for (int kk = 0; kk < kFaD / 16; ++kk)
+                mma_f16(tmem + kFaSOff + i * kFaBN, smem_desc_k_sw128(q_addr + kk * 32),
+                        smem_desc_k_sw128(k_addr + kk * 32), idesc_qk, kk > 0 ? 1u : 0u);
+              mma_commit(&s_full[i]);
+            }
+          }
+          if (t >= 1) {  // P V of key tile u = t - 1, both query tiles; then its K / V stage is free
+            const int u = t - 1, st = u % kFaStages;
+            const uint32_t v_addr = smem_u32(smem + FaSmem::KV + (2 * st + 1) * kFaTile);
+            const uint32_t ones_addr = smem_u32(smem + FaSmem::ONES);
+            for (int i = 0; ok && i < nq; ++i) {
+              if (!mbar_wait(&p_full[i], u & 1u, status, kDevWaitMma, abort_flag) ||
+                  !mbar_wait(&pv_empty[i], (u & 1u) ^ 1u, status, kDevWaitMma, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t p_addr = smem_u32(smem + FaSmem::P + 2 * i * kFaTile);
+#pragma unroll
+              for (int kk = 0; kk < kFaBN / 16; ++kk)  // 16 keys per MMA
+                mma_f16(tmem + kFaPvOff + i * kFaPvPitch,
+                        smem_desc_k_sw128(p_addr + (kk >> 2) * kFaTile + (kk & 3) * 32),
+                        smem_desc_mn_sw128(v_addr + kk * 2048, ones_addr - v_addr), idesc_pv, kk > 0 ? 1u : 0u);
+              mma_commit(&pv_full[i]);
+              mma_commit(&p_empty[i]);
+            }
+            if (ok) mma_commit(&kv_empty[st]);
+          }
+        }
+        mma_commit(done);
+        mbar_wait(done, 0, status, kDevWaitDrain, nullptr);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax
+    setmaxnreg_inc<kFaRegsSoftmax>();
+    const int i = (warp - 4) >> 2;     // query tile of this warpgroup
+    const int qw = warp & 3;           // TMEM lane quarter
+    const int row = qw * 32 + lane;    // query row within the tile
+    if (i < nq) {
+      const uint32_t lane_addr = static_cast<uint32_t>(qw * 32) << 16;
+      const uint32_t ts = tmem + lane_addr + kFaSOff + i * kFaBN;
+      const uint32_t tpv = tmem + lane_addr + kFaPvOff + i * kFaPvPitch;
+      float o[kFaD + 1];  // o[64]: the row sum of P
+#pragma unroll
+      for (int d = 0; d <= kFaD; ++d) o[d] = 0.0f;
+      float m = -INFINITY, alpha_prev = 0.0f;
+      bool ok = true;
+      uint8_t* prow = smem + FaSmem::P + 2 * i * kFaTile + (row >> 3) * 1024 + (row & 7) * 128;
+      for (int t = 0; t < ntiles; ++t) {
+        const uint32_t par = t & 1u;
+        if (!mbar_wait(&s_full[i], par, status, kDevWaitEpilogue, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t sr[kFaBN];
+#pragma unroll
+        for (int c = 0; c < kFaBN; c += 32) tmem_ld_32x32b_x32(ts + c, *reinterpret_cast<uint32_t(*)[32]>(&sr[c]));
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty[i]);
+        const bool second = t >= p.n1;
+        const int64_t k0 = static_cast<int64_t>(second ? t - p.n1 : t) * kFaBN;
+        const int64_t valid64 = (second ? p.Tk2 : p.Tk) - k0;
+        if (valid64 < kFaBN) {  // a partial last tile of its source: the missing keys score -inf
+#pragma unroll
+          for (int c = 0; c < kFaBN; ++c)
+            if (c >= valid64) sr[c] = __float_as_uint(-INFINITY);
+        }
+        // Row max over raw scores in 8 independent chains (scale > 0 commutes with max).
+        float mx8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mx8[j] = __uint_as_float(sr[j]);
+#pragma unroll
+        for (int c = 8; c < kFaBN; c += 8)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) mx8[j] = fmaxf(mx8[j], __uint_as_float(sr[c + j]));
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        const float m_new = fmaxf(m, __fmul_rn(mx, p.c2));
+        const float alpha = fa_ex2(m - m_new);
+        const float nm = -m_new;
+        // exp2 of the whole row into packed fp16 registers first; only the
+        // stores wait for P_i to be free (the previous key tile's P V MMA).
+        uint32_t pk[kFaBN / 2];
+#pragma unroll
+        for (int c = 0; c < kFaBN; c += 2)
+          pk[c >> 1] = fa_ex2_h2(__fmaf_rn(__uint_as_float(sr[c]), p.c2, nm), __fmaf_rn(__uint_as_float(sr[c + 1]), p.c2, nm));
+        if (!mbar_wait(&p_empty[i], par ^ 1u, status, kDevWaitEpilogue, abort_flag)) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int c = 0; c < kFaBN; c += 8) {
+          const int panel = c >> 6, chunk = (c & 63) >> 3;
+          *reinterpret_cast<uint4*>(prow + panel * kFaTile + ((chunk ^ (row & 7)) << 4)) =
+              make_uint4(pk[c / 2], pk[c / 2 + 1], pk[c / 2 + 2], pk[c / 2 + 3]);
+        }
+        fence_proxy_async_smem();  // P (generic-proxy writes) -> visible to the tensor core
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[i]);
+        m = m_new;
+        if (t >= 1 && !fa_o_update(o, t - 1, alpha_prev, tpv, &pv_full[i], &pv_empty[i], status, abort_flag, lane)) {
+          ok = false;
+          break;
+        }
+        alpha_prev = alpha;
+      }
+      if (ok && ntiles > 0) ok = fa_o_update(o, ntiles - 1, alpha_prev, tpv, &pv_full[i], &pv_empty[i], status,
+                                             abort_flag, lane);
+      const int64_t tq = q0 + i * kFaBM + row;
+      if (ok && tq < p.Tq) {
+        const float inv = 1.0f / o[kFaD];
+        __half* dst = p.o + (static_cast<int64_t>(blockIdx.z) * p.Tq + tq) * p.ldo +
+                      static_cast<int64_t>(blockIdx.y) * kFaD;
+#pragma unroll
+        for (int d = 0; d < kFaD; d += 8) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const __half2 h2 = __floats2half2_rn(o[d + 2 * j] * inv, o[d + 2 * j + 1] * inv);
+            pk[j] = *reinterpret_cast<const uint32_t*>(&h2);
+          }
+          *reinterpret_cast<uint4*>(dst + d) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kFaTmemCols);
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_attention_f32(const float* q, const float* k, const float* v, const float* k2, const float* v2,
@@ -222,6 +590,58 @@ cudaError_t launch_attention_f32(const float* q, const float* k, const float* v,
     case 128: return launch_attention_f32_d<128>(q, k, v, k2, v2, B, H, Tq, Tk, Tk2, scale, o, ldo_floats, s);
     default: return cudaErrorInvalidValue;
   }
+}
+
+cudaError_t launch_attention_f16(const void* q, const void* k, const void* v, const void* k2, const void* v2,
+                                 int64_t B, int H, int64_t Tq, int64_t Tk, int64_t Tk2, float scale, void* o,
+                                 int64_t ldo_halves, cudaStream_t s) {
+  if (B == 0 || Tq == 0) return cudaSuccess;
+  CUtensorMap tq, tk, tv, tk2, tv2;
+  const uint64_t bh = static_cast<uint64_t>(B) * H;
+  auto map = [](CUtensorMap* m, const void* base, uint64_t rows) {
+    return make_tensor_map_2d(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, base, kFaD, rows, kFaD * 2, kFaD, kFaBN,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+  };
+  if (!map(&tq, q, bh * Tq) || !map(&tk, k, bh * Tk) || !map(&tv, v, bh * Tk)) return cudaErrorInvalidValue;
+  const bool second = k2 && Tk2 > 0;
+  if (!map(&tk2, second ? k2 : k, second ? bh * Tk2 : bh * Tk) || !map(&tv2, second ? v2 : v, second ? bh * Tk2 : bh * Tk))
+    return cudaErrorInvalidValue;
+  FaParams p;
+  p.n1 = static_cast<int>((Tk + kFaBN - 1) / kFaBN);
+  p.n2 = second ? static_cast<int>((Tk2 + kFaBN - 1) / kFaBN) : 0;
+  p.Tq = Tq;
+  p.Tk = Tk;
+  p.Tk2 = second ? Tk2 : 0;
+  p.H = H;
+  p.c2 = scale * 1.4426950408889634f;  // log2(e)
+  p.o = static_cast<__half*>(o);
+  p.ldo = ldo_halves;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    // The register split needs the kernel compiled at exactly kFaLaunchRegs, or
+    // setmaxnreg.inc could wait for registers that do not exist.
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, attention_f16_kernel);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs != kFaLaunchRegs) return cudaErrorInvalidConfiguration;
+    e = cudaFuncSetAttribute(attention_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FaSmem::BYTES);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const dim3 grid(static_cast<unsigned>((Tq + 2 * kFaBM - 1) / (2 * kFaBM)), static_cast<unsigned>(H),
+                  static_cast<unsigned>(B));
+  attention_f16_kernel<<<grid, kFaThreads, FaSmem::BYTES, s>>>(tq, tk, tv, tk2, tv2, p);
+  return cudaGetLastError();
+}
+
+cudaError_t read_attention_status(unsigned int* value, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(value, g_attn_status, sizeof(unsigned int));
+  if (e != cudaSuccess || !clear) return e;
+  const unsigned int zero = 0;
+  return cudaMemcpyToSymbol(g_attn_status, &zero, sizeof(unsigned int));
 }
 
 }  // namespace b2q

@@ -51,6 +51,8 @@
 // copies and MMAs, frees TMEM and exits, leaving a code in g_device_status.
 #include <atomic>
 
+#include <cuda_fp16.h>
+
 #include "b2q_internal.h"
 #include "b2q_ptx.cuh"
 #include "b2q_q8.cuh"
@@ -88,7 +90,7 @@ constexpr float kNegTwoPowM129 = -0x1p-129f;  // subnormal, exact
 
 // BN: tokens per tile (MMA N), 64..128 in steps of 16; the host picks it per
 // shape so that the tiles spread evenly over the SMs (see pick_bn).
-template <int STAGES, int BN>
+template <int STAGES, int BN, bool Q4C = false>
 struct Cfg {
   static_assert(BN % 16 == 0 && BN >= 64 && BN <= kSlotCols, "tile width");
   static constexpr int COLS = BN / 2;  // token columns per epilogue thread
@@ -96,11 +98,21 @@ struct Cfg {
   static constexpr int B_BYTES = BN * kStageK;
   static constexpr int SW_BYTES = kKBS * kBM * 4;
   static constexpr int SA_BYTES = kKBS * BN * 4;
-  static constexpr int TX_BYTES = A_BYTES + B_BYTES + SW_BYTES + SA_BYTES;  // bytes the TMA delivers per stage
-  static constexpr int STAGE_BYTES = (TX_BYTES + 1023) / 1024 * 1024;          // stage pitch in smem
+  // Compact Q4_0 weights: the TMA brings the stage's nibble blocks (128 rows x
+  // 64 bytes) and fp16 scales (4 x 128); the converter warps widen them into the
+  // A (int8 codes) and SW (fp32 scales) regions that the other roles read.
+  static constexpr int PK_OFF = A_BYTES + B_BYTES + SW_BYTES + SA_BYTES;
+  static constexpr int PK_BYTES = Q4C ? kBM * kStageK / 2 : 0;
+  static constexpr int SWH_OFF = PK_OFF + PK_BYTES;
+  static constexpr int SWH_BYTES = Q4C ? kKBS * kBM * 2 : 0;
+  // bytes the TMA delivers per stage
+  static constexpr int TX_BYTES = Q4C ? B_BYTES + SA_BYTES + PK_BYTES + SWH_BYTES
+                                      : A_BYTES + B_BYTES + SW_BYTES + SA_BYTES;
+  static constexpr int STAGE_BYTES = (SWH_OFF + SWH_BYTES + 1023) / 1024 * 1024;  // stage pitch in smem
   static constexpr int OFF_TILE = STAGES * STAGE_BYTES;
   static constexpr int BAR_OFF = OFF_TILE + kOffsetTileBytes;
-  static constexpr int NBARS = 2 * STAGES + 2 * kSlots + 1;  // stage and slot barrier pairs, MMA drain
+  // stage full / empty (+ converted), slot full / empty, MMA drain
+  static constexpr int NBARS = (Q4C ? 3 : 2) * STAGES + 2 * kSlots + 1;
   static constexpr int SMEM = BAR_OFF + NBARS * 8 + 16 + 1024;  // + alignment slack
   // GELU + Q8_0 variant only: a 32 x 33 fp32 transpose buffer per epilogue warp.
   static constexpr int XPOSE_OFF = (BAR_OFF + NBARS * 8 + 16 + 127) / 128 * 128;
@@ -189,12 +201,12 @@ __device__ __forceinline__ void load_slot(uint32_t taddr, uint32_t (&r)[COLS]) {
 // load this thread's COLS columns, scale them into acc, then hand the slot
 // back.  j: block within the stage (selects the stage's scales).  Returns
 // false when a bounded wait gave up.
-template <int STAGES, int BN, bool DUMP, int COLS = BN / 2>
+template <int STAGES, int BN, bool DUMP, bool Q4C, int COLS = BN / 2>
 __device__ __forceinline__ bool epi_block(uint32_t (&cur)[COLS], float2 (&acc)[COLS / 2], int slot, uint32_t sphase,
                                           int j, int kb, int tile, const TcParams& p, const uint8_t* sb,
                                           uint64_t* acc_full, uint64_t* acc_empty, volatile int* abort_flag,
                                           uint32_t tbase, int row, int chalf, int lane) {
-  using C = Cfg<STAGES, BN>;
+  using C = Cfg<STAGES, BN, Q4C>;
   if (!mbar_wait(&acc_full[slot], sphase, &g_device_status, kDevWaitEpilogue, abort_flag)) return false;
   tc_fence_after();
   load_slot<COLS>(tbase + slot * kSlotCols, cur);
@@ -274,14 +286,14 @@ __device__ __forceinline__ void geluq_cols(const float2 (&acc)[NACC], float bv, 
   if constexpr (COLS > 32) geluq_chunk<VARIANT, 32, COLS - 32>(acc, bv, has_bias, m0, M, lane, codes, q_k, qs, xp);
 }
 
-template <int STAGES, int BN, int MODE>
+template <int STAGES, int BN, int MODE, bool Q4C>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_wc, const __grid_constant__ CUtensorMap tm_ac,
                    const __grid_constant__ CUtensorMap tm_ws, const __grid_constant__ CUtensorMap tm_as,
                    const TcParams p, const __grid_constant__ OutParams pp) {
   constexpr bool DUMP = MODE == kModeDump, PEERS = MODE == kModePeers, STALL = MODE == kModeStall;
   constexpr bool GELUQ = MODE == kModeGeluQ8, GATERES = MODE == kModeGateRes;
-  using C = Cfg<STAGES, BN>;
+  using C = Cfg<STAGES, BN, Q4C>;
   constexpr int COLS = C::COLS;
   extern __shared__ uint8_t smem_raw[];
   // Offset arithmetic on the __shared__ array itself (no integer round trip), so
@@ -292,8 +304,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + kSlots;
   uint64_t* mma_done = acc_empty + kSlots;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* conv = mma_done + 1;  // Q4C: the stage's weight codes and scales are widened
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(conv + (Q4C ? STAGES : 0));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  // The MMA and the epilogue read a stage once it is complete: its copies landed
+  // and, for compact Q4_0 weights, its codes and scales are widened.
+  uint64_t* ready = Q4C ? conv : full;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -308,6 +324,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_empty[a], kEpiWarps);  // one arrival per epilogue warp
     }
     mbar_init(mma_done, 1);
+    if (Q4C)
+      for (int st = 0; st < STAGES; ++st) mbar_init(&conv[st], 2);  // the two converter warps
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -355,9 +373,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             uint8_t* sb = smem + stage * C::STAGE_BYTES;
             mbar_arrive_expect_tx(&full[stage], C::TX_BYTES);
-            tma_load_2d(sb, &tm_wc, &full[stage], ks * kStageK, n0);
+            if (Q4C) {  // nibble blocks and fp16 scales; the converters fill A and SW
+              tma_load_2d(sb + C::PK_OFF, &tm_wc, &full[stage], ks * kStageK / 2, n0);
+              tma_load_2d(sb + C::SWH_OFF, &tm_ws, &full[stage], n0, ks * kKBS);
+            } else {
+              tma_load_2d(sb, &tm_wc, &full[stage], ks * kStageK, n0);
+              tma_load_2d(sb + C::A_BYTES + C::B_BYTES, &tm_ws, &full[stage], n0, ks * kKBS);
+            }
             tma_load_2d(sb + C::A_BYTES, &tm_ac, &full[stage], ks * kStageK, m0);
-            tma_load_2d(sb + C::A_BYTES + C::B_BYTES, &tm_ws, &full[stage], n0, ks * kKBS);
             tma_load_2d(sb + C::A_BYTES + C::B_BYTES + C::SW_BYTES, &tm_as, &full[stage], m0, ks * kKBS);
             issued_mask |= 1u << stage;
             issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
@@ -382,7 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
           for (int ks = 0; ok && ks < n_ks; ++ks) {
-            if (!mbar_wait(&full[stage], phase, &g_device_status, kDevWaitMma, abort_flag)) {
+            if (!mbar_wait(&ready[stage], phase, &g_device_status, kDevWaitMma, abort_flag)) {
               ok = false;
               break;
             }
@@ -411,6 +434,51 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(mma_done);
         mbar_wait(mma_done, 0, &g_device_status, kDevWaitDrain, nullptr);
       }
+    } else if (Q4C) {
+      // -------------------------------------------- warps 2, 3: Q4_0 converters
+      // Per stage: 128 rows x 4 blocks of nibbles -> int8 codes (value - 8) in
+      // the 128-byte-swizzled K-major tile the MMA reads (chunk c of row r at
+      // chunk c ^ (r % 8) of its 8-row atom), and the fp16 scales -> fp32 times
+      // 2^100 (the stored form of the int8 layout's weight scales).  Consecutive
+      // threads read consecutive 16-byte nibble blocks.
+      const int ct = threadIdx.x - 64;  // 0..63
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        for (int ks = 0; ks < n_ks; ++ks) {
+          if (!mbar_wait(&full[stage], phase, &g_device_status, kDevWaitProducer, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sb = smem + stage * C::STAGE_BYTES;
+#pragma unroll 2
+          for (int i = 0; i < 8; ++i) {
+            const int u = ct + 64 * i;
+            const int row = u >> 2, blk = u & 3;
+            const uint4 nb = *reinterpret_cast<const uint4*>(sb + C::PK_OFF + row * (kStageK / 2) + blk * 16);
+            uint8_t* arow = sb + row * kStageK;  // row r of the 1024-byte-aligned tile: r * 128
+            const uint4 lo = make_uint4(__vsub4(nb.x & 0x0f0f0f0fu, 0x08080808u), __vsub4(nb.y & 0x0f0f0f0fu, 0x08080808u),
+                                        __vsub4(nb.z & 0x0f0f0f0fu, 0x08080808u), __vsub4(nb.w & 0x0f0f0f0fu, 0x08080808u));
+            const uint4 hi = make_uint4(__vsub4((nb.x >> 4) & 0x0f0f0f0fu, 0x08080808u),
+                                        __vsub4((nb.y >> 4) & 0x0f0f0f0fu, 0x08080808u),
+                                        __vsub4((nb.z >> 4) & 0x0f0f0f0fu, 0x08080808u),
+                                        __vsub4((nb.w >> 4) & 0x0f0f0f0fu, 0x08080808u));
+            *reinterpret_cast<uint4*>(arow + (((2 * blk) ^ (row & 7)) << 4)) = lo;
+            *reinterpret_cast<uint4*>(arow + (((2 * blk + 1) ^ (row & 7)) << 4)) = hi;
+          }
+          const __half* swh = reinterpret_cast<const __half*>(sb + C::SWH_OFF);
+          float* sw = reinterpret_cast<float*>(sb + C::A_BYTES + C::B_BYTES);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) sw[ct + 64 * i] = __half2float(swh[ct + 64 * i]) * kWeightScaleMul;
+          fence_proxy_async_smem();  // the codes (generic-proxy writes) -> visible to the tensor core
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&conv[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
     }
   } else {
     // ------------------------------------------------ warpgroups 1-2: epilogue
@@ -427,15 +495,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < COLS / 2; ++c) acc[c] = make_float2(0.0f, 0.0f);
       for (int ks = 0; ks < n_ks; ++ks) {
-        // The stage's scales are read from shared memory: wait for its copies.
-        if (!mbar_wait(&full[stage], phase, &g_device_status, kDevWaitEpilogue, abort_flag)) {
+        // The stage's scales are read from shared memory: wait for the stage.
+        if (!mbar_wait(&ready[stage], phase, &g_device_status, kDevWaitEpilogue, abort_flag)) {
           ok = false;
           break;
         }
         const uint8_t* sb = smem + stage * C::STAGE_BYTES;
 #pragma unroll
         for (int j = 0; j < kKBS; ++j, ++q) {
-          if (!epi_block<STAGES, BN, DUMP>(ra, acc, static_cast<int>(q & (kSlots - 1)), (q / kSlots) & 1u, j,
+          if (!epi_block<STAGES, BN, DUMP, Q4C>(ra, acc, static_cast<int>(q & (kSlots - 1)), (q / kSlots) & 1u, j,
                                            ks * kKBS + j, tile, p, sb, acc_full, acc_empty, abort_flag, tbase, row,
                                            chalf, lane)) {
             ok = false;
@@ -561,18 +629,24 @@ bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uin
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int STAGES, int BN, int MODE>
+template <int STAGES, int BN, int MODE, bool Q4C>
 cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
   constexpr bool PEERS = MODE == kModePeers;
-  using C = Cfg<STAGES, BN>;
+  using C = Cfg<STAGES, BN, Q4C>;
   const int64_t KB = g.K / kQK;
   CUtensorMap tm_wc, tm_ac, tm_ws, tm_as;
-  if (!make_map_2d(&tm_wc, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.w.codes, g.K, g.N, g.K, kStageK, kBM,
-                   CU_TENSOR_MAP_SWIZZLE_128B) ||
+  const bool wmaps =
+      Q4C ? make_map_2d(&tm_wc, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.q4c.nibbles, g.K / 2, g.N, g.K / 2, kStageK / 2, kBM,
+                        CU_TENSOR_MAP_SWIZZLE_NONE) &&
+                make_map_2d(&tm_ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, g.q4c.scales, g.N, KB, g.q4c.ld * 2, kBM, kKBS,
+                            CU_TENSOR_MAP_SWIZZLE_NONE)
+          : make_map_2d(&tm_wc, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.w.codes, g.K, g.N, g.K, kStageK, kBM,
+                        CU_TENSOR_MAP_SWIZZLE_128B) &&
+                make_map_2d(&tm_ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, g.w.scales, g.N, KB, g.w.ld * 4, kBM, kKBS,
+                            CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!wmaps ||
       !make_map_2d(&tm_ac, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.a.codes, g.K, g.M, g.K, kStageK, BN,
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map_2d(&tm_ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, g.w.scales, g.N, KB, g.w.ld * 4, kBM,
-                   kKBS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
       !make_map_2d(&tm_as, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, g.a.scales, g.M, KB, g.a.ld * 4, BN,
                    kKBS, CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
@@ -600,7 +674,7 @@ cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
   pp.gate = g.gate;
   pp.resid = g.resid;
   pp.ldr = g.ldr;
-  auto kern = gemm_tc_kernel<STAGES, BN, MODE>;
+  auto kern = gemm_tc_kernel<STAGES, BN, MODE, Q4C>;
   constexpr int smem_bytes = MODE == kModeGeluQ8 ? C::SMEM_XPOSE : C::SMEM;
   static_assert(smem_bytes <= 227 * 1024, "shared memory per CTA");
   // Checked and set once per device (a bit per device; the calls cost more
@@ -654,14 +728,14 @@ cudaError_t read_device_status(unsigned int* value, bool clear) {
   return cudaMemcpyToSymbol(g_device_status, &zero, sizeof(unsigned int));
 }
 
-template <int MODE>
+template <int MODE, bool Q4C = false>
 cudaError_t launch_picked(const GemmArgs& g, int num_sms, cudaStream_t s) {
   switch (pick_bn(g.M, g.N, num_sms)) {
-    case 112: return launch_cfg<4, 112, MODE>(g, num_sms, s);
-    case 96: return launch_cfg<4, 96, MODE>(g, num_sms, s);
-    case 80: return launch_cfg<4, 80, MODE>(g, num_sms, s);
-    case 64: return launch_cfg<4, 64, MODE>(g, num_sms, s);
-    default: return launch_cfg<4, 128, MODE>(g, num_sms, s);
+    case 112: return launch_cfg<4, 112, MODE, Q4C>(g, num_sms, s);
+    case 96: return launch_cfg<4, 96, MODE, Q4C>(g, num_sms, s);
+    case 80: return launch_cfg<4, 80, MODE, Q4C>(g, num_sms, s);
+    case 64: return launch_cfg<4, 64, MODE, Q4C>(g, num_sms, s);
+    default: return launch_cfg<4, 128, MODE, Q4C>(g, num_sms, s);
   }
 }
 
@@ -673,8 +747,17 @@ bool make_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* ba
 
 cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, cudaStream_t s) {
   if (g.M == 0 || g.N == 0) return cudaSuccess;
-  if (g.dots) return launch_cfg<4, 128, kModeDump>(g, num_sms, s);
-  if (g.inject_stall) return launch_cfg<4, 128, kModeStall>(g, num_sms, s);
+  if (g.q4c.nibbles) {  // compact Q4_0 weights: plain, bias, gate + residual and GELU + Q8_0 tile ends
+    if (g.dots || g.inject_stall || g.n_peers > 0) return cudaErrorInvalidValue;
+    if (g.q_codes) {
+      if (g.N % kQK != 0 || !g.q_scales) return cudaErrorInvalidValue;
+      return launch_picked<kModeGeluQ8, true>(g, num_sms, s);
+    }
+    if (g.resid) return launch_picked<kModeGateRes, true>(g, num_sms, s);
+    return launch_picked<kModePlain, true>(g, num_sms, s);
+  }
+  if (g.dots) return launch_cfg<4, 128, kModeDump, false>(g, num_sms, s);
+  if (g.inject_stall) return launch_cfg<4, 128, kModeStall, false>(g, num_sms, s);
   if (g.q_codes) {
     if (g.N % kQK != 0 || !g.q_scales) return cudaErrorInvalidValue;
     return launch_picked<kModeGeluQ8>(g, num_sms, s);

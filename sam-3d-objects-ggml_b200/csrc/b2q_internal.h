@@ -58,6 +58,28 @@ struct SplitOperand {
 };
 
 inline int64_t scale_ld(int64_t rows) { return round_up(rows, 4); }
+
+// Compact Q4_0 weight layout (the GGUF footprint, 0.5625 bytes per value): the
+// 16 nibble bytes of every block, rows of k/2 bytes (GGUF order inside a block:
+// byte j holds element j low and element j + 16 high), then the fp16 scales
+// block-major [k/32][ld] with ld = round_up(n, 8) (16-byte TMA strides).  The
+// GEMM widens the nibbles on chip.
+inline int64_t q4c_scale_ld(int64_t n) { return round_up(n, 8); }
+inline size_t q4c_bytes(int64_t n, int64_t k) {
+  return static_cast<size_t>(round_up(n * (k / 2), 256) + round_up((k / kQK) * q4c_scale_ld(n) * 2, 256));
+}
+struct Q4cWeight {
+  const uint8_t* nibbles;  // [n][k/2]
+  const uint16_t* scales;  // fp16 [k/32][ld]
+  int64_t ld;
+};
+inline Q4cWeight q4c_at(const uint8_t* base, int64_t n, int64_t k) {
+  Q4cWeight w;
+  w.nibbles = base;
+  w.scales = reinterpret_cast<const uint16_t*>(base + round_up(n * (k / 2), 256));
+  w.ld = q4c_scale_ld(n);
+  return w;
+}
 inline size_t split_bytes(int64_t rows, int64_t k) {
   return static_cast<size_t>(round_up(rows * k, 256) + round_up((k / kQK) * scale_ld(rows) * 4, 256));
 }
@@ -98,6 +120,9 @@ cudaError_t launch_quantize_q8_k(const float* x, int64_t m, int64_t k, int64_t l
 cudaError_t launch_pack_weights(int wtype, const uint8_t* w, int64_t n, int64_t k,
                                 int64_t ldw_bytes, int8_t* codes, float* scales, int64_t ld,
                                 cudaStream_t s);
+// GGUF Q4_0 rows -> the compact layout above.
+cudaError_t launch_pack_q4c(const uint8_t* w, int64_t n, int64_t k, int64_t ldw_bytes, uint8_t* nibbles,
+                            uint16_t* scales, int64_t ld, cudaStream_t s);
 cudaError_t launch_gemm_simt(int wtype, const uint8_t* w, int64_t ldw_bytes, int64_t n, int64_t k,
                              const uint8_t* a, int64_t lda_bytes, int64_t m, float* y,
                              int64_t ldy_floats, cudaStream_t s);
@@ -121,6 +146,14 @@ cudaError_t launch_heads_q8(const void* o16, int64_t B, int64_t T, int H, int D,
 cudaError_t launch_attention_f32(const float* q, const float* k, const float* v, const float* k2, const float* v2,
                                  int64_t B, int H, int64_t Tq, int64_t Tk, int64_t Tk2, int D, float scale, float* o,
                                  int64_t ldo_floats, cudaStream_t s);
+
+// Tensor-core attention, D = 64, fp16 q / k / v / o (b2q_attention.cu): q [B][H][Tq][64],
+// k, v [B][H][Tk][64] (+ k2, v2 [B][H][Tk2][64]), o rows [B*Tq][ldo halves] at column h*64.
+cudaError_t launch_attention_f16(const void* q, const void* k, const void* v, const void* k2, const void* v2,
+                                 int64_t B, int H, int64_t Tq, int64_t Tk, int64_t Tk2, float scale, void* o,
+                                 int64_t ldo_halves, cudaStream_t s);
+// Status word of the attention kernels' bounded waits (its own translation unit).
+cudaError_t read_attention_status(unsigned int* value, bool clear);
 
 cudaError_t launch_gelu(const float* x, int64_t rows, int64_t cols, int64_t ldx_floats, float* y,
                         int64_t ldy_floats, cudaStream_t s);
@@ -151,6 +184,9 @@ struct GemmArgs {
   const float* gate = nullptr;
   const float* resid = nullptr;
   int64_t ldr = 0;
+  // Compact Q4_0 weights (q4c.nibbles != nullptr): w is unused; the kernel reads
+  // the nibble blocks and fp16 scales and widens them on chip.
+  Q4cWeight q4c = {nullptr, nullptr, 0};
 };
 cudaError_t launch_gemm_tc(const GemmArgs& args, int num_sms, cudaStream_t s);
 // 2-D tensor map (cuTensorMapEncodeTiled through the runtime's driver entry point).

@@ -162,7 +162,39 @@ __global__ void __launch_bounds__(256) pack_weights_kernel(const uint8_t* __rest
   }
 }
 
+// GGUF Q4_0 rows -> compact layout: one thread per (row, block) moves the 16
+// nibble bytes to a 16-byte-aligned slot and the fp16 scale to the block-major
+// scale table.
+__global__ void __launch_bounds__(256) pack_q4c_kernel(const uint8_t* __restrict__ w, int64_t n, int64_t k,
+                                                       int64_t ldw, uint8_t* __restrict__ nibbles,
+                                                       uint16_t* __restrict__ scales, int64_t ld) {
+  const int64_t kb = k / kQK;
+  const int64_t total = n * kb;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / kb, b = i - row * kb;
+    const uint16_t* b16 = reinterpret_cast<const uint16_t*>(w + row * ldw + b * kQ4Bytes);  // 18-byte blocks
+    uint32_t q[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) q[j] = static_cast<uint32_t>(b16[1 + 2 * j]) | (static_cast<uint32_t>(b16[2 + 2 * j]) << 16);
+    *reinterpret_cast<uint4*>(nibbles + row * (k / 2) + b * 16) = make_uint4(q[0], q[1], q[2], q[3]);
+    scales[b * ld + row] = b16[0];
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_pack_q4c(const uint8_t* w, int64_t n, int64_t k, int64_t ldw_bytes, uint8_t* nibbles,
+                            uint16_t* scales, int64_t ld, cudaStream_t s) {
+  const int64_t total = n * (k / kQK);
+  if (total == 0) return cudaSuccess;
+  int sms = current_device_sms();
+  if (sms <= 0) sms = 148;
+  const int64_t blocks = (total + 255) / 256;
+  const int grid = static_cast<int>(blocks < sms * 16 ? blocks : sms * 16);
+  pack_q4c_kernel<<<grid, 256, 0, s>>>(w, n, k, ldw_bytes, nibbles, scales, ld);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_quantize_q8_0_blocks(const float* x, int64_t m, int64_t k, int64_t ldx_floats,
                                         uint8_t* y, int64_t ldy_bytes, int variant, bool vec4,

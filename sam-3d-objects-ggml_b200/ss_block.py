@@ -13,9 +13,10 @@ cpp_ggml/src/ss_flow_graph.cpp:180-388), built from libb2q's entry points:
     h = modulate(norm(x), scale_mlp, shift_mlp)          b2q_norm_modulate_q8
     x = x + gate_mlp * (gelu(h . W1 + b1) . W2 + b2)     _gelu_q8 + _gate_residual
 
-Every linear, norm, quantize and epilogue is libb2q's.  The attention core is
-torch's scaled_dot_product_attention on the fp16 q, k, v: a library kernel,
-outside the path this repository rebuilds.  Modulation vectors are shared by
+Every linear, norm, quantize, epilogue and attention core is libb2q's (the
+attention: b2q_attention_f16, tensor cores, fp16 q, k, v and o, fp32 softmax;
+its token-major fp16 rows go to b2q_heads_act_prepare as a strided view).
+Modulation vectors are shared by
 the batch (the CFG branches of one step share the timestep embedding).  The
 4-token pose group (whose tiny linears run on the few-token kernel) and the
 adaLN projection are not part of this step.
@@ -61,15 +62,18 @@ class SsBlock:
 
     def forward(self, x, B: int, T: int, cond, n_cond: int, stream=None):
         """x: fp32 [B*T, C] residual stream, updated in place and returned;
-        cond: fp32 [B*n_cond, C] condition tokens.  The attention core runs on
-        torch's current stream: pass that stream (or None) as `stream`."""
-        import torch.nn.functional as F
+        cond: fp32 [B*n_cond, C] condition tokens."""
         C, H, D, v = self.C, self.H, self.D, self.vec
+
+        def attend(q, k, vv):
+            Tq = q.shape[2]
+            return b2q.attention_f16(q, k, vv, stream=stream).view(B, Tq, H, D).permute(0, 2, 1, 3)
+
         M = B * T
         act = b2q.norm_modulate_q8(x, 1e-6, v["scale_msa"], v["shift_msa"], stream=stream)
         qkv = b2q.mul_mat_prepared(self.packed["qkv"], 3 * C, C, act, M, bias=v["b_qkv"], stream=stream)
         q, k, vv = b2q.qkv_heads(qkv, B, T, H, D, v["gq"], v["gk"], 1e-6, stream=stream)
-        o = F.scaled_dot_product_attention(q, k, vv)  # [B, H, T, D] fp16
+        o = attend(q, k, vv)  # [B, H, T, D] fp16 view of token-major rows
         act_o = b2q.heads_act_prepare(o, stream=stream)
         b2q.mul_mat_prepared_gate_residual(self.packed["out"], C, C, act_o, M, x, bias=v["b_out"],
                                            gate=v["gate_msa"], out=x, stream=stream)
@@ -80,7 +84,7 @@ class SsBlock:
         xkv = b2q.mul_mat_prepared(self.packed["xkv"], 2 * C, C, act_c, B * n_cond, bias=v["b_xkv"], stream=stream)
         (q,) = b2q.rows_to_heads(xq, B, T, H, D, 1, stream=stream)
         k, vv = b2q.rows_to_heads(xkv, B, n_cond, H, D, 2, stream=stream)
-        o = F.scaled_dot_product_attention(q, k, vv)
+        o = attend(q, k, vv)
         act_o = b2q.heads_act_prepare(o, stream=stream)
         b2q.mul_mat_prepared_gate_residual(self.packed["xout"], C, C, act_o, M, x, bias=v["b_xout"], out=x,
                                            stream=stream)

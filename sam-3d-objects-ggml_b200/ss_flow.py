@@ -26,10 +26,11 @@ GEMM); the adaLN weights of all blocks are stacked into one [blocks*6C, C]
 mul_mat (its input SiLU(mod) is the same for every block); the condition
 tokens are quantized once per forward for all blocks and both groups; the
 pose group runs on a second stream beside the shape group; the whole step is
-captured into one CUDA graph (`capture`), both streams included.  Library pieces, not
-the mul_mat path: the attention cores (torch SDPA, fp16), the F32 input layers
-(K <= 8, not block-quantizable: torch matmul), the timestep embedding's cos /
-sin and SiLU on 256 / 1024 values, and the Euler update (torch elementwise).
+captured into one CUDA graph (`capture`), both streams included.  The attention
+cores are libb2q's (tensor-core fp16 form, or the F32 contract).  Torch pieces,
+not the mul_mat path: the F32 input layers (K <= 8, not block-quantizable: torch
+matmul), the timestep embedding's cos / sin and SiLU on 256 / 1024 values, and
+the Euler update (torch elementwise).
 """
 from __future__ import annotations
 
@@ -164,16 +165,14 @@ class SsFlow:
         return heads(qkv, B, T, H, D, self.V[p + "gq"], self.V[p + "gk"], EPS)
 
     def _attend(self, q, k, v, k2=None, v2=None):
-        """The attention core: fp16 heads -> fp16 o [B, H, T, D] (production), or
-        fp32 heads -> fp32 rows [B*T, C] (F32 contract).  k2 / v2: a second key
+        """The attention core: fp16 heads -> libb2q's tensor-core attention, fp16
+        o viewed as [B, H, T, D] over its token-major rows (production), or fp32
+        heads -> fp32 rows [B*T, C] (F32 contract).  k2 / v2: a second key
         source appended after k / v."""
-        import torch
-        import torch.nn.functional as F
         if self.attn == "f32":
             return b2q.attention_f32(q, k, v, k2, v2)
-        if k2 is not None:
-            k, v = torch.cat([k, k2], 2), torch.cat([v, v2], 2)
-        return F.scaled_dot_product_attention(q, k, v)
+        B, H, T, D = q.shape
+        return b2q.attention_f16(q, k, v, k2, v2).view(B, T, H, D).permute(0, 2, 1, 3)
 
     def _attn_out(self, g: str, i: int, o, x, gate, name: str = "out"):
         p = f"b{i}.{g}.{name}"
