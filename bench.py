@@ -417,6 +417,8 @@ def run_gpu(args, rank, world, local_rank):
         result["slat_linears"] = slat_side(b2q, stream, dev)
         result["f16"] = f16_side(b2q, flush, stream, dev, peaks)
         result["slat_sparse"] = slat_sparse_side(b2q, flush, stream, dev, peaks)
+    if not args.only and not args.no_colpar:
+        result["colpar"] = colpar_side(args, rank, world, dev, dist)
     if args.only:
         result["config"]["workload"] = f"single GEMM {args.only} (profiling case)"
         result["config"]["l2"] = "not flushed (profiling case)"
@@ -1126,105 +1128,162 @@ def slat_side(b2q, stream, dev, iters=3):
 
 # ------------------------------------------------- column-parallel (multi-GPU)
 COLPAR_SHAPE = ("slat_qkv_q4_0", 2, 20480, 3072, 1024)  # name, wtype, M tokens, N out, K in
+COLPAR_Q8_SHAPE = ("slat_fc1_q4_0", 2, 20480, 4096, 1024)  # fc1 -> GELU -> Q8_0: the next layer's input
+NVLINK_PEER_GBS = 770.0  # measured peer copy per direction per GPU on this pool's B200s
 
 
-def run_colpar(args, rank, world, local_rank):
+def colpar_side(args, rank, world, dev, dist=None):
     """One large SLat linear split by output rows over the ranks (the
-    column-parallel variant of BASELINE configs[4]): every rank needs the whole
-    [M][N] output.  Times the fused kernel (GEMM
-    epilogue storing each tile into every rank's buffer over NVLink) against
-    GEMM + NCCL all-gather + transpose.  Each iteration ends with a one-element
-    all-reduce so that every rank's work of the iteration is complete; both
-    variants pay it."""
-    import datetime
+    column-parallel variant of BASELINE configs[4]); every rank needs the whole
+    output.  Two exchanges, each timed fused (the GEMM epilogue stores each
+    finished tile into every rank's buffer over NVLink, overlapping the
+    remaining tiles' math) against GEMM + NCCL all-gather + transpose:
+      fp32: the qkv linear's fp32 output, 4 bytes per value;
+      q8:   fc1 with GELU + Q8_0 in the epilogue, so what crosses the links is
+            the next layer's prepared input, 1.125 bytes per value.
+    Each iteration ends with a one-element all-reduce so that every rank's work
+    of the iteration is complete; both variants pay it.  Rank 0 checks the
+    gathered bytes against a single-GPU run of the whole weight."""
     import torch
-    import torch.distributed as dist
     import b2q
     import colpar
 
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    name, wtype, M, N, K = COLPAR_SHAPE
-    rng = np.random.default_rng(4321)  # same weights and inputs on every rank
-    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
-    x = rng.standard_normal((M, K)).astype(np.float32)
-    wq = synth_blocks(wtype, w, N, K)
-    start, stop = colpar.slices(N, world)[rank]
-    n = stop - start
     stream = torch.cuda.current_stream()
-    w_d = torch.from_numpy(wq[start:stop]).to(dev)
-    packed = b2q.weight_pack(wtype, w_d, K)
-    act = b2q.act_prepare(torch.from_numpy(x).to(dev))
-    bufs = colpar.PeerBuffers(M, N)
     tick = torch.zeros(1, device=dev)
-    equal = all(b - a == n for a, b in colpar.slices(N, world))
-    slice_out = torch.empty((M, n), dtype=torch.float32, device=dev)
-    gathered = torch.empty((world * M, n), dtype=torch.float32, device=dev) if equal else None
-    out = torch.empty((M, N), dtype=torch.float32, device=dev)
-
-    def fused():
-        colpar.fused(packed, n, K, act, M, bufs, start, stream=stream)
-        if world > 1:
-            dist.all_reduce(tick)
-
-    def baseline():
-        if world > 1:
-            colpar.nccl_baseline(packed, n, K, act, M, N, slice_out, gathered, out, stream=stream)
-            dist.all_reduce(tick)
-        else:
-            b2q.mul_mat_prepared(packed, n, K, act, M, out=out, stream=stream)
+    iters = max(5, min(args.steps, 30))
 
     def timed(fn):
-        for _ in range(args.warmup):
+        for _ in range(3):
             fn()
         torch.cuda.synchronize()
-        if world > 1:
+        if dist:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(iters):
             fn()
         e1.record(stream)
         torch.cuda.synchronize()
-        return max_over_ranks(e0.elapsed_time(e1) / args.steps, dist if world > 1 else None, dev)
+        return max_over_ranks(e0.elapsed_time(e1) / iters, dist, dev)
 
-    ms_fused = timed(fused)
-    ms_base = timed(baseline) if (equal or world == 1) else None
-    # parity of the fused result against a single-GPU GEMM of the whole weight (rank 0)
-    ok = None
-    if rank == 0:
-        full = b2q.mul_mat(wtype, torch.from_numpy(wq).to(dev), torch.from_numpy(x).to(dev))
-        ok = bool(torch.equal(bufs.to_tensor(dev), full))
-    status = b2q.device_status(clear=True)
+    def sync_tick():
+        if dist:
+            dist.all_reduce(tick)
+
+    out = {"n_gpus": world, "iterations": iters, "nvlink_peer_gbs_per_direction": NVLINK_PEER_GBS,
+           "sync": "one-element all_reduce per iteration (both variants)"}
+    for kind, (name, wtype, M, N, K) in (("fp32", COLPAR_SHAPE), ("q8", COLPAR_Q8_SHAPE)):
+        rng = np.random.default_rng(4321 if kind == "fp32" else 4322)  # same weights and inputs on every rank
+        w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+        x = rng.standard_normal((M, K)).astype(np.float32)
+        wq = synth_blocks(wtype, w, N, K)
+        start, stop = colpar.slices(N, world)[rank]
+        n = stop - start
+        equal = all(b - a == n for a, b in colpar.slices(N, world))
+        packed = b2q.weight_pack(wtype, torch.from_numpy(wq[start:stop]).to(dev), K)
+        act = b2q.act_prepare(torch.from_numpy(x).to(dev))
+        bias = torch.from_numpy((rng.standard_normal(N) * 0.1).astype(np.float32)).to(dev)
+        if kind == "fp32":
+            bufs = colpar.PeerBuffers(M, N)
+            slice_out = torch.empty((M, n), dtype=torch.float32, device=dev)
+            gathered = torch.empty((world * M, n), dtype=torch.float32, device=dev) if equal else None
+            full_out = torch.empty((M, N), dtype=torch.float32, device=dev)
+
+            def fused():
+                colpar.fused(packed, n, K, act, M, bufs, start, stream=stream)
+                sync_tick()
+
+            def baseline():
+                if dist:
+                    colpar.nccl_baseline(packed, n, K, act, M, N, slice_out, gathered, full_out, stream=stream)
+                else:
+                    b2q.mul_mat_prepared(packed, n, K, act, M, out=full_out, stream=stream)
+                sync_tick()
+            value_bytes = 4.0
+        else:
+            bufs = colpar.activation_buffers(M, N)
+            ld = (M + 3) // 4 * 4
+            local = b2q._empty_aligned(b2q.act_prepared_size(M, n), dev)
+            gcodes = torch.empty((world * M, n), dtype=torch.int8, device=dev) if equal else None
+            gscales = torch.empty((world * (n // 32), ld), dtype=torch.float32, device=dev) if equal else None
+            full_act = b2q._empty_aligned(b2q.act_prepared_size(M, N), dev)
+            b_slice = bias[start:stop]
+
+            def fused():
+                colpar.fused_gelu_q8(packed, n, K, act, M, bufs, start, bias=b_slice, stream=stream)
+                sync_tick()
+
+            def baseline():
+                if dist:
+                    colpar.nccl_baseline_gelu_q8(packed, n, K, act, M, N, local, gcodes, gscales, full_act,
+                                                 bias=b_slice, stream=stream)
+                else:
+                    b2q.mul_mat_prepared_gelu_q8(packed, n, K, act, M, bias=b_slice, out=full_act, stream=stream)
+                sync_tick()
+            value_bytes = 1.125
+        ms_fused = timed(fused)
+        ms_base = timed(baseline) if (equal or world == 1) else None
+        ok = None
+        if rank == 0:  # the fused result against one GPU running the whole weight
+            full_packed = b2q.weight_pack(wtype, torch.from_numpy(wq).to(dev), K)
+            got = bufs.to_tensor(dev)
+            if kind == "fp32":
+                ok = bool(torch.equal(got, b2q.mul_mat_prepared(full_packed, N, K, act, M)))
+            else:
+                want = b2q.mul_mat_prepared_gelu_q8(full_packed, N, K, act, M, bias=bias)
+                gc, gs = colpar.split_views(got, M, N)
+                wc, wsc = colpar.split_views(want, M, N)
+                ok = bool(torch.equal(gc, wc) and torch.equal(gs[:, :M], wsc[:, :M]))
+            del full_packed
+        status = b2q.device_status(clear=True)
+        if dist:
+            dist.barrier()
+        bufs.close()
+        ops = 2.0 * M * N * K
+        bytes_in = M * N * value_bytes * (world - 1) / world  # each rank receives the others' slices
+        link_ms = bytes_in / (NVLINK_PEER_GBS * 1e9) * 1e3
+        out[kind] = {
+            "workload": f"{name}: M={M} tokens, K={K} -> N={N}, weight rows split over {world} rank(s), every "
+                        f"rank ends with the whole output ({'fp32' if kind == 'fp32' else 'GELU + Q8_0 prepared'})",
+            "fused_ms": round(ms_fused, 4), "fused_tops": round(ops / (ms_fused * 1e-3) / 1e12, 2),
+            "nccl_baseline_ms": None if ms_base is None else round(ms_base, 4),
+            "speedup_vs_nccl": None if ms_base is None else round(ms_base / ms_fused, 3),
+            "nvlink_bytes_in_per_rank": int(bytes_in),
+            "nvlink_gbs_in_per_rank": round(bytes_in / (ms_fused * 1e-3) / 1e9, 1) if world > 1 else 0.0,
+            # the time the gathered bytes need at the measured peer bandwidth, as a share of the fused time
+            "nvlink_bound_frac": round(link_ms / ms_fused, 3) if world > 1 else 0.0,
+            "parity_rank0_bitwise_vs_single_gpu": ok, "device_status": status,
+            "path": ("b2q_mul_mat_prepared_peers" if kind == "fp32" else "b2q_mul_mat_prepared_gelu_q8_peers")
+                    + " (CUDA-IPC peer pointers, P2P stores from the epilogue); baseline: the single-rank "
+                    "kernel on the slice + all_gather_into_tensor + transpose copy",
+        }
+        del packed, act
+    return out
+
+
+def run_colpar(args, rank, world, local_rank):
+    """--colpar: only the column-parallel measurement, as its own JSON line."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    d = None
     if world > 1:
-        dist.barrier()
-    bufs.close()
-    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        d = dist
+    side = colpar_side(args, rank, world, dev, d)
+    if d:
         dist.destroy_process_group()
-    ops = 2.0 * M * N * K
-    gathered_bytes = M * N * 4 * (world - 1) // world  # each rank receives the others' slices
+    q8 = side["q8"]
     return {
-        "metric": "column-parallel Q4_0 mul_mat effective TOPS (output all-gathered to every rank)",
-        "value": round(ops / (ms_fused * 1e-3) / 1e12, 2), "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_fused, 4),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "i8",
-        "data": "synthetic",
-        "config": {"workload": f"{name}: M={M} tokens, K={K} -> N={N}, weight rows split over {world} rank(s), "
-                               "every rank ends with the full [M][N] fp32 output",
-                   "parallelism": f"column-parallel tp{world}"},
-        "fused": {"ms": round(ms_fused, 4), "tops": round(ops / (ms_fused * 1e-3) / 1e12, 2),
-                  "path": "b2q_mul_mat_prepared_peers: GEMM epilogue stores tiles into every rank's "
-                          "buffer (CUDA-IPC peer pointers, NVLink)"},
-        "nccl_baseline": None if ms_base is None else {
-            "ms": round(ms_base, 4), "tops": round(ops / (ms_base * 1e-3) / 1e12, 2),
-            "path": "b2q_mul_mat_prepared on the slice + all_gather_into_tensor + transpose copy"
-                    if world > 1 else "b2q_mul_mat_prepared on the whole weight"},
-        "nvlink_bytes_in_per_rank": gathered_bytes,
-        "nvlink_gbs_in_per_rank": round(gathered_bytes / (ms_fused * 1e-3) / 1e9, 1) if world > 1 else 0.0,
-        "parity_rank0_bitwise_vs_single_gpu": ok,
-        "device_status": status,
+        "metric": "column-parallel fc1 (GELU + Q8_0 exchange) effective TOPS, output on every rank",
+        "value": q8["fused_tops"], "unit": UNIT, "n_gpus": world, "steps": side["iterations"],
+        "warmup": 3, "ms_per_step": q8["fused_ms"], "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "i8", "data": "synthetic",
+        "config": {"workload": q8["workload"], "parallelism": f"column-parallel tp{world}"},
+        "colpar": side,
     }
 
 
@@ -1317,6 +1376,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-mlp", action="store_true", help="skip the fused-MLP side measurement")
     ap.add_argument("--only", default=None, help="run one workload entry (profiling case)")
+    ap.add_argument("--no-colpar", action="store_true", help="skip the column-parallel side measurement")
     ap.add_argument("--colpar", action="store_true",
                     help="column-parallel SLat linear (one GEMM split over the ranks, all-gathered output)")
     args = ap.parse_args()

@@ -358,6 +358,33 @@ B2Q_API int b2q_attention_f32(const float* q, const float* k, const float* v, in
                               int64_t Tk, int64_t D, const float* k2, const float* v2, int64_t Tk2, float scale,
                               float* o, int64_t o_row_stride_bytes, void* stream);
 
+/* ----------------------------------------- dequantize-to-float form (strict)
+ * matmul_weight with keep_quant_gemm false (cpp_ggml/src/ss_flow_graph.cpp:
+ * 13-34, slat_flow_graph.cpp:89-94): the quantized weight is cast to F32
+ * (as_f32) or to F32 then F16 (as_f16) with ggml_cast, and gb_linear
+ * (graph_builder.cpp:44-60) multiplies with GGML_PREC_F32.
+ *
+ * b2q_dequantize: n GGUF rows of wtype (Q8_0, Q4_0, Q4_K; w_row_stride_bytes
+ * apart, 2-byte aligned) -> [n][k] out_type (B2Q_TYPE_F32 or B2Q_TYPE_F16) rows
+ * out_row_stride_bytes apart (16-byte aligned).  Values as ggml's
+ * dequantize_row_*: Q8_0 / Q4_0 fp32(d) * code (Q4_0 code - 8); Q4_K
+ * (d * sc) * q - (dmin * m), each product and the difference rounded once;
+ * F16 by one round-to-nearest-even of that fp32 value.  k % 32 == 0 (Q4_K:
+ * k % 256 == 0).
+ *
+ * b2q_mul_mat_f32: the strict F32 mul_mat, y[m][n] = sum_k x[m][k] * w[n][k]
+ * (+ bias[n], one more rounding: ggml's separate ADD) -- F32 weights (the
+ * as_f32 result) times F32 activations with every product and sum in fp32
+ * (one FMA chain per output, in k order; the CUDA cores, no tensor-core
+ * rounding).  w, x 16-byte aligned with row strides multiples of 16 bytes,
+ * k % 4 == 0; y 4-byte aligned.  The as_f16 form is b2q_dequantize(...,
+ * B2Q_TYPE_F16, ...) followed by b2q_mul_mat with wtype B2Q_TYPE_F16. */
+B2Q_API int b2q_dequantize(int wtype, const void* w, int64_t w_row_stride_bytes, int64_t n, int64_t k,
+                           int out_type, void* out, int64_t out_row_stride_bytes, void* stream);
+B2Q_API int b2q_mul_mat_f32(const float* w, int64_t w_row_stride_bytes, int64_t n, int64_t k, const float* x,
+                            int64_t x_row_stride_bytes, int64_t m, const float* bias, float* y,
+                            int64_t y_row_stride_bytes, void* stream);
+
 /* ------------------------------------------- column-parallel form (multi-GPU)
  * One rank of a tensor-parallel group for a single large mul_mat (the SLat
  * flow transformer's linears at 8k-20k tokens): the weight is split by output
@@ -377,6 +404,25 @@ B2Q_API int b2q_mul_mat_prepared_peers(const void* packed, int64_t n, int64_t k,
                                        int64_t m, const float* bias, float* const* y_peers,
                                        int n_peers, int64_t y_col0, int64_t y_row_stride_bytes,
                                        void* stream);
+
+/* Column-parallel form of b2q_mul_mat_prepared_gelu_q8: the exchange is the
+ * next layer's Q8_0 input (1.125 bytes per value over NVLink instead of 4).
+ * This rank holds the packed rows [col0, col0 + n) of the weight (n and col0
+ * multiples of 32, col0 + n <= n_total); it writes quantize_q8_0(gelu(w.x +
+ * bias)) of those output columns, which are the next layer's activation
+ * columns [col0, col0 + n), into EVERY rank's prepared-activation buffer:
+ * act_peers[q] (n_peers <= 8 device pointers, 256-byte aligned, each
+ * act_bytes >= b2q_act_prepared_size(m, n_total) long, this rank's own and
+ * its peers' CUDA-IPC mappings).  Once every rank's kernel is complete each
+ * buffer holds b2q_act_prepare(gelu(x . W^T + b)) of the whole weight,
+ * bit-identical to the single-GPU b2q_mul_mat_prepared_gelu_q8; the next
+ * mul_mat reads it directly.  Launch only: the ranks synchronise before any
+ * rank reads the buffers.  No counterpart in the reference (one process per
+ * GPU, no tensor parallelism). */
+B2Q_API int b2q_mul_mat_prepared_gelu_q8_peers(const void* packed, int64_t n, int64_t k, const void* act,
+                                               int64_t m, const float* bias, void* const* act_peers,
+                                               int n_peers, int64_t n_total, int64_t col0, size_t act_bytes,
+                                               int variant, void* stream);
 
 /* ------------------------------------------------------------ debug / check
  * int32 per-block dot products S_b computed by the tensor-core GEMM itself

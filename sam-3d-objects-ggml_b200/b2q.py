@@ -91,6 +91,10 @@ def _lib_obj():
             "b2q_norm_modulate_q8": (I, [P, I64, I64, I64, ctypes.c_float, P, P, I, P, SZ, P]),
             "b2q_mul_mat_prepared_peers": (I, [P, I64, I64, P, I64, P, ctypes.POINTER(ctypes.c_void_p), I, I64,
                                                I64, P]),
+            "b2q_mul_mat_prepared_gelu_q8_peers": (I, [P, I64, I64, P, I64, P, ctypes.POINTER(ctypes.c_void_p), I,
+                                                       I64, I64, SZ, I, P]),
+            "b2q_dequantize": (I, [I, P, I64, I64, I64, I, P, I64, P]),
+            "b2q_mul_mat_f32": (I, [P, I64, I64, I64, P, I64, I64, P, P, I64, P]),
             "b2q_block_dots": (I, [I, P, I64, I64, I64, P, I64, I64, P, P, SZ, P]),
             "b2q_block_dots_workspace_size": (SZ, [I64, I64, I64]),
             "b2q_mul_mat_q_simt": (I, [I, P, I64, I64, I64, P, I64, I64, P, I64, P]),
@@ -322,6 +326,46 @@ def mul_mat_prepared_peers(packed, n: int, k: int, act, m: int, y_peers, y_col0:
     rc = lib().b2q_mul_mat_prepared_peers(_ptr(packed), n, k, _ptr(act), m, _ptr(bias), arr, len(y_peers),
                                           y_col0, y_row_stride_bytes, _stream(stream))
     _check("b2q_mul_mat_prepared_peers", rc)
+
+
+def mul_mat_prepared_gelu_q8_peers(packed, n: int, k: int, act, m: int, act_peers, n_total: int, col0: int,
+                                   act_bytes: int, bias=None, variant: int = ACT_X86, stream=None):
+    """Column-parallel GELU + Q8_0: this rank's weight rows [col0, col0 + n)
+    quantized straight into every prepared-activation buffer of act_peers (a
+    list of device addresses, each laid out for [m, n_total])."""
+    arr = (ctypes.c_void_p * len(act_peers))(*[int(p) for p in act_peers])
+    rc = lib().b2q_mul_mat_prepared_gelu_q8_peers(_ptr(packed), n, k, _ptr(act), m, _ptr(bias), arr,
+                                                  len(act_peers), n_total, col0, act_bytes, variant,
+                                                  _stream(stream))
+    _check("b2q_mul_mat_prepared_gelu_q8_peers", rc)
+
+
+def dequantize(wtype: int, w, k: int, out_type: int = TYPE_F32, out=None, stream=None):
+    """GGUF rows uint8 [N, >= row bytes] (device) -> fp32 (or fp16) [N, k]:
+    the reference's as_f32 / as_f16 cast of a quantized weight."""
+    torch = _torch()
+    n = w.shape[0]
+    dt = torch.float32 if out_type == TYPE_F32 else torch.float16
+    if out is None:
+        out = torch.empty((n, k), dtype=dt, device=w.device)
+    rc = lib().b2q_dequantize(wtype, _ptr(w), w.stride(0), n, k, out_type, _ptr(out),
+                              out.stride(0) * out.element_size(), _stream(stream))
+    _check("b2q_dequantize", rc)
+    return out
+
+
+def mul_mat_f32(w, x, bias=None, out=None, stream=None):
+    """Strict F32 mul_mat: fp32 w [N, K] (the as_f32 weight) x fp32 x [M, K]
+    -> fp32 [M, N] (+ bias), every product and sum in fp32."""
+    torch = _torch()
+    n, k = w.shape
+    m = x.shape[0]
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=x.device)
+    rc = lib().b2q_mul_mat_f32(_ptr(w), w.stride(0) * 4, n, k, _ptr(x), x.stride(0) * 4, m, _ptr(bias), _ptr(out),
+                               out.stride(0) * 4, _stream(stream))
+    _check("b2q_mul_mat_f32", rc)
+    return out
 
 
 def act_prepared_size(m: int, k: int) -> int:

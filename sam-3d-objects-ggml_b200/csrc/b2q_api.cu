@@ -939,6 +939,83 @@ int b2q_mul_mat_prepared_peers(const void* packed, int64_t n, int64_t k, const v
   return from_cuda(launch_gemm_tc(g, sms, static_cast<cudaStream_t>(stream)));
 }
 
+int b2q_mul_mat_prepared_gelu_q8_peers(const void* packed, int64_t n, int64_t k, const void* act, int64_t m,
+                                       const float* bias, void* const* act_peers, int n_peers, int64_t n_total,
+                                       int64_t col0, size_t act_bytes, int variant, void* stream) {
+  if (n < 0 || m < 0 || k <= 0 || k % kQK != 0 || n % kQK != 0) return B2Q_ERR_INVALID_ARG;
+  if (col0 < 0 || col0 % kQK != 0 || n_total % kQK != 0 || col0 + n > n_total) return B2Q_ERR_INVALID_ARG;
+  if (n > INT_MAX || m > INT_MAX || k > INT_MAX || n_total > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (variant != B2Q_ACT_X86 && variant != B2Q_ACT_REF) return B2Q_ERR_INVALID_ARG;
+  if (n_peers < 1 || n_peers > kMaxPeers || !act_peers) return B2Q_ERR_INVALID_ARG;
+  if (m > 0 && n > 0 && (!packed || !act)) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(packed, 256) || !aligned(act, 256) || (bias && !aligned(bias, 4))) return B2Q_ERR_MISALIGNED;
+  for (int q = 0; q < n_peers; ++q) {
+    if (!act_peers[q]) return B2Q_ERR_INVALID_ARG;
+    if (!aligned(act_peers[q], 256)) return B2Q_ERR_MISALIGNED;
+  }
+  if (n > 0 && act_bytes < split_bytes(m, n_total)) return B2Q_ERR_WORKSPACE;
+  if (m == 0 || n == 0) return B2Q_OK;
+  int sms = 0;
+  if (int rc = check_device(&sms)) return rc;
+  // Every rank's buffer has the same split layout [m][n_total]: one pair of
+  // offsets from the buffer base serves them all.
+  uint8_t* base0 = static_cast<uint8_t*>(act_peers[0]);
+  const SplitOperand out = split_at(base0, m, n_total);
+  GemmArgs g;
+  g.w = split_at(static_cast<uint8_t*>(const_cast<void*>(packed)), n, k);
+  g.a = split_at(static_cast<uint8_t*>(const_cast<void*>(act)), m, k);
+  g.M = m;
+  g.N = n;
+  g.K = k;
+  g.y = nullptr;
+  g.ldy = 0;
+  g.bias = bias;
+  g.dots = nullptr;
+  g.n_peers = n_peers;
+  for (int q = 0; q < n_peers; ++q) g.y_peer[q] = static_cast<float*>(act_peers[q]);
+  g.q_peers = true;
+  g.q_k = n_total;
+  g.q_ld = out.ld;
+  g.q_code_off = reinterpret_cast<const uint8_t*>(out.codes) - base0 + col0;
+  g.q_scale_off = reinterpret_cast<const uint8_t*>(out.scales + (col0 / kQK) * out.ld) - base0;
+  g.q_variant = variant;
+  return from_cuda(launch_gemm_tc(g, sms, static_cast<cudaStream_t>(stream)));
+}
+
+int b2q_dequantize(int wtype, const void* w, int64_t w_row_stride_bytes, int64_t n, int64_t k, int out_type,
+                   void* out, int64_t out_row_stride_bytes, void* stream) {
+  if (wtype != B2Q_TYPE_Q8_0 && wtype != B2Q_TYPE_Q4_0 && wtype != B2Q_TYPE_Q4_K) return B2Q_ERR_UNSUPPORTED;
+  if (out_type != B2Q_TYPE_F32 && out_type != B2Q_TYPE_F16) return B2Q_ERR_UNSUPPORTED;
+  const int64_t unit = wtype == B2Q_TYPE_Q4_K ? kQKK : kQK;
+  const int64_t esz = out_type == B2Q_TYPE_F32 ? 4 : 2;
+  if (n < 0 || k <= 0 || k % unit != 0) return B2Q_ERR_INVALID_ARG;
+  if (w_row_stride_bytes < raw_row_bytes(wtype, k) || out_row_stride_bytes < k * esz) return B2Q_ERR_INVALID_ARG;
+  if (n > 0 && (!w || !out)) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(w, 2) || w_row_stride_bytes % 2 != 0 || !aligned(out, 16) || out_row_stride_bytes % 16 != 0)
+    return B2Q_ERR_MISALIGNED;
+  if (n == 0) return B2Q_OK;
+  if (int rc = check_device(nullptr)) return rc;
+  return from_cuda(launch_dequantize(wtype, w, w_row_stride_bytes, n, k, out_type == B2Q_TYPE_F16, out,
+                                     out_row_stride_bytes / esz, static_cast<cudaStream_t>(stream)));
+}
+
+int b2q_mul_mat_f32(const float* w, int64_t w_row_stride_bytes, int64_t n, int64_t k, const float* x,
+                    int64_t x_row_stride_bytes, int64_t m, const float* bias, float* y, int64_t y_row_stride_bytes,
+                    void* stream) {
+  if (n < 0 || m < 0 || k <= 0 || k % 4 != 0) return B2Q_ERR_INVALID_ARG;
+  if (w_row_stride_bytes < k * 4 || x_row_stride_bytes < k * 4 || y_row_stride_bytes < n * 4)
+    return B2Q_ERR_INVALID_ARG;
+  if (m > 0 && n > 0 && (!w || !x || !y)) return B2Q_ERR_INVALID_ARG;
+  if (!aligned(w, 16) || !aligned(x, 16) || w_row_stride_bytes % 16 != 0 || x_row_stride_bytes % 16 != 0 ||
+      !aligned(y, 4) || y_row_stride_bytes % 4 != 0 || (bias && !aligned(bias, 4)))
+    return B2Q_ERR_MISALIGNED;
+  if (m == 0 || n == 0) return B2Q_OK;
+  if ((m + 127) / 128 > 65535) return B2Q_ERR_TOO_LARGE;
+  if (int rc = check_device(nullptr)) return rc;
+  return from_cuda(launch_sgemm(x, x_row_stride_bytes / 4, m, w, w_row_stride_bytes / 4, n, k, bias, y,
+                                y_row_stride_bytes / 4, static_cast<cudaStream_t>(stream)));
+}
+
 size_t b2q_block_dots_workspace_size(int64_t m, int64_t n, int64_t k) {
   if (m < 0 || n < 0 || k <= 0 || k % kQK != 0) return 0;
   return split_bytes(m, k) + split_bytes(n, k);

@@ -280,7 +280,7 @@ __device__ __forceinline__ float fa_ex2(float x) {
 __device__ __forceinline__ bool fa_o_update(float (&o)[kFaD + 1], int u, float alpha, uint32_t tpv, uint64_t* pv_full,
                                             uint64_t* pv_empty, unsigned int* status, volatile int* abort_flag,
                                             int lane) {
-  if (!mbar_wait(pv_full, u & 1u, status, kDevWaitEpilogue, abort_flag)) return false;
+  if (!__all_sync(0xffffffffu, mbar_wait(pv_full, u & 1u, status, kDevWaitEpilogue, abort_flag))) return false;
   tc_fence_after();
   uint32_t r[kFaD + 8];
   tmem_ld_32x32b_x32(tpv, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
@@ -295,14 +295,37 @@ __device__ __forceinline__ bool fa_o_update(float (&o)[kFaD + 1], int u, float a
   return true;
 }
 
-// ex2 of two fp32 values as one fp16x2 MUFU operation: the inputs are rounded to
-// fp16 first (P is fp16 anyway; the largest p, at x - m near 0, keep their
-// precision), two results per instruction.
+// exp2 of two fp32 arguments, each rounded once to fp16 (P's type for the P V
+// MMA).  The argument stays fp32: an fp16 argument near -10 carries an absolute
+// error of 2^-8, 0.3% in p, six times the fp16 rounding of the result.
 __device__ __forceinline__ uint32_t fa_ex2_h2(float a, float b) {
-  const __half2 x = __floats2half2_rn(a, b);
-  uint32_t y;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(*reinterpret_cast<const uint32_t*>(&x)));
-  return y;
+  const __half2 y = __floats2half2_rn(fa_ex2(a), fa_ex2(b));
+  return *reinterpret_cast<const uint32_t*>(&y);
+}
+
+// exp2 of an fp32 pair on the FMA pipe (the MUFU pipe is the softmax's
+// bottleneck), rounded to fp16 like fa_ex2_h2.  Cody-Waite reduction
+// 2^x = 2^n * 2^f with n = rint(x), f = x - n in [-0.5, 0.5]; 2^f by a cubic
+// fitted here for least maximum relative error on [-0.5, 0.5] (Lawson's
+// reweighted least squares on Chebyshev nodes): 7.5e-5 at most, under half
+// an fp16 ulp (2^-12).  x <= 0 always (scores minus the row max); x is
+// clamped at -125 so 2^n stays a normal exponent, and 2^-125 rounds to fp16 0
+// as the -inf of a masked key does.
+__device__ __forceinline__ uint32_t fa_ex2_poly_h2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: x + kRound holds rint(x) in its low mantissa bits
+  const float2 one = make_float2(1.0f, 1.0f), neg = make_float2(-1.0f, -1.0f);
+  x = make_float2(fmaxf(x.x, -125.0f), fmaxf(x.y, -125.0f));
+  const float2 r = ffma2(x, one, make_float2(kRound, kRound));
+  const float2 n = ffma2(r, one, make_float2(-kRound, -kRound));
+  const float2 f = ffma2(n, neg, x);
+  float2 q = ffma2(make_float2(0.0551716685f, 0.0551716685f), f, make_float2(0.242611140f, 0.242611140f));
+  q = ffma2(q, f, make_float2(0.693260968f, 0.693260968f));
+  q = ffma2(q, f, make_float2(0.999928057f, 0.999928057f));
+  // 2^n: n (two's complement in r's low bits) added to q's exponent field.
+  const float ya = __uint_as_float(__float_as_uint(q.x) + (__float_as_uint(r.x) << 23));
+  const float yb = __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(r.y) << 23));
+  const __half2 y = __floats2half2_rn(ya, yb);
+  return *reinterpret_cast<const uint32_t*>(&y);
 }
 
 // Shared-memory descriptor for an MN-major operand with the 128-byte swizzle
@@ -318,6 +341,8 @@ __device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t addr, uint32_t l
   return d;
 }
 
+// EMU: of every 4 exp pairs, how many run as the FMA-pipe polynomial.
+template <int EMU>
 __global__ void __launch_bounds__(kFaThreads, 1)
     attention_f16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_k2,
@@ -489,12 +514,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       float m = -INFINITY, alpha_prev = 0.0f;
       bool ok = true;
       uint8_t* prow = smem + FaSmem::P + 2 * i * kFaTile + (row >> 3) * 1024 + (row & 7) * 128;
-      for (int t = 0; t < ntiles; ++t) {
+      for (int t = 0; t < ntiles && ok; ++t) {
         const uint32_t par = t & 1u;
-        if (!mbar_wait(&s_full[i], par, status, kDevWaitEpilogue, abort_flag)) {
-          ok = false;
-          break;
-        }
+        ok = __all_sync(0xffffffffu, mbar_wait(&s_full[i], par, status, kDevWaitEpilogue, abort_flag));
+        if (!ok) break;
         tc_fence_after();
         uint32_t sr[kFaBN];
 #pragma unroll
@@ -502,10 +525,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&s_empty[i]);
+        if (lane == 0) mbar_arrive(&s_empty[i]);  // S_i is free for the next key tile's Q K^T
         const bool second = t >= p.n1;
-        const int64_t k0 = static_cast<int64_t>(second ? t - p.n1 : t) * kFaBN;
-        const int64_t valid64 = (second ? p.Tk2 : p.Tk) - k0;
+        const int64_t valid64 = (second ? p.Tk2 : p.Tk) - static_cast<int64_t>(second ? t - p.n1 : t) * kFaBN;
         if (valid64 < kFaBN) {  // a partial last tile of its source: the missing keys score -inf
 #pragma unroll
           for (int c = 0; c < kFaBN; ++c)
@@ -523,17 +545,20 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         const float m_new = fmaxf(m, __fmul_rn(mx, p.c2));
         const float alpha = fa_ex2(m - m_new);
-        const float nm = -m_new;
-        // exp2 of the whole row into packed fp16 registers first; only the
-        // stores wait for P_i to be free (the previous key tile's P V MMA).
+        // exp2 of the whole row into packed fp16 registers, EMU of every 4
+        // pairs on the FMA pipe; only the stores wait for P_i to be free (the
+        // previous key tile's P V MMA).
         uint32_t pk[kFaBN / 2];
+        {
+          const float2 c2 = make_float2(p.c2, p.c2), nm = make_float2(-m_new, -m_new);
 #pragma unroll
-        for (int c = 0; c < kFaBN; c += 2)
-          pk[c >> 1] = fa_ex2_h2(__fmaf_rn(__uint_as_float(sr[c]), p.c2, nm), __fmaf_rn(__uint_as_float(sr[c + 1]), p.c2, nm));
-        if (!mbar_wait(&p_empty[i], par ^ 1u, status, kDevWaitEpilogue, abort_flag)) {
-          ok = false;
-          break;
+          for (int c = 0; c < kFaBN; c += 2) {
+            const float2 x = ffma2(make_float2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), c2, nm);
+            pk[c >> 1] = (EMU > 0 && ((c >> 1) & 3) < EMU) ? fa_ex2_poly_h2(x) : fa_ex2_h2(x.x, x.y);
+          }
         }
+        ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[i], par ^ 1u, status, kDevWaitEpilogue, abort_flag));
+        if (!ok) break;
 #pragma unroll
         for (int c = 0; c < kFaBN; c += 8) {
           const int panel = c >> 6, chunk = (c & 63) >> 3;
@@ -544,10 +569,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[i]);
         m = m_new;
-        if (t >= 1 && !fa_o_update(o, t - 1, alpha_prev, tpv, &pv_full[i], &pv_empty[i], status, abort_flag, lane)) {
-          ok = false;
-          break;
-        }
+        if (t >= 1) ok = fa_o_update(o, t - 1, alpha_prev, tpv, &pv_full[i], &pv_empty[i], status, abort_flag, lane);
         alpha_prev = alpha;
       }
       if (ok && ntiles > 0) ok = fa_o_update(o, ntiles - 1, alpha_prev, tpv, &pv_full[i], &pv_empty[i], status,
@@ -616,6 +638,8 @@ cudaError_t launch_attention_f16(const void* q, const void* k, const void* v, co
   p.c2 = scale * 1.4426950408889634f;  // log2(e)
   p.o = static_cast<__half*>(o);
   p.ldo = ldo_halves;
+  // A quarter of the exps on the FMA pipe.
+  constexpr auto kernel = attention_f16_kernel<1>;
   static bool attr_set[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
@@ -624,16 +648,16 @@ cudaError_t launch_attention_f16(const void* q, const void* k, const void* v, co
     // The register split needs the kernel compiled at exactly kFaLaunchRegs, or
     // setmaxnreg.inc could wait for registers that do not exist.
     cudaFuncAttributes fa;
-    cudaError_t e = cudaFuncGetAttributes(&fa, attention_f16_kernel);
+    cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
     if (e != cudaSuccess) return e;
     if (fa.numRegs != kFaLaunchRegs) return cudaErrorInvalidConfiguration;
-    e = cudaFuncSetAttribute(attention_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FaSmem::BYTES);
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FaSmem::BYTES);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
   const dim3 grid(static_cast<unsigned>((Tq + 2 * kFaBM - 1) / (2 * kFaBM)), static_cast<unsigned>(H),
                   static_cast<unsigned>(B));
-  attention_f16_kernel<<<grid, kFaThreads, FaSmem::BYTES, s>>>(tq, tk, tv, tk2, tv2, p);
+  kernel<<<grid, kFaThreads, FaSmem::BYTES, s>>>(tq, tk, tv, tk2, tv2, p);
   return cudaGetLastError();
 }
 

@@ -140,6 +140,7 @@ enum Mode : int {
   kModeStall = 3,   // failure-path self-test: the producer withholds every stage
   kModeGeluQ8 = 4,  // fused GELU + Q8_0 quantize of the output (next layer's input)
   kModeGateRes = 5, // y = resid + gate * (w . x + bias): the DiT branch's gated residual
+  kModeGeluQ8Peers = 6,  // column-parallel GELU + Q8_0: the quantized tile goes into every rank's activations
 };
 
 // Output arguments of the non-plain variants, a separate kernel parameter:
@@ -151,7 +152,11 @@ enum Mode : int {
 //          mul_mat's activations: codes q_codes[m * q_k + n], scales
 //          q_scales[(n / 32) * q_ld + m];
 //   gate+residual: y[m * ldy + n] = resid[m * ldr + n] + gate[n] * (w . x + bias)[m][n],
-//          each step rounded as ggml's separate mul and add (gate may be null).
+//          each step rounded as ggml's separate mul and add (gate may be null);
+//   gelu+q8 peers: as gelu+q8, into every rank's split activation buffer:
+//          codes at ptr[q] + q_code_off (this rank's first column of the next
+//          layer's K), scales at ptr[q] + q_scale_off (its first scale row),
+//          codes row pitch q_k = the whole next-layer K.
 struct OutParams {
   int n;
   int64_t col0;
@@ -163,6 +168,7 @@ struct OutParams {
   const float* gate;
   const float* resid;
   int64_t ldr;
+  int64_t q_code_off, q_scale_off;
 };
 
 // Shared-memory descriptor for the constant offset tile: K-major, no swizzle,
@@ -246,9 +252,10 @@ __device__ __forceinline__ bool epi_block(uint32_t (&cur)[COLS], float2 (&acc)[C
 // which lane c holds the whole block of column CB+c and quantizes it exactly as
 // the stand-alone quantizer does: fmaxf absmax from 0, one scale, 32 codes as
 // two 16-byte stores, and the lanes' scales as one coalesced store.
-template <int VARIANT, int CB, int W, int NACC>
+template <int VARIANT, int CB, int W, bool PQ, int NACC>
 __device__ __forceinline__ void geluq_chunk(const float2 (&acc)[NACC], float bv, bool has_bias, int64_t m0,
-                                            int64_t M, int lane, int8_t* codes, int64_t q_k, float* qs, float* xp) {
+                                            int64_t M, int lane, int8_t* codes, int64_t q_k, float* qs, float* xp,
+                                            const OutParams& pp, int64_t nq) {
 #pragma unroll
   for (int c = 0; c < W; ++c) {
     const float v = ((CB + c) & 1) ? acc[(CB + c) / 2].y : acc[(CB + c) / 2].x;
@@ -271,19 +278,36 @@ __device__ __forceinline__ void geluq_chunk(const float2 (&acc)[NACC], float bv,
     for (int i = 0; i < 8; ++i)
       q[i] = quantize_code<VARIANT>(z[4 * i], inv) | (quantize_code<VARIANT>(z[4 * i + 1], inv) << 8) |
              (quantize_code<VARIANT>(z[4 * i + 2], inv) << 16) | (quantize_code<VARIANT>(z[4 * i + 3], inv) << 24);
-    uint4* dst = reinterpret_cast<uint4*>(codes + m * q_k);
-    dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
-    dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
-    qs[m] = q8_split_scale(d);
+    if constexpr (!PQ) {
+      uint4* dst = reinterpret_cast<uint4*>(codes + m * q_k);
+      dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
+      dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
+      qs[m] = q8_split_scale(d);
+    } else {
+      // The same 36 bytes into every rank's activations (NVLink stores for the
+      // peers): the exchange is the next layer's Q8_0 input, not fp32.
+      const float sc = q8_split_scale(d);
+#pragma unroll
+      for (int r = 0; r < kMaxPeers; ++r) {  // static indices: the pointers stay in the param bank
+        if (r >= pp.n) break;
+        uint8_t* base = reinterpret_cast<uint8_t*>(pp.ptr[r]);
+        uint4* dst = reinterpret_cast<uint4*>(base + pp.q_code_off + nq + m * q_k);
+        dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
+        dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
+        reinterpret_cast<float*>(base + pp.q_scale_off)[(nq / kQK) * pp.q_ld + m] = sc;
+      }
+    }
   }
   __syncwarp();
 }
 
-template <int VARIANT, int COLS, int NACC>
+template <int VARIANT, int COLS, bool PQ, int NACC>
 __device__ __forceinline__ void geluq_cols(const float2 (&acc)[NACC], float bv, bool has_bias, int64_t m0, int64_t M,
-                                           int lane, int8_t* codes, int64_t q_k, float* qs, float* xp) {
-  geluq_chunk<VARIANT, 0, (COLS < 32 ? COLS : 32)>(acc, bv, has_bias, m0, M, lane, codes, q_k, qs, xp);
-  if constexpr (COLS > 32) geluq_chunk<VARIANT, 32, COLS - 32>(acc, bv, has_bias, m0, M, lane, codes, q_k, qs, xp);
+                                           int lane, int8_t* codes, int64_t q_k, float* qs, float* xp,
+                                           const OutParams& pp, int64_t nq) {
+  geluq_chunk<VARIANT, 0, (COLS < 32 ? COLS : 32), PQ>(acc, bv, has_bias, m0, M, lane, codes, q_k, qs, xp, pp, nq);
+  if constexpr (COLS > 32)
+    geluq_chunk<VARIANT, 32, COLS - 32, PQ>(acc, bv, has_bias, m0, M, lane, codes, q_k, qs, xp, pp, nq);
 }
 
 template <int STAGES, int BN, int MODE, bool Q4C>
@@ -292,7 +316,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ CUtensorMap tm_ws, const __grid_constant__ CUtensorMap tm_as,
                    const TcParams p, const __grid_constant__ OutParams pp) {
   constexpr bool DUMP = MODE == kModeDump, PEERS = MODE == kModePeers, STALL = MODE == kModeStall;
-  constexpr bool GELUQ = MODE == kModeGeluQ8, GATERES = MODE == kModeGateRes;
+  constexpr bool PQ = MODE == kModeGeluQ8Peers;
+  constexpr bool GELUQ = MODE == kModeGeluQ8 || PQ, GATERES = MODE == kModeGateRes;
   using C = Cfg<STAGES, BN, Q4C>;
   constexpr int COLS = C::COLS;
   extern __shared__ uint8_t smem_raw[];
@@ -527,13 +552,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t nq = static_cast<int64_t>(tile % p.n_tiles) * kBM + quarter * 32;
         if (nq < p.N && m0 < p.M) {
           const float bv = p.bias ? p.bias[n] : 0.0f;
-          int8_t* codes = pp.q_codes + nq;
-          float* qs = pp.q_scales + (nq / kQK) * pp.q_ld;
+          int8_t* codes = PQ ? nullptr : pp.q_codes + nq;
+          float* qs = PQ ? nullptr : pp.q_scales + (nq / kQK) * pp.q_ld;
           float* xp = reinterpret_cast<float*>(smem + C::XPOSE_OFF) + (warp - kEpiWarp0) * C::XPOSE_FLOATS;
           if (pp.q_variant == 0)
-            geluq_cols<0, COLS>(acc, bv, p.bias != nullptr, m0, p.M, lane, codes, pp.q_k, qs, xp);
+            geluq_cols<0, COLS, PQ>(acc, bv, p.bias != nullptr, m0, p.M, lane, codes, pp.q_k, qs, xp, pp, nq);
           else
-            geluq_cols<1, COLS>(acc, bv, p.bias != nullptr, m0, p.M, lane, codes, pp.q_k, qs, xp);
+            geluq_cols<1, COLS, PQ>(acc, bv, p.bias != nullptr, m0, p.M, lane, codes, pp.q_k, qs, xp, pp, nq);
         }
       } else if (n < p.N) {
         const float bv = p.bias ? p.bias[n] : 0.0f;
@@ -631,7 +656,7 @@ bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uin
 
 template <int STAGES, int BN, int MODE, bool Q4C>
 cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
-  constexpr bool PEERS = MODE == kModePeers;
+  constexpr bool PEERS = MODE == kModePeers || MODE == kModeGeluQ8Peers;
   using C = Cfg<STAGES, BN, Q4C>;
   const int64_t KB = g.K / kQK;
   CUtensorMap tm_wc, tm_ac, tm_ws, tm_as;
@@ -669,13 +694,15 @@ cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
   pp.q_codes = g.q_codes;
   pp.q_scales = g.q_scales;
   pp.q_ld = g.q_ld;
-  pp.q_k = g.N;
+  pp.q_k = MODE == kModeGeluQ8Peers ? g.q_k : g.N;
+  pp.q_code_off = g.q_code_off;
+  pp.q_scale_off = g.q_scale_off;
   pp.q_variant = g.q_variant;
   pp.gate = g.gate;
   pp.resid = g.resid;
   pp.ldr = g.ldr;
   auto kern = gemm_tc_kernel<STAGES, BN, MODE, Q4C>;
-  constexpr int smem_bytes = MODE == kModeGeluQ8 ? C::SMEM_XPOSE : C::SMEM;
+  constexpr int smem_bytes = (MODE == kModeGeluQ8 || MODE == kModeGeluQ8Peers) ? C::SMEM_XPOSE : C::SMEM;
   static_assert(smem_bytes <= 227 * 1024, "shared memory per CTA");
   // Checked and set once per device (a bit per device; the calls cost more
   // host time than the rest of the launch).
@@ -761,6 +788,10 @@ cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, cudaStream_t s) {
   if (g.q_codes) {
     if (g.N % kQK != 0 || !g.q_scales) return cudaErrorInvalidValue;
     return launch_picked<kModeGeluQ8>(g, num_sms, s);
+  }
+  if (g.q_peers) {  // column-parallel GELU + Q8_0: q_code_off, q_scale_off and q_k describe the buffers
+    if (g.N % kQK != 0 || g.q_k % kQK != 0 || g.n_peers < 1) return cudaErrorInvalidValue;
+    return launch_picked<kModeGeluQ8Peers>(g, num_sms, s);
   }
   // A handful of tokens: the weight streamed once on CUDA cores, same bits.
   if (g.M <= kGemvMaxM && g.n_peers == 0) return launch_gemv(g, s);

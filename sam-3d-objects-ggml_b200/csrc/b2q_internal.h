@@ -155,6 +155,13 @@ cudaError_t launch_attention_f16(const void* q, const void* k, const void* v, co
 // Status word of the attention kernels' bounded waits (its own translation unit).
 cudaError_t read_attention_status(unsigned int* value, bool clear);
 
+// Dequantize-to-float form (b2q_dense_f32.cu): GGUF rows -> fp32 / fp16 rows,
+// and the strict fp32 mul_mat y = x . w^T (+ bias).
+cudaError_t launch_dequantize(int wtype, const void* w, int64_t ldw_bytes, int64_t n, int64_t k, bool f16_out,
+                              void* out, int64_t ldo_elems, cudaStream_t s);
+cudaError_t launch_sgemm(const float* x, int64_t ldx, int64_t m, const float* w, int64_t ldw, int64_t n, int64_t k,
+                         const float* bias, float* y, int64_t ldy, cudaStream_t s);
+
 cudaError_t launch_gelu(const float* x, int64_t rows, int64_t cols, int64_t ldx_floats, float* y,
                         int64_t ldy_floats, cudaStream_t s);
 
@@ -179,6 +186,12 @@ struct GemmArgs {
   float* q_scales = nullptr;
   int64_t q_ld = 0;
   int q_variant = 0;
+  // The same, column-parallel (q_peers): every one of the n_peers split
+  // buffers at y_peer[q] (as bytes) receives this rank's columns; codes at
+  // + q_code_off with row pitch q_k (the whole next-layer K), scales at
+  // + q_scale_off with row stride q_ld.
+  bool q_peers = false;
+  int64_t q_k = 0, q_code_off = 0, q_scale_off = 0;
   // Gated residual epilogue (resid != nullptr): y = resid + gate[n] * (w.x + bias),
   // resid [M][ldr]; gate [N] or nullptr (no gate).
   const float* gate = nullptr;

@@ -1,7 +1,9 @@
-"""Column-parallel mul_mat (b2q_mul_mat_prepared_peers): each rank holds a slice
-of the weight's output rows and its GEMM epilogue writes the slice into every
-rank's full-width output over peer memory.  The GPU case needs two GPUs of one
-box (it is skipped otherwise); the slice plan is checked on CPU."""
+"""Column-parallel mul_mat (b2q_mul_mat_prepared_peers) and its Q8_0-exchange
+form (b2q_mul_mat_prepared_gelu_q8_peers): each rank holds a slice of the
+weight's output rows and its GEMM epilogue writes the slice into every rank's
+full-width output -- fp32, or the next layer's prepared Q8_0 activations --
+over peer memory.  The GPU cases need two GPUs of one box (they are skipped
+otherwise); the slice plan and the entry's argument checks run on CPU."""
 import os
 import socket
 import time
@@ -95,3 +97,102 @@ def test_fused_column_parallel_matches_single_gpu(b2q_mod, M, N, K, wtype):
         for p in ctx.processes:
             if p.is_alive():
                 p.kill()
+
+
+def _rank_main_q8(rank, world, port, M, N, K, wtype):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import b2q
+    from helpers import make_case
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        _, wq, x = make_case(M + N + K + 1, M, N, K, wtype)  # same seed on every rank
+        bias = np.random.default_rng(N + 1).standard_normal(N).astype(np.float32)
+        w_d = torch.from_numpy(np.ascontiguousarray(wq)).to(dev)
+        b_d = torch.from_numpy(bias).to(dev)
+        start, stop = colpar.slices(N, world)[rank]
+        n = stop - start
+        full_packed = b2q.weight_pack(wtype, w_d, K)
+        packed = b2q.weight_pack(wtype, w_d[start:stop], K)
+        act = b2q.act_prepare(torch.from_numpy(x).to(dev))
+        abufs = colpar.activation_buffers(M, N)
+        torch.cuda.synchronize()
+        dist.barrier()
+        colpar.fused_gelu_q8(packed, n, K, act, M, abufs, start, bias=b_d[start:stop])
+        torch.cuda.synchronize()
+        dist.barrier()  # every rank's kernel has finished writing every buffer
+        got = abufs.to_tensor(dev)
+        want = b2q.mul_mat_prepared_gelu_q8(full_packed, N, K, act, M, bias=b_d)
+        torch.cuda.synchronize()
+        gc, gs = colpar.split_views(got, M, N)
+        wc, ws = colpar.split_views(want, M, N)
+        assert torch.equal(gc, wc), "Q8_0 codes differ from the single-GPU GELU + Q8_0 epilogue"
+        assert torch.equal(gs[:, :M], ws[:, :M]), "Q8_0 scales differ from the single-GPU epilogue"
+        # the NCCL baseline moves the same bytes to the same places
+        local = b2q._empty_aligned(b2q.act_prepared_size(M, n), dev)
+        gcodes = torch.empty((world * M, n), dtype=torch.int8, device=dev)
+        ld = (M + 3) // 4 * 4
+        gscales = torch.empty((world * (n // 32), ld), dtype=torch.float32, device=dev)
+        out = b2q._empty_aligned(b2q.act_prepared_size(M, N), dev)
+        colpar.nccl_baseline_gelu_q8(packed, n, K, act, M, N, local, gcodes, gscales, out, bias=b_d[start:stop])
+        torch.cuda.synchronize()
+        oc, osc = colpar.split_views(out, M, N)
+        assert torch.equal(oc, wc) and torch.equal(osc[:, :M], ws[:, :M])
+        assert b2q.device_status(clear=True) == 0
+        dist.barrier()
+        abufs.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K,wtype", [(300, 256, 512, 2), (129, 1024, 1024, 8), (2048, 4096, 1024, 2)])
+def test_q8_exchange_column_parallel_matches_single_gpu(b2q_mod, M, N, K, wtype):
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs of one box")
+    world = 2
+    ctx = mp.start_processes(_rank_main_q8, args=(world, _free_port(), M, N, K, wtype), nprocs=world,
+                             join=False, start_method="spawn")
+    deadline = time.time() + 240
+    try:
+        while not ctx.join(timeout=5):
+            if time.time() > deadline:
+                raise TimeoutError("column-parallel ranks did not finish")
+    finally:
+        for p in ctx.processes:
+            if p.is_alive():
+                p.kill()
+
+
+INVALID_ARG = 1
+
+
+@pytest.mark.parametrize("n,n_total,col0,expect", [
+    (64, 256, 16, INVALID_ARG),   # col0 not a whole Q8_0 block
+    (48, 256, 0, INVALID_ARG),    # slice not a whole number of blocks
+    (64, 100, 64, INVALID_ARG),   # next-layer K not a whole number of blocks
+    (128, 192, 128, INVALID_ARG),  # slice runs past the next-layer K
+])
+def test_q8_exchange_rejects_bad_slices(b2q_mod, n, n_total, col0, expect):
+    import ctypes
+    lib = b2q_mod.lib()
+    arr = (ctypes.c_void_p * 1)(256)
+    rc = lib.b2q_mul_mat_prepared_gelu_q8_peers(256, n, 64, 256, 8, None, arr, 1, n_total, col0, 1 << 20,
+                                                b2q_mod.ACT_X86, None)
+    assert rc == expect
+
+
+def test_q8_exchange_rejects_too_many_peers(b2q_mod):
+    import ctypes
+    lib = b2q_mod.lib()
+    arr = (ctypes.c_void_p * 9)(*([256] * 9))
+    rc = lib.b2q_mul_mat_prepared_gelu_q8_peers(256, 64, 64, 256, 8, None, arr, 9, 256, 0, 1 << 20,
+                                                b2q_mod.ACT_X86, None)
+    assert rc == INVALID_ARG

@@ -130,8 +130,9 @@ def reference_forward(blk, x, B: int, T: int, cond, n_cond: int):
 
     def attend(q, k, vv):
         s = q @ k.transpose(0, 1, 3, 2) / np.sqrt(D)
-        s = np.exp(s - s.max(-1, keepdims=True))
-        o = (s / s.sum(-1, keepdims=True)) @ vv
+        # the flash kernel's P operand is fp16; its row sum adds those fp16 values
+        s = np.exp(s - s.max(-1, keepdims=True)).astype(np.float16).astype(np.float64)
+        o = (s @ vv) / s.sum(-1, keepdims=True)
         return o.astype(np.float16).astype(np.float32).transpose(0, 2, 1, 3).reshape(-1, C)
 
     q, k, vv = heads(qkv[:, :C], v["gq"]), heads(qkv[:, C:2 * C], v["gk"]), heads(qkv[:, 2 * C:], None)

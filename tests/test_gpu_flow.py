@@ -11,7 +11,12 @@ import ss_flow
 
 CFG = dict(C=256, heads=4, n_blocks=2, n_shape=64, in_ch=8, mlp_ratio=4)
 N_COND = 40
-TOL = 3e-3  # fp16 attention cores (both sides round q, k, v and o to fp16)
+TOL = 3e-3  # fp16 attention cores (both sides round q, k, v, P and o to fp16)
+# The pose outputs are 2 values each after a Q8_0 linear: one code flip moves
+# them by ~0.4%.  The CPU graph itself moves translation_scale by 3.7e-3 between
+# fp16 and fp32 attention cores (q, k, v, o rounding only), so their bar sits
+# above that sensitivity.
+POSE_TOL = 1e-2
 
 
 def make_params(wtype, seed=0, cfg=None):
@@ -67,7 +72,9 @@ def cpu_forward(p, wtype, xs, xp, t, d, cond, B, cfg=None, n_cond=None, attn="f1
     def attend(q, k, v):
         s = q @ k.transpose(0, 1, 3, 2) / np.sqrt(D)
         s = np.exp(s - s.max(-1, keepdims=True))
-        o = (s / s.sum(-1, keepdims=True)) @ v
+        if attn == "f16":  # the flash kernel's P operand is fp16; its row sum adds those fp16 values
+            s = rnd(s)
+        o = (s @ v) / s.sum(-1, keepdims=True)
         return rnd(o).astype(f32).transpose(0, 2, 1, 3).reshape(-1, C)
 
     for i in range(nb):
@@ -131,7 +138,7 @@ def test_flow_forward_matches_cpu_graph(b2q_mod, dev, wtype):
     rs, rp = cpu_forward(p, wtype, xs, xp, t_model, d, cond2, B)
     assert rel(vs.cpu().numpy(), rs) <= TOL
     for m, _ in ss_flow.POSE:
-        assert rel(vp[m].cpu().numpy(), rp[m]) <= TOL, m
+        assert rel(vp[m].cpu().numpy(), rp[m]) <= POSE_TOL, m
     assert b2q.device_status() == 0
 
 
