@@ -416,6 +416,7 @@ def run_gpu(args, rank, world, local_rank):
         result["ss_step"] = ss_step_side(b2q, stream, dev, cpu=(rank == 0 and world == 1 and not args.no_cpu_baseline))
         result["slat_linears"] = slat_side(b2q, stream, dev)
         result["f16"] = f16_side(b2q, flush, stream, dev, peaks)
+        result["attention"] = attention_side(b2q, stream, dev, peaks)
         result["slat_sparse"] = slat_sparse_side(b2q, flush, stream, dev, peaks)
     if not args.only and not args.no_colpar:
         result["colpar"] = colpar_side(args, rank, world, dev, dist)
@@ -830,6 +831,91 @@ def ss_step_side(b2q, stream, dev, cpu=False, iters=5):
 
 
 F16_CASES = {"f16_fc1": (4096, 4096, 1024), "f16_fc2": (4096, 1024, 4096)}
+# SS block attention cores (B = 2 CFG branches, 16 heads, D = 64): self over the
+# 4096 shape tokens, cross to the 1374 condition tokens.
+ATTN_CASES = {"attn_self": (2, 16, 4096, 4096), "attn_cross": (2, 16, 4096, 1374)}
+
+
+def _attn_inputs(dev, B, H, Tq, Tk, seed=41):
+    import torch
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.randn(B, H, Tq, 64, device=dev, generator=gen).half()
+    k = torch.randn(B, H, Tk, 64, device=dev, generator=gen).half()
+    v = torch.randn(B, H, Tk, 64, device=dev, generator=gen).half()
+    o = torch.empty(B * Tq, H * 64, device=dev, dtype=torch.half)
+    return q, k, v, o
+
+
+def run_attn_case(args):
+    """Profiling case: --steps b2q_attention_f16 calls of one shape (after
+    --warmup); prints the median CUDA-event time per call."""
+    import torch
+    import b2q
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, H, Tq, Tk = ATTN_CASES[args.only]
+    q, k, v, o = _attn_inputs(dev, B, H, Tq, Tk)
+    for _ in range(args.warmup):
+        b2q.attention_f16(q, k, v, out=o)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for e0, e1 in evs:
+        e0.record()
+        b2q.attention_f16(q, k, v, out=o)
+        e1.record()
+    torch.cuda.synchronize()
+    us = statistics.median(e0.elapsed_time(e1) for e0, e1 in evs) * 1e3
+    flops = 4.0 * B * H * Tq * Tk * 64
+    return {"case": args.only, "B": B, "H": H, "Tq": Tq, "Tk": Tk, "D": 64, "us_median_hot_l2": round(us, 2),
+            "tflops": round(flops / (us * 1e-6) / 1e12, 1), "launches_per_call": 1,
+            "device_status": b2q.device_status(clear=True)}
+
+
+def attention_side(b2q, stream, dev, peaks, iters=20):
+    """The SS block's attention cores on their own: b2q_attention_f16 (tcgen05
+    S = Q K^T and P V, fp16 P, fp32 softmax) against torch SDPA on the same
+    fp16 tensors (cuDNN's flash kernel, the library path it replaces).  Both are
+    timed as CUDA-graph replays of `iters` calls, so host launch cost (SDPA's is
+    above its kernel time) is out of both numbers.  Inputs (q 16 MB, k / v up
+    to 16 MB each) stay in L2 between calls, as they do in the block."""
+    import torch
+    out = {"kernel": "attention_f16_kernel (tcgen05 kind::f16, fp32 TMEM S, fp16 P in smem, 1/4 of the exps "
+                     "on the FMA pipe)", "timing": "CUDA-graph replay of back-to-back calls, both sides",
+           "cases": []}
+
+    def timed(fn):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(iters):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del g
+        return e0.elapsed_time(e1) / iters * 1e3
+    for name, (B, H, Tq, Tk) in ATTN_CASES.items():
+        q, k, v, o = _attn_inputs(dev, B, H, Tq, Tk)
+        mine = timed(lambda: b2q.attention_f16(q, k, v, out=o))
+        sdpa = timed(lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v))
+        flops = 4.0 * B * H * Tq * Tk * 64
+        peak = peaks.get("bf16_tflops")
+        out["cases"].append({"name": name, "B": B, "H": H, "Tq": Tq, "Tk": Tk, "D": 64, "us": round(mine, 2),
+                             "tflops": round(flops / (mine * 1e-6) / 1e12, 1),
+                             "frac_of_measured_bf16": round(flops / (mine * 1e-6) / 1e12 / peak, 4) if peak else None,
+                             "torch_sdpa_us": round(sdpa, 2), "speedup_vs_sdpa": round(sdpa / mine, 3)})
+        del q, k, v, o
+    out["status"] = b2q.device_status(clear=True)
+    return out
 
 
 def run_f16_case(args):
@@ -1389,7 +1475,9 @@ def main():
         if rank == 0:
             print(json.dumps(run_reference(args)), flush=True)
         return
-    if args.only in F16_CASES:
+    if args.only in ATTN_CASES:
+        res = run_attn_case(args)
+    elif args.only in F16_CASES:
         res = run_f16_case(args)
     elif args.only in SPARSE_CASES:
         res = run_sparse_case(args)

@@ -230,16 +230,19 @@ cudaError_t launch_attention_f32_d(const float* q, const float* k, const float* 
 //   warps 2, 3   idle (complete warpgroup 0, which runs on 40 registers)
 //   warpgroups 1 and 2: softmax of query tile 0 and 1 (232 registers each):
 //                thread t owns one query row (its TMEM lane) and reads the row's
-//                128 scores, so the row max and sum need no shuffles (eight
-//                independent chains each); writes P as fp16 into shared memory in
-//                the swizzled K-major layout the P V MMA reads; keeps the fp32
-//                output row in registers (o = o * alpha + P V per tile), so no
-//                TMEM rescale has to be ordered between MMAs.
-// The two warpgroups ping-pong: while one computes its softmax, the tensor core
-// works on the other's tile.  exp2 is the hardware ex2.approx (scores
-// pre-multiplied by scale * log2(e)).  Keys of a partial last tile of a source
-// are masked to -inf.  Every wait is bounded; on give-up the CTA drains and
-// frees TMEM.  A CTA whose second query tile lies wholly past Tq runs one tile.
+//                128 scores, so the row max needs no shuffles (three-input max,
+//                eight independent chains); exp2 of the scores (pre-multiplied
+//                by scale * log2(e)) in fp32, three pairs in four on the MUFU
+//                (ex2.approx) and one on the FMA pipe (fa_ex2_poly_h2), each
+//                rounded once to fp16; writes P into shared memory in the
+//                swizzled K-major layout the P V MMA reads; keeps the fp32 output
+//                row in registers (o = o * alpha + P V per tile), so no TMEM
+//                rescale has to be ordered between MMAs.  The row sum of P comes
+//                out of the P V MMA itself (a constant ones column next to V).
+// While one warpgroup computes its softmax, the tensor core works on the other
+// tile's S and P V.  Keys of a partial last tile of a source are masked to
+// -inf.  Every wait is bounded; on give-up the CTA drains and frees TMEM.  A
+// CTA whose second query tile lies wholly past Tq runs one tile.
 __device__ unsigned int g_attn_status = 0;
 
 constexpr int kFaBM = 128, kFaBN = 128, kFaD = 64, kFaStages = 3;
@@ -269,6 +272,12 @@ struct FaParams {
   int64_t ldo;         // halves
 };
 
+__device__ __forceinline__ float fa_max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ float fa_ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -290,8 +299,14 @@ __device__ __forceinline__ bool fa_o_update(float (&o)[kFaD + 1], int u, float a
   tc_fence_before();
   __syncwarp();
   if (lane == 0) mbar_arrive(pv_empty);
+  const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll
-  for (int d = 0; d <= kFaD; ++d) o[d] = __fmaf_rn(o[d], alpha, __uint_as_float(r[d]));
+  for (int d = 0; d < kFaD; d += 2) {
+    const float2 v = ffma2(make_float2(o[d], o[d + 1]), a2, make_float2(__uint_as_float(r[d]), __uint_as_float(r[d + 1])));
+    o[d] = v.x;
+    o[d + 1] = v.y;
+  }
+  o[kFaD] = __fmaf_rn(o[kFaD], alpha, __uint_as_float(r[kFaD]));
   return true;
 }
 
@@ -449,49 +464,50 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         constexpr uint32_t idesc_qk = idesc_f16(kFaBM, kFaBN);
         constexpr uint32_t idesc_pv = idesc_f16(kFaBM, kFaPvN) | (1u << 16);  // B (V | ones) MN-major
         bool ok = mbar_wait(q_full, 0, status, kDevWaitMma, abort_flag);
+        // S_i(t) = Q_i K(t)^T once the softmax has read S_i(t-1).
+        auto issue_s = [&](int i, int t) {
+          const int st = t % kFaStages;
+          if (!mbar_wait(&s_empty[i], (t & 1u) ^ 1u, status, kDevWaitMma, abort_flag)) return false;
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(smem + FaSmem::KV + 2 * st * kFaTile);
+          const uint32_t q_addr = smem_u32(smem + FaSmem::Q + i * kFaTile);
+#pragma unroll
+          for (int kk = 0; kk < kFaD / 16; ++kk)
+            mma_f16(tmem + kFaSOff + i * kFaBN, smem_desc_k_sw128(q_addr + kk * 32),
+                    smem_desc_k_sw128(k_addr + kk * 32), idesc_qk, kk > 0 ? 1u : 0u);
+          mma_commit(&s_full[i]);
+          return true;
+        };
+        // (P V)_i of key tile u once P_i(u) is stored and (P V)_i(u-1) read.
+        auto issue_pv = [&](int i, int u) {
+          const int st = u % kFaStages;
+          if (!mbar_wait(&p_full[i], u & 1u, status, kDevWaitMma, abort_flag) ||
+              !mbar_wait(&pv_empty[i], (u & 1u) ^ 1u, status, kDevWaitMma, abort_flag))
+            return false;
+          tc_fence_after();
+          const uint32_t v_addr = smem_u32(smem + FaSmem::KV + (2 * st + 1) * kFaTile);
+          const uint32_t ones_addr = smem_u32(smem + FaSmem::ONES);
+          const uint32_t p_addr = smem_u32(smem + FaSmem::P + 2 * i * kFaTile);
+#pragma unroll
+          for (int kk = 0; kk < kFaBN / 16; ++kk)  // 16 keys per MMA
+            mma_f16(tmem + kFaPvOff + i * kFaPvPitch, smem_desc_k_sw128(p_addr + (kk >> 2) * kFaTile + (kk & 3) * 32),
+                    smem_desc_mn_sw128(v_addr + kk * 2048, ones_addr - v_addr), idesc_pv, kk > 0 ? 1u : 0u);
+          mma_commit(&pv_full[i]);
+          mma_commit(&p_empty[i]);
+          return true;
+        };
+        // Per key tile t: S_i(t) for both query tiles as soon as the softmax
+        // has read S_i(t-1), then (P V)_i(t-1); a K / V stage is released after
+        // both tiles' P V of it.  (Issuing S_0(t+1) only after (P V)_0(t) left
+        // the softmax waiting for S: measured 13% slower.)
         for (int t = 0; ok && t <= ntiles; ++t) {
           if (t < ntiles) {
-            const int st = t % kFaStages;
-            if (!mbar_wait(&kv_full[st], (t / kFaStages) & 1u, status, kDevWaitMma, abort_flag)) {
-              ok = false;
-              break;
-            }
-            const uint32_t k_addr = smem_u32(smem + FaSmem::KV + 2 * st * kFaTile);
-            for (int i = 0; ok && i < nq; ++i) {
-              if (!mbar_wait(&s_empty[i], (t & 1u) ^ 1u, status, kDevWaitMma, abort_flag)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              const uint32_t q_addr = smem_u32(smem + FaSmem::Q + i * kFaTile);
-#pragma unroll
-              for (int kk = 0; kk < kFaD / 16; ++kk)
-                mma_f16(tmem + kFaSOff + i * kFaBN, smem_desc_k_sw128(q_addr + kk * 32),
-                        smem_desc_k_sw128(k_addr + kk * 32), idesc_qk, kk > 0 ? 1u : 0u);
-              mma_commit(&s_full[i]);
-            }
+            ok = mbar_wait(&kv_full[t % kFaStages], (t / kFaStages) & 1u, status, kDevWaitMma, abort_flag);
+            for (int i = 0; ok && i < nq; ++i) ok = issue_s(i, t);
           }
-          if (t >= 1) {  // P V of key tile u = t - 1, both query tiles; then its K / V stage is free
-            const int u = t - 1, st = u % kFaStages;
-            const uint32_t v_addr = smem_u32(smem + FaSmem::KV + (2 * st + 1) * kFaTile);
-            const uint32_t ones_addr = smem_u32(smem + FaSmem::ONES);
-            for (int i = 0; ok && i < nq; ++i) {
-              if (!mbar_wait(&p_full[i], u & 1u, status, kDevWaitMma, abort_flag) ||
-                  !mbar_wait(&pv_empty[i], (u & 1u) ^ 1u, status, kDevWaitMma, abort_flag)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              const uint32_t p_addr = smem_u32(smem + FaSmem::P + 2 * i * kFaTile);
-#pragma unroll
-              for (int kk = 0; kk < kFaBN / 16; ++kk)  // 16 keys per MMA
-                mma_f16(tmem + kFaPvOff + i * kFaPvPitch,
-                        smem_desc_k_sw128(p_addr + (kk >> 2) * kFaTile + (kk & 3) * 32),
-                        smem_desc_mn_sw128(v_addr + kk * 2048, ones_addr - v_addr), idesc_pv, kk > 0 ? 1u : 0u);
-              mma_commit(&pv_full[i]);
-              mma_commit(&p_empty[i]);
-            }
-            if (ok) mma_commit(&kv_empty[st]);
+          if (ok && t >= 1) {
+            for (int i = 0; ok && i < nq; ++i) ok = issue_pv(i, t - 1);
+            if (ok) mma_commit(&kv_empty[(t - 1) % kFaStages]);
           }
         }
         mma_commit(done);
@@ -533,16 +549,16 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           for (int c = 0; c < kFaBN; ++c)
             if (c >= valid64) sr[c] = __float_as_uint(-INFINITY);
         }
-        // Row max over raw scores in 8 independent chains (scale > 0 commutes with max).
+        // Row max over raw scores (scale > 0 commutes with max): three-input
+        // max, 8 independent chains.
         float mx8[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) mx8[j] = __uint_as_float(sr[j]);
 #pragma unroll
-        for (int c = 8; c < kFaBN; c += 8)
+        for (int c = 8; c < kFaBN; c += 16)
 #pragma unroll
-          for (int j = 0; j < 8; ++j) mx8[j] = fmaxf(mx8[j], __uint_as_float(sr[c + j]));
-        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+          for (int j = 0; j < 8; ++j) mx8[j] = fa_max3(mx8[j], __uint_as_float(sr[c + j]), __uint_as_float(sr[c + 8 + j]));
+        const float mx = fa_max3(fa_max3(mx8[0], mx8[1], mx8[2]), fa_max3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
         const float m_new = fmaxf(m, __fmul_rn(mx, p.c2));
         const float alpha = fa_ex2(m - m_new);
         // exp2 of the whole row into packed fp16 registers, EMU of every 4
