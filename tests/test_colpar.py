@@ -196,3 +196,21 @@ def test_q8_exchange_rejects_too_many_peers(b2q_mod):
     rc = lib.b2q_mul_mat_prepared_gelu_q8_peers(256, 64, 64, 256, 8, None, arr, 9, 256, 0, 1 << 20,
                                                 b2q_mod.ACT_X86, None)
     assert rc == INVALID_ARG
+
+
+@pytest.mark.parametrize("m,n", [(1, 32), (129, 1024), (300, 256), (20480, 4096)])
+def test_split_views_match_the_library_layout(b2q_mod, m, n):
+    """colpar.split_views (the NCCL baseline's view of a prepared-activation
+    buffer) against the library's own size arithmetic: codes [m][n] at 0,
+    scales [n/32][round_up(m, 4)] fp32 at the next 256-byte boundary."""
+    import torch
+    size = b2q_mod.act_prepared_size(m, n)
+    buf = torch.zeros(size, dtype=torch.uint8)
+    codes, scales = colpar.split_views(buf, m, n)
+    ld = (m + 3) // 4 * 4
+    assert codes.shape == (m, n) and scales.shape == (n // 32, ld)
+    assert codes.data_ptr() == buf.data_ptr()
+    off = scales.data_ptr() - buf.data_ptr()
+    assert off == (m * n + 255) // 256 * 256
+    assert off + scales.numel() * 4 <= size
+    assert size == off + ((n // 32) * ld * 4 + 255) // 256 * 256
