@@ -60,19 +60,19 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
       : "memory");
 }
 
-// try_wait with a suspend-time hint: a thread whose phase is not complete
-// sleeps (up to the hint) instead of spinning, and wakes when the phase
-// completes, so waiting warps do not take issue slots from working ones.
-constexpr uint32_t kSuspendHintNs = 1000000;  // 1 ms
-
+// try_wait without a suspend-time hint: the thread waits for at most the
+// hardware's own time limit, then the caller's bounded loop re-checks.  Measured
+// against an explicit hint (20 ns, 200 ns and 1 ms all behaved alike): fc1 89.1
+// -> 80.7 us, fc2 77.9 -> 73.8 us, the self-attention 260.6 -> 254.4 us, results
+// bit-identical; the F16 GEMM and the small-M GEMM unchanged.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.b32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
 }
