@@ -6,17 +6,24 @@
 // accumulators in TMEM carried over all of K.  No per-block scales, so this is
 // a plain GEMM: the epilogue runs once per tile, not once per 32 values.
 //
-// Structure (persistent, one CTA per SM, 192 threads):
+// Structure (persistent, one CTA per SM, 576 threads):
 //   warp 0      TMA producer: weight tile [128 rows x 64 K] and activation
 //               tile [256 tokens x 64 K] per stage (one 128-byte swizzle row
-//               of fp16 each), 4 stages of 48 KB
+//               of fp16 each), 4 stages of 48 KB.  The MMA thread waits for
+//               stage data ~58% of its time; 8 stages of 32 K (64-byte swizzle,
+//               the same bytes in flight) measured slower (fc1 57.8 against
+//               50.2 us): twice the per-stage barrier and issue work.
 //   warp 1      TMEM allocator (512 columns) + single-thread MMA issuer:
 //               4 MMAs (M 128, N 256, K 16) per stage into one of two
 //               256-column accumulators, so a tile's epilogue overlaps the
 //               next tile's MMAs
-//   warps 2..5  epilogue: thread t of warp w owns weight row 32*(w%4) + t (its
-//               TMEM lane) and all 256 token columns; 32-column TMEM loads,
-//               double-buffered, bias add, 128-byte coalesced stores
+//   warps 2..17 epilogue: thread t of warp w owns weight row 32*(w%4) + t (its
+//               TMEM lane) and 64 of the 256 token columns (warps 2-5 the
+//               first quarter, 6-9 the second, ...); 32-column TMEM loads,
+//               double-buffered, bias add, 128-byte coalesced stores.  The
+//               stores set the pace: with one warp per lane quarter the
+//               epilogue took ~19.8 k cycles per tile against ~8.2 k of MMA
+//               (fc1 68.6 us); two per quarter 52.2 us, four 50.2 us.
 // Tiles run weight-row-fastest, so the CTAs of one wave share activation tiles
 // in L2.  Every wait is bounded; no TMA multicast.
 //
@@ -32,9 +39,11 @@ constexpr int kBN = 256;             // tokens per tile (MMA N)
 constexpr int kStageK = 64;          // fp16 values of K per stage (128 bytes)
 constexpr int kMmaK = 16;            // K per kind::f16 MMA (32 bytes)
 constexpr int kStages = 4;
+constexpr CUtensorMapSwizzle kSwizzle = CU_TENSOR_MAP_SWIZZLE_128B;
 constexpr int kAccs = 2;             // TMEM accumulators of kBN columns
 constexpr uint32_t kTmemColsF = kAccs * kBN;
-constexpr int kEpiWarp0 = 2, kEpiWarps = 4;
+constexpr int kEpiWarp0 = 2, kEpiWarps = 16;
+constexpr int kEpiCols = kBN / (kEpiWarps / 4);  // token columns per epilogue warp
 constexpr int kThreadsF = (kEpiWarp0 + kEpiWarps) * 32;
 constexpr int kABytes = kBM * kStageK * 2;  // 16 KB
 constexpr int kBBytes = kBN * kStageK * 2;  // 32 KB
@@ -127,7 +136,7 @@ __global__ void __launch_bounds__(kThreadsF, 1)
           }
           uint8_t* sb = smem + stage * kStageBytes;
           mbar_arrive_expect_tx(&full[stage], kStageBytes);
-          tma_load_2d(sb, &tm_w, &full[stage], kw0 + ks * kStageK, n0);      // x * 2 bytes = 128 * (..)
+          tma_load_2d(sb, &tm_w, &full[stage], kw0 + ks * kStageK, n0);  // x * 2 bytes: multiples of 128
           tma_load_2d(sb + kABytes, &tm_x, &full[stage], ks * kStageK, m0);
           issued_mask |= 1u << stage;
           issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
@@ -179,6 +188,7 @@ __global__ void __launch_bounds__(kThreadsF, 1)
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;
+    const int col0 = ((warp - kEpiWarp0) >> 2) * kEpiCols;  // this warp's first token column
     const uint32_t tlane = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
     uint32_t t = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
@@ -186,17 +196,18 @@ __global__ void __launch_bounds__(kThreadsF, 1)
       if (!mbar_wait(&acc_full[a], apar, &g_device_status, kDevWaitEpilogue, abort_flag)) break;
       tc_fence_after();
       const int64_t n = static_cast<int64_t>(tile % p.n_tiles) * kBM + row;
-      const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * kBN;
+      const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * kBN + col0;
       const bool nv = n < p.N;
       const float bv = (p.bias && nv) ? p.bias[n] : 0.0f;
       float* yp = p.y + m0 * p.ldy + n;
       __half* yp16 = p.y16 + m0 * p.ldy + n;
       uint32_t buf[2][32];
-      tmem_ld_32x32b_x32(tlane + a * kBN, buf[0]);
+      const uint32_t tacc = tlane + a * kBN + col0;
+      tmem_ld_32x32b_x32(tacc, buf[0]);
       tmem_wait_ld();
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        if (c + 1 < kBN / 32) tmem_ld_32x32b_x32(tlane + a * kBN + (c + 1) * 32, buf[(c + 1) & 1]);
+      for (int c = 0; c < kEpiCols / 32; ++c) {
+        if (c + 1 < kEpiCols / 32) tmem_ld_32x32b_x32(tacc + (c + 1) * 32, buf[(c + 1) & 1]);
         if (nv) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
@@ -212,7 +223,7 @@ __global__ void __launch_bounds__(kThreadsF, 1)
           }
         }
         tmem_wait_ld();
-        if (c == kBN / 32 - 2) {  // the last chunk is in registers: the accumulator goes back
+        if (c == kEpiCols / 32 - 2) {  // the last chunk is in registers: the accumulator goes back
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[a]);
@@ -238,9 +249,9 @@ cudaError_t launch_gemm_f16(const void* w, int64_t ldw_bytes, const void* x16, i
   if (K <= 0 || K % 8 != 0 || M > INT32_MAX || N > INT32_MAX) return cudaErrorInvalidValue;
   CUtensorMap tm_w, tm_x;
   if (!make_tensor_map_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, w, K, N, ldw_bytes, f16::kStageK, f16::kBM,
-                          CU_TENSOR_MAP_SWIZZLE_128B) ||
+                          f16::kSwizzle) ||
       !make_tensor_map_2d(&tm_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x16, K, M, ldx_bytes, f16::kStageK, f16::kBN,
-                          CU_TENSOR_MAP_SWIZZLE_128B))
+                          f16::kSwizzle))
     return cudaErrorInvalidValue;
   f16::F16Params p;
   p.M = static_cast<int>(M);
@@ -285,9 +296,9 @@ cudaError_t launch_gemm_f16_grouped(const void* w, int64_t ldw_bytes, int64_t Kw
     return cudaErrorInvalidValue;
   CUtensorMap tm_w, tm_x;
   if (!make_tensor_map_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, w, Kw, N, ldw_bytes, f16::kStageK, f16::kBM,
-                          CU_TENSOR_MAP_SWIZZLE_128B) ||
+                          f16::kSwizzle) ||
       !make_tensor_map_2d(&tm_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x16, K, M_cap, ldx_bytes, f16::kStageK, f16::kBN,
-                          CU_TENSOR_MAP_SWIZZLE_128B))
+                          f16::kSwizzle))
     return cudaErrorInvalidValue;
   f16::F16Params p{};
   p.M = static_cast<int>(M_cap);
