@@ -102,7 +102,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 
 // 2-D tiled TMA load into shared memory, completion counted on `bar` in bytes.
 // x is the innermost coordinate (elements); callers keep x * elem_size a
-// multiple of 16 bytes.  No cluster multicast anywhere in this library.
+// multiple of 16 bytes.  No TMA load in this library has a multicast qualifier.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
                                             int32_t x, int32_t y) {
   asm volatile(
