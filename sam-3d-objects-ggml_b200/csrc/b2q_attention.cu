@@ -235,10 +235,13 @@ cudaError_t launch_attention_f32_d(const float* q, const float* k, const float* 
 //                by scale * log2(e)) in fp32, three pairs in four on the MUFU
 //                (ex2.approx) and one on the FMA pipe (fa_ex2_poly_h2), each
 //                rounded once to fp16; writes P into shared memory in the
-//                swizzled K-major layout the P V MMA reads; keeps the fp32 output
-//                row in registers (o = o * alpha + P V per tile), so no TMEM
-//                rescale has to be ordered between MMAs.  The row sum of P comes
-//                out of the P V MMA itself (a constant ones column next to V).
+//                swizzled K-major layout the P V MMA reads.  O accumulates in
+//                TMEM over the key tiles (the P V MMA adds into it).  The row
+//                max used for the exps is raised only when a tile's max exceeds
+//                it by more than 8 (so p <= 2^8, as exact in fp16 as p <= 1);
+//                then the warp rescales its rows of O in TMEM between the
+//                previous P V and the next.  The row sum of P comes out of the
+//                P V MMA itself (a constant ones column next to V).
 // While one warpgroup computes its softmax, the tensor core works on the other
 // tile's S and P V.  Keys of a partial last tile of a source are masked to
 // -inf.  Every wait is bounded; on give-up the CTA drains and frees TMEM.  A
@@ -259,7 +262,7 @@ struct FaSmem {
   static constexpr int P = KV + kFaStages * 2 * kFaTile;  // P_i: two 64-key panels at P + 2i * tile
   static constexpr int ONES = P + 2 * 2 * kFaTile;       // V's 65th column: 1.0 for every key (MN-major atom)
   static constexpr int BAR = ONES + kFaTile;
-  static constexpr int NBAR = 1 + 2 * kFaStages + 12 + 1;
+  static constexpr int NBAR = 1 + 2 * kFaStages + 10 + 1;
   static constexpr int BYTES = BAR + NBAR * 8 + 16 + 1024;
 };
 
@@ -284,32 +287,6 @@ __device__ __forceinline__ float fa_ex2(float x) {
   return y;
 }
 
-// The P V result of key tile u joins the output row: o = o * alpha_u + (P V)_u
-// for the 64 outputs and, in o[64], for the row sum of P (the ones column).
-__device__ __forceinline__ bool fa_o_update(float (&o)[kFaD + 1], int u, float alpha, uint32_t tpv, uint64_t* pv_full,
-                                            uint64_t* pv_empty, unsigned int* status, volatile int* abort_flag,
-                                            int lane) {
-  if (!__all_sync(0xffffffffu, mbar_wait(pv_full, u & 1u, status, kDevWaitEpilogue, abort_flag))) return false;
-  tc_fence_after();
-  uint32_t r[kFaD + 8];
-  tmem_ld_32x32b_x32(tpv, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-  tmem_ld_32x32b_x32(tpv + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-  tmem_ld_32x32b_x8(tpv + 64, &r[64]);
-  tmem_wait_ld();
-  tc_fence_before();
-  __syncwarp();
-  if (lane == 0) mbar_arrive(pv_empty);
-  const float2 a2 = make_float2(alpha, alpha);
-#pragma unroll
-  for (int d = 0; d < kFaD; d += 2) {
-    const float2 v = ffma2(make_float2(o[d], o[d + 1]), a2, make_float2(__uint_as_float(r[d]), __uint_as_float(r[d + 1])));
-    o[d] = v.x;
-    o[d + 1] = v.y;
-  }
-  o[kFaD] = __fmaf_rn(o[kFaD], alpha, __uint_as_float(r[kFaD]));
-  return true;
-}
-
 // exp2 of two fp32 arguments, each rounded once to fp16 (P's type for the P V
 // MMA).  The argument stays fp32: an fp16 argument near -10 carries an absolute
 // error of 2^-8, 0.3% in p, six times the fp16 rounding of the result.
@@ -323,9 +300,9 @@ __device__ __forceinline__ uint32_t fa_ex2_h2(float a, float b) {
 // 2^x = 2^n * 2^f with n = rint(x), f = x - n in [-0.5, 0.5]; 2^f by a cubic
 // fitted here for least maximum relative error on [-0.5, 0.5] (Lawson's
 // reweighted least squares on Chebyshev nodes): 7.5e-5 at most, under half
-// an fp16 ulp (2^-12).  x <= 0 always (scores minus the row max); x is
-// clamped at -125 so 2^n stays a normal exponent, and 2^-125 rounds to fp16 0
-// as the -inf of a masked key does.
+// an fp16 ulp (2^-12).  x <= 8 (scores minus a row max that trails the true
+// one by at most 8); x is clamped at -125 so 2^n stays a normal exponent, and
+// 2^-125 rounds to fp16 0 as the -inf of a masked key does.
 __device__ __forceinline__ uint32_t fa_ex2_poly_h2(float2 x) {
   constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: x + kRound holds rint(x) in its low mantissa bits
   const float2 one = make_float2(1.0f, 1.0f), neg = make_float2(-1.0f, -1.0f);
@@ -373,8 +350,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   uint64_t* p_full = s_empty + 2;
   uint64_t* p_empty = p_full + 2;
   uint64_t* pv_full = p_empty + 2;
-  uint64_t* pv_empty = pv_full + 2;
-  uint64_t* done = pv_empty + 2;
+  uint64_t* done = pv_full + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   unsigned int* status = &g_attn_status;
@@ -396,7 +372,6 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       mbar_init(&p_full[i], 4);
       mbar_init(&p_empty[i], 1);
       mbar_init(&pv_full[i], 1);
-      mbar_init(&pv_empty[i], 4);
     }
     mbar_init(done, 1);
     *abort_flag = 0;
@@ -481,9 +456,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         // (P V)_i of key tile u once P_i(u) is stored and (P V)_i(u-1) read.
         auto issue_pv = [&](int i, int u) {
           const int st = u % kFaStages;
-          if (!mbar_wait(&p_full[i], u & 1u, status, kDevWaitMma, abort_flag) ||
-              !mbar_wait(&pv_empty[i], (u & 1u) ^ 1u, status, kDevWaitMma, abort_flag))
-            return false;
+          if (!mbar_wait(&p_full[i], u & 1u, status, kDevWaitMma, abort_flag)) return false;
           tc_fence_after();
           const uint32_t v_addr = smem_u32(smem + FaSmem::KV + (2 * st + 1) * kFaTile);
           const uint32_t ones_addr = smem_u32(smem + FaSmem::ONES);
@@ -491,7 +464,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kFaBN / 16; ++kk)  // 16 keys per MMA
             mma_f16(tmem + kFaPvOff + i * kFaPvPitch, smem_desc_k_sw128(p_addr + (kk >> 2) * kFaTile + (kk & 3) * 32),
-                    smem_desc_mn_sw128(v_addr + kk * 2048, ones_addr - v_addr), idesc_pv, kk > 0 ? 1u : 0u);
+                    smem_desc_mn_sw128(v_addr + kk * 2048, ones_addr - v_addr), idesc_pv,
+                    (kk > 0 || u > 0) ? 1u : 0u);  // O accumulates over the key tiles
           mma_commit(&pv_full[i]);
           mma_commit(&p_empty[i]);
           return true;
@@ -524,10 +498,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       const uint32_t lane_addr = static_cast<uint32_t>(qw * 32) << 16;
       const uint32_t ts = tmem + lane_addr + kFaSOff + i * kFaBN;
       const uint32_t tpv = tmem + lane_addr + kFaPvOff + i * kFaPvPitch;
-      float o[kFaD + 1];  // o[64]: the row sum of P
-#pragma unroll
-      for (int d = 0; d <= kFaD; ++d) o[d] = 0.0f;
-      float m = -INFINITY, alpha_prev = 0.0f;
+      float m = -INFINITY;
       bool ok = true;
       uint8_t* prow = smem + FaSmem::P + 2 * i * kFaTile + (row >> 3) * 1024 + (row & 7) * 128;
       for (int t = 0; t < ntiles && ok; ++t) {
@@ -559,8 +530,13 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 #pragma unroll
           for (int j = 0; j < 8; ++j) mx8[j] = fa_max3(mx8[j], __uint_as_float(sr[c + j]), __uint_as_float(sr[c + 8 + j]));
         const float mx = fa_max3(fa_max3(mx8[0], mx8[1], mx8[2]), fa_max3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
-        const float m_new = fmaxf(m, __fmul_rn(mx, p.c2));
-        const float alpha = fa_ex2(m - m_new);
+        float m_new = fmaxf(m, __fmul_rn(mx, p.c2));
+        bool grow = true;
+        if (t > 0 && !(m_new > m + 8.0f)) {  // keep the row max: p stays <= 2^8
+          m_new = m;
+          grow = false;
+        }
+        const float alpha = grow ? fa_ex2(m - m_new) : 1.0f;
         // exp2 of the whole row into packed fp16 registers, EMU of every 4
         // pairs on the FMA pipe; only the stores wait for P_i to be free (the
         // previous key tile's P V MMA).
@@ -575,6 +551,23 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         }
         ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[i], par ^ 1u, status, kDevWaitEpilogue, abort_flag));
         if (!ok) break;
+        if (t > 0 && __any_sync(0xffffffffu, grow)) {
+          // The previous P V is complete (p_empty): rescale this warp's rows of O
+          // (and of the row sum in column 64) before the next P V adds into it.
+          tc_fence_after();
+          uint32_t r[kFaD + 8];
+          tmem_ld_32x32b_x32(tpv, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+          tmem_ld_32x32b_x32(tpv + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+          tmem_ld_32x32b_x8(tpv + 64, &r[64]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int d = 0; d < kFaD + 8; ++d) r[d] = __float_as_uint(__fmul_rn(__uint_as_float(r[d]), alpha));
+          tmem_st_32x32b_x32(tpv, *reinterpret_cast<const uint32_t(*)[32]>(&r[0]));
+          tmem_st_32x32b_x32(tpv + 32, *reinterpret_cast<const uint32_t(*)[32]>(&r[32]));
+          tmem_st_32x32b_x8(tpv + 64, &r[64]);
+          tmem_wait_st();
+          tc_fence_before();
+        }
 #pragma unroll
         for (int c = 0; c < kFaBN; c += 8) {
           const int panel = c >> 6, chunk = (c & 63) >> 3;
@@ -585,11 +578,21 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[i]);
         m = m_new;
-        if (t >= 1) ok = fa_o_update(o, t - 1, alpha_prev, tpv, &pv_full[i], &pv_empty[i], status, abort_flag, lane);
-        alpha_prev = alpha;
       }
-      if (ok && ntiles > 0) ok = fa_o_update(o, ntiles - 1, alpha_prev, tpv, &pv_full[i], &pv_empty[i], status,
-                                             abort_flag, lane);
+      float o[kFaD + 1];  // o[64]: the row sum of P
+      if (ok && ntiles > 0) {  // O and the row sum from TMEM once the last P V is complete
+        ok = __all_sync(0xffffffffu, mbar_wait(&pv_full[i], (ntiles - 1) & 1u, status, kDevWaitEpilogue, abort_flag));
+        if (ok) {
+          tc_fence_after();
+          uint32_t r[kFaD + 8];
+          tmem_ld_32x32b_x32(tpv, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+          tmem_ld_32x32b_x32(tpv + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+          tmem_ld_32x32b_x8(tpv + 64, &r[64]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int d = 0; d <= kFaD; ++d) o[d] = __uint_as_float(r[d]);
+        }
+      }
       const int64_t tq = q0 + i * kFaBM + row;
       if (ok && tq < p.Tq) {
         const float inv = 1.0f / o[kFaD];
