@@ -25,7 +25,6 @@ import json
 import os
 import statistics
 import sys
-import threading
 import time
 
 REPO = os.path.dirname(os.path.abspath(__file__))
@@ -143,8 +142,32 @@ def make_inputs(seed=1234):
 
 
 # --------------------------------------------------------------------- clocks
+# The sampler runs in a child process: a thread of this process gets the GIL
+# too rarely while the timed loop enqueues its launches (one sample in a 44 ms
+# region was seen).  The child prints "<wall time> <SM MHz> <reason bits>"
+# every period; the parent keeps the samples inside its timed window.
+_SAMPLER_CODE = r"""
+import sys, time, pynvml
+pynvml.nvmlInit()
+uuid, period = sys.argv[1], float(sys.argv[2])
+try:
+    h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+except Exception:
+    h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[3]))
+print("max", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
+while True:
+    try:
+        print(time.time(), pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+              pynvml.nvmlDeviceGetCurrentClocksEventReasons(h), flush=True)
+    except Exception:
+        pass
+    time.sleep(period)
+"""
+
+
 class ClockSampler:
-    """Samples SM clock and throttle reasons through NVML while running."""
+    """Samples SM clock and throttle reasons through NVML (in a child process)
+    during the `with` block."""
 
     REASONS = {
         0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
@@ -152,55 +175,50 @@ class ClockSampler:
         0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
     }
 
-    def __init__(self, device_index: int, period_s: float = 0.005):
-        self.samples = []
-        self.reasons = 0
-        self.max_mhz = None
-        self._stop = threading.Event()
-        self._period = period_s
-        self._h = None
+    def __init__(self, device_index: int, period_s: float = 0.002):
+        self.samples, self.reasons, self.max_mhz, self.error = [], 0, None, ""
+        self._proc = None
         try:
-            import pynvml
-            pynvml.nvmlInit()
+            import subprocess
             import torch
             uuid = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
-            try:
-                self._h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
-            except Exception:
-                self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
-            self._nv = pynvml
+            self._proc = subprocess.Popen([sys.executable, "-c", _SAMPLER_CODE, uuid, str(period_s),
+                                           str(device_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                          text=True)
+            first = self._proc.stdout.readline().split()  # the child is sampling once it prints this
+            if len(first) != 2 or first[0] != "max":
+                raise RuntimeError("sampler did not start")
+            self.max_mhz = int(first[1])
         except Exception as e:  # noqa: BLE001
             self.error = f"nvml unavailable: {e}"
-        self._t = threading.Thread(target=self._run, daemon=True)
-
-    def _run(self):
-        nv = self._nv
-        while not self._stop.is_set():
-            try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
-                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-            except Exception:
-                pass
-            time.sleep(self._period)
+            if self._proc is not None:
+                self._proc.kill()
+            self._proc = None
 
     def __enter__(self):
-        if self._h is not None:
-            self._t.start()
+        self._t0 = time.time()
         return self
 
     def __exit__(self, *a):
-        self._stop.set()
-        if self._h is not None:
-            self._t.join()
+        t1 = time.time()
+        if self._proc is None:
+            return
+        time.sleep(0.01)  # the child's samples up to t1 are written
+        self._proc.kill()
+        out, _ = self._proc.communicate()
+        for line in out.splitlines():
+            f = line.split()
+            if len(f) == 3 and self._t0 <= float(f[0]) <= t1:
+                self.samples.append(int(f[1]))
+                self.reasons |= int(f[2])
 
     def summary(self):
-        if self._h is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": getattr(self, "error", "")}
+        if self.max_mhz is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": self.error}
         rs = [v for k, v in self.REASONS.items() if self.reasons & k and k != 0x1]
         return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
                 "sm_max_mhz": self.max_mhz, "reasons": rs, "samples": len(self.samples),
-                "source": "nvml, sampled every 5 ms during the timed region"}
+                "source": "nvml in a child process, sampled every 2 ms during the timed region"}
 
 
 # -------------------------------------------------------------------- GPU arm
