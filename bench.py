@@ -1362,7 +1362,70 @@ def colpar_side(args, rank, world, dev, dist=None):
                     "kernel on the slice + all_gather_into_tensor + transpose copy",
         }
         del packed, act
+    out["mlp"] = colpar_mlp(args, rank, world, dev, dist, timed, sync_tick)
     return out
+
+
+COLPAR_MLP = (20480, 1024, 4096)  # tokens, model width C, hidden width (SLat feed-forward, Q4_0)
+
+
+def colpar_mlp(args, rank, world, dev, dist, timed, sync_tick):
+    """The SLat feed-forward branch sharded over the ranks end to end:
+    fc1 (C -> hidden, GELU + Q8_0) column-parallel with the Q8_0 exchange into
+    every rank's fc2 input, then fc2 (hidden -> C) column-parallel with the
+    fp32 gather into every rank's output -- two fused exchanges per step, the
+    ranks synchronised between them (fc2 reads what the peers wrote).  Rank 0's
+    output is checked bit for bit against one GPU running both whole weights."""
+    import torch
+    import b2q
+    import colpar
+
+    M, C, H = COLPAR_MLP
+    rng = np.random.default_rng(4323)  # same weights and inputs on every rank
+    w1 = synth_blocks(2, (rng.standard_normal((H, C)) * 0.02).astype(np.float32), H, C)
+    w2 = synth_blocks(2, (rng.standard_normal((C, H)) * 0.02).astype(np.float32), C, H)
+    x = rng.standard_normal((M, C)).astype(np.float32)
+    b1 = torch.from_numpy((rng.standard_normal(H) * 0.1).astype(np.float32)).to(dev)
+    b2 = torch.from_numpy((rng.standard_normal(C) * 0.1).astype(np.float32)).to(dev)
+    s1, e1 = colpar.slices(H, world)[rank]
+    s2, e2 = colpar.slices(C, world)[rank]
+    p1 = b2q.weight_pack(2, torch.from_numpy(w1[s1:e1]).to(dev), C)
+    p2 = b2q.weight_pack(2, torch.from_numpy(w2[s2:e2]).to(dev), H)
+    act = b2q.act_prepare(torch.from_numpy(x).to(dev))
+    hid = colpar.activation_buffers(M, H)  # every rank's fc2 input
+    ybuf = colpar.PeerBuffers(M, C)        # every rank's output
+    hid_t = hid.local_tensor(dev)  # this rank's copy, as the fc2 operand (no copy)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        colpar.fused_gelu_q8(p1, e1 - s1, C, act, M, hid, s1, bias=b1[s1:e1], stream=stream)
+        sync_tick()  # every rank's fc1 tiles have landed before any rank's fc2 reads them
+        colpar.fused(p2, e2 - s2, H, hid_t, M, ybuf, s2, bias=b2[s2:e2], stream=stream)
+        sync_tick()
+
+    ms = timed(step)
+    ok = None
+    if rank == 0:
+        f1 = b2q.weight_pack(2, torch.from_numpy(w1).to(dev), C)
+        f2 = b2q.weight_pack(2, torch.from_numpy(w2).to(dev), H)
+        h_ref = b2q.mul_mat_prepared_gelu_q8(f1, H, C, act, M, bias=b1)
+        y_ref = b2q.mul_mat_prepared(f2, C, H, h_ref, M, bias=b2)
+        ok = bool(torch.equal(ybuf.to_tensor(dev), y_ref))
+        del f1, f2, h_ref, y_ref
+    status = b2q.device_status(clear=True)
+    if dist:
+        dist.barrier()
+    del hid_t
+    hid.close()
+    ybuf.close()
+    ops = 2.0 * M * C * H * 2
+    bytes_in = M * (H * 1.125 + C * 4.0) * (world - 1) / world
+    return {"workload": f"SLat MLP, {M} tokens: fc1 {C} -> {H} (GELU + Q8_0, exchanged as Q8_0), fc2 {H} -> {C} "
+                        f"(fp32, gathered), Q4_0 weights, both split by output rows over {world} rank(s)",
+            "ms": round(ms, 4), "tops": round(ops / (ms * 1e-3) / 1e12, 2),
+            "nvlink_bytes_in_per_rank": int(bytes_in),
+            "parity_rank0_bitwise_vs_single_gpu": ok, "device_status": status,
+            "path": "b2q_mul_mat_prepared_gelu_q8_peers, rank sync, b2q_mul_mat_prepared_peers, rank sync"}
 
 
 def run_colpar(args, rank, world, local_rank):

@@ -94,6 +94,17 @@ class PeerBuffers:
         _ok(err, "cudaMemcpy")
         return t
 
+    def local_tensor(self, device):
+        """This rank's buffer as a uint8 torch tensor sharing its memory (no
+        copy), e.g. as the next GEMM's operand; valid until close()."""
+        import torch
+        ptr, nbytes = self.local, self.nbytes
+
+        class _Mem:
+            __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                        "version": 3, "strides": None}
+        return torch.as_tensor(_Mem(), device=device)
+
     def close(self) -> None:
         for p in self._opened:
             self._cudart.cudaIpcCloseMemHandle(p)

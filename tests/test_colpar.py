@@ -214,3 +214,73 @@ def test_split_views_match_the_library_layout(b2q_mod, m, n):
     assert off == (m * n + 255) // 256 * 256
     assert off + scales.numel() * 4 <= size
     assert size == off + ((n // 32) * ld * 4 + 255) // 256 * 256
+
+
+def _rank_main_mlp(rank, world, port, M, C, H):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import b2q
+    from helpers import make_case
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        _, w1, x = make_case(11, M, H, C, 2)
+        _, w2, _ = make_case(12, 1, C, H, 2)
+        b1 = torch.from_numpy(np.random.default_rng(3).standard_normal(H).astype(np.float32)).to(dev)
+        b2 = torch.from_numpy(np.random.default_rng(4).standard_normal(C).astype(np.float32)).to(dev)
+        s1, e1 = colpar.slices(H, world)[rank]
+        s2, e2 = colpar.slices(C, world)[rank]
+        p1 = b2q.weight_pack(2, torch.from_numpy(w1[s1:e1]).to(dev), C)
+        p2 = b2q.weight_pack(2, torch.from_numpy(w2[s2:e2]).to(dev), H)
+        act = b2q.act_prepare(torch.from_numpy(x).to(dev))
+        hid = colpar.activation_buffers(M, H)
+        ybuf = colpar.PeerBuffers(M, C)
+        hid_t = hid.local_tensor(dev)
+        torch.cuda.synchronize()
+        dist.barrier()
+        colpar.fused_gelu_q8(p1, e1 - s1, C, act, M, hid, s1, bias=b1[s1:e1])
+        torch.cuda.synchronize()
+        dist.barrier()  # every rank's fc1 slice is in every rank's fc2 input
+        colpar.fused(p2, e2 - s2, H, hid_t, M, ybuf, s2, bias=b2[s2:e2])
+        torch.cuda.synchronize()
+        dist.barrier()
+        got = ybuf.to_tensor(dev)
+        h_ref = b2q.mul_mat_prepared_gelu_q8(b2q.weight_pack(2, torch.from_numpy(w1).to(dev), C), H, C, act, M,
+                                             bias=b1)
+        y_ref = b2q.mul_mat_prepared(b2q.weight_pack(2, torch.from_numpy(w2).to(dev), H), C, H, h_ref, M, bias=b2)
+        torch.cuda.synchronize()
+        assert torch.equal(got, y_ref), "sharded MLP differs from the single-GPU MLP"
+        assert b2q.device_status(clear=True) == 0
+        dist.barrier()
+        del hid_t
+        hid.close()
+        ybuf.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,C,H", [(300, 256, 1024), (1000, 1024, 4096)])
+def test_sharded_mlp_matches_single_gpu(b2q_mod, M, C, H):
+    """fc1 column-parallel with the Q8_0 exchange, then fc2 column-parallel with
+    the fp32 gather: every rank ends with the single-GPU MLP's output, bit for bit."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs of one box")
+    world = 2
+    ctx = mp.start_processes(_rank_main_mlp, args=(world, _free_port(), M, C, H), nprocs=world, join=False,
+                             start_method="spawn")
+    deadline = time.time() + 240
+    try:
+        while not ctx.join(timeout=5):
+            if time.time() > deadline:
+                raise TimeoutError("sharded MLP ranks did not finish")
+    finally:
+        for p in ctx.processes:
+            if p.is_alive():
+                p.kill()
