@@ -223,12 +223,12 @@ cudaError_t launch_attention_f32_d(const float* q, const float* k, const float* 
 //   warp 0       TMA producer: both Q tiles once, then K and V tiles of 128 keys
 //                (fp16, 128-byte swizzle) through a 3-stage ring shared by the
 //                two query tiles
-//   warp 1       TMEM allocator + MMA issuer: per key tile, S_i = Q_i K^T
-//                (kind::f16, M 128, N 128, K 64) for both query tiles, then
-//                (P V)_i of the previous key tile (M 128, N 64, K 128; V read as
-//                an MN-major operand straight from its TMA tile)
-//   warps 2, 3   idle (complete warpgroup 0, which runs on 40 registers)
-//   warpgroups 1 and 2: softmax of query tile 0 and 1 (232 registers each):
+//   warp 1       TMEM allocator + MMA issuer: S_i = Q_i K^T (kind::f16, M 128,
+//                N 128, K 64) and (P V)_i (M 128, N 64, K 128; V read as an
+//                MN-major operand straight from its TMA tile), each issued as
+//                soon as its own barriers complete (polled, S first)
+//   warps 2, 3   idle (complete warpgroup 0, which runs on 56 registers)
+//   warpgroups 1 and 2: softmax of query tile 0 and 1 (224 registers each):
 //                thread t owns one query row (its TMEM lane) and reads the row's
 //                128 scores, so the row max needs no shuffles (three-input max,
 //                eight independent chains); exp2 of the scores (pre-multiplied
@@ -250,7 +250,7 @@ __device__ unsigned int g_attn_status = 0;
 
 constexpr int kFaBM = 128, kFaBN = 128, kFaD = 64, kFaStages = 3;
 constexpr int kFaThreads = 384;
-constexpr int kFaLaunchRegs = 168, kFaRegsControl = 40, kFaRegsSoftmax = 232;
+constexpr int kFaLaunchRegs = 168, kFaRegsControl = 56, kFaRegsSoftmax = 224;
 static_assert(128 * kFaRegsControl + 256 * kFaRegsSoftmax <= kFaThreads * kFaLaunchRegs, "register split");
 constexpr int kFaTile = 128 * 128;  // bytes of a 128-row x 64-fp16 tile
 constexpr uint32_t kFaTmemCols = 512;
@@ -439,11 +439,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         constexpr uint32_t idesc_qk = idesc_f16(kFaBM, kFaBN);
         constexpr uint32_t idesc_pv = idesc_f16(kFaBM, kFaPvN) | (1u << 16);  // B (V | ones) MN-major
         bool ok = mbar_wait(q_full, 0, status, kDevWaitMma, abort_flag);
-        // S_i(t) = Q_i K(t)^T once the softmax has read S_i(t-1).
+        // S_i(t) = Q_i K(t)^T (issued once K(t) has landed and the softmax has read S_i(t-1)).
         auto issue_s = [&](int i, int t) {
           const int st = t % kFaStages;
-          if (!mbar_wait(&s_empty[i], (t & 1u) ^ 1u, status, kDevWaitMma, abort_flag)) return false;
-          tc_fence_after();
           const uint32_t k_addr = smem_u32(smem + FaSmem::KV + 2 * st * kFaTile);
           const uint32_t q_addr = smem_u32(smem + FaSmem::Q + i * kFaTile);
 #pragma unroll
@@ -451,13 +449,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             mma_f16(tmem + kFaSOff + i * kFaBN, smem_desc_k_sw128(q_addr + kk * 32),
                     smem_desc_k_sw128(k_addr + kk * 32), idesc_qk, kk > 0 ? 1u : 0u);
           mma_commit(&s_full[i]);
-          return true;
         };
-        // (P V)_i of key tile u once P_i(u) is stored and (P V)_i(u-1) read.
+        // (P V)_i of key tile u (issued once P_i(u) is stored).
         auto issue_pv = [&](int i, int u) {
           const int st = u % kFaStages;
-          if (!mbar_wait(&p_full[i], u & 1u, status, kDevWaitMma, abort_flag)) return false;
-          tc_fence_after();
           const uint32_t v_addr = smem_u32(smem + FaSmem::KV + (2 * st + 1) * kFaTile);
           const uint32_t ones_addr = smem_u32(smem + FaSmem::ONES);
           const uint32_t p_addr = smem_u32(smem + FaSmem::P + 2 * i * kFaTile);
@@ -468,20 +463,49 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                     (kk > 0 || u > 0) ? 1u : 0u);  // O accumulates over the key tiles
           mma_commit(&pv_full[i]);
           mma_commit(&p_empty[i]);
-          return true;
         };
-        // Per key tile t: S_i(t) for both query tiles as soon as the softmax
-        // has read S_i(t-1), then (P V)_i(t-1); a K / V stage is released after
-        // both tiles' P V of it.  (Issuing S_0(t+1) only after (P V)_0(t) left
-        // the softmax waiting for S: measured 13% slower.)
-        for (int t = 0; ok && t <= ntiles; ++t) {
-          if (t < ntiles) {
-            ok = mbar_wait(&kv_full[t % kFaStages], (t / kFaStages) & 1u, status, kDevWaitMma, abort_flag);
-            for (int i = 0; ok && i < nq; ++i) ok = issue_s(i, t);
+        // Each query tile's chain advances on its own barriers: the issuer polls
+        // them without blocking and issues whatever is ready, S before P V, so
+        // that one softmax warpgroup's next S never waits behind the other's P.
+        // A K / V stage is released once both tiles' P V of it are issued.  The
+        // loop gives up (status kDevWaitMma) after kWaitBudgetNs without progress.
+        int ns[2] = {0, 0}, npv[2] = {0, 0}, rel = 0;
+        unsigned long long t_last = globaltimer_ns();
+        uint32_t idle = 0;
+        while (ok && rel < ntiles) {
+          bool progress = false;
+          for (int i = 0; i < nq; ++i) {
+            const int t = ns[i];
+            if (t < ntiles && mbar_test(&kv_full[t % kFaStages], (t / kFaStages) & 1u) &&
+                mbar_test(&s_empty[i], (t & 1u) ^ 1u)) {
+              tc_fence_after();
+              issue_s(i, t);
+              ns[i] = t + 1;
+              progress = true;
+            }
           }
-          if (ok && t >= 1) {
-            for (int i = 0; ok && i < nq; ++i) ok = issue_pv(i, t - 1);
-            if (ok) mma_commit(&kv_empty[(t - 1) % kFaStages]);
+          for (int i = 0; i < nq; ++i) {
+            const int u = npv[i];
+            if (u < ns[i] && mbar_test(&p_full[i], u & 1u)) {
+              tc_fence_after();
+              issue_pv(i, u);
+              npv[i] = u + 1;
+              progress = true;
+            }
+          }
+          const int pv_done = nq > 1 ? min(npv[0], npv[1]) : npv[0];
+          for (; rel < pv_done; ++rel) mma_commit(&kv_empty[rel % kFaStages]);
+          if (progress) {
+            t_last = globaltimer_ns();
+            idle = 0;
+          } else if ((++idle & 63u) == 0) {
+            if (*abort_flag) {
+              ok = false;
+            } else if (globaltimer_ns() - t_last > kWaitBudgetNs) {
+              record_device_error(status, kDevWaitMma);
+              *abort_flag = 1;
+              ok = false;
+            }
           }
         }
         mma_commit(done);

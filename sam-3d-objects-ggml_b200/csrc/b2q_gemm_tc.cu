@@ -66,7 +66,7 @@ __device__ unsigned int g_device_status = 0;
 namespace {
 
 constexpr int kBM = 128;             // weight rows per tile (MMA M, TMEM lanes)
-constexpr int kSlotCols = 128;       // TMEM columns per accumulator slot (the widest tile)
+constexpr int kMaxBN = 128;          // the widest tile (MMA N)
 constexpr int kKBS = 4;              // 32-value blocks per pipeline stage
 constexpr int kStageK = kKBS * kQK;  // 128 bytes of K per operand row per stage
 constexpr int kEpiWarps = 8;
@@ -83,7 +83,6 @@ constexpr int kRegsControl = 40;
 constexpr int kRegsEpilogue = 232;
 static_assert(128 * kRegsControl + 256 * kRegsEpilogue <= kThreads * kLaunchRegs, "register split");
 constexpr uint32_t kTmemCols = 512;
-constexpr int kSlots = static_cast<int>(kTmemCols) / kSlotCols;  // accumulator slots (blocks in flight)
 constexpr uint32_t kOffset = 1u << 20;        // added to every S by the constant MMA
 constexpr int kOffsetTileBytes = 4096;        // 128 rows x 32 bytes, every 16-byte chunk = P
 constexpr float kNegTwoPowM129 = -0x1p-129f;  // subnormal, exact
@@ -92,8 +91,13 @@ constexpr float kNegTwoPowM129 = -0x1p-129f;  // subnormal, exact
 // shape so that the tiles spread evenly over the SMs (see pick_bn).
 template <int STAGES, int BN, bool Q4C = false>
 struct Cfg {
-  static_assert(BN % 16 == 0 && BN >= 64 && BN <= kSlotCols, "tile width");
+  static_assert(BN % 16 == 0 && BN >= 64 && BN <= kMaxBN, "tile width");
   static constexpr int COLS = BN / 2;  // token columns per epilogue thread
+  // Accumulator slots (blocks in flight): as many BN-column slots as TMEM
+  // holds.  A block's MMA-to-epilogue round trip takes about the same time
+  // whatever its width, so the blocks in flight set the rate: 4 at BN 128 or
+  // 112, 5 at 96, 6 at 80, 8 at 64.
+  static constexpr int SLOTS = static_cast<int>(kTmemCols) / BN;
   static constexpr int A_BYTES = kBM * kStageK;
   static constexpr int B_BYTES = BN * kStageK;
   static constexpr int SW_BYTES = kKBS * kBM * 4;
@@ -112,7 +116,7 @@ struct Cfg {
   static constexpr int OFF_TILE = STAGES * STAGE_BYTES;
   static constexpr int BAR_OFF = OFF_TILE + kOffsetTileBytes;
   // stage full / empty (+ converted), slot full / empty, MMA drain
-  static constexpr int NBARS = (Q4C ? 3 : 2) * STAGES + 2 * kSlots + 1;
+  static constexpr int NBARS = (Q4C ? 3 : 2) * STAGES + 2 * SLOTS + 1;
   static constexpr int SMEM = BAR_OFF + NBARS * 8 + 16 + 1024;  // + alignment slack
   // GELU + Q8_0 variant only: a 32 x 33 fp32 transpose buffer per epilogue warp.
   static constexpr int XPOSE_OFF = (BAR_OFF + NBARS * 8 + 16 + 127) / 128 * 128;
@@ -215,7 +219,7 @@ __device__ __forceinline__ bool epi_block(uint32_t (&cur)[COLS], float2 (&acc)[C
   using C = Cfg<STAGES, BN, Q4C>;
   if (!mbar_wait(&acc_full[slot], sphase, &g_device_status, kDevWaitEpilogue, abort_flag)) return false;
   tc_fence_after();
-  load_slot<COLS>(tbase + slot * kSlotCols, cur);
+  load_slot<COLS>(tbase + slot * BN, cur);
   const float* sw = reinterpret_cast<const float*>(sb + C::A_BYTES + C::B_BYTES);
   const float* sa = sw + kKBS * kBM;
   const float w = sw[j * kBM + row];
@@ -327,8 +331,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
-  uint64_t* acc_empty = acc_full + kSlots;
-  uint64_t* mma_done = acc_empty + kSlots;
+  uint64_t* acc_empty = acc_full + C::SLOTS;
+  uint64_t* mma_done = acc_empty + C::SLOTS;
   uint64_t* conv = mma_done + 1;  // Q4C: the stage's weight codes and scales are widened
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(conv + (Q4C ? STAGES : 0));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
@@ -344,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kEpiWarps);
     }
-    for (int a = 0; a < kSlots; ++a) {
+    for (int a = 0; a < C::SLOTS; ++a) {
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], kEpiWarps);  // one arrival per epilogue warp
     }
@@ -426,7 +430,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr uint32_t idesc = idesc_i8(kBM, BN);
         constexpr uint32_t idesc_off = idesc_u8(kBM, BN);
         const uint64_t off_desc = smem_desc_k_noswz(smem_u32(smem + C::OFF_TILE));
-        uint32_t stage = 0, phase = 0, q = 0;  // q: block counter; block q fills slot q % kSlots
+        uint32_t stage = 0, phase = 0;
+        uint32_t slot = 0, sphase = 0;  // block q fills slot q % SLOTS; sphase = (q / SLOTS) & 1
         bool ok = true;
         for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
           for (int ks = 0; ok && ks < n_ks; ++ks) {
@@ -437,17 +442,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const uint32_t a_base = smem_u32(smem + stage * C::STAGE_BYTES);
             const uint32_t b_base = a_base + C::A_BYTES;
-            for (int j = 0; j < kKBS; ++j, ++q) {
-              const uint32_t slot = q & (kSlots - 1);
-              if (!mbar_wait(&acc_empty[slot], ((q / kSlots) & 1u) ^ 1u, &g_device_status, kDevWaitMma, abort_flag)) {
+            for (int j = 0; j < kKBS; ++j) {
+              if (!mbar_wait(&acc_empty[slot], sphase ^ 1u, &g_device_status, kDevWaitMma, abort_flag)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
-              const uint32_t d = tmem_base + slot * kSlotCols;
+              const uint32_t d = tmem_base + slot * BN;
               mma_i8(d, smem_desc_k_sw128(a_base + j * kQK), smem_desc_k_sw128(b_base + j * kQK), idesc, 0u);
               mma_i8(d, off_desc, off_desc, idesc_off, 1u);
               mma_commit(&acc_full[slot]);
+              if (++slot == C::SLOTS) {
+                slot = 0;
+                sphase ^= 1u;
+              }
             }
             if (++stage == STAGES) {
               stage = 0;
@@ -514,7 +522,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + chalf * COLS;
     uint32_t ra[COLS];
     float2 acc[COLS / 2];
-    uint32_t stage = 0, phase = 0, q = 0;  // q: block counter, as the MMA issuer's
+    uint32_t stage = 0, phase = 0;
+    uint32_t slot = 0, sphase = 0;  // accumulator slot and its parity, as the MMA issuer's
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
 #pragma unroll
@@ -527,12 +536,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const uint8_t* sb = smem + stage * C::STAGE_BYTES;
 #pragma unroll
-        for (int j = 0; j < kKBS; ++j, ++q) {
-          if (!epi_block<STAGES, BN, DUMP, Q4C>(ra, acc, static_cast<int>(q & (kSlots - 1)), (q / kSlots) & 1u, j,
-                                           ks * kKBS + j, tile, p, sb, acc_full, acc_empty, abort_flag, tbase, row,
-                                           chalf, lane)) {
+        for (int j = 0; j < kKBS; ++j) {
+          if (!epi_block<STAGES, BN, DUMP, Q4C>(ra, acc, static_cast<int>(slot), sphase, j, ks * kKBS + j, tile, p, sb,
+                                           acc_full, acc_empty, abort_flag, tbase, row, chalf, lane)) {
             ok = false;
             break;
+          }
+          if (++slot == C::SLOTS) {
+            slot = 0;
+            sphase ^= 1u;
           }
         }
         if (!ok) break;
