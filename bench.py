@@ -896,8 +896,9 @@ def attention_side(b2q, stream, dev, peaks, iters=20):
     above its kernel time) is out of both numbers.  Inputs (q 16 MB, k / v up
     to 16 MB each) stay in L2 between calls, as they do in the block."""
     import torch
-    out = {"kernel": "attention_f16_kernel (tcgen05 kind::f16, fp32 TMEM S, fp16 P in smem, 1/4 of the exps "
-                     "on the FMA pipe)", "timing": "CUDA-graph replay of back-to-back calls, both sides",
+    out = {"kernel": "attention_f16_kernel (tcgen05 kind::f16, fp32 TMEM S and O, fp16 P in TMEM as the P V "
+                     "MMA's A operand, 1/2 of the exps on the FMA pipe)",
+           "timing": "CUDA-graph replay of back-to-back calls, both sides",
            "cases": []}
 
     def timed(fn):

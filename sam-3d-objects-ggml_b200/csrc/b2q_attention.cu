@@ -221,47 +221,46 @@ cudaError_t launch_attention_f32_d(const float* q, const float* k, const float* 
 // softmax.  One CTA per 256 queries (two 128-query tiles) of one (b, h);
 // 384 threads = 3 warpgroups:
 //   warp 0       TMA producer: both Q tiles once, then K and V tiles of 128 keys
-//                (fp16, 128-byte swizzle) through a 3-stage ring shared by the
+//                (fp16, 128-byte swizzle) through a kFaStages ring shared by the
 //                two query tiles
 //   warp 1       TMEM allocator + MMA issuer: S_i = Q_i K^T (kind::f16, M 128,
-//                N 128, K 64) and (P V)_i (M 128, N 64, K 128; V read as an
-//                MN-major operand straight from its TMA tile), each issued as
-//                soon as its own barriers complete (polled, S first)
+//                N 128, K 64) and (P V)_i (M 128, N 64, K 128; P read from
+//                tensor memory as the A operand, V as an MN-major operand
+//                straight from its TMA tile), each issued as soon as its own
+//                barriers complete (polled, S first)
 //   warps 2, 3   idle (complete warpgroup 0, which runs on 56 registers)
 //   warpgroups 1 and 2: softmax of query tile 0 and 1 (224 registers each):
 //                thread t owns one query row (its TMEM lane) and reads the row's
 //                128 scores, so the row max needs no shuffles (three-input max,
 //                eight independent chains); exp2 of the scores (pre-multiplied
-//                by scale * log2(e)) in fp32, three pairs in four on the MUFU
-//                (ex2.approx) and one on the FMA pipe (fa_ex2_poly_h2), each
-//                rounded once to fp16; writes P into shared memory in the
-//                swizzled K-major layout the P V MMA reads.  O accumulates in
-//                TMEM over the key tiles (the P V MMA adds into it).  The row
-//                max used for the exps is raised only when a tile's max exceeds
-//                it by more than 8 (so p <= 2^8, as exact in fp16 as p <= 1);
-//                then the warp rescales its rows of O in TMEM between the
-//                previous P V and the next.  The row sum of P comes out of the
-//                P V MMA itself (a constant ones column next to V).
+//                by scale * log2(e)) in fp32, two pairs in four on the MUFU
+//                (ex2.approx) and two on the FMA pipe (fa_ex2_poly_f2), each
+//                rounded once to fp16 and stored into tensor memory (row =
+//                lane, two keys per column: the A layout of the P V MMA); the
+//                row sum of P accumulates in fp32 from the unrounded values.
+//                O accumulates in TMEM over the key tiles (the P V MMA adds
+//                into it).  The row max used for the exps is raised only when a
+//                tile's max exceeds it by more than 8 (so p <= 2^8, as exact in
+//                fp16 as p <= 1); then the warp rescales its rows of O in TMEM
+//                (and its row sum) between the previous P V and the next.
 // While one warpgroup computes its softmax, the tensor core works on the other
 // tile's S and P V.  Keys of a partial last tile of a source are masked to
 // -inf.  Every wait is bounded; on give-up the CTA drains and frees TMEM.  A
 // CTA whose second query tile lies wholly past Tq runs one tile.
 __device__ unsigned int g_attn_status = 0;
 
-constexpr int kFaBM = 128, kFaBN = 128, kFaD = 64, kFaStages = 3;
+constexpr int kFaBM = 128, kFaBN = 128, kFaD = 64, kFaStages = 4;
 constexpr int kFaThreads = 384;
 constexpr int kFaLaunchRegs = 168, kFaRegsControl = 56, kFaRegsSoftmax = 224;
 static_assert(128 * kFaRegsControl + 256 * kFaRegsSoftmax <= kFaThreads * kFaLaunchRegs, "register split");
 constexpr int kFaTile = 128 * 128;  // bytes of a 128-row x 64-fp16 tile
 constexpr uint32_t kFaTmemCols = 512;
-// TMEM columns: S_i at 128 i; (P V)_i at 256 + 96 i, 80 wide: o in 0..63, the row sum of P in 64
-constexpr int kFaSOff = 0, kFaPvOff = 256, kFaPvPitch = 96, kFaPvN = 80;
+// TMEM columns: S_i at 128 i (fp32), O_i at 256 + 64 i (fp32), P_i at 384 + 64 i (fp16 pairs).
+constexpr int kFaSOff = 0, kFaOOff = 256, kFaPOff = 384;
 struct FaSmem {
   static constexpr int Q = 0;                            // Q_i at Q + i * tile
   static constexpr int KV = Q + 2 * kFaTile;             // stage s: K at KV + 2s * tile, V next
-  static constexpr int P = KV + kFaStages * 2 * kFaTile;  // P_i: two 64-key panels at P + 2i * tile
-  static constexpr int ONES = P + 2 * 2 * kFaTile;       // V's 65th column: 1.0 for every key (MN-major atom)
-  static constexpr int BAR = ONES + kFaTile;
+  static constexpr int BAR = KV + kFaStages * 2 * kFaTile;
   static constexpr int NBAR = 1 + 2 * kFaStages + 10 + 1;
   static constexpr int BYTES = BAR + NBAR * 8 + 16 + 1024;
 };
@@ -290,20 +289,20 @@ __device__ __forceinline__ float fa_ex2(float x) {
 // exp2 of two fp32 arguments, each rounded once to fp16 (P's type for the P V
 // MMA).  The argument stays fp32: an fp16 argument near -10 carries an absolute
 // error of 2^-8, 0.3% in p, six times the fp16 rounding of the result.
-__device__ __forceinline__ uint32_t fa_ex2_h2(float a, float b) {
-  const __half2 y = __floats2half2_rn(fa_ex2(a), fa_ex2(b));
+__device__ __forceinline__ uint32_t fa_pack_h2(float2 v) {
+  const __half2 y = __floats2half2_rn(v.x, v.y);
   return *reinterpret_cast<const uint32_t*>(&y);
 }
 
 // exp2 of an fp32 pair on the FMA pipe (the MUFU pipe is the softmax's
-// bottleneck), rounded to fp16 like fa_ex2_h2.  Cody-Waite reduction
+// bottleneck).  Cody-Waite reduction
 // 2^x = 2^n * 2^f with n = rint(x), f = x - n in [-0.5, 0.5]; 2^f by a cubic
 // fitted here for least maximum relative error on [-0.5, 0.5] (Lawson's
 // reweighted least squares on Chebyshev nodes): 7.5e-5 at most, under half
 // an fp16 ulp (2^-12).  x <= 8 (scores minus a row max that trails the true
 // one by at most 8); x is clamped at -125 so 2^n stays a normal exponent, and
 // 2^-125 rounds to fp16 0 as the -inf of a masked key does.
-__device__ __forceinline__ uint32_t fa_ex2_poly_h2(float2 x) {
+__device__ __forceinline__ float2 fa_ex2_poly_f2(float2 x) {
   constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: x + kRound holds rint(x) in its low mantissa bits
   const float2 one = make_float2(1.0f, 1.0f), neg = make_float2(-1.0f, -1.0f);
   x = make_float2(fmaxf(x.x, -125.0f), fmaxf(x.y, -125.0f));
@@ -316,13 +315,12 @@ __device__ __forceinline__ uint32_t fa_ex2_poly_h2(float2 x) {
   // 2^n: n (two's complement in r's low bits) added to q's exponent field.
   const float ya = __uint_as_float(__float_as_uint(q.x) + (__float_as_uint(r.x) << 23));
   const float yb = __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(r.y) << 23));
-  const __half2 y = __floats2half2_rn(ya, yb);
-  return *reinterpret_cast<const uint32_t*>(&y);
+  return make_float2(ya, yb);
 }
 
 // Shared-memory descriptor for an MN-major operand with the 128-byte swizzle
-// whose MN extent spans two 64-element atoms `lbo` bytes apart (V and the ones
-// column); 8-row K groups 1024 bytes apart.
+// (MN atoms `lbo` bytes apart; V is one atom wide); 8-row K groups 1024 bytes
+// apart.
 __device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t addr, uint32_t lbo) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((addr >> 4) & 0x3fffu);
@@ -377,16 +375,6 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     *abort_flag = 0;
     fence_mbarrier_init();
   }
-  {
-    // The ones atom: MN element 0 (the row-sum column) is 1.0 in every key row;
-    // in the 128-byte swizzle, row r keeps its chunk 0 at chunk r % 8.
-    uint4* ones = reinterpret_cast<uint4*>(smem + FaSmem::ONES);
-    for (int c = threadIdx.x; c < kFaTile / 16; c += kFaThreads) {
-      const int r = c >> 3, chunk = c & 7;
-      ones[c] = make_uint4(chunk == (r & 7) ? 0x3C00u : 0u, 0u, 0u, 0u);  // fp16 1.0 in the low half
-    }
-    fence_proxy_async_smem();
-  }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
@@ -437,7 +425,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       // -------------------------------------------------------- MMA issuer
       if (elect_one()) {
         constexpr uint32_t idesc_qk = idesc_f16(kFaBM, kFaBN);
-        constexpr uint32_t idesc_pv = idesc_f16(kFaBM, kFaPvN) | (1u << 16);  // B (V | ones) MN-major
+        constexpr uint32_t idesc_pv = idesc_f16(kFaBM, kFaD) | (1u << 16);  // B (V) MN-major
         bool ok = mbar_wait(q_full, 0, status, kDevWaitMma, abort_flag);
         // S_i(t) = Q_i K(t)^T (issued once K(t) has landed and the softmax has read S_i(t-1)).
         auto issue_s = [&](int i, int t) {
@@ -454,13 +442,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         auto issue_pv = [&](int i, int u) {
           const int st = u % kFaStages;
           const uint32_t v_addr = smem_u32(smem + FaSmem::KV + (2 * st + 1) * kFaTile);
-          const uint32_t ones_addr = smem_u32(smem + FaSmem::ONES);
-          const uint32_t p_addr = smem_u32(smem + FaSmem::P + 2 * i * kFaTile);
 #pragma unroll
-          for (int kk = 0; kk < kFaBN / 16; ++kk)  // 16 keys per MMA
-            mma_f16(tmem + kFaPvOff + i * kFaPvPitch, smem_desc_k_sw128(p_addr + (kk >> 2) * kFaTile + (kk & 3) * 32),
-                    smem_desc_mn_sw128(v_addr + kk * 2048, ones_addr - v_addr), idesc_pv,
-                    (kk > 0 || u > 0) ? 1u : 0u);  // O accumulates over the key tiles
+          for (int kk = 0; kk < kFaBN / 16; ++kk)  // 16 keys (8 columns of P) per MMA; O accumulates over the key tiles
+            mma_f16_ts(tmem + kFaOOff + i * kFaD, tmem + kFaPOff + i * (kFaBN / 2) + kk * 8,
+                       smem_desc_mn_sw128(v_addr + kk * 2048, 0), idesc_pv, (kk > 0 || u > 0) ? 1u : 0u);
           mma_commit(&pv_full[i]);
           mma_commit(&p_empty[i]);
         };
@@ -521,10 +506,11 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     if (i < nq) {
       const uint32_t lane_addr = static_cast<uint32_t>(qw * 32) << 16;
       const uint32_t ts = tmem + lane_addr + kFaSOff + i * kFaBN;
-      const uint32_t tpv = tmem + lane_addr + kFaPvOff + i * kFaPvPitch;
+      const uint32_t tpv = tmem + lane_addr + kFaOOff + i * kFaD;
+      const uint32_t tp = tmem + lane_addr + kFaPOff + i * (kFaBN / 2);
       float m = -INFINITY;
+      float l = 0.0f;  // the row sum of P (fp32, unrounded values)
       bool ok = true;
-      uint8_t* prow = smem + FaSmem::P + 2 * i * kFaTile + (row >> 3) * 1024 + (row & 7) * 128;
       for (int t = 0; t < ntiles && ok; ++t) {
         const uint32_t par = t & 1u;
         ok = __all_sync(0xffffffffu, mbar_wait(&s_full[i], par, status, kDevWaitEpilogue, abort_flag));
@@ -566,55 +552,54 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         // previous key tile's P V MMA).
         uint32_t pk[kFaBN / 2];
         {
-          const float2 c2 = make_float2(p.c2, p.c2), nm = make_float2(-m_new, -m_new);
+          const float2 c2 = make_float2(p.c2, p.c2), nm = make_float2(-m_new, -m_new), one = make_float2(1.0f, 1.0f);
+          float2 ls[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f),
+                          make_float2(0.0f, 0.0f)};
 #pragma unroll
           for (int c = 0; c < kFaBN; c += 2) {
             const float2 x = ffma2(make_float2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), c2, nm);
-            pk[c >> 1] = (EMU > 0 && ((c >> 1) & 3) < EMU) ? fa_ex2_poly_h2(x) : fa_ex2_h2(x.x, x.y);
+            const float2 y = (EMU > 0 && ((c >> 1) & 3) < EMU) ? fa_ex2_poly_f2(x) : make_float2(fa_ex2(x.x), fa_ex2(x.y));
+            pk[c >> 1] = fa_pack_h2(y);
+            ls[(c >> 1) & 3] = ffma2(y, one, ls[(c >> 1) & 3]);
           }
+          l = __fmaf_rn(l, alpha, ((ls[0].x + ls[0].y) + (ls[1].x + ls[1].y)) + ((ls[2].x + ls[2].y) + (ls[3].x + ls[3].y)));
         }
         ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[i], par ^ 1u, status, kDevWaitEpilogue, abort_flag));
         if (!ok) break;
         if (t > 0 && __any_sync(0xffffffffu, grow)) {
           // The previous P V is complete (p_empty): rescale this warp's rows of O
-          // (and of the row sum in column 64) before the next P V adds into it.
+          // before the next P V adds into it (the row sum was rescaled above).
           tc_fence_after();
-          uint32_t r[kFaD + 8];
+          uint32_t r[kFaD];
           tmem_ld_32x32b_x32(tpv, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
           tmem_ld_32x32b_x32(tpv + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-          tmem_ld_32x32b_x8(tpv + 64, &r[64]);
           tmem_wait_ld();
 #pragma unroll
-          for (int d = 0; d < kFaD + 8; ++d) r[d] = __float_as_uint(__fmul_rn(__uint_as_float(r[d]), alpha));
+          for (int d = 0; d < kFaD; ++d) r[d] = __float_as_uint(__fmul_rn(__uint_as_float(r[d]), alpha));
           tmem_st_32x32b_x32(tpv, *reinterpret_cast<const uint32_t(*)[32]>(&r[0]));
           tmem_st_32x32b_x32(tpv + 32, *reinterpret_cast<const uint32_t(*)[32]>(&r[32]));
-          tmem_st_32x32b_x8(tpv + 64, &r[64]);
-          tmem_wait_st();
-          tc_fence_before();
         }
-#pragma unroll
-        for (int c = 0; c < kFaBN; c += 8) {
-          const int panel = c >> 6, chunk = (c & 63) >> 3;
-          *reinterpret_cast<uint4*>(prow + panel * kFaTile + ((chunk ^ (row & 7)) << 4)) =
-              make_uint4(pk[c / 2], pk[c / 2 + 1], pk[c / 2 + 2], pk[c / 2 + 3]);
-        }
-        fence_proxy_async_smem();  // P (generic-proxy writes) -> visible to the tensor core
+        // P_i into tensor memory (row = lane, two keys per column), then to the MMA.
+        tmem_st_32x32b_x32(tp, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
+        tmem_st_32x32b_x32(tp + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
+        tmem_wait_st();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[i]);
         m = m_new;
       }
       float o[kFaD + 1];  // o[64]: the row sum of P
-      if (ok && ntiles > 0) {  // O and the row sum from TMEM once the last P V is complete
+      if (ok && ntiles > 0) {  // O from TMEM once the last P V is complete
         ok = __all_sync(0xffffffffu, mbar_wait(&pv_full[i], (ntiles - 1) & 1u, status, kDevWaitEpilogue, abort_flag));
         if (ok) {
           tc_fence_after();
-          uint32_t r[kFaD + 8];
+          uint32_t r[kFaD];
           tmem_ld_32x32b_x32(tpv, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
           tmem_ld_32x32b_x32(tpv + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-          tmem_ld_32x32b_x8(tpv + 64, &r[64]);
           tmem_wait_ld();
 #pragma unroll
-          for (int d = 0; d <= kFaD; ++d) o[d] = __uint_as_float(r[d]);
+          for (int d = 0; d < kFaD; ++d) o[d] = __uint_as_float(r[d]);
+          o[kFaD] = l;
         }
       }
       const int64_t tq = q0 + i * kFaBM + row;
@@ -681,8 +666,8 @@ cudaError_t launch_attention_f16(const void* q, const void* k, const void* v, co
   p.c2 = scale * 1.4426950408889634f;  // log2(e)
   p.o = static_cast<__half*>(o);
   p.ldo = ldo_halves;
-  // A quarter of the exps on the FMA pipe.
-  constexpr auto kernel = attention_f16_kernel<1>;
+  // Half of the exps on the FMA pipe.
+  constexpr auto kernel = attention_f16_kernel<2>;
   static bool attr_set[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
