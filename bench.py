@@ -632,8 +632,9 @@ def ss_block_side(b2q, flush, stream, dev, cpu=False, iters=10):
     out = {"config": dict(SS_BLOCK, weights="Q8_0", mlp_ratio=4), "block_ms": round(ms, 4),
            "linear_int_ops": lin_ops, "attention_flops": attn_flops,
            "path": "libb2q: norm_modulate_q8, layer_norm_q8, act_prepare, mul_mat_prepared, qkv_heads, "
-                   "rows_to_heads, heads_act_prepare, mul_mat_prepared_gate_residual, mul_mat_prepared_gelu_q8; "
-                   "b2q_attention_f16 (self and cross attention cores, tensor cores)",
+                   "rows_to_heads, mul_mat_prepared_gate_residual, mul_mat_prepared_gelu_q8; "
+                   "b2q_attention_f16_q8 (self and cross attention cores on tensor cores, the to_out Q8_0 "
+                   "quantize in their epilogue)",
            "not_included": "the 4-token pose group, the adaLN projection (both are in ss_step)"}
     if cpu:
         out["cpu"] = cpu_block_seconds(weights, B, T, C, H, nc)
@@ -838,7 +839,7 @@ def ss_step_side(b2q, stream, dev, cpu=False, iters=5):
            "linear_tops_effective": round(lin_ops / (graph_ms * 1e-3) / 1e12, 1),
            "state_finite": finite,
            "path": "ss_flow.SsSampler: libb2q for every quantized linear, norm, quantize, head layout and "
-                   "fused epilogue and the attention cores (b2q_attention_f16); torch for the K<=8 F32 input layers, "
+                   "fused epilogue and the attention cores (b2q_attention_f16_q8); torch for the K<=8 F32 input layers, "
                    "timestep cos/sin/SiLU and the Euler update"}
     if cpu:
         out["cpu"] = cpu_ss_step()

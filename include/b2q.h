@@ -349,6 +349,16 @@ B2Q_API int b2q_heads_act_prepare(const void* o16, int64_t B, int64_t T, int64_t
 B2Q_API int b2q_attention_f16(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t Tq,
                               int64_t Tk, int64_t D, const void* k2, const void* v2, int64_t Tk2, float scale,
                               void* o, int64_t o_row_stride_bytes, void* stream);
+/* b2q_attention_f16 with the output going straight into the output projection's
+ * Q8_0 prepared activations (b2q_act_prepare layout, rows b*Tq + t, K = H*64,
+ * act 256-byte aligned, act_bytes >= b2q_act_prepared_size(B*Tq, H*64)): each
+ * output is rounded to fp16 as b2q_attention_f16 stores it and quantized with
+ * `variant`'s arithmetic, so the bytes equal b2q_attention_f16 followed by
+ * b2q_heads_act_prepare (the self- and cross-attention outputs of
+ * cpp_ggml/src/ss_flow_graph.cpp:277-289 and 346-349 feeding their to_out linears). */
+B2Q_API int b2q_attention_f16_q8(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t Tq,
+                                 int64_t Tk, int64_t D, const void* k2, const void* v2, int64_t Tk2, float scale,
+                                 int variant, void* act, size_t act_bytes, void* stream);
 B2Q_API int b2q_qkv_heads_f32(const float* qkv, int64_t B, int64_t T, int64_t H, int64_t D,
                               int64_t qkv_row_stride_bytes, const float* gamma_q, const float* gamma_k, float eps,
                               float* q, float* k, float* v, void* stream);

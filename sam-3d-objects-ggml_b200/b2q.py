@@ -85,6 +85,7 @@ def _lib_obj():
             "b2q_rows_to_heads_f32": (I, [P, I64, I64, I64, I64, I, I64, P, P, P]),
             "b2q_attention_f32": (I, [P, P, P, I64, I64, I64, I64, I64, P, P, I64, ctypes.c_float, P, I64, P]),
             "b2q_attention_f16": (I, [P, P, P, I64, I64, I64, I64, I64, P, P, I64, ctypes.c_float, P, I64, P]),
+            "b2q_attention_f16_q8": (I, [P, P, P, I64, I64, I64, I64, I64, P, P, I64, ctypes.c_float, I, P, SZ, P]),
             "b2q_layer_norm_q8": (I, [P, I64, I64, I64, ctypes.c_float, P, P, I, P, SZ, P]),
             "b2q_mul_mat_prepared_gate_residual": (I, [P, I64, I64, P, I64, P, P, P, I64, P, I64, P]),
             "b2q_norm_modulate": (I, [P, I64, I64, I64, ctypes.c_float, P, P, P, I64, P]),
@@ -514,6 +515,29 @@ def attention_f16(q, k, v, k2=None, v2=None, scale: float | None = None, out=Non
     rc = lib().b2q_attention_f16(_ptr(q), _ptr(k), _ptr(v), B, H, Tq, Tk, D, _ptr(k2), _ptr(v2), Tk2, scale,
                                  _ptr(out), out.stride(0) * 2, _stream(stream))
     _check("b2q_attention_f16", rc)
+    return out
+
+
+def attention_f16_q8(q, k, v, k2=None, v2=None, scale: float | None = None, variant: int = ACT_X86, out=None,
+                     stream=None):
+    """attention_f16 with the output as the output projection's Q8_0 prepared
+    activations (rows b*Tq + t, K = H*64): the bytes of heads_act_prepare of
+    attention_f16's output, in one launch."""
+    import math
+    torch = _torch()
+    B, H, Tq, D = q.shape
+    Tk = k.shape[2]
+    Tk2 = k2.shape[2] if k2 is not None else 0
+    for t in (q, k, v, k2, v2):
+        assert t is None or (t.dtype == torch.float16 and t.is_contiguous())
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    size = act_prepared_size(B * Tq, H * D)
+    if out is None:
+        out = _empty_aligned(size, q.device)
+    rc = lib().b2q_attention_f16_q8(_ptr(q), _ptr(k), _ptr(v), B, H, Tq, Tk, D, _ptr(k2), _ptr(v2), Tk2, scale,
+                                    variant, _ptr(out), out.numel(), _stream(stream))
+    _check("b2q_attention_f16_q8", rc)
     return out
 
 

@@ -872,6 +872,31 @@ int b2q_attention_f16(const void* q, const void* k, const void* v, int64_t B, in
                                         o_row_stride_bytes / 2, static_cast<cudaStream_t>(stream)));
 }
 
+int b2q_attention_f16_q8(const void* q, const void* k, const void* v, int64_t B, int64_t H, int64_t Tq, int64_t Tk,
+                         int64_t D, const void* k2, const void* v2, int64_t Tk2, float scale, int variant, void* act,
+                         size_t act_bytes, void* stream) {
+  if (B < 0 || Tq < 0 || Tk < 0 || H <= 0 || !std::isfinite(scale)) return B2Q_ERR_INVALID_ARG;
+  if (D != 64) return B2Q_ERR_UNSUPPORTED;
+  if (variant != B2Q_ACT_X86 && variant != B2Q_ACT_REF) return B2Q_ERR_INVALID_ARG;
+  if ((k2 == nullptr) != (v2 == nullptr) || (k2 && Tk2 < 0)) return B2Q_ERR_INVALID_ARG;
+  const int64_t tk_all = Tk + (k2 ? Tk2 : 0);
+  if (B * Tq > 0 && (!q || !act || tk_all <= 0 || (Tk > 0 && (!k || !v)))) return B2Q_ERR_INVALID_ARG;
+  const int64_t rows = B * H * (Tq > tk_all ? Tq : tk_all);
+  if (B > 65535 || H > 65535 || rows + 128 > INT_MAX || (Tq + 127) / 128 > INT_MAX || B * Tq > INT_MAX ||
+      H * D > INT_MAX)
+    return B2Q_ERR_TOO_LARGE;
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(k2, 16) || !aligned(v2, 16) ||
+      !aligned(act, 256))
+    return B2Q_ERR_MISALIGNED;
+  if (act_bytes < split_bytes(B * Tq, H * D)) return B2Q_ERR_WORKSPACE;
+  if (B * Tq == 0) return B2Q_OK;
+  if (int rc = check_device(nullptr)) return rc;
+  const SplitOperand a = split_at(static_cast<uint8_t*>(act), B * Tq, H * D);
+  return from_cuda(launch_attention_f16_q8(q, k, v, k2, v2, B, static_cast<int>(H), Tq, Tk, k2 ? Tk2 : 0, scale,
+                                           const_cast<int8_t*>(a.codes), const_cast<float*>(a.scales), a.ld, variant,
+                                           static_cast<cudaStream_t>(stream)));
+}
+
 int b2q_layer_norm_q8(const float* x, int64_t m, int64_t c, int64_t x_row_stride_bytes, float eps, const float* weight,
                       const float* bias, int variant, void* act, size_t act_bytes, void* stream) {
   if (int rc = check_norm(x, m, c, x_row_stride_bytes, eps, weight, bias)) return rc;

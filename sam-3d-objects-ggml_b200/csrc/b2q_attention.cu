@@ -26,6 +26,7 @@
 // and row sum are 16-lane shuffles.
 #include "b2q_internal.h"
 #include "b2q_ptx.cuh"
+#include "b2q_q8.cuh"
 
 #include <cuda_fp16.h>
 
@@ -272,6 +273,12 @@ struct FaParams {
   float c2;            // scale * log2(e)
   __half* o;
   int64_t ldo;         // halves
+  // Q8_0 form: the output projection's prepared activations (codes [B*Tq][H*64],
+  // fp32 split scales [H*2][qld]) instead of o; qvar: the quantizer variant.
+  int8_t* qc;
+  float* qs;
+  int64_t qld;
+  int qvar;
 };
 
 __device__ __forceinline__ float fa_max3(float a, float b, float c) {
@@ -331,8 +338,35 @@ __device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t addr, uint32_t l
   return d;
 }
 
-// EMU: of every 4 exp pairs, how many run as the FMA-pipe polynomial.
-template <int EMU>
+// One thread's row of one head (64 fp16-rounded outputs) -> two Q8_0 blocks of
+// the prepared activations: the stand-alone quantizer's arithmetic on the same
+// fp16 values, so the bytes equal b2q_heads_act_prepare of the fp16 output.
+template <int VARIANT>
+__device__ __forceinline__ void fa_store_q8(const float (&hv)[kFaD], int8_t* codes, float* scales, int64_t ld) {
+#pragma unroll
+  for (int j = 0; j < kFaD / kQK; ++j) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kQK; ++i) amax = fmaxf(amax, fabsf(hv[j * kQK + i]));
+    float d, inv;
+    q8_scale<VARIANT>(amax, d, inv);
+    uint32_t q[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float* v = &hv[j * kQK + 4 * i];
+      q[i] = quantize_code<VARIANT>(v[0], inv) | (quantize_code<VARIANT>(v[1], inv) << 8) |
+             (quantize_code<VARIANT>(v[2], inv) << 16) | (quantize_code<VARIANT>(v[3], inv) << 24);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(codes + j * kQK);
+    dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
+    dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
+    scales[j * ld] = q8_split_scale(d);
+  }
+}
+
+// EMU: of every 4 exp pairs, how many run as the FMA-pipe polynomial.  Q8: the
+// output goes out as Q8_0 prepared activations (FaParams::qc / qs).
+template <int EMU, bool Q8>
 __global__ void __launch_bounds__(kFaThreads, 1)
     attention_f16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_k2,
@@ -603,7 +637,19 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         }
       }
       const int64_t tq = q0 + i * kFaBM + row;
-      if (ok && tq < p.Tq) {
+      if (Q8 && ok && tq < p.Tq) {
+        const float inv = 1.0f / o[kFaD];
+        float hv[kFaD];  // the fp16 output values, as the fp16 form stores them
+#pragma unroll
+        for (int d = 0; d < kFaD; ++d) hv[d] = __half2float(__float2half_rn(o[d] * inv));
+        const int64_t r = static_cast<int64_t>(blockIdx.z) * p.Tq + tq;
+        int8_t* codes = p.qc + r * (static_cast<int64_t>(p.H) * kFaD) + static_cast<int64_t>(blockIdx.y) * kFaD;
+        float* scales = p.qs + static_cast<int64_t>(blockIdx.y) * (kFaD / kQK) * p.qld + r;
+        if (p.qvar == 0)
+          fa_store_q8<0>(hv, codes, scales, p.qld);
+        else
+          fa_store_q8<1>(hv, codes, scales, p.qld);
+      } else if (ok && tq < p.Tq) {
         const float inv = 1.0f / o[kFaD];
         __half* dst = p.o + (static_cast<int64_t>(blockIdx.z) * p.Tq + tq) * p.ldo +
                       static_cast<int64_t>(blockIdx.y) * kFaD;
@@ -642,9 +688,12 @@ cudaError_t launch_attention_f32(const float* q, const float* k, const float* v,
   }
 }
 
-cudaError_t launch_attention_f16(const void* q, const void* k, const void* v, const void* k2, const void* v2,
-                                 int64_t B, int H, int64_t Tq, int64_t Tk, int64_t Tk2, float scale, void* o,
-                                 int64_t ldo_halves, cudaStream_t s) {
+namespace {
+
+template <bool Q8>
+cudaError_t launch_attention_f16_t(const void* q, const void* k, const void* v, const void* k2, const void* v2,
+                                   int64_t B, int H, int64_t Tq, int64_t Tk, int64_t Tk2, float scale, FaParams p,
+                                   cudaStream_t s) {
   if (B == 0 || Tq == 0) return cudaSuccess;
   CUtensorMap tq, tk, tv, tk2, tv2;
   const uint64_t bh = static_cast<uint64_t>(B) * H;
@@ -656,7 +705,6 @@ cudaError_t launch_attention_f16(const void* q, const void* k, const void* v, co
   const bool second = k2 && Tk2 > 0;
   if (!map(&tk2, second ? k2 : k, second ? bh * Tk2 : bh * Tk) || !map(&tv2, second ? v2 : v, second ? bh * Tk2 : bh * Tk))
     return cudaErrorInvalidValue;
-  FaParams p;
   p.n1 = static_cast<int>((Tk + kFaBN - 1) / kFaBN);
   p.n2 = second ? static_cast<int>((Tk2 + kFaBN - 1) / kFaBN) : 0;
   p.Tq = Tq;
@@ -664,10 +712,8 @@ cudaError_t launch_attention_f16(const void* q, const void* k, const void* v, co
   p.Tk2 = second ? Tk2 : 0;
   p.H = H;
   p.c2 = scale * 1.4426950408889634f;  // log2(e)
-  p.o = static_cast<__half*>(o);
-  p.ldo = ldo_halves;
   // Half of the exps on the FMA pipe.
-  constexpr auto kernel = attention_f16_kernel<2>;
+  constexpr auto kernel = attention_f16_kernel<2, Q8>;
   static bool attr_set[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
@@ -687,6 +733,28 @@ cudaError_t launch_attention_f16(const void* q, const void* k, const void* v, co
                   static_cast<unsigned>(B));
   kernel<<<grid, kFaThreads, FaSmem::BYTES, s>>>(tq, tk, tv, tk2, tv2, p);
   return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_attention_f16(const void* q, const void* k, const void* v, const void* k2, const void* v2,
+                                 int64_t B, int H, int64_t Tq, int64_t Tk, int64_t Tk2, float scale, void* o,
+                                 int64_t ldo_halves, cudaStream_t s) {
+  FaParams p{};
+  p.o = static_cast<__half*>(o);
+  p.ldo = ldo_halves;
+  return launch_attention_f16_t<false>(q, k, v, k2, v2, B, H, Tq, Tk, Tk2, scale, p, s);
+}
+
+cudaError_t launch_attention_f16_q8(const void* q, const void* k, const void* v, const void* k2, const void* v2,
+                                    int64_t B, int H, int64_t Tq, int64_t Tk, int64_t Tk2, float scale,
+                                    int8_t* codes, float* scales, int64_t ld, int variant, cudaStream_t s) {
+  FaParams p{};
+  p.qc = codes;
+  p.qs = scales;
+  p.qld = ld;
+  p.qvar = variant;
+  return launch_attention_f16_t<true>(q, k, v, k2, v2, B, H, Tq, Tk, Tk2, scale, p, s);
 }
 
 cudaError_t read_attention_status(unsigned int* value, bool clear) {

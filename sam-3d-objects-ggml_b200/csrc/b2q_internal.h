@@ -152,6 +152,12 @@ cudaError_t launch_attention_f32(const float* q, const float* k, const float* v,
 cudaError_t launch_attention_f16(const void* q, const void* k, const void* v, const void* k2, const void* v2,
                                  int64_t B, int H, int64_t Tq, int64_t Tk, int64_t Tk2, float scale, void* o,
                                  int64_t ldo_halves, cudaStream_t s);
+// The same with the output as the output projection's Q8_0 prepared activations
+// (rows b*Tq + t, K = H*64; codes [rows][K], fp32 split scales [K/32][ld]),
+// byte-equal to launch_attention_f16 followed by launch_heads_q8.
+cudaError_t launch_attention_f16_q8(const void* q, const void* k, const void* v, const void* k2, const void* v2,
+                                    int64_t B, int H, int64_t Tq, int64_t Tk, int64_t Tk2, float scale,
+                                    int8_t* codes, float* scales, int64_t ld, int variant, cudaStream_t s);
 // Status word of the attention kernels' bounded waits (its own translation unit).
 cudaError_t read_attention_status(unsigned int* value, bool clear);
 

@@ -4,18 +4,19 @@ cpp_ggml/src/ss_flow_graph.cpp:180-388), built from libb2q's entry points:
     h = modulate(norm(x), scale_msa, shift_msa)          b2q_norm_modulate_q8
     qkv = h . W_qkv + b_qkv                               b2q_mul_mat_prepared
     q, k = rms_norm_head(q) * gq, rms_norm_head(k) * gk   b2q_qkv_heads (fp16 q, k, v)
-    o = softmax(q k^T / sqrt(D)) v                        attention core (see below)
-    x = x + gate_msa * (o . W_out + b_out)               b2q_heads_act_prepare + _gate_residual
+    o = softmax(q k^T / sqrt(D)) v                        attention core (see below), Q8_0 out
+    x = x + gate_msa * (o . W_out + b_out)               _gate_residual
     h = norm(x) * w2 + b2n                                b2q_layer_norm_q8           (cross-attention,
     q = h . W_xq + b_xq;  k | v = cond . W_xkv + b_xkv    b2q_mul_mat_prepared         :308-352)
     o = softmax(q k^T / sqrt(D)) v                        b2q_rows_to_heads, attention core
-    x = x + (o . W_xout + b_xout)                         b2q_heads_act_prepare + _gate_residual
+    x = x + (o . W_xout + b_xout)                         _gate_residual
     h = modulate(norm(x), scale_mlp, shift_mlp)          b2q_norm_modulate_q8
     x = x + gate_mlp * (gelu(h . W1 + b1) . W2 + b2)     _gelu_q8 + _gate_residual
 
 Every linear, norm, quantize, epilogue and attention core is libb2q's (the
-attention: b2q_attention_f16, tensor cores, fp16 q, k, v and o, fp32 softmax;
-its token-major fp16 rows go to b2q_heads_act_prepare as a strided view).
+attention: b2q_attention_f16_q8, tensor cores, fp16 q, k, v and o, fp32 softmax,
+its fp16 output quantized in the same kernel into the to_out linear's Q8_0
+activations -- the bytes of b2q_heads_act_prepare of b2q_attention_f16's rows).
 Modulation vectors are shared by
 the batch (the CFG branches of one step share the timestep embedding).  The
 4-token pose group (whose tiny linears run on the few-token kernel) and the
@@ -65,16 +66,14 @@ class SsBlock:
         cond: fp32 [B*n_cond, C] condition tokens."""
         C, H, D, v = self.C, self.H, self.D, self.vec
 
-        def attend(q, k, vv):
-            Tq = q.shape[2]
-            return b2q.attention_f16(q, k, vv, stream=stream).view(B, Tq, H, D).permute(0, 2, 1, 3)
+        def attend(q, k, vv):  # -> the to_out linear's Q8_0 prepared activations
+            return b2q.attention_f16_q8(q, k, vv, stream=stream)
 
         M = B * T
         act = b2q.norm_modulate_q8(x, 1e-6, v["scale_msa"], v["shift_msa"], stream=stream)
         qkv = b2q.mul_mat_prepared(self.packed["qkv"], 3 * C, C, act, M, bias=v["b_qkv"], stream=stream)
         q, k, vv = b2q.qkv_heads(qkv, B, T, H, D, v["gq"], v["gk"], 1e-6, stream=stream)
-        o = attend(q, k, vv)  # [B, H, T, D] fp16 view of token-major rows
-        act_o = b2q.heads_act_prepare(o, stream=stream)
+        act_o = attend(q, k, vv)
         b2q.mul_mat_prepared_gate_residual(self.packed["out"], C, C, act_o, M, x, bias=v["b_out"],
                                            gate=v["gate_msa"], out=x, stream=stream)
         # cross-attention to the condition tokens
@@ -84,8 +83,7 @@ class SsBlock:
         xkv = b2q.mul_mat_prepared(self.packed["xkv"], 2 * C, C, act_c, B * n_cond, bias=v["b_xkv"], stream=stream)
         (q,) = b2q.rows_to_heads(xq, B, T, H, D, 1, stream=stream)
         k, vv = b2q.rows_to_heads(xkv, B, n_cond, H, D, 2, stream=stream)
-        o = attend(q, k, vv)
-        act_o = b2q.heads_act_prepare(o, stream=stream)
+        act_o = attend(q, k, vv)
         b2q.mul_mat_prepared_gate_residual(self.packed["xout"], C, C, act_o, M, x, bias=v["b_xout"], out=x,
                                            stream=stream)
         act2 = b2q.norm_modulate_q8(x, 1e-6, v["scale_mlp"], v["shift_mlp"], stream=stream)

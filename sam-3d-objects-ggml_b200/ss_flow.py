@@ -165,18 +165,17 @@ class SsFlow:
         return heads(qkv, B, T, H, D, self.V[p + "gq"], self.V[p + "gk"], EPS)
 
     def _attend(self, q, k, v, k2=None, v2=None):
-        """The attention core: fp16 heads -> libb2q's tensor-core attention, fp16
-        o viewed as [B, H, T, D] over its token-major rows (production), or fp32
-        heads -> fp32 rows [B*T, C] (F32 contract).  k2 / v2: a second key
-        source appended after k / v."""
+        """The attention core, its output as the to_out linear's Q8_0 prepared
+        activations: fp16 heads -> libb2q's tensor-core attention with the
+        quantize in its epilogue (production; the bytes of heads_act_prepare of
+        its fp16 rows), or fp32 heads -> fp32 rows [B*T, C] -> act_prepare (F32
+        contract).  k2 / v2: a second key source appended after k / v."""
         if self.attn == "f32":
-            return b2q.attention_f32(q, k, v, k2, v2)
-        B, H, T, D = q.shape
-        return b2q.attention_f16(q, k, v, k2, v2).view(B, T, H, D).permute(0, 2, 1, 3)
+            return b2q.act_prepare(b2q.attention_f32(q, k, v, k2, v2))
+        return b2q.attention_f16_q8(q, k, v, k2, v2)
 
-    def _attn_out(self, g: str, i: int, o, x, gate, name: str = "out"):
+    def _attn_out(self, g: str, i: int, act, x, gate, name: str = "out"):
         p = f"b{i}.{g}.{name}"
-        act = b2q.act_prepare(o) if self.attn == "f32" else b2q.heads_act_prepare(o)
         b2q.mul_mat_prepared_gate_residual(self.W[p], self.C, self.C, act, x.shape[0], x, bias=self.V[p + ".b"],
                                            gate=gate, out=x)
 

@@ -71,3 +71,51 @@ def test_attention_f16_output_feeds_the_projection_quantizer(b2q_mod, dev):
     a = b2q.heads_act_prepare(o_bhtd)
     b = b2q.heads_act_prepare(o_bhtd.contiguous())
     assert torch.equal(a, b)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("variant", [0, 1])
+@pytest.mark.parametrize("B,H,Tq,Tk,Tk2", [
+    (2, 16, 4096, 4096, 0),   # SS self-attention
+    (2, 16, 4096, 1374, 0),   # SS cross-attention
+    (2, 16, 4, 4, 4096),      # pose group: its own keys, then the shape keys
+    (1, 2, 100, 70, 0),       # ragged query and key tiles
+    (3, 3, 257, 129, 5),      # a partial second query tile; second source of five
+])
+def test_attention_f16_q8_equals_attention_then_quantize(b2q_mod, dev, variant, B, H, Tq, Tk, Tk2):
+    """The fused Q8_0 output writes the bytes of heads_act_prepare applied to
+    attention_f16's fp16 rows, codes and split scales alike."""
+    import torch
+    g = torch.Generator(device=dev).manual_seed(B * 1000 + Tq + Tk + Tk2 + variant)
+    q = torch.randn(B, H, Tq, 64, device=dev, generator=g).half()
+    k, v = (torch.randn(B, H, Tk, 64, device=dev, generator=g).half() for _ in range(2))
+    k2 = v2 = None
+    if Tk2:
+        k2, v2 = (torch.randn(B, H, Tk2, 64, device=dev, generator=g).half() for _ in range(2))
+    o = b2q.attention_f16(q, k, v, k2, v2).view(B, Tq, H, 64).permute(0, 2, 1, 3)
+    ref = b2q.heads_act_prepare(o, variant=variant)
+    got = b2q.attention_f16_q8(q, k, v, k2, v2, variant=variant)
+    torch.cuda.synchronize()
+    M, K = B * Tq, H * 64
+    mp = (M + 3) // 4 * 4
+    code_bytes = M * K
+    scale_off = (code_bytes + 255) // 256 * 256
+    assert torch.equal(got[:code_bytes], ref[:code_bytes])
+    gs = got[scale_off:scale_off + 4 * mp * (K // 32)].view(torch.float32).view(K // 32, mp)[:, :M]
+    rs = ref[scale_off:scale_off + 4 * mp * (K // 32)].view(torch.float32).view(K // 32, mp)[:, :M]
+    assert torch.equal(gs, rs)
+    assert b2q.device_status() == 0
+
+
+FAKE = 1 << 20
+
+
+@pytest.mark.parametrize("args,expect", [
+    ((FAKE, FAKE, FAKE, 1, 2, 64, 64, 32, None, None, 0, 0.125, 0, FAKE, 1 << 20), 2),   # D != 64: unsupported
+    ((FAKE, FAKE, FAKE, 1, 2, 64, 64, 64, None, None, 0, 0.125, 7, FAKE, 1 << 20), 1),   # variant
+    ((FAKE, FAKE, FAKE, 1, 2, 64, 64, 64, FAKE, None, 4, 0.125, 0, FAKE, 1 << 20), 1),   # k2 without v2
+    ((FAKE, FAKE, FAKE, 1, 2, 64, 64, 64, None, None, 0, 0.125, 0, FAKE + 16, 1 << 20), 3),  # act alignment
+    ((FAKE, FAKE, FAKE, 1, 2, 64, 64, 64, None, None, 0, 0.125, 0, FAKE, 100), 4),       # act too small
+])
+def test_attention_f16_q8_argument_checks(b2q_mod, args, expect):
+    assert b2q_mod.lib().b2q_attention_f16_q8(*args, None) == expect
