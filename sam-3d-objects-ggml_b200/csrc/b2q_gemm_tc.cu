@@ -122,6 +122,11 @@ struct Cfg {
   static constexpr int XPOSE_OFF = (BAR_OFF + NBARS * 8 + 16 + 127) / 128 * 128;
   static constexpr int XPOSE_FLOATS = 32 * 33;
   static constexpr int SMEM_XPOSE = XPOSE_OFF + 8 * XPOSE_FLOATS * 4 + 1024;
+  // Plain tile end through TMA stores only: one [COLS tokens][32 rows] fp32 box
+  // per epilogue warp (128-byte rows, the layout of y), stored asynchronously.
+  static constexpr int STO_OFF = XPOSE_OFF;
+  static constexpr int STO_WARP_FLOATS = COLS * 32;
+  static constexpr int SMEM_STO = STO_OFF + kEpiWarps * STO_WARP_FLOATS * 4 + 1024;
   static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte swizzle alignment");
   static_assert(STAGES <= 16, "stage bitmasks");
 };
@@ -145,6 +150,7 @@ enum Mode : int {
   kModeGeluQ8 = 4,  // fused GELU + Q8_0 quantize of the output (next layer's input)
   kModeGateRes = 5, // y = resid + gate * (w . x + bias): the DiT branch's gated residual
   kModeGeluQ8Peers = 6,  // column-parallel GELU + Q8_0: the quantized tile goes into every rank's activations
+  kModeStoreTma = 7,     // as plain, each epilogue warp's part of the tile leaves by one TMA store
 };
 
 // Output arguments of the non-plain variants, a separate kernel parameter:
@@ -318,8 +324,10 @@ template <int STAGES, int BN, int MODE, bool Q4C>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_wc, const __grid_constant__ CUtensorMap tm_ac,
                    const __grid_constant__ CUtensorMap tm_ws, const __grid_constant__ CUtensorMap tm_as,
-                   const TcParams p, const __grid_constant__ OutParams pp) {
+                   const __grid_constant__ CUtensorMap tm_y, const TcParams p, const __grid_constant__ OutParams pp) {
   constexpr bool DUMP = MODE == kModeDump, PEERS = MODE == kModePeers, STALL = MODE == kModeStall;
+  constexpr bool TST = MODE == kModeStoreTma;
+  static_assert(!(TST && Q4C), "the compact Q4_0 stages leave no room for the store boxes");
   constexpr bool PQ = MODE == kModeGeluQ8Peers;
   constexpr bool GELUQ = MODE == kModeGeluQ8 || PQ, GATERES = MODE == kModeGateRes;
   using C = Cfg<STAGES, BN, Q4C>;
@@ -558,6 +566,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok || (!GELUQ && !p.y)) continue;
       const int64_t n = static_cast<int64_t>(tile % p.n_tiles) * kBM + row;
       const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * BN + chalf * COLS;
+      if (TST) {
+        // The warp's 32 rows x COLS tokens go through its own box in shared
+        // memory and leave by one TMA store, so the next tile's blocks start at
+        // once instead of behind 2*COLS global stores per thread.  N % 32 == 0:
+        // the warp's rows are all valid or all not; rows and tokens past the
+        // tensor's edge are not written by the store.
+        const int64_t nq = static_cast<int64_t>(tile % p.n_tiles) * kBM + quarter * 32;
+        if (nq < p.N && m0 < p.M) {
+          float* st = reinterpret_cast<float*>(smem + C::STO_OFF) + (warp - kEpiWarp0) * C::STO_WARP_FLOATS;
+          const float bv = p.bias ? p.bias[n] : 0.0f;
+          const float2 b2 = make_float2(bv, bv), one = make_float2(1.0f, 1.0f);  // as the plain tile end
+          if (lane == 0) bulk_wait_read_all();  // the warp's previous box has left shared memory
+          __syncwarp();
+#pragma unroll
+          for (int c = 0; c < COLS / 2; ++c) {
+            const float2 v = ffma2(acc[c], one, b2);
+            st[(2 * c) * 32 + lane] = v.x;
+            st[(2 * c + 1) * 32 + lane] = v.y;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tm_y, st, static_cast<int32_t>(nq), static_cast<int32_t>(m0));
+            bulk_commit();
+          }
+        }
+        continue;
+      }
       if (GELUQ) {
         // The warp's 32 weight rows are one Q8_0 block of the next layer's K
         // (N % 32 == 0, so they are all valid or all not).
@@ -624,6 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    if (TST && lane == 0) bulk_wait_all();  // the warp's stores complete before the CTA exits
   }
 
   tc_fence_before();
@@ -713,8 +750,18 @@ cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
   pp.gate = g.gate;
   pp.resid = g.resid;
   pp.ldr = g.ldr;
+  CUtensorMap tm_y{};
+  if constexpr (MODE == kModeStoreTma) {
+    // y as [M][ldy] fp32, one box = one epilogue warp's 32 rows x COLS tokens.
+    // A shape the map cannot describe takes the plain tile end instead.
+    if (!make_map_2d(&tm_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, g.y, g.N, g.M, g.ldy * 4, 32, C::COLS,
+                     CU_TENSOR_MAP_SWIZZLE_NONE))
+      return launch_cfg<STAGES, BN, kModePlain, Q4C>(g, num_sms, s);
+  }
   auto kern = gemm_tc_kernel<STAGES, BN, MODE, Q4C>;
-  constexpr int smem_bytes = (MODE == kModeGeluQ8 || MODE == kModeGeluQ8Peers) ? C::SMEM_XPOSE : C::SMEM;
+  constexpr int smem_bytes = (MODE == kModeGeluQ8 || MODE == kModeGeluQ8Peers) ? C::SMEM_XPOSE
+                             : MODE == kModeStoreTma                           ? C::SMEM_STO
+                                                                               : C::SMEM;
   static_assert(smem_bytes <= 227 * 1024, "shared memory per CTA");
   // Checked and set once per device (a bit per device; the calls cost more
   // host time than the rest of the launch).
@@ -732,7 +779,7 @@ cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
     ready.fetch_or(bit, std::memory_order_acq_rel);
   }
   const int grid = p.num_tiles < num_sms ? p.num_tiles : num_sms;
-  kern<<<grid, kThreads, smem_bytes, s>>>(tm_wc, tm_ac, tm_ws, tm_as, p, pp);
+  kern<<<grid, kThreads, smem_bytes, s>>>(tm_wc, tm_ac, tm_ws, tm_as, tm_y, p, pp);
   return cudaGetLastError();
 }
 
@@ -809,6 +856,9 @@ cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, cudaStream_t s) {
   if (g.M <= kGemvMaxM && g.n_peers == 0) return launch_gemv(g, s);
   if (g.resid) return launch_picked<kModeGateRes>(g, num_sms, s);
   if (g.n_peers > 0) return launch_picked<kModePeers>(g, num_sms, s);
+  // TMA-stored tile ends when y's rows are 16-byte aligned and whole 32-row boxes.
+  if (g.y && reinterpret_cast<uintptr_t>(g.y) % 16 == 0 && g.ldy % 4 == 0 && g.N % 32 == 0)
+    return launch_picked<kModeStoreTma>(g, num_sms, s);
   return launch_picked<kModePlain>(g, num_sms, s);
 }
 
