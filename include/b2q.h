@@ -314,6 +314,19 @@ B2Q_API int b2q_qkv_heads(const float* qkv, int64_t B, int64_t T, int64_t H, int
  * fp16 [B][H][T][D] each (out1 used when parts == 2). */
 B2Q_API int b2q_rows_to_heads(const float* src, int64_t B, int64_t T, int64_t H, int64_t D, int parts,
                               int64_t src_row_stride_bytes, void* out0, void* out1, void* stream);
+/* b2q_mul_mat_prepared (+ bias) with the head layout as its tile end: the
+ * cross-attention's q projection (parts = 1) or its fused k | v projection of
+ * the condition tokens (parts = 2) straight into fp16 [B][H][T][64] heads
+ * (cpp_ggml/src/ss_flow_graph.cpp:297-345: ggml_mul_mat + ggml_add, then the
+ * reshape / permute / cast to F16 that gb_attention's flash path reads,
+ * graph_builder.cpp:151-171).  n = parts*H*64, m = B*T; each output is the fp32
+ * value b2q_mul_mat_prepared writes, rounded once to fp16, so the bytes equal
+ * b2q_mul_mat_prepared followed by b2q_rows_to_heads.  D other than 64 and
+ * m <= 8 (the few-token path; use the two calls) return B2Q_ERR_UNSUPPORTED;
+ * packed and act 256-byte aligned, out0 / out1 2-byte aligned. */
+B2Q_API int b2q_mul_mat_prepared_heads_f16(const void* packed, int64_t n, int64_t k, const void* act, int64_t m,
+                                           const float* bias, int64_t B, int64_t T, int64_t H, int64_t D,
+                                           int parts, void* out0, void* out1, void* stream);
 B2Q_API int b2q_heads_act_prepare(const void* o16, int64_t B, int64_t T, int64_t H, int64_t D, int64_t stride_b,
                                   int64_t stride_h, int64_t stride_t, int variant, void* act, size_t act_bytes,
                                   void* stream);

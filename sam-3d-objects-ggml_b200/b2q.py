@@ -25,6 +25,7 @@ TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q8_0, TYPE_Q4_K = 0, 1, 2, 8, 12
 ACT_X86, ACT_REF, ACT_Q8_K = 0, 1, 2
 QK, QK_K = 32, 256
 BLOCK_BYTES = {TYPE_Q8_0: 34, TYPE_Q4_0: 18}
+GEMV_MAX_M = 8  # token counts up to this run on the CUDA-core few-token kernel
 
 OK = 0
 STATUS = {
@@ -81,6 +82,7 @@ def _lib_obj():
             "b2q_qkv_heads": (I, [P, I64, I64, I64, I64, I64, P, P, ctypes.c_float, P, P, P, P]),
             "b2q_heads_act_prepare": (I, [P, I64, I64, I64, I64, I64, I64, I64, I, P, SZ, P]),
             "b2q_rows_to_heads": (I, [P, I64, I64, I64, I64, I, I64, P, P, P]),
+            "b2q_mul_mat_prepared_heads_f16": (I, [P, I64, I64, P, I64, P, I64, I64, I64, I64, I, P, P, P]),
             "b2q_qkv_heads_f32": (I, [P, I64, I64, I64, I64, I64, P, P, ctypes.c_float, P, P, P, P]),
             "b2q_rows_to_heads_f32": (I, [P, I64, I64, I64, I64, I, I64, P, P, P]),
             "b2q_attention_f32": (I, [P, P, P, I64, I64, I64, I64, I64, P, P, I64, ctypes.c_float, P, I64, P]),
@@ -454,6 +456,21 @@ def rows_to_heads(src, B: int, T: int, H: int, D: int, parts: int = 1, stream=No
     rc = lib().b2q_rows_to_heads(_ptr(src), B, T, H, D, parts, src.stride(0) * 4, _ptr(outs[0]),
                                  _ptr(outs[1]) if parts == 2 else None, _stream(stream))
     _check("b2q_rows_to_heads", rc)
+    return outs
+
+
+def mul_mat_prepared_heads(packed, n: int, k: int, act, B: int, T: int, H: int, D: int = 64, bias=None,
+                           stream=None):
+    """mul_mat_prepared (+ bias) straight into fp16 attention heads: n = parts*H*D
+    output columns -> parts tensors [B, H, T, D], the bytes of mul_mat_prepared
+    followed by rows_to_heads.  Tensor-core path only (B*T > 8, D = 64)."""
+    torch = _torch()
+    parts = n // (H * D)
+    outs = [torch.empty((B, H, T, D), dtype=torch.float16, device=act.device) for _ in range(parts)]
+    rc = lib().b2q_mul_mat_prepared_heads_f16(_ptr(packed), n, k, _ptr(act), B * T, _ptr(bias), B, T, H, D, parts,
+                                              _ptr(outs[0]), _ptr(outs[1]) if parts == 2 else None,
+                                              _stream(stream))
+    _check("b2q_mul_mat_prepared_heads_f16", rc)
     return outs
 
 

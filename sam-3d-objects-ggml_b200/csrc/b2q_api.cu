@@ -652,6 +652,39 @@ int b2q_mul_mat_prepared_gate_residual(const void* packed, int64_t n, int64_t k,
   return from_cuda(launch_gemm_tc(g, sms, static_cast<cudaStream_t>(stream)));
 }
 
+int b2q_mul_mat_prepared_heads_f16(const void* packed, int64_t n, int64_t k, const void* act, int64_t m,
+                                   const float* bias, int64_t B, int64_t T, int64_t H, int64_t D, int parts,
+                                   void* out0, void* out1, void* stream) {
+  if (n < 0 || m < 0 || k <= 0 || k % kQK != 0 || B < 0 || T < 0 || H <= 0) return B2Q_ERR_INVALID_ARG;
+  if (parts != 1 && parts != 2) return B2Q_ERR_INVALID_ARG;
+  if (D != 64) return B2Q_ERR_UNSUPPORTED;
+  if (n != parts * H * D || m != B * T) return B2Q_ERR_INVALID_ARG;
+  if (n > INT_MAX || m > INT_MAX || k > INT_MAX || H > INT_MAX) return B2Q_ERR_TOO_LARGE;
+  if (m > 0 && (!packed || !act || !out0 || (parts == 2 && !out1))) return B2Q_ERR_INVALID_ARG;
+  if (m > 0 && m <= kGemvMaxM) return B2Q_ERR_UNSUPPORTED;  // few tokens: b2q_mul_mat_prepared + b2q_rows_to_heads
+  if (!aligned(packed, 256) || !aligned(act, 256) || !aligned(out0, 2) || (out1 && !aligned(out1, 2)) ||
+      (bias && !aligned(bias, 4)))
+    return B2Q_ERR_MISALIGNED;
+  if (m == 0) return B2Q_OK;
+  int sms = 0;
+  if (int rc = check_device(&sms)) return rc;
+  GemmArgs g;
+  g.w = split_at(static_cast<uint8_t*>(const_cast<void*>(packed)), n, k);
+  g.a = split_at(static_cast<uint8_t*>(const_cast<void*>(act)), m, k);
+  g.M = m;
+  g.N = n;
+  g.K = k;
+  g.y = nullptr;
+  g.ldy = n;
+  g.bias = bias;
+  g.dots = nullptr;
+  g.heads[0] = out0;
+  g.heads[1] = parts == 2 ? out1 : nullptr;
+  g.heads_T = T;
+  g.heads_H = static_cast<int>(H);
+  return from_cuda(launch_gemm_tc(g, sms, static_cast<cudaStream_t>(stream)));
+}
+
 int b2q_gelu(const float* x, int64_t rows, int64_t cols, int64_t x_row_stride_bytes, float* y,
              int64_t y_row_stride_bytes, void* stream) {
   if (rows < 0 || cols < 0) return B2Q_ERR_INVALID_ARG;

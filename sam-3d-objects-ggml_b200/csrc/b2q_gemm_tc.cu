@@ -151,6 +151,7 @@ enum Mode : int {
   kModeGateRes = 5, // y = resid + gate * (w . x + bias): the DiT branch's gated residual
   kModeGeluQ8Peers = 6,  // column-parallel GELU + Q8_0: the quantized tile goes into every rank's activations
   kModeStoreTma = 7,     // as plain, each epilogue warp's part of the tile leaves by one TMA store
+  kModeHeadsF16 = 8,     // as plain, each output rounded to fp16 into its attention head's [T][64] rows
 };
 
 // Output arguments of the non-plain variants, a separate kernel parameter:
@@ -179,6 +180,9 @@ struct OutParams {
   const float* resid;
   int64_t ldr;
   int64_t q_code_off, q_scale_off;
+  __half* heads[2];  // heads tile end: the [B][H][T][64] fp16 outputs of column parts 0 and 1
+  int64_t heads_T;
+  int heads_H;
 };
 
 // Shared-memory descriptor for the constant offset tile: K-major, no swizzle,
@@ -327,6 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ CUtensorMap tm_y, const TcParams p, const __grid_constant__ OutParams pp) {
   constexpr bool DUMP = MODE == kModeDump, PEERS = MODE == kModePeers, STALL = MODE == kModeStall;
   constexpr bool TST = MODE == kModeStoreTma;
+  constexpr bool HEADS = MODE == kModeHeadsF16;
   static_assert(!(TST && Q4C), "the compact Q4_0 stages leave no room for the store boxes");
   constexpr bool PQ = MODE == kModeGeluQ8Peers;
   constexpr bool GELUQ = MODE == kModeGeluQ8 || PQ, GATERES = MODE == kModeGateRes;
@@ -563,9 +568,39 @@ __global__ void __launch_bounds__(kThreads, 1)
           phase ^= 1u;
         }
       }
-      if (!ok || (!GELUQ && !p.y)) continue;
+      if (!ok || (!GELUQ && !HEADS && !p.y)) continue;
       const int64_t n = static_cast<int64_t>(tile % p.n_tiles) * kBM + row;
       const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * BN + chalf * COLS;
+      if (HEADS) {
+        // Column n is dimension d of head h of part `part` (the cross-attention's
+        // q, or its k | v): bias added as the plain tile end adds it (one fp32
+        // rounding), then one fp16 rounding as b2q_rows_to_heads stores it.  For
+        // each token the warp's 32 lanes write 32 consecutive halves of one row.
+        if (n < p.N && m0 < p.M) {
+          const int64_t C = static_cast<int64_t>(pp.heads_H) * 64;
+          const int part = n >= C ? 1 : 0;
+          const int64_t nc = n - part * C;
+          const int64_t T = pp.heads_T;
+          __half* base = pp.heads[part] + (nc >> 6) * T * 64 + (nc & 63);
+          const int64_t b = m0 / T;
+          int64_t t = m0 - b * T;
+          int64_t off = (b * pp.heads_H * T + t) * 64;  // of token m0
+          const float bv = p.bias ? p.bias[n] : 0.0f;
+          const float2 b2 = make_float2(bv, bv), one = make_float2(1.0f, 1.0f);
+#pragma unroll
+          for (int c = 0; c < COLS; ++c) {
+            if (m0 + c >= p.M) break;
+            if ((c & 1) == 0) acc[c / 2] = ffma2(acc[c / 2], one, b2);
+            base[off] = __float2half_rn((c & 1) ? acc[c / 2].y : acc[c / 2].x);
+            off += 64;
+            if (++t == T) {  // the next token is the next sequence's first
+              t = 0;
+              off += (static_cast<int64_t>(pp.heads_H) - 1) * T * 64;
+            }
+          }
+        }
+        continue;
+      }
       if (TST) {
         // The warp's 32 rows x COLS tokens go through its own box in shared
         // memory and leave by one TMA store, so the next tile's blocks start at
@@ -750,6 +785,10 @@ cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
   pp.gate = g.gate;
   pp.resid = g.resid;
   pp.ldr = g.ldr;
+  pp.heads[0] = static_cast<__half*>(g.heads[0]);
+  pp.heads[1] = static_cast<__half*>(g.heads[1]);
+  pp.heads_T = g.heads_T;
+  pp.heads_H = g.heads_H;
   CUtensorMap tm_y{};
   if constexpr (MODE == kModeStoreTma) {
     // y as [M][ldy] fp32, one box = one epilogue warp's 32 rows x COLS tokens.
@@ -759,7 +798,8 @@ cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
       return launch_cfg<STAGES, BN, kModePlain, Q4C>(g, num_sms, s);
   }
   auto kern = gemm_tc_kernel<STAGES, BN, MODE, Q4C>;
-  constexpr int smem_bytes = (MODE == kModeGeluQ8 || MODE == kModeGeluQ8Peers) ? C::SMEM_XPOSE
+  constexpr bool GELUQ = MODE == kModeGeluQ8 || MODE == kModeGeluQ8Peers;
+  constexpr int smem_bytes = GELUQ ? C::SMEM_XPOSE
                              : MODE == kModeStoreTma                           ? C::SMEM_STO
                                                                                : C::SMEM;
   static_assert(smem_bytes <= 227 * 1024, "shared memory per CTA");
@@ -851,6 +891,11 @@ cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, cudaStream_t s) {
   if (g.q_peers) {  // column-parallel GELU + Q8_0: q_code_off, q_scale_off and q_k describe the buffers
     if (g.N % kQK != 0 || g.q_k % kQK != 0 || g.n_peers < 1) return cudaErrorInvalidValue;
     return launch_picked<kModeGeluQ8Peers>(g, num_sms, s);
+  }
+  if (g.heads[0]) {  // tensor-core tiles only (the caller checks the shape)
+    if (g.M <= kGemvMaxM || g.resid || g.n_peers > 0 || g.heads_T <= 0 || g.heads_H <= 0)
+      return cudaErrorInvalidValue;
+    return launch_picked<kModeHeadsF16>(g, num_sms, s);
   }
   // A handful of tokens: the weight streamed once on CUDA cores, same bits.
   if (g.M <= kGemvMaxM && g.n_peers == 0) return launch_gemv(g, s);

@@ -206,6 +206,12 @@ struct GemmArgs {
   // Compact Q4_0 weights (q4c.nibbles != nullptr): w is unused; the kernel reads
   // the nibble blocks and fp16 scales and widens them on chip.
   Q4cWeight q4c = {nullptr, nullptr, 0};
+  // Attention-head tile end (heads[0] != nullptr): instead of y, column
+  // n = part*H*64 + h*64 + d of token m = b*heads_T + t goes, rounded to fp16,
+  // to heads[part][((b*H + h)*heads_T + t)*64 + d] (N = parts*H*64).
+  void* heads[2] = {nullptr, nullptr};
+  int64_t heads_T = 0;
+  int heads_H = 0;
 };
 cudaError_t launch_gemm_tc(const GemmArgs& args, int num_sms, cudaStream_t s);
 // 2-D tensor map (cuTensorMapEncodeTiled through the runtime's driver entry point).

@@ -182,11 +182,22 @@ class SsFlow:
     def _cross(self, g: str, i: int, x, B: int, T: int, act_c, n_cond: int):
         C, H, D, p = self.C, self.H, self.D, f"b{i}.{g}."
         act = b2q.layer_norm_q8(x, EPS, self.V[p + "n2w"], self.V[p + "n2b"])
-        xq = b2q.mul_mat_prepared(self.W[p + "xq"], C, C, act, B * T, bias=self.V[p + "xq.b"])
-        xkv = b2q.mul_mat_prepared(self.W[p + "xkv"], 2 * C, C, act_c, B * n_cond, bias=self.V[p + "xkv.b"])
-        heads = b2q.rows_to_heads_f32 if self.attn == "f32" else b2q.rows_to_heads
-        (q,) = heads(xq, B, T, H, D, 1)
-        k, v = heads(xkv, B, n_cond, H, D, 2)
+        if self.attn == "f16" and D == 64:
+            # the projections' tile ends write the fp16 heads (the few-token q keeps
+            # the two-step form: its GEMM runs on the CUDA cores)
+            if B * T > b2q.GEMV_MAX_M:
+                (q,) = b2q.mul_mat_prepared_heads(self.W[p + "xq"], C, C, act, B, T, H, D, bias=self.V[p + "xq.b"])
+            else:
+                xq = b2q.mul_mat_prepared(self.W[p + "xq"], C, C, act, B * T, bias=self.V[p + "xq.b"])
+                (q,) = b2q.rows_to_heads(xq, B, T, H, D, 1)
+            k, v = b2q.mul_mat_prepared_heads(self.W[p + "xkv"], 2 * C, C, act_c, B, n_cond, H, D,
+                                              bias=self.V[p + "xkv.b"])
+        else:
+            xq = b2q.mul_mat_prepared(self.W[p + "xq"], C, C, act, B * T, bias=self.V[p + "xq.b"])
+            xkv = b2q.mul_mat_prepared(self.W[p + "xkv"], 2 * C, C, act_c, B * n_cond, bias=self.V[p + "xkv.b"])
+            heads = b2q.rows_to_heads_f32 if self.attn == "f32" else b2q.rows_to_heads
+            (q,) = heads(xq, B, T, H, D, 1)
+            k, v = heads(xkv, B, n_cond, H, D, 2)
         self._attn_out(g, i, self._attend(q, k, v), x, None, "xout")
 
     def _mlp(self, g: str, i: int, x, scale, shift, gate):

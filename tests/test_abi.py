@@ -221,6 +221,16 @@ def test_attention_io_validation(b2q_mod):
     assert r2h(FAKE + 2, 2, 8, 4, 64, 1, 4 * 64 * 4, FAKE, None, None) == 3              # src alignment
     assert r2h(FAKE, 2, 8, 4, 64, 1, 4 * 64 * 4, FAKE + 1, None, None) == 3              # out alignment
     assert r2h(FAKE, 0, 8, 4, 64, 1, 4 * 64 * 4, FAKE, None, None) == 0                  # empty: no-op
+    mh = L.b2q_mul_mat_prepared_heads_f16
+    assert mh(FAKE, 512, 256, FAKE, 32, None, 2, 16, 4, 64, 3, FAKE, FAKE, None) == 1     # parts > 2
+    assert mh(FAKE, 512, 256, FAKE, 32, None, 2, 16, 4, 64, 2, FAKE, None, None) == 1     # parts 2, null out1
+    assert mh(FAKE, 500, 256, FAKE, 32, None, 2, 16, 4, 64, 2, FAKE, FAKE, None) == 1     # n != parts*H*D
+    assert mh(FAKE, 512, 256, FAKE, 30, None, 2, 16, 4, 64, 2, FAKE, FAKE, None) == 1     # m != B*T
+    assert mh(FAKE, 256, 256, FAKE, 32, None, 2, 16, 8, 32, 1, FAKE, None, None) == 2     # D != 64
+    assert mh(FAKE, 512, 256, FAKE, 8, None, 2, 4, 4, 64, 2, FAKE, FAKE, None) == 2       # few tokens
+    assert mh(FAKE + 16, 512, 256, FAKE, 32, None, 2, 16, 4, 64, 2, FAKE, FAKE, None) == 3  # weight alignment
+    assert mh(FAKE, 512, 256, FAKE, 32, None, 2, 16, 4, 64, 2, FAKE + 1, FAKE, None) == 3  # out alignment
+    assert mh(FAKE, 512, 256, FAKE, 0, None, 0, 16, 4, 64, 2, FAKE, FAKE, None) == 0      # empty: no-op
     need = L.b2q_act_prepared_size(16, 256)
     assert hq(FAKE, 2, 8, 4, 48, 0, 0, 0, 0, FAKE, need, None) == 1                       # D % 32
     assert hq(FAKE, 2, 8, 4, 64, -1, 0, 0, 0, FAKE, need, None) == 1                      # negative stride

@@ -76,6 +76,33 @@ def test_rows_to_heads_is_fp16_transpose(dev, parts, D):
         assert np.array_equal(got.cpu().numpy().view(np.uint16), np.ascontiguousarray(want).view(np.uint16))
 
 
+@pytest.mark.parametrize("parts,B,T,H,wtype", [(1, 2, 300, 16, O.TYPE_Q8_0),   # cross q: token tiles cross a sequence
+                                                (2, 2, 1374, 16, O.TYPE_Q8_0),  # k | v of the condition tokens
+                                                (2, 1, 45, 4, O.TYPE_Q4_0),     # one sequence, ragged last tile
+                                                (1, 3, 9, 2, O.TYPE_Q8_0)])     # sequences shorter than a tile
+def test_mul_mat_heads_equals_two_steps(dev, parts, B, T, H, wtype):
+    """The projection's tile end writing fp16 heads: the same bytes as
+    mul_mat_prepared (+ bias) followed by rows_to_heads, with and without a bias."""
+    import torch
+    D, K = 64, 256
+    N, M = parts * H * D, B * T
+    rng = np.random.default_rng(100 + parts * T)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    bias = (0.1 * rng.standard_normal(N)).astype(np.float32)
+    packed = b2q.weight_pack(wtype, to_dev(O.quantize(w, wtype), dev), K)
+    act = b2q.act_prepare(to_dev(x, dev))
+    for bb in (None, to_dev(bias, dev)):
+        y = b2q.mul_mat_prepared(packed, N, K, act, M, bias=bb)
+        want = b2q.rows_to_heads(y, B, T, H, D, parts)
+        got = b2q.mul_mat_prepared_heads(packed, N, K, act, B, T, H, D, bias=bb)
+        torch.cuda.synchronize()
+        assert len(got) == parts
+        for g, wnt in zip(got, want):
+            assert tuple(g.shape) == (B, H, T, D)
+            assert np.array_equal(g.cpu().numpy().view(np.uint16), wnt.cpu().numpy().view(np.uint16))
+
+
 @pytest.mark.parametrize("variant", [0, 1])
 def test_layer_norm_q8_matches_oracle(dev, variant):
     """gb_layer_norm (ggml_norm, * weight, + bias) with the Q8_0 quantize of
