@@ -115,8 +115,9 @@ struct Cfg {
   static constexpr int STAGE_BYTES = (SWH_OFF + SWH_BYTES + 1023) / 1024 * 1024;  // stage pitch in smem
   static constexpr int OFF_TILE = STAGES * STAGE_BYTES;
   static constexpr int BAR_OFF = OFF_TILE + kOffsetTileBytes;
-  // stage full / empty (+ converted), slot full / empty, MMA drain
-  static constexpr int NBARS = (Q4C ? 3 : 2) * STAGES + 2 * SLOTS + 1;
+  // stage full / empty (+ converted), slot full / empty, MMA drain, one
+  // residual-box barrier per epilogue warp
+  static constexpr int NBARS = (Q4C ? 3 : 2) * STAGES + 2 * SLOTS + 1 + kEpiWarps;
   static constexpr int SMEM = BAR_OFF + NBARS * 8 + 16 + 1024;  // + alignment slack
   // GELU + Q8_0 variant only: a 32 x 33 fp32 transpose buffer per epilogue warp.
   static constexpr int XPOSE_OFF = (BAR_OFF + NBARS * 8 + 16 + 127) / 128 * 128;
@@ -152,6 +153,7 @@ enum Mode : int {
   kModeGeluQ8Peers = 6,  // column-parallel GELU + Q8_0: the quantized tile goes into every rank's activations
   kModeStoreTma = 7,     // as plain, each epilogue warp's part of the tile leaves by one TMA store
   kModeHeadsF16 = 8,     // as plain, each output rounded to fp16 into its attention head's [T][64] rows
+  kModeGateResTma = 9,   // as gate + residual, the residual box loaded and the result box stored by TMA
 };
 
 // Output arguments of the non-plain variants, a separate kernel parameter:
@@ -328,10 +330,13 @@ template <int STAGES, int BN, int MODE, bool Q4C>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_wc, const __grid_constant__ CUtensorMap tm_ac,
                    const __grid_constant__ CUtensorMap tm_ws, const __grid_constant__ CUtensorMap tm_as,
-                   const __grid_constant__ CUtensorMap tm_y, const TcParams p, const __grid_constant__ OutParams pp) {
+                   const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_r, const TcParams p,
+                   const __grid_constant__ OutParams pp) {
   constexpr bool DUMP = MODE == kModeDump, PEERS = MODE == kModePeers, STALL = MODE == kModeStall;
   constexpr bool TST = MODE == kModeStoreTma;
   constexpr bool HEADS = MODE == kModeHeadsF16;
+  constexpr bool GRT = MODE == kModeGateResTma;  // TMA residual box in, TMA result box out
+  static_assert(!(GRT && Q4C), "the compact Q4_0 stages leave no room for the boxes");
   static_assert(!(TST && Q4C), "the compact Q4_0 stages leave no room for the store boxes");
   constexpr bool PQ = MODE == kModeGeluQ8Peers;
   constexpr bool GELUQ = MODE == kModeGeluQ8 || PQ, GATERES = MODE == kModeGateRes;
@@ -347,7 +352,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_empty = acc_full + C::SLOTS;
   uint64_t* mma_done = acc_empty + C::SLOTS;
   uint64_t* conv = mma_done + 1;  // Q4C: the stage's weight codes and scales are widened
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(conv + (Q4C ? STAGES : 0));
+  uint64_t* rbar = conv + (Q4C ? STAGES : 0);  // [kEpiWarps]: each warp's residual box landed
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(rbar + kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   // The MMA and the epilogue read a stage once it is complete: its copies landed
   // and, for compact Q4_0 weights, its codes and scales are widened.
@@ -366,6 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_empty[a], kEpiWarps);  // one arrival per epilogue warp
     }
     mbar_init(mma_done, 1);
+    for (int w = 0; w < kEpiWarps; ++w) mbar_init(&rbar[w], 1);
     if (Q4C)
       for (int st = 0; st < STAGES; ++st) mbar_init(&conv[st], 2);  // the two converter warps
     *abort_flag = 0;
@@ -538,6 +545,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t stage = 0, phase = 0;
     uint32_t slot = 0, sphase = 0;  // accumulator slot and its parity, as the MMA issuer's
     bool ok = true;
+    // GRT: this warp's box, its residual barrier's parity, a residual load in flight.
+    float* rbox = reinterpret_cast<float*>(smem + C::STO_OFF) + (warp - kEpiWarp0) * C::STO_WARP_FLOATS;
+    uint64_t* my_rbar = &rbar[warp - kEpiWarp0];
+    uint32_t rphase = 0;
+    bool rpending = false;
     for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
 #pragma unroll
       for (int c = 0; c < COLS / 2; ++c) acc[c] = make_float2(0.0f, 0.0f);
@@ -566,6 +578,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1u;
+        }
+        if (GRT && ks == 0) {
+          // The tile's residual box is fetched once the first stage is done (the
+          // previous tile's result box has long left it by then).
+          const int rnq = (tile % p.n_tiles) * kBM + quarter * 32;
+          const int rm0 = (tile / p.n_tiles) * BN + chalf * COLS;
+          if (rnq < p.N && rm0 < p.M) {
+            if (lane == 0) {
+              bulk_wait_read_all();  // the previous result box has been read out
+              mbar_arrive_expect_tx(my_rbar, C::STO_WARP_FLOATS * 4);
+              tma_load_2d(rbox, &tm_r, my_rbar, rnq, rm0);
+            }
+            rpending = true;
+          }
         }
       }
       if (!ok || (!GELUQ && !HEADS && !p.y)) continue;
@@ -597,6 +623,40 @@ __global__ void __launch_bounds__(kThreads, 1)
               t = 0;
               off += (static_cast<int64_t>(pp.heads_H) - 1) * T * 64;
             }
+          }
+        }
+        continue;
+      }
+      if (GRT) {
+        // y = resid + gate * (w.x + bias) as the gate + residual tile end rounds
+        // it (bias by the packed FMA, __fmul_rn by the row's gate, __fadd_rn of
+        // the residual), with the residual read from the warp's box (TMA-loaded
+        // during the tile) and the result written back into it for one TMA store.
+        // y may be the residual itself: each box is read before it is stored.
+        const int64_t rnq = static_cast<int64_t>(tile % p.n_tiles) * kBM + quarter * 32;
+        if (rnq < p.N && m0 < p.M) {
+          if (!__all_sync(0xffffffffu, mbar_wait(my_rbar, rphase, &g_device_status, kDevWaitEpilogue, abort_flag))) {
+            ok = false;
+            continue;
+          }
+          rphase ^= 1u;
+          rpending = false;
+          const float bv = p.bias ? p.bias[n] : 0.0f;
+          const float gv = pp.gate ? pp.gate[n] : 1.0f;
+          const float2 b2 = make_float2(bv, bv), one = make_float2(1.0f, 1.0f);
+#pragma unroll
+          for (int c = 0; c < COLS / 2; ++c) {
+            const float2 h = ffma2(acc[c], one, b2);
+            const float t0 = pp.gate ? __fmul_rn(h.x, gv) : h.x;
+            const float t1 = pp.gate ? __fmul_rn(h.y, gv) : h.y;
+            rbox[(2 * c) * 32 + lane] = __fadd_rn(rbox[(2 * c) * 32 + lane], t0);
+            rbox[(2 * c + 1) * 32 + lane] = __fadd_rn(rbox[(2 * c + 1) * 32 + lane], t1);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tm_y, rbox, static_cast<int32_t>(rnq), static_cast<int32_t>(m0));
+            bulk_commit();
           }
         }
         continue;
@@ -695,7 +755,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    if (TST && lane == 0) bulk_wait_all();  // the warp's stores complete before the CTA exits
+    // A residual load still in flight (a wait gave up) lands before the CTA exits.
+    if (GRT && rpending) mbar_wait(my_rbar, rphase, &g_device_status, kDevWaitDrain, nullptr);
+    if ((TST || GRT) && lane == 0) bulk_wait_all();  // the warp's stores complete before the CTA exits
   }
 
   tc_fence_before();
@@ -789,7 +851,7 @@ cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
   pp.heads[1] = static_cast<__half*>(g.heads[1]);
   pp.heads_T = g.heads_T;
   pp.heads_H = g.heads_H;
-  CUtensorMap tm_y{};
+  CUtensorMap tm_y{}, tm_r{};
   if constexpr (MODE == kModeStoreTma) {
     // y as [M][ldy] fp32, one box = one epilogue warp's 32 rows x COLS tokens.
     // A shape the map cannot describe takes the plain tile end instead.
@@ -797,10 +859,18 @@ cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
                      CU_TENSOR_MAP_SWIZZLE_NONE))
       return launch_cfg<STAGES, BN, kModePlain, Q4C>(g, num_sms, s);
   }
+  if constexpr (MODE == kModeGateResTma) {
+    // y and the residual as [M][ld] fp32, the same boxes; else the global-memory form.
+    if (!make_map_2d(&tm_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, g.y, g.N, g.M, g.ldy * 4, 32, C::COLS,
+                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map_2d(&tm_r, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, g.resid, g.N, g.M, g.ldr * 4, 32, C::COLS,
+                     CU_TENSOR_MAP_SWIZZLE_NONE))
+      return launch_cfg<STAGES, BN, kModeGateRes, Q4C>(g, num_sms, s);
+  }
   auto kern = gemm_tc_kernel<STAGES, BN, MODE, Q4C>;
   constexpr bool GELUQ = MODE == kModeGeluQ8 || MODE == kModeGeluQ8Peers;
   constexpr int smem_bytes = GELUQ ? C::SMEM_XPOSE
-                             : MODE == kModeStoreTma                           ? C::SMEM_STO
+                             : (MODE == kModeStoreTma || MODE == kModeGateResTma) ? C::SMEM_STO
                                                                                : C::SMEM;
   static_assert(smem_bytes <= 227 * 1024, "shared memory per CTA");
   // Checked and set once per device (a bit per device; the calls cost more
@@ -819,7 +889,7 @@ cudaError_t launch_cfg(const GemmArgs& g, int num_sms, cudaStream_t s) {
     ready.fetch_or(bit, std::memory_order_acq_rel);
   }
   const int grid = p.num_tiles < num_sms ? p.num_tiles : num_sms;
-  kern<<<grid, kThreads, smem_bytes, s>>>(tm_wc, tm_ac, tm_ws, tm_as, tm_y, p, pp);
+  kern<<<grid, kThreads, smem_bytes, s>>>(tm_wc, tm_ac, tm_ws, tm_as, tm_y, tm_r, p, pp);
   return cudaGetLastError();
 }
 
@@ -899,7 +969,13 @@ cudaError_t launch_gemm_tc(const GemmArgs& g, int num_sms, cudaStream_t s) {
   }
   // A handful of tokens: the weight streamed once on CUDA cores, same bits.
   if (g.M <= kGemvMaxM && g.n_peers == 0) return launch_gemv(g, s);
-  if (g.resid) return launch_picked<kModeGateRes>(g, num_sms, s);
+  if (g.resid) {
+    // TMA boxes when y's and the residual's rows are 16-byte aligned and whole 32-row boxes.
+    if (g.y && reinterpret_cast<uintptr_t>(g.y) % 16 == 0 && g.ldy % 4 == 0 &&
+        reinterpret_cast<uintptr_t>(g.resid) % 16 == 0 && g.ldr % 4 == 0 && g.N % 32 == 0)
+      return launch_picked<kModeGateResTma>(g, num_sms, s);
+    return launch_picked<kModeGateRes>(g, num_sms, s);
+  }
   if (g.n_peers > 0) return launch_picked<kModePeers>(g, num_sms, s);
   // TMA-stored tile ends when y's rows are 16-byte aligned and whole 32-row boxes.
   if (g.y && reinterpret_cast<uintptr_t>(g.y) % 16 == 0 && g.ldy % 4 == 0 && g.N % 32 == 0)
