@@ -37,8 +37,13 @@
 // measured slower than this single-buffered, release-after-scaling order.
 // K is padded to whole stages (the padding blocks read zero codes and scales
 // through the tensor maps' out-of-bounds fill and add exactly nothing).
-// Output stores: for each token, the 32 threads of a warp write 32 consecutive
-// floats of y's row (128-byte coalesced), bias fused.
+// Output stores, bias fused: when y's rows are 16-byte aligned and N is a
+// multiple of 32, each epilogue warp writes its 32 rows x BN/2 tokens into its
+// own shared-memory box and leaves it by one TMA store (the gate + residual
+// form first TMA-loads the residual box during the tile); otherwise, for each
+// token, the 32 threads of a warp write 32 consecutive floats of y's row
+// (128-byte coalesced).  Other tile ends: GELU + Q8_0 of the next layer's
+// input, fp16 attention heads, the column-parallel peer stores.
 //
 // Roles (384 threads = 3 warpgroups, 1 CTA per SM, persistent over tiles):
 //   warp 0      TMA producer: weight codes [128 x 128B], activation codes
